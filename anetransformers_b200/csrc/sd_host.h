@@ -1,0 +1,16 @@
+// sd_host.h -- host-side helpers shared by the C ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include "sd_internal.h"
+
+namespace sd {
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+void clear_error();
+int device_sm_count(int dev);
+int device_max_smem(int dev);
+int* device_error_word(int dev);
+int check_device_error(int* word, cudaStream_t st);
+int repack_matrix(const uint8_t* aos_dev, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st);
+int run_gemv(int epi, const GemvArgs& a, int dev, cudaStream_t st, bool pdl);
+}  // namespace sd

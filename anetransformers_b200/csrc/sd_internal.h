@@ -1,0 +1,116 @@
+// sd_internal.h -- internal (non-ABI) definitions shared by the CUDA sources of libspecdec_b200.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sd {
+
+// ---------------------------------------------------------------------------------------------
+// Repacked Q4_0 weight layout ("tile16x4") in HBM.
+//
+// A matrix [rows][cols] of 18-byte Q4_0 blocks is stored as row-groups of 16 rows; each row-group
+// as cols/128 tiles ("quads" of 4 consecutive blocks), each tile 1152 bytes:
+//   bytes [0, 1024): nibbles.  Half h (rows 8h..8h+7), lane L = 4*g + t (g = row in half, t = word):
+//                    16 bytes at h*512 + L*16 = word t (qs[4t..4t+3]) of blocks 4q..4q+3 of row 8h+g.
+//   bytes [1024, 1152): fp16 scales, [h][g][blk] -> 8 bytes per row.
+// Each lane of a warp then reads its int8 MMA A-fragment for 4 blocks with two conflict-free 16-byte
+// loads, and one row-group's whole K range is contiguous (cols/128 * 1152 bytes), so a CTA's range of
+// row-groups is one contiguous stream for the bulk-copy engine.
+// ---------------------------------------------------------------------------------------------
+constexpr int kTileRows = 16;
+constexpr int kTileBytes = 1152;
+constexpr int kChunkQuads = 8;                           // tiles per ring stage = consumer warps
+constexpr int kStageBytes = kTileBytes * kChunkQuads;    // 9216
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;  // + 1 producer warp
+constexpr int kMaxStages = 16;
+constexpr int kMaxS = 8;                                 // tokens per forward (n8 MMA tile)
+
+inline size_t qmat_bytes(int rows, int cols) {
+    int n_rg = (rows + kTileRows - 1) / kTileRows;
+    return (size_t)n_rg * (cols / 128) * kTileBytes;
+}
+
+// Row placement used while repacking: destination row of source row r is
+//   (r / unit) * stride + offset + (r % unit)
+struct RowMap {
+    int unit, stride, offset;
+};
+
+// Q8_0 activations on device as planes (codes, fp32 scale, per-block code sum).
+struct Q8Planes {
+    int8_t* qs;     // [S][n]
+    float* d;       // [S][n/32]
+    int32_t* sum;   // [S][n/32]
+};
+
+// Per-forward control block in device memory.  Kernels read positions / valid-token counts from it
+// so a captured CUDA graph replays for any position.
+struct DevCtrl {
+    int pos;          // position of token 0 of this forward
+    int n_valid;      // tokens of this forward that are real (<= S of the launch)
+    int done;         // generation finished: every kernel of an iteration returns immediately
+    int tokens[kMaxS];
+};
+
+enum GemvEpi : int {
+    EPI_STORE = 0,      // out[tok][row] = y
+    EPI_QKV = 1,        // RoPE(q) * 1/sqrt(hd) -> q buffer; RoPE(k), v -> fp16 KV ring
+    EPI_SILU_Q8 = 2,    // h = silu(gate) * up, quantised to Q8_0 planes (gate/up row-groups interleaved)
+    EPI_BLOCKSUMS = 3,  // raw int32 block dot products of token 0 (parity checks)
+};
+
+struct GemvArgs {
+    const uint8_t* w;
+    int n_rg, nq, K;
+    int rg_per_unit, n_units;
+    Q8Planes act;
+    int S;
+    const DevCtrl* ctrl;  // may be null: then all S tokens are valid, pos = 0
+    int* err;
+    int nstage;
+    // EPI_STORE
+    float* out;
+    int out_ld, out_rows;
+    // EPI_QKV
+    float* q_out;         // [S][q_rows]
+    __half* k_cache;      // layer base: [max_seq][kv_rows]
+    __half* v_cache;
+    int q_rows, kv_rows, max_seq, head_dim;
+    const float* theta_inv;
+    float q_scale;
+    // EPI_SILU_Q8
+    Q8Planes h;
+    int hidden;
+    // EPI_BLOCKSUMS
+    int32_t* isum;        // [rows][K/32]
+};
+
+size_t gemv_smem_bytes(int K, int nstage);
+int gemv_pick_stages(int K, int max_smem);
+cudaError_t launch_gemv(int epi, const GemvArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl);
+
+cudaError_t launch_repack(const uint8_t* aos, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st);
+cudaError_t launch_quantize(const float* x, Q8Planes out, int S, int n, cudaStream_t st);
+cudaError_t launch_q8_to_blocks(Q8Planes in, void* blocks, int S, int n, cudaStream_t st);
+cudaError_t launch_blocks_to_q8(const void* blocks, Q8Planes out, int S, int n, cudaStream_t st);
+
+// Residual add + RMSNorm + Q8_0 quantisation of S tokens (one CTA per token).
+//   mode 0: x = embed(tokens) (Q4_0 rows of tok_embd) ; 1: x += y ; 2: x unchanged
+struct NormArgs {
+    float* x;             // [S][dim] residual stream
+    const float* y;       // [S][dim] to add (mode 1)
+    const uint8_t* embd;  // Q4_0 AoS [vocab][dim/32] (mode 0)
+    const float* w;       // [dim] RMSNorm weight
+    Q8Planes out;
+    int dim, S;
+    float eps;
+    const DevCtrl* ctrl;
+    const int* tokens;    // host-independent token ids (mode 0); defaults to ctrl->tokens
+    float* xn_out;        // optional: normalised fp32 output [S][dim]
+};
+cudaError_t launch_norm_quant(int mode, const NormArgs& a, cudaStream_t st, bool pdl);
+
+}  // namespace sd

@@ -1,0 +1,162 @@
+// sd_quant.cu -- Q8_0 activation quantizer, residual add + RMSNorm + quantise, token embedding.
+//
+// Quantizer: mistral/dequant.h:545-599 (bit-exact: IEEE d = amax/127, id = 1/d, RNE, saturate).
+// RMSNorm:   mistral/mistral_model.h:202-208 (s = 1/sqrt(sum(x^2)/dim + eps); out = (x*s)*w).
+// Embedding: Q4_0 row dequant d*((q&15)-8), mistral/mistral_model.h:134-145 (exact).
+// Outputs are Q8 planes: codes [S][n], fp32 scales [S][n/32] and per-block code sums [S][n/32]
+// (the sum feeds the -8*sum accumulator init of the u8 x s8 MMA in the matvec).
+#include "sd_common.cuh"
+
+namespace sd {
+
+// One warp per 32-value block; grid-stride over S * n/32 blocks.
+__global__ void k_quantize(const float* __restrict__ x, Q8Planes out, int S, int n) {
+    const int nb = n >> 5;
+    const int lane = threadIdx.x & 31;
+    const long long wid = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long blk = wid; blk < (long long)S * nb; blk += nw) {
+        const float v = x[blk * 32 + lane];
+        float d;
+        int sum;
+        const int q = q8_quant_lane(v, &d, &sum);
+        out.qs[blk * 32 + lane] = (int8_t)q;
+        if (lane == 0) {
+            out.d[blk] = d;
+            out.sum[blk] = sum;
+        }
+    }
+}
+
+cudaError_t launch_quantize(const float* x, Q8Planes out, int S, int n, cudaStream_t st) {
+    long long blocks = (long long)S * (n / 32);
+    int grid = (int)((blocks * 32 + 255) / 256);
+    if (grid > 4096) grid = 4096;
+    k_quantize<<<grid, 256, 0, st>>>(x, out, S, n);
+    return cudaGetLastError();
+}
+
+// Planes <-> reference AoS block_q8_0 (fp32 d + 32 int8, 36 bytes).
+__global__ void k_q8_to_blocks(Q8Planes in, uint8_t* blocks, long long nblk) {
+    for (long long b = blockIdx.x * (long long)blockDim.x + threadIdx.x; b < nblk; b += (long long)gridDim.x * blockDim.x) {
+        uint8_t* o = blocks + b * 36;
+        float d = in.d[b];
+        memcpy(o, &d, 4);
+        for (int j = 0; j < 32; ++j) o[4 + j] = (uint8_t)in.qs[b * 32 + j];
+    }
+}
+
+__global__ void k_blocks_to_q8(const uint8_t* blocks, Q8Planes out, long long nblk) {
+    for (long long b = blockIdx.x * (long long)blockDim.x + threadIdx.x; b < nblk; b += (long long)gridDim.x * blockDim.x) {
+        const uint8_t* o = blocks + b * 36;
+        float d;
+        memcpy(&d, o, 4);
+        int s = 0;
+        for (int j = 0; j < 32; ++j) {
+            const int8_t q = (int8_t)o[4 + j];
+            out.qs[b * 32 + j] = q;
+            s += q;
+        }
+        out.d[b] = d;
+        out.sum[b] = s;
+    }
+}
+
+cudaError_t launch_q8_to_blocks(Q8Planes in, void* blocks, int S, int n, cudaStream_t st) {
+    long long nblk = (long long)S * (n / 32);
+    int grid = (int)((nblk + 255) / 256);
+    k_q8_to_blocks<<<grid > 4096 ? 4096 : grid, 256, 0, st>>>(in, (uint8_t*)blocks, nblk);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_blocks_to_q8(const void* blocks, Q8Planes out, int S, int n, cudaStream_t st) {
+    long long nblk = (long long)S * (n / 32);
+    int grid = (int)((nblk + 255) / 256);
+    k_blocks_to_q8<<<grid > 4096 ? 4096 : grid, 256, 0, st>>>((const uint8_t*)blocks, out, nblk);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------
+// Residual add / embed + RMSNorm + Q8_0 quantisation, one CTA (256 threads) per token.
+// Warp w owns blocks w, w+8, ...; lane j owns element j of each block, so the sum of squares is
+// accumulated in a fixed order per lane, reduced by a butterfly within the warp and then across the
+// 8 warps in order -- identical for every S (batch invariant).
+// ---------------------------------------------------------------------------------------------
+constexpr int kNormThreads = 256;
+
+template <int MODE>
+__global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
+    __shared__ float wsum[kNormThreads / 32];
+    const int tok = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (a.ctrl && a.ctrl->done) return;
+    pdl_trigger();
+    pdl_wait();
+    const int nv = a.ctrl ? min(a.ctrl->n_valid, a.S) : a.S;
+    if (tok >= nv) return;
+    const int nb = a.dim >> 5;
+    float* x = a.x + (size_t)tok * a.dim;
+
+    float ss = 0.f;
+    if constexpr (MODE == 0) {
+        const int token = a.tokens ? a.tokens[tok] : a.ctrl->tokens[tok];
+        const uint8_t* row = a.embd + (size_t)token * nb * 18;
+        for (int b = warp; b < nb; b += kNormThreads / 32) {
+            const uint8_t* blk = row + (size_t)b * 18;
+            const float dd = __half2float(__ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8))));
+            const uint8_t byte = blk[2 + (lane & 15)];
+            const int q = (lane < 16) ? (byte & 0x0F) : (byte >> 4);
+            const float v = dd * ((float)q - 8.0f);
+            x[b * 32 + lane] = v;
+            ss = fmaf(v, v, ss);
+        }
+    } else {
+        for (int b = warp; b < nb; b += kNormThreads / 32) {
+            float v = x[b * 32 + lane];
+            if constexpr (MODE == 1) {
+                v = v + a.y[(size_t)tok * a.dim + b * 32 + lane];
+                x[b * 32 + lane] = v;
+            }
+            ss = fmaf(v, v, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) wsum[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) tot += wsum[w];
+    const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)a.dim) + a.eps));
+
+    for (int b = warp; b < nb; b += kNormThreads / 32) {
+        const float xn = (x[b * 32 + lane] * s) * a.w[b * 32 + lane];
+        if (a.xn_out) a.xn_out[(size_t)tok * a.dim + b * 32 + lane] = xn;
+        float d;
+        int sum;
+        const int q = q8_quant_lane(xn, &d, &sum);
+        a.out.qs[(size_t)tok * a.dim + b * 32 + lane] = (int8_t)q;
+        if (lane == 0) {
+            a.out.d[(size_t)tok * nb + b] = d;
+            a.out.sum[(size_t)tok * nb + b] = sum;
+        }
+    }
+}
+
+cudaError_t launch_norm_quant(int mode, const NormArgs& a, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.S);
+    cfg.blockDim = dim3(kNormThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    switch (mode) {
+        case 0: return cudaLaunchKernelEx(&cfg, k_norm_quant<0>, a);
+        case 1: return cudaLaunchKernelEx(&cfg, k_norm_quant<1>, a);
+        default: return cudaLaunchKernelEx(&cfg, k_norm_quant<2>, a);
+    }
+}
+
+}  // namespace sd

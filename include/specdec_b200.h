@@ -1,0 +1,226 @@
+/*
+ * specdec_b200.h -- C ABI of libspecdec_b200.so, the B200 (sm_100a) implementation of the
+ * speculative-decode hot path of m0at/ANEtransformers (Mistral-architecture Q4_0 models).
+ *
+ * Plain C: opaque handles, plain pointers and sizes, int status codes.  No CUDA, torch or C++
+ * types appear in any signature (a CUDA stream is passed as void*; NULL = the legacy default
+ * stream).  "_dev" entry points take device pointers and are stream-ordered; the others take host
+ * pointers and return when their results are in host memory.
+ *
+ * Each declaration names the reference interface it replaces (path:line in the reference repo).
+ * The reference has no ABI of its own -- every hot-path symbol is a `static` function in a header
+ * compiled as one translation unit (mistral/Makefile:11-14) -- so the drop-in for those headers is
+ * include/compat/{dequant.h,speculative.h,metal_matvec.h}, whose inline bodies call the functions
+ * below.
+ */
+#ifndef SPECDEC_B200_H
+#define SPECDEC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SD_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SD_API __attribute__((visibility("default")))
+#else
+#define SD_API
+#endif
+
+/* Status codes.  The reference reports failure as NULL / -1 plus a stderr line
+ * (e.g. metal_alloc_batch_buffers, mistral/metal_matvec.h:253-293); this ABI keeps 0 = success and
+ * negative = failure, with a message from sd_last_error(). */
+enum {
+    SD_OK = 0,
+    SD_ERR_INVALID = -1,      /* bad argument / unsupported shape */
+    SD_ERR_OOM = -2,          /* device or host allocation failed */
+    SD_ERR_CUDA = -3,         /* CUDA runtime error */
+    SD_ERR_TIMEOUT = -4,      /* a bounded device wait ran out (device error word set) */
+    SD_ERR_FORMAT = -5,       /* malformed GGUF / unsupported tensor type */
+    SD_ERR_UNSUPPORTED = -6,  /* feature not available in this build or configuration */
+    SD_ERR_NO_DEVICE = -7     /* no CUDA device */
+};
+
+/* Last error message of the calling thread ("" if none). */
+SD_API const char *sd_last_error(void);
+SD_API int sd_abi_version(void);
+/* Number of visible CUDA devices (0 without a GPU; never fails). */
+SD_API int sd_device_count(void);
+
+/* Reference block layouts: mistral/dequant.h:17-21 (18-byte Q4_0, fp16 scale bits) and
+ * mistral/dequant.h:537-541 (36-byte Q8_0 with an fp32 scale). */
+typedef struct { uint16_t d; uint8_t qs[16]; } sd_block_q4_0;
+typedef struct { float d; int8_t qs[32]; } sd_block_q8_0;
+
+/* ======================================================================================
+ * Single-op layer: Q8_0 quantizer and W4A8 matvec
+ * ====================================================================================== */
+
+/* Device-resident Q4_0 matrix, repacked from the reference's AoS blocks into the 16-row tile
+ * layout the matvec streams.  rows % 16 == 0 is not required (padded); cols % 1024 == 0. */
+typedef struct sd_qmat sd_qmat;
+
+/* q4_0_host: [rows][cols/32] sd_block_q4_0 in host memory (e.g. an mmap'd GGUF tensor). */
+SD_API int sd_qmat_create(const void *q4_0_host, int rows, int cols, int device, sd_qmat **out);
+SD_API void sd_qmat_free(sd_qmat *m);
+SD_API int sd_qmat_shape(const sd_qmat *m, int *rows, int *cols, size_t *device_bytes);
+
+/* Q8_0 activations for S rows of n values in device memory, as three planes:
+ *   qs [S][n] int8 codes, d [S][n/32] fp32 scales, sum [S][n/32] int32 (sum of the 32 codes). */
+typedef struct { int8_t *qs; float *d; int32_t *sum; } sd_q8_dev;
+
+/* Replaces quantize_f32_to_q8_0 (mistral/dequant.h:545-599) for S rows; bit-exact codes and scales.
+ * x: device [S][n] fp32, n % 32 == 0. */
+SD_API int sd_quantize_q8_0_dev(const float *x, sd_q8_dev out, int S, int n, void *stream);
+/* Planes <-> reference AoS blocks (device buffers of S*n/32 sd_block_q8_0). */
+SD_API int sd_q8_to_blocks_dev(sd_q8_dev in, sd_block_q8_0 *out, int S, int n, void *stream);
+SD_API int sd_blocks_to_q8_dev(const sd_block_q8_0 *in, sd_q8_dev out, int S, int n, void *stream);
+
+/* Replaces q4_0_q8_0_matvec_sdot_parallel (mistral/dequant.h:1022-1137) for S <= 8 activation
+ * rows sharing one weight read (the S=K+1 verify shape of mistral/mistral_infer.m:134-164).
+ * y: device [S][rows] fp32. */
+SD_API int sd_matvec_q4_0_q8_0_dev(const sd_qmat *W, sd_q8_dev x, float *y, int S, void *stream);
+
+/* Exact int32 block dot products of activation row 0: isum[r][b] = sum_j (q_j - 8) * x8_j, the
+ * per-block SDOT result of mistral/dequant.h:1078-1083.  isum: device [rows][cols/32]. */
+SD_API int sd_block_sums_dev(const sd_qmat *W, sd_q8_dev x, int32_t *isum, void *stream);
+
+/* Host-pointer drop-ins with the reference signatures (mistral/dequant.h:545 and :1022).  They run
+ * on the current device; the matvec uploads and repacks W on first use and caches it keyed by the
+ * host address and shape (weights are immutable mmap'd tensors in the reference).  Errors are
+ * reported on stderr and through sd_last_error(); y is left unchanged on failure. */
+SD_API void sd_host_quantize_f32_to_q8_0(const float *x, sd_block_q8_0 *out, int n);
+SD_API void sd_host_q4_0_q8_0_matvec(const void *W, const sd_block_q8_0 *x, float *y, int out_dim, int in_dim);
+/* Drop the host-drop-in weight cache (frees its device copies). */
+SD_API void sd_host_cache_clear(void);
+
+/* ======================================================================================
+ * Model context: weights in HBM, fp16 KV ring, verify / decode forward, generation loops
+ * ====================================================================================== */
+
+typedef struct sd_ctx sd_ctx;
+
+typedef struct {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, head_dim, vocab_size;
+    int max_seq;          /* KV ring slots (--context, mistral/mistral_infer.m:518-523) */
+    float rope_theta, rms_eps;
+    int bos_id, eos_id;
+    int tp_rank, tp_size;
+    size_t weight_bytes;  /* device bytes of repacked weights held by this rank */
+    size_t kv_bytes;      /* device bytes of this rank's KV ring */
+} sd_model_info;
+
+typedef struct {
+    int device;           /* CUDA device ordinal */
+    int max_seq;          /* 0 = 65536, capped at 131072 (mistral/mistral_infer.m:518-523) */
+    int max_batch;        /* tokens per forward, 1..8 (0 = 8) */
+    int tp_rank, tp_size; /* tensor parallelism (tp_size 1 = single GPU) */
+    void *nccl_comm;      /* ncclComm_t for tp_size > 1, created by the caller */
+    int use_graphs;       /* capture per-S forwards in CUDA graphs (default 1) */
+    int use_pdl;          /* programmatic dependent launch between kernels (default 1) */
+} sd_ctx_opts;
+
+SD_API void sd_ctx_opts_default(sd_ctx_opts *o);
+
+/* Replaces metal_context_init (mistral/metal_matvec.h:134-225) + mistral_load
+ * (mistral/mistral_model.h:262-357): parses the GGUF v3 image at gguf_base (the mmap'd file, as
+ * metal_context_init receives it), uploads every tensor and repacks the Q4_0 matrices in HBM,
+ * computes the RoPE inverse frequencies (mistral/mistral_model.h:69-74) and allocates the fp16 KV
+ * ring [n_layers][max_seq][kv_dim] (mistral/kv_cache.h:22-35) and per-forward buffers
+ * (metal_alloc_batch_buffers, mistral/metal_matvec.h:253-293). */
+SD_API int sd_ctx_create(const void *gguf_base, size_t gguf_len, const sd_ctx_opts *opts, sd_ctx **out);
+SD_API int sd_ctx_create_file(const char *gguf_path, const sd_ctx_opts *opts, sd_ctx **out);
+/* Replaces metal_context_free (mistral/metal_matvec.h:540-565). */
+SD_API void sd_ctx_free(sd_ctx *ctx);
+SD_API int sd_ctx_info(const sd_ctx *ctx, sd_model_info *out);
+/* Read and clear the context's device error word (non-zero after a bounded wait ran out). */
+SD_API int sd_ctx_device_error(sd_ctx *ctx);
+/* Stream the context launches on (cudaStream_t as void*). */
+SD_API void *sd_ctx_stream(sd_ctx *ctx);
+
+/* Forward S tokens at positions pos..pos+S-1 through all layers (writing their K/V into the ring)
+ * and the LM head.  Replaces metal_forward (S=1, mistral/mistral_infer.m:31-92),
+ * metal_forward_batch (S=K+1, :103-179) with the CPU logits of metal_spec_verify (:224-248), and
+ * spec_verify (mistral/speculative.h:81-105).  logits: host [S][vocab] or NULL; argmax: host [S]
+ * (first index on ties, mistral/mistral_model.h:1136-1143) or NULL.  S <= max_batch. */
+SD_API int sd_forward(sd_ctx *ctx, const int32_t *tokens, int S, int pos, float *logits, int32_t *argmax);
+/* Same with device buffers, stream-ordered, no host synchronisation. */
+SD_API int sd_forward_dev(sd_ctx *ctx, const int32_t *tokens_dev, int S, int pos, float *logits_dev,
+                   int32_t *argmax_dev, void *stream);
+/* Prefill n prompt tokens at positions start_pos.. in chunks of max_batch (fills the KV ring). */
+SD_API int sd_prefill(sd_ctx *ctx, const int32_t *tokens, int n, int start_pos);
+/* First n_layers layers only (self-speculative drafter depth); same contract as sd_forward. */
+SD_API int sd_forward_layers(sd_ctx *ctx, int n_layers, const int32_t *tokens, int S, int pos, float *logits,
+                      int32_t *argmax);
+/* Copy n ring slots [pos0, pos0+n) of one layer's K and V (fp16 bits) to host buffers
+ * [n][kv_dim_local].  The ring itself lives in HBM (mistral/kv_cache.h layout). */
+SD_API int sd_kv_read(sd_ctx *ctx, int layer, int pos0, int n, uint16_t *k, uint16_t *v);
+
+/* ======================================================================================
+ * Speculative primitives on the device
+ * ====================================================================================== */
+
+/* Replaces ngram_draft_fn (mistral/speculative.h:425-464): earliest exact match of
+ * history[hlen-n+1..hlen-1] ++ [current] among history[i..i+n-1], i in [0, hlen-n-1]; drafts
+ * history[match+n ..] up to max_draft.  Runs as a device scan.  Returns the draft count (>= 0) or
+ * a negative status; *match_pos gets the match start + n (or -1). */
+SD_API int sd_ngram_draft(const int32_t *history, int hlen, int ngram_n, int max_draft, int current,
+                   int32_t *draft_out, int *match_pos);
+
+/* Replaces spec_accept (mistral/speculative.h:121-198) on the device.  logits: host
+ * [n_draft+1][vocab] (row n_draft is the bonus row the callers use, speculative.h:312-317).
+ * temp <= 0: greedy; else the Leviathan et al. rule with the seeded Philox stream (seed, *counter),
+ * advanced in *counter.  bonus_mode: 0 = argmax bonus at temp 0 (fixed), 1 = the reference's
+ * uniform draw.  accepted: host [n_draft+1].  Returns n_accepted in [1, n_draft+1] or < 0. */
+SD_API int sd_spec_accept(sd_ctx *ctx, const float *draft_probs, const float *logits, const int32_t *draft,
+                   int n_draft, float temp, int bonus_mode, uint64_t seed, uint64_t *counter,
+                   int32_t *accepted);
+
+/* ======================================================================================
+ * Generation loops (mistral/mistral_infer.m:579-716, speculative.h:217-379)
+ * ====================================================================================== */
+enum { SD_GEN_GREEDY = 0, SD_GEN_NGRAM = 1, SD_GEN_SELF_SPEC = 2 };
+enum { SD_BONUS_ARGMAX = 0, SD_BONUS_REFERENCE = 1 };
+
+typedef struct {
+    int mode;                 /* SD_GEN_* */
+    int max_tokens;           /* --tokens */
+    float temp, top_p;        /* --temp, --top-p */
+    int top_k;                /* --top-k */
+    float rep_penalty;        /* --rep-penalty */
+    int rep_window;           /* --rep-window */
+    int ignore_eos;
+    int spec_k;               /* drafts per iteration (<= 7 with max_batch 8) */
+    int ngram_n;              /* n-gram order */
+    int draft_layers;         /* self-speculative drafter depth */
+    int history_has_current;  /* 1 = reference n-gram wiring (history ends with the current token) */
+    int bonus_mode;           /* SD_BONUS_* */
+    uint64_t seed;            /* Philox seed replacing arc4random */
+} sd_gen_params;
+
+typedef struct {
+    int n_generated;
+    int64_t total_draft, total_accepted, total_iterations;
+    double ms_prefill, ms_decode;
+} sd_gen_stats;
+
+SD_API void sd_gen_params_default(sd_gen_params *p);
+
+/* Prefill the prompt, sample the first token, then decode.  out_tokens receives the generated
+ * tokens (first token included); returns their count (<= out_cap) or a negative status. */
+SD_API int sd_generate(sd_ctx *ctx, const sd_gen_params *p, const int32_t *prompt, int n_prompt,
+                int32_t *out_tokens, int out_cap, sd_gen_stats *stats);
+
+/* Decode only (the prompt already prefilled into positions [0, n_prompt)): starts from
+ * first_token at position n_prompt with the drafter history = history[0..n_hist). */
+SD_API int sd_decode(sd_ctx *ctx, const sd_gen_params *p, const int32_t *history, int n_hist, int first_token,
+              int32_t *out_tokens, int out_cap, sd_gen_stats *stats);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPECDEC_B200_H */
