@@ -24,9 +24,9 @@ enum : int {
     DEV_ERR_PEER_WAIT = 4,     // a cross-GPU flag wait gave up
 };
 
-// ~2^26 polls of try_wait (each try_wait itself blocks for a hardware-defined window) is seconds;
+// 2^24 polls of try_wait (each poll may itself block for a short hardware-defined window): seconds,
 // far beyond any legitimate wait in these kernels.
-constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint32_t kSpinLimit = 1u << 24;
 
 __device__ __forceinline__ void set_dev_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);

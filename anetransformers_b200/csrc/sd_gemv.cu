@@ -150,13 +150,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
     // ---------------- main loop ----------------
     float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
     int sidx = 0;
+    // A stage that never arrives (only possible if the producer gave up) marks the warp aborted: it
+    // stops waiting and computing but still takes part in every named barrier, so no warp is left
+    // waiting on a barrier a returned warp would never reach.  Every stage issued before the give-up
+    // has been waited for, so no bulk copy is in flight when the CTA exits.
+    bool aborted = false;
     for (int rg = rg0; rg < rg1; ++rg) {
         for (int ch = 0; ch < cpr; ++ch, ++sidx) {
             const int slot = sidx % nstage;
-            if (!mbar_wait(&full[slot], (sidx / nstage) & 1)) {
+            if (!aborted && !mbar_wait(&full[slot], (sidx / nstage) & 1)) {
                 set_dev_error(a.err, DEV_ERR_FULL_WAIT);
-                return;
+                aborted = true;
             }
+            if (aborted) continue;
             const uint8_t* tile = ring + (size_t)slot * kStageBytes + warp * kTileBytes;
             const uint4 wl = *reinterpret_cast<const uint4*>(tile + lane * 16);
             const uint4 wh = *reinterpret_cast<const uint4*>(tile + 512 + lane * 16);
