@@ -21,17 +21,20 @@ namespace sd {
 // ---------------------------------------------------------------------------------------------
 constexpr int kTileRows = 16;
 constexpr int kTileBytes = 1152;
-constexpr int kChunkQuads = 8;                           // tiles per ring stage = consumer warps
-constexpr int kStageBytes = kTileBytes * kChunkQuads;    // 9216
-constexpr int kConsumerWarps = 8;
-constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;  // + 1 producer warp
+constexpr int kConsumerWarps = 16;                       // one tile of each row-group per ring stage
+constexpr int kEpiWarps = 2;                             // reduce + epilogue, one row-group each
+constexpr int kGemvThreads = (kConsumerWarps + kEpiWarps + 1) * 32;  // + 1 producer warp
+constexpr int kRedSlots = 2;                             // row-group pairs in flight to the epilogue
 constexpr int kMaxStages = 16;
 constexpr int kMaxS = 8;                                 // tokens per forward (n8 MMA tile)
+constexpr int kRPW = 2;                                  // row-groups per warp per stage (share B fragments)
 
-inline size_t qmat_bytes(int rows, int cols) {
+// Row-groups are allocated in whole pairs (a zero row-group pads an odd count).
+inline int qmat_row_groups(int rows) {
     int n_rg = (rows + kTileRows - 1) / kTileRows;
-    return (size_t)n_rg * (cols / 128) * kTileBytes;
+    return (n_rg + kRPW - 1) / kRPW * kRPW;
 }
+inline size_t qmat_bytes(int rows, int cols) { return (size_t)qmat_row_groups(rows) * (cols / 128) * kTileBytes; }
 
 // Row placement used while repacking: destination row of source row r is
 //   (r / unit) * stride + offset + (r % unit)
@@ -70,7 +73,11 @@ struct GemvArgs {
     int S;
     const DevCtrl* ctrl;  // may be null: then all S tokens are valid, pos = 0
     int* err;
-    int nstage;
+    int nstage;           // ring stages (each: chunk tiles of each row-group of a pair)
+    int chunk;            // tiles per stage per row-group = consumer warps with tiles: min(16, nq/kparts)
+    int kparts;           // K split into kparts slices (EPI_STORE / EPI_BLOCKSUMS only); CTAs
+                          // [p*G/kparts, (p+1)*G/kparts) handle slice p and write out + p*part_stride
+    size_t part_stride;   // floats between the partial outputs of consecutive K slices
     // EPI_STORE
     float* out;
     int out_ld, out_rows;
@@ -88,9 +95,11 @@ struct GemvArgs {
     int32_t* isum;        // [rows][K/32]
 };
 
-size_t gemv_smem_bytes(int K, int nstage);
-int gemv_pick_stages(int K, int max_smem);
+size_t gemv_smem_bytes(int Kp, int S, int chunk, int nstage);
+int gemv_pick_stages(int Kp, int S, int chunk, int max_smem);
+inline int gemv_chunk(int nq_part) { return nq_part >= kConsumerWarps ? kConsumerWarps : nq_part; }
 cudaError_t launch_gemv(int epi, const GemvArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl);
+cudaError_t launch_sum_parts(const float* parts, float* out, int n, int kparts, size_t stride, cudaStream_t st);
 
 cudaError_t launch_repack(const uint8_t* aos, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st);
 cudaError_t launch_quantize(const float* x, Q8Planes out, int S, int n, cudaStream_t st);

@@ -98,19 +98,62 @@ int repack_matrix(const uint8_t* aos_dev, int rows, int cols, RowMap map, uint8_
     return SD_OK;
 }
 
-int run_gemv(int epi, const GemvArgs& base, int dev, cudaStream_t st, bool pdl) {
-    GemvArgs a = base;
+int gemv_plan(GemvArgs& a, int dev, int* grid_out, size_t* smem_out) {
     if (a.K % 1024 != 0 || a.K <= 0) return fail(SD_ERR_INVALID, "matvec: in_dim %d is not a multiple of 1024", a.K);
     if (a.S < 1 || a.S > kMaxS) return fail(SD_ERR_INVALID, "matvec: S=%d outside 1..%d", a.S, kMaxS);
     const int max_smem = device_max_smem(dev);
-    if (a.nstage <= 0) a.nstage = gemv_pick_stages(a.K, max_smem);
-    if (a.nstage < 2) return fail(SD_ERR_INVALID, "matvec: in_dim %d does not fit shared memory", a.K);
-    const size_t smem = gemv_smem_bytes(a.K, a.nstage);
-    int grid = device_sm_count(dev);
-    if (grid > a.n_units) grid = a.n_units;
+    const int sms = device_sm_count(dev);
+    const int want = a.kparts;  // <= 0: choose, 1: forced single slice
+    int best = -1;
+    for (int kp = 1; kp <= a.nq; ++kp) {
+        if (a.nq % kp) continue;
+        if (want > 0 && kp != want) continue;
+        const int nqp = a.nq / kp, ch = gemv_chunk(nqp);
+        if (nqp % ch) continue;
+        if (kp > sms) break;
+        const int ns = gemv_pick_stages(nqp * 128, a.S, ch, max_smem);
+        if (ns >= 3 || (want > 0 && ns >= 2)) {
+            best = kp;
+            a.chunk = ch;
+            a.nstage = ns;
+            break;
+        }
+    }
+    if (best < 0) return fail(SD_ERR_INVALID, "matvec: in_dim %d / S=%d has no shared-memory plan", a.K, a.S);
+    a.kparts = best;
+    *smem_out = gemv_smem_bytes(a.K / best, a.S, a.chunk, a.nstage);
+    int grid = sms;
+    if (grid > a.n_units * best) grid = a.n_units * best;
+    *grid_out = grid;
+    return SD_OK;
+}
+
+int run_gemv(int epi, const GemvArgs& base, int dev, cudaStream_t st, bool pdl) {
+    GemvArgs a = base;
+    int grid;
+    size_t smem;
+    int rc = gemv_plan(a, dev, &grid, &smem);
+    if (rc) return rc;
     cudaError_t e = launch_gemv(epi, a, grid, smem, st, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
     return SD_OK;
+}
+
+// Grow-only per-device workspace for partial outputs of K-split single-op matvecs.
+float* op_workspace(int dev, size_t floats) {
+    static float* ws[64] = {nullptr};
+    static size_t cap[64] = {0};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (cap[dev] < floats) {
+        cudaFree(ws[dev]);
+        ws[dev] = nullptr;
+        cap[dev] = 0;
+        if (cudaMalloc(&ws[dev], floats * sizeof(float)) != cudaSuccess) return nullptr;
+        cap[dev] = floats;
+    }
+    return ws[dev];
 }
 
 }  // namespace sd
@@ -200,22 +243,41 @@ int sd_blocks_to_q8_dev(const sd_block_q8_0* in, sd_q8_dev out, int S, int n, vo
 static int matvec_common(int epi, const sd_qmat* W, sd_q8_dev x, float* y, int32_t* isum, int S, void* stream) {
     if (!W || !x.qs || !x.d || !x.sum) return fail(SD_ERR_INVALID, "matvec: null argument");
     int dev = W->device;
+    cudaStream_t st = (cudaStream_t)stream;
     GemvArgs a = {};
     a.w = W->w;
-    a.n_rg = (W->rows + kTileRows - 1) / kTileRows;
+    a.n_rg = qmat_row_groups(W->rows);
     a.nq = W->cols / 128;
     a.K = W->cols;
-    a.rg_per_unit = 1;
-    a.n_units = a.n_rg;
+    a.rg_per_unit = kRPW;
+    a.n_units = a.n_rg / kRPW;
     a.act = Q8Planes{x.qs, x.d, x.sum};
     a.S = S;
     a.ctrl = nullptr;
     a.err = device_error_word(dev);
-    a.out = y;
     a.out_ld = W->rows;
     a.out_rows = W->rows;
     a.isum = isum;
-    return run_gemv(epi, a, dev, (cudaStream_t)stream, false);
+    a.kparts = 0;
+    int grid;
+    size_t smem;
+    int rc = gemv_plan(a, dev, &grid, &smem);
+    if (rc) return rc;
+    const size_t n_out = (size_t)S * W->rows;
+    float* parts = nullptr;
+    if (epi == EPI_STORE) {
+        if (a.kparts > 1) {
+            parts = op_workspace(dev, n_out * a.kparts);
+            if (!parts) return fail(SD_ERR_OOM, "matvec workspace");
+            a.out = parts;
+            a.part_stride = n_out;
+        } else {
+            a.out = y;
+        }
+    }
+    cudaError_t e = launch_gemv(epi, a, grid, smem, st, false);
+    if (e == cudaSuccess && parts) e = launch_sum_parts(parts, y, (int)n_out, a.kparts, n_out, st);
+    return e == cudaSuccess ? SD_OK : cuda_fail(e, "matvec launch");
 }
 
 int sd_matvec_q4_0_q8_0_dev(const sd_qmat* W, sd_q8_dev x, float* y, int S, void* stream) {
