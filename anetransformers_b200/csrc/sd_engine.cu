@@ -1,0 +1,1151 @@
+// sd_engine.cu -- model context: GGUF parsing, weight upload + repack, KV ring, the S-token forward
+// (captured in CUDA graphs with programmatic dependent launch between kernels) and the device-driven
+// generation loops, behind the C ABI of include/specdec_b200.h.
+//
+// Forward of S tokens at positions pos..pos+S-1 (mistral/mistral_model.h:818-899 per token,
+// batched like metal_forward_batch, mistral/mistral_infer.m:103-179):
+//   embed + RMSNorm + Q8_0            k_norm_quant<0>
+//   per layer:
+//     QKV matvec + RoPE + KV write    k_gemv<EPI_QKV>      (Wq|Wk|Wv stacked rows)
+//     GQA attention + Q8_0            k_attn_partial, k_attn_combine
+//     o-proj matvec                   k_gemv<EPI_STORE>    (K-split partials)
+//     [TP: all-reduce]
+//     residual + RMSNorm + Q8_0       k_norm_quant<1>
+//     gate|up matvec + SiLU + Q8_0    k_gemv<EPI_SILU_Q8>  (gate/up row-groups interleaved)
+//     down matvec                     k_gemv<EPI_STORE>
+//     [TP: all-reduce]
+//     residual + next RMSNorm + Q8_0  k_norm_quant<1>
+//   LM head                           k_gemv<EPI_STORE>, k_argmax
+// Every kernel reads the position and valid-token count from a device control block, so one graph per
+// S replays for any position; every kernel is batch invariant, so a token's logits in an S=K+1 verify
+// are bit-identical to its S=1 decode logits.
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include "sd_attn.h"
+#include "sd_common.cuh"
+#include "sd_host.h"
+#include "sd_spec.h"
+#include "specdec_b200.h"
+
+using namespace sd;
+
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// GGUF v3 (the format mistral/gguf_loader.h:148-325 reads)
+// ---------------------------------------------------------------------------------------------
+struct GTensor {
+    std::string name;
+    uint32_t type;
+    uint64_t ne[4];
+    uint32_t nd;
+    uint64_t off;  // absolute byte offset in the image
+};
+
+struct GGUF {
+    const uint8_t* base = nullptr;
+    size_t len = 0;
+    int dim = 0, hidden = 0, n_layers = 0, n_heads = 0, n_kv = 0, vocab = 0, ctx_len = 0;
+    float theta = 10000.f, eps = 1e-5f;
+    int bos = 1, eos = 2;
+    std::vector<GTensor> t;
+    const GTensor* find(const std::string& n) const {
+        for (auto& x : t)
+            if (x.name == n) return &x;
+        return nullptr;
+    }
+};
+
+struct Rd {
+    const uint8_t* b;
+    size_t pos, len;
+    bool ok = true;
+    bool need(size_t n) {
+        if (pos + n > len) ok = false;
+        return ok;
+    }
+    uint64_t u(int n) {
+        if (!need(n)) return 0;
+        uint64_t v = 0;
+        memcpy(&v, b + pos, n);
+        pos += n;
+        return v;
+    }
+    float f32() {
+        uint32_t v = (uint32_t)u(4);
+        float f;
+        memcpy(&f, &v, 4);
+        return f;
+    }
+    double f64() {
+        uint64_t v = u(8);
+        double d;
+        memcpy(&d, &v, 8);
+        return d;
+    }
+    std::string str() {
+        uint64_t n = u(8);
+        if (!need(n)) return std::string();
+        std::string s((const char*)b + pos, n);
+        pos += n;
+        return s;
+    }
+};
+
+enum { GV_U8 = 0, GV_I8, GV_U16, GV_I16, GV_U32, GV_I32, GV_F32, GV_BOOL, GV_STR, GV_ARR, GV_U64, GV_I64, GV_F64 };
+
+int gv_size(uint32_t t) {
+    switch (t) {
+        case GV_U8: case GV_I8: case GV_BOOL: return 1;
+        case GV_U16: case GV_I16: return 2;
+        case GV_U32: case GV_I32: case GV_F32: return 4;
+        case GV_U64: case GV_I64: case GV_F64: return 8;
+    }
+    return -1;
+}
+
+double gv_num(Rd& r, uint32_t t) {
+    switch (t) {
+        case GV_U8: case GV_BOOL: return (double)(uint8_t)r.u(1);
+        case GV_I8: return (double)(int8_t)r.u(1);
+        case GV_U16: return (double)(uint16_t)r.u(2);
+        case GV_I16: return (double)(int16_t)r.u(2);
+        case GV_U32: return (double)(uint32_t)r.u(4);
+        case GV_I32: return (double)(int32_t)r.u(4);
+        case GV_U64: return (double)r.u(8);
+        case GV_I64: return (double)(int64_t)r.u(8);
+        case GV_F32: return (double)r.f32();
+        case GV_F64: return r.f64();
+    }
+    r.ok = false;
+    return 0;
+}
+
+void gv_skip(Rd& r, uint32_t t, int depth = 0) {
+    if (depth > 4) { r.ok = false; return; }
+    if (t == GV_STR) { r.str(); return; }
+    if (t == GV_ARR) {
+        uint32_t at = (uint32_t)r.u(4);
+        uint64_t n = r.u(8);
+        int sz = gv_size(at);
+        if (sz > 0) {
+            if (r.need(n * sz)) r.pos += n * sz;
+            return;
+        }
+        for (uint64_t i = 0; i < n && r.ok; ++i) gv_skip(r, at, depth + 1);
+        return;
+    }
+    int sz = gv_size(t);
+    if (sz < 0) { r.ok = false; return; }
+    if (r.need(sz)) r.pos += sz;
+}
+
+bool key_is(const std::string& k, const char* suffix) {
+    return k == std::string("llama.") + suffix || k == std::string("mistral.") + suffix;
+}
+
+int gguf_parse(const void* base, size_t len, GGUF& g) {
+    Rd r{(const uint8_t*)base, 0, len};
+    g.base = (const uint8_t*)base;
+    g.len = len;
+    if (r.u(4) != 0x46554747u) return fail(SD_ERR_FORMAT, "not a GGUF file");
+    uint32_t ver = (uint32_t)r.u(4);
+    if (ver < 2) return fail(SD_ERR_FORMAT, "GGUF version %u unsupported", ver);
+    uint64_t n_t = r.u(8), n_kv = r.u(8);
+    if (!r.ok || n_t > 100000 || n_kv > 100000) return fail(SD_ERR_FORMAT, "GGUF header truncated");
+    for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
+        std::string k = r.str();
+        uint32_t vt = (uint32_t)r.u(4);
+        if (key_is(k, "embedding_length")) g.dim = (int)gv_num(r, vt);
+        else if (key_is(k, "feed_forward_length")) g.hidden = (int)gv_num(r, vt);
+        else if (key_is(k, "block_count")) g.n_layers = (int)gv_num(r, vt);
+        else if (key_is(k, "attention.head_count")) g.n_heads = (int)gv_num(r, vt);
+        else if (key_is(k, "attention.head_count_kv")) g.n_kv = (int)gv_num(r, vt);
+        else if (key_is(k, "context_length")) g.ctx_len = (int)gv_num(r, vt);
+        else if (key_is(k, "rope.freq_base")) g.theta = (float)gv_num(r, vt);
+        else if (key_is(k, "attention.layer_norm_rms_epsilon")) g.eps = (float)gv_num(r, vt);
+        else if (k == "tokenizer.ggml.bos_token_id") g.bos = (int)gv_num(r, vt);
+        else if (k == "tokenizer.ggml.eos_token_id") g.eos = (int)gv_num(r, vt);
+        else if (k == "tokenizer.ggml.tokens" && vt == GV_ARR) {
+            size_t save = r.pos;
+            uint32_t at = (uint32_t)r.u(4);
+            uint64_t n = r.u(8);
+            (void)at;
+            g.vocab = (int)n;
+            r.pos = save;
+            gv_skip(r, vt);
+        } else gv_skip(r, vt);
+    }
+    for (uint64_t i = 0; i < n_t && r.ok; ++i) {
+        GTensor t;
+        t.name = r.str();
+        t.nd = (uint32_t)r.u(4);
+        if (t.nd > 4) return fail(SD_ERR_FORMAT, "tensor %s: %u dims", t.name.c_str(), t.nd);
+        for (int d = 0; d < 4; ++d) t.ne[d] = 1;
+        for (uint32_t d = 0; d < t.nd; ++d) t.ne[d] = r.u(8);
+        t.type = (uint32_t)r.u(4);
+        t.off = r.u(8);
+        g.t.push_back(t);
+    }
+    if (!r.ok) return fail(SD_ERR_FORMAT, "GGUF metadata truncated");
+    const size_t data_start = (r.pos + 31) / 32 * 32;   // gguf_loader.h:280-281
+    for (auto& t : g.t) {
+        t.off += data_start;
+        uint64_t nel = t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3];
+        uint64_t bytes = t.type == 2 ? nel / 32 * 18 : t.type == 0 ? nel * 4 : t.type == 1 ? nel * 2 : 0;
+        if (bytes == 0 || t.off + bytes > len) return fail(SD_ERR_FORMAT, "tensor %s out of range", t.name.c_str());
+    }
+    if (g.dim <= 0 || g.n_layers <= 0 || g.n_heads <= 0 || g.n_kv <= 0 || g.hidden <= 0)
+        return fail(SD_ERR_FORMAT, "GGUF lacks model hyper-parameters");
+    if (g.vocab <= 0) {
+        const GTensor* e = g.find("token_embd.weight");
+        if (e) g.vocab = (int)e->ne[1];
+    }
+    return SD_OK;
+}
+
+struct LayerW {
+    uint8_t *qkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr;
+    float *rms_att = nullptr, *rms_ffn = nullptr;
+};
+
+struct Plan {  // a matvec launch configuration
+    GemvArgs a;
+    int grid = 0;
+    size_t smem = 0;
+};
+
+}  // namespace
+
+struct sd_ctx {
+    int dev = 0;
+    cudaStream_t st = nullptr;
+    bool use_graphs = true, use_pdl = true;
+    // model
+    int dim, hidden, n_layers, n_heads, n_kv, hd, vocab, max_seq, bos, eos;
+    float theta, eps;
+    int tp_rank = 0, tp_size = 1;
+    int nh_l, nkv_l, q_rows, kv_rows, hid_l, qkv_rows;
+    int MB;  // max tokens per forward
+    std::vector<LayerW> L;
+    uint8_t* embd = nullptr;
+    uint8_t* lm = nullptr;
+    float *rms_final = nullptr, *theta_inv = nullptr;
+    __half *kc = nullptr, *vc = nullptr;      // [n_layers][max_seq][kv_rows]
+    __half *dkc = nullptr, *dvc = nullptr;    // self-spec drafter KV [draft_layers][max_seq][kv_rows]
+    int draft_layers_alloc = 0;
+    size_t weight_bytes = 0, kv_bytes = 0;
+    // buffers
+    float* x = nullptr;        // [MB][dim]
+    float* y = nullptr;        // [ypart][MB][dim]
+    int ypart_max = 8;
+    Q8Planes act{}, hact{};
+    float* q = nullptr;        // [MB][q_rows]
+    float2* part_ml = nullptr;
+    float* part_acc = nullptr;
+    int attn_chunk = 64, max_chunks = 0;
+    float* logits = nullptr;   // [MB][vocab]
+    float* probs = nullptr;    // [vocab]
+    int* argmax = nullptr;     // [MB]
+    DevCtrl* ctrl = nullptr;   // verify / decode forward
+    DevCtrl* dctrl = nullptr;  // self-spec drafter chain
+    DevCtrl* ctrl_h = nullptr; // pinned staging
+    int* err = nullptr;
+    int32_t* tok_h = nullptr;  // pinned token staging
+    // generation
+    GenState* gs = nullptr;
+    GenState* gs_h = nullptr;
+    int* g_out = nullptr;
+    int* g_hist = nullptr;
+    int g_cap = 0;
+    // graphs
+    cudaGraphExec_t fwd_graph[kMaxS + 1] = {};
+    cudaGraphExec_t iter_graph = nullptr;
+    int iter_key[6] = {-1, -1, -1, -1, -1, -1};
+    GenParamsDev iter_p{};
+    unsigned long long rng_start = 1ull << 20;  // Philox counter the next decode loop starts from
+    // TP
+    void* nccl = nullptr;
+};
+
+namespace {
+
+int ck(cudaError_t e, const char* what) { return e == cudaSuccess ? SD_OK : cuda_fail(e, what); }
+
+#define CK(expr, what)                                   \
+    do {                                                 \
+        int _rc = ck((expr), (what));                    \
+        if (_rc) return _rc;                             \
+    } while (0)
+
+template <class T>
+int dalloc(T** p, size_t n, size_t* acc = nullptr) {
+    cudaError_t e = cudaMalloc((void**)p, n * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    if (acc) *acc += n * sizeof(T);
+    return SD_OK;
+}
+
+// Upload AoS rows [r0, r0+rows) x column blocks [cb0, cb0 + cols/32) of a GGUF Q4_0 tensor and repack
+// them into dst at the rows given by map.
+int upload_q4(sd_ctx* c, const GGUF& g, const GTensor* t, int r0, int rows, int cb0, int cols, RowMap map,
+              uint8_t* dst, uint8_t* staging, size_t staging_bytes) {
+    if (!t || t->type != 2) return fail(SD_ERR_FORMAT, "tensor %s missing or not Q4_0", t ? t->name.c_str() : "?");
+    const size_t row_bytes = (size_t)t->ne[0] / 32 * 18;
+    const uint8_t* src = g.base + t->off + (size_t)r0 * row_bytes;
+    // contiguous rows (whole width) are uploaded once; column slices upload the needed row span
+    const size_t span = (size_t)rows * row_bytes;
+    if (span > staging_bytes) return fail(SD_ERR_INVALID, "staging buffer too small");
+    CK(cudaMemcpyAsync(staging, src, span, cudaMemcpyHostToDevice, c->st), "weight upload");
+    CK(launch_repack(staging + (size_t)cb0 * 18, rows, cols, row_bytes, map, dst, c->st), "repack");
+    CK(cudaStreamSynchronize(c->st), "repack");
+    return SD_OK;
+}
+
+int upload_f32(sd_ctx* c, const GGUF& g, const char* name, float** out, int n) {
+    const GTensor* t = g.find(name);
+    if (!t || t->type != 0 || (int)(t->ne[0] * t->ne[1]) != n) return fail(SD_ERR_FORMAT, "tensor %s missing or not F32[%d]", name, n);
+    int rc = dalloc(out, n, &c->weight_bytes);
+    if (rc) return rc;
+    CK(cudaMemcpy(*out, g.base + t->off, (size_t)n * 4, cudaMemcpyHostToDevice), "upload");
+    return SD_OK;
+}
+
+int build_plan(sd_ctx* c, Plan& p, int epi, const uint8_t* w, int rows, int K, int rg_per_unit, int S, int kparts) {
+    GemvArgs& a = p.a;
+    a = GemvArgs{};
+    a.w = w;
+    a.n_rg = qmat_row_groups(rows);
+    a.nq = K / 128;
+    a.K = K;
+    a.rg_per_unit = rg_per_unit;
+    a.n_units = a.n_rg / rg_per_unit;
+    a.S = S;
+    a.kparts = kparts;
+    a.out_rows = rows;
+    a.err = c->err;
+    return gemv_plan(a, c->dev, &p.grid, &p.smem);
+}
+
+int launch_plan(sd_ctx* c, int epi, Plan& p) {
+    cudaError_t e = launch_gemv(epi, p.a, p.grid, p.smem, c->st, c->use_pdl);
+    return e == cudaSuccess ? SD_OK : cuda_fail(e, "matvec launch");
+}
+
+// Enqueue one forward of S (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the
+// position, the tokens and how many of the S are valid.
+int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
+    const bool pdl = c->use_pdl;
+    NormArgs na{};
+    na.x = c->x;
+    na.y = c->y;
+    na.embd = c->embd;
+    na.out = c->act;
+    na.dim = c->dim;
+    na.S = S;
+    na.eps = c->eps;
+    na.ctrl = ctrl;
+    na.w = c->L[0].rms_att;
+    na.yparts = 1;
+    na.ystride = (size_t)c->MB * c->dim;
+    CK(launch_norm_quant(0, na, c->st, pdl), "embed");
+    const size_t kv_layer = (size_t)c->max_seq * c->kv_rows;
+    for (int l = 0; l < n_layers; ++l) {
+        LayerW& W = c->L[l];
+        // QKV + RoPE + KV write
+        Plan pq;
+        int rc = build_plan(c, pq, EPI_QKV, W.qkv, c->qkv_rows, c->dim, kRPW, S, 1);
+        if (rc) return rc;
+        pq.a.act = c->act;
+        pq.a.ctrl = ctrl;
+        pq.a.q_out = c->q;
+        pq.a.k_cache = k + l * kv_layer;
+        pq.a.v_cache = v + l * kv_layer;
+        pq.a.q_rows = c->q_rows;
+        pq.a.kv_rows = c->kv_rows;
+        pq.a.max_seq = c->max_seq;
+        pq.a.head_dim = c->hd;
+        pq.a.theta_inv = c->theta_inv;
+        pq.a.q_scale = 1.0f / sqrtf((float)c->hd);
+        if ((rc = launch_plan(c, EPI_QKV, pq))) return rc;
+        // attention
+        AttnArgs aa{};
+        aa.q = c->q;
+        aa.q_ld = c->q_rows;
+        aa.k = k + l * kv_layer;
+        aa.v = v + l * kv_layer;
+        aa.kv_ld = c->kv_rows;
+        aa.n_heads = c->nh_l;
+        aa.n_kvh = c->nkv_l;
+        aa.S = S;
+        aa.max_seq = c->max_seq;
+        aa.chunk = c->attn_chunk;
+        aa.max_chunks = c->max_chunks;
+        aa.part_ml = c->part_ml;
+        aa.part_acc = c->part_acc;
+        aa.out = c->act;
+        aa.ctrl = ctrl;
+        CK(launch_attention(aa, 2 * device_sm_count(c->dev), c->st, pdl), "attention");
+        // o-proj (K-split partials summed by the next norm)
+        Plan po;
+        if ((rc = build_plan(c, po, EPI_STORE, W.wo, c->dim, c->q_rows, kRPW, S, 0))) return rc;
+        po.a.act = c->act;
+        po.a.ctrl = ctrl;
+        po.a.out = c->y;
+        po.a.out_ld = c->dim;
+        po.a.part_stride = (size_t)c->MB * c->dim;
+        if (po.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "o-proj K split %d too wide", po.a.kparts);
+        if ((rc = launch_plan(c, EPI_STORE, po))) return rc;
+        // TODO(tp): all-reduce of y across ranks goes here
+        na.w = W.rms_ffn;
+        na.yparts = po.a.kparts;
+        CK(launch_norm_quant(1, na, c->st, pdl), "norm");
+        // gate/up + SiLU + Q8_0
+        Plan pg;
+        if ((rc = build_plan(c, pg, EPI_SILU_Q8, W.w13, 2 * c->hid_l, c->dim, 4, S, 1))) return rc;
+        pg.a.act = c->act;
+        pg.a.ctrl = ctrl;
+        pg.a.h = c->hact;
+        pg.a.hidden = c->hid_l;
+        if ((rc = launch_plan(c, EPI_SILU_Q8, pg))) return rc;
+        // down
+        Plan pd;
+        if ((rc = build_plan(c, pd, EPI_STORE, W.w2, c->dim, c->hid_l, kRPW, S, 0))) return rc;
+        pd.a.act = c->hact;
+        pd.a.ctrl = ctrl;
+        pd.a.out = c->y;
+        pd.a.out_ld = c->dim;
+        pd.a.part_stride = (size_t)c->MB * c->dim;
+        if (pd.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "down K split %d too wide", pd.a.kparts);
+        if ((rc = launch_plan(c, EPI_STORE, pd))) return rc;
+        na.w = (l + 1 < n_layers) ? c->L[l + 1].rms_att : c->rms_final;
+        na.yparts = pd.a.kparts;
+        CK(launch_norm_quant(1, na, c->st, pdl), "norm");
+    }
+    if (!logits_and_argmax) return SD_OK;
+    Plan pl;
+    int rc = build_plan(c, pl, EPI_STORE, c->lm, c->vocab, c->dim, kRPW, S, 1);
+    if (rc) return rc;
+    pl.a.act = c->act;
+    pl.a.ctrl = ctrl;
+    pl.a.out = c->logits;
+    pl.a.out_ld = c->vocab;
+    if ((rc = launch_plan(c, EPI_STORE, pl))) return rc;
+    CK(launch_argmax(c->logits, c->vocab, S, c->argmax, ctrl, c->st, pdl), "argmax");
+    return SD_OK;
+}
+
+// Forward graph for S tokens (full depth, target KV, ctrl), built on first use.
+int forward_graph(sd_ctx* c, int S, cudaGraphExec_t* out) {
+    if (c->fwd_graph[S]) {
+        *out = c->fwd_graph[S];
+        return SD_OK;
+    }
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal), "capture");
+    int rc = enqueue_forward(c, S, c->n_layers, c->kc, c->vc, c->ctrl, true);
+    cudaError_t e = cudaStreamEndCapture(c->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "end capture");
+    e = cudaGraphInstantiate(&c->fwd_graph[S], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+    *out = c->fwd_graph[S];
+    return SD_OK;
+}
+
+int run_forward(sd_ctx* c, int S) {
+    if (c->use_graphs) {
+        cudaGraphExec_t ge;
+        int rc = forward_graph(c, S, &ge);
+        if (rc) return rc;
+        CK(cudaGraphLaunch(ge, c->st), "graph launch");
+        return SD_OK;
+    }
+    return enqueue_forward(c, S, c->n_layers, c->kc, c->vc, c->ctrl, true);
+}
+
+int set_ctrl(sd_ctx* c, DevCtrl* dst, const int32_t* tokens, int S, int pos, bool host_tokens) {
+    DevCtrl h{};
+    h.pos = pos;
+    h.n_valid = S;
+    h.done = 0;
+    if (host_tokens)
+        for (int i = 0; i < S; ++i) h.tokens[i] = tokens[i];
+    *c->ctrl_h = h;
+    CK(cudaMemcpyAsync(dst, c->ctrl_h, sizeof(DevCtrl), cudaMemcpyHostToDevice, c->st), "ctrl upload");
+    if (!host_tokens && tokens)
+        CK(cudaMemcpyAsync(&dst->tokens[0], tokens, S * sizeof(int), cudaMemcpyDeviceToDevice, c->st), "tokens");
+    return SD_OK;
+}
+
+int check_tokens(sd_ctx* c, const int32_t* t, int n) {
+    for (int i = 0; i < n; ++i)
+        if (t[i] < 0 || t[i] >= c->vocab) return fail(SD_ERR_INVALID, "token %d out of range [0, %d)", t[i], c->vocab);
+    return SD_OK;
+}
+
+int finish(sd_ctx* c) {
+    CK(cudaStreamSynchronize(c->st), "stream sync");
+    return check_device_error(c->err, c->st);
+}
+
+}  // namespace
+
+// =============================================================================================
+extern "C" {
+
+void sd_ctx_opts_default(sd_ctx_opts* o) {
+    if (!o) return;
+    memset(o, 0, sizeof(*o));
+    o->device = 0;
+    o->max_seq = 0;
+    o->max_batch = 0;
+    o->tp_rank = 0;
+    o->tp_size = 1;
+    o->use_graphs = 1;
+    o->use_pdl = 1;
+}
+
+void sd_ctx_free(sd_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->dev);
+    if (c->st) cudaStreamSynchronize(c->st);
+    for (auto& g : c->fwd_graph)
+        if (g) cudaGraphExecDestroy(g);
+    if (c->iter_graph) cudaGraphExecDestroy(c->iter_graph);
+    for (auto& W : c->L) {
+        cudaFree(W.qkv); cudaFree(W.wo); cudaFree(W.w13); cudaFree(W.w2); cudaFree(W.rms_att); cudaFree(W.rms_ffn);
+    }
+    cudaFree(c->embd); cudaFree(c->lm); cudaFree(c->rms_final); cudaFree(c->theta_inv);
+    cudaFree(c->kc); cudaFree(c->vc); cudaFree(c->dkc); cudaFree(c->dvc);
+    cudaFree(c->x); cudaFree(c->y); cudaFree(c->act.qs); cudaFree(c->act.d); cudaFree(c->act.sum);
+    cudaFree(c->hact.qs); cudaFree(c->hact.d); cudaFree(c->hact.sum); cudaFree(c->q);
+    cudaFree(c->part_ml); cudaFree(c->part_acc); cudaFree(c->logits); cudaFree(c->probs); cudaFree(c->argmax);
+    cudaFree(c->ctrl); cudaFree(c->dctrl); cudaFree(c->err); cudaFree(c->gs); cudaFree(c->g_out); cudaFree(c->g_hist);
+    if (c->ctrl_h) cudaFreeHost(c->ctrl_h);
+    if (c->tok_h) cudaFreeHost(c->tok_h);
+    if (c->gs_h) cudaFreeHost(c->gs_h);
+    if (c->st) cudaStreamDestroy(c->st);
+    delete c;
+}
+
+static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_ctx** out) {
+    clear_error();
+    if (!base || !out) return fail(SD_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (sd_device_count() == 0) return fail(SD_ERR_NO_DEVICE, "no CUDA device");
+    sd_ctx_opts o;
+    sd_ctx_opts_default(&o);
+    if (opts) o = *opts;
+    GGUF g;
+    int rc = gguf_parse(base, len, g);
+    if (rc) return rc;
+    sd_ctx* c = new sd_ctx();
+    c->dev = o.device;
+    c->use_graphs = o.use_graphs != 0;
+    c->use_pdl = o.use_pdl != 0;
+    c->tp_rank = o.tp_rank;
+    c->tp_size = o.tp_size < 1 ? 1 : o.tp_size;
+    c->nccl = o.nccl_comm;
+    c->dim = g.dim; c->hidden = g.hidden; c->n_layers = g.n_layers; c->n_heads = g.n_heads; c->n_kv = g.n_kv;
+    c->hd = g.dim / g.n_heads; c->vocab = g.vocab; c->theta = g.theta; c->eps = g.eps; c->bos = g.bos; c->eos = g.eos;
+    // --context default 65536, capped at 131072 (mistral/mistral_infer.m:518-523)
+    c->max_seq = o.max_seq > 0 ? o.max_seq : 65536;
+    if (c->max_seq > 131072) c->max_seq = 131072;
+    c->MB = (o.max_batch > 0 && o.max_batch <= kMaxS) ? o.max_batch : kMaxS;
+    auto bail = [&](int code) { sd_ctx_free(c); return code; };
+    if (c->hd != 128) return bail(fail(SD_ERR_UNSUPPORTED, "head_dim %d (kernels are built for 128)", c->hd));
+    if (c->n_heads % c->n_kv || c->n_heads / c->n_kv != 4)
+        return bail(fail(SD_ERR_UNSUPPORTED, "GQA ratio %d:%d (kernels are built for 4:1)", c->n_heads, c->n_kv));
+    if (c->n_kv % c->tp_size || c->hidden % (c->tp_size * 32) || c->tp_rank < 0 || c->tp_rank >= c->tp_size)
+        return bail(fail(SD_ERR_INVALID, "tp %d/%d does not divide the model", c->tp_rank, c->tp_size));
+    if (c->tp_size > 1 && !c->nccl) return bail(fail(SD_ERR_INVALID, "tp_size > 1 needs an NCCL communicator"));
+    c->nkv_l = c->n_kv / c->tp_size;
+    c->nh_l = c->nkv_l * 4;
+    c->q_rows = c->nh_l * c->hd;
+    c->kv_rows = c->nkv_l * c->hd;
+    c->qkv_rows = c->q_rows + 2 * c->kv_rows;
+    c->hid_l = c->hidden / c->tp_size;
+    if (c->dim % 1024 || c->q_rows % 1024 || c->hid_l % 1024 || c->hid_l % 64)
+        return bail(fail(SD_ERR_UNSUPPORTED, "dims %d / %d / %d must be multiples of 1024", c->dim, c->q_rows, c->hid_l));
+    if (cudaSetDevice(c->dev) != cudaSuccess) return bail(fail(SD_ERR_INVALID, "bad device %d", c->dev));
+    if ((rc = ck(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking), "stream"))) return bail(rc);
+    if ((rc = gemv_prepare_device(c->dev))) return bail(rc);
+
+    // ---- weights ----
+    size_t stage_bytes = 0;
+    for (auto& t : g.t)
+        if (t.type == 2) stage_bytes = std::max(stage_bytes, (size_t)(t.ne[0] * t.ne[1] / 32 * 18));
+    uint8_t* staging = nullptr;
+    if ((rc = dalloc(&staging, stage_bytes))) return bail(rc);
+    auto cleanup_stage = [&]() { cudaFree(staging); };
+    c->L.resize(c->n_layers);
+    const int r0q = c->tp_rank * c->q_rows, r0kv = c->tp_rank * c->kv_rows, r0h = c->tp_rank * c->hid_l;
+    for (int l = 0; l < c->n_layers && !rc; ++l) {
+        LayerW& W = c->L[l];
+        char nm[128];
+        auto T = [&](const char* f) {
+            snprintf(nm, sizeof nm, f, l);
+            return g.find(nm);
+        };
+        size_t b;
+        b = qmat_bytes(c->qkv_rows, c->dim);
+        if ((rc = dalloc(&W.qkv, b, &c->weight_bytes))) break;
+        cudaMemset(W.qkv, 0, b);
+        if ((rc = upload_q4(c, g, T("blk.%d.attn_q.weight"), r0q, c->q_rows, 0, c->dim, RowMap{c->q_rows, 0, 0}, W.qkv, staging, stage_bytes))) break;
+        if ((rc = upload_q4(c, g, T("blk.%d.attn_k.weight"), r0kv, c->kv_rows, 0, c->dim, RowMap{c->kv_rows, 0, c->q_rows}, W.qkv, staging, stage_bytes))) break;
+        if ((rc = upload_q4(c, g, T("blk.%d.attn_v.weight"), r0kv, c->kv_rows, 0, c->dim, RowMap{c->kv_rows, 0, c->q_rows + c->kv_rows}, W.qkv, staging, stage_bytes))) break;
+        b = qmat_bytes(c->dim, c->q_rows);
+        if ((rc = dalloc(&W.wo, b, &c->weight_bytes))) break;
+        cudaMemset(W.wo, 0, b);
+        if ((rc = upload_q4(c, g, T("blk.%d.attn_output.weight"), 0, c->dim, r0q / 32, c->q_rows, RowMap{c->dim, 0, 0}, W.wo, staging, stage_bytes))) break;
+        b = qmat_bytes(2 * c->hid_l, c->dim);
+        if ((rc = dalloc(&W.w13, b, &c->weight_bytes))) break;
+        cudaMemset(W.w13, 0, b);
+        // gate rows -> row-groups 4u, 4u+1 ; up rows -> 4u+2, 4u+3 (units of 32 hidden units)
+        if ((rc = upload_q4(c, g, T("blk.%d.ffn_gate.weight"), r0h, c->hid_l, 0, c->dim, RowMap{32, 64, 0}, W.w13, staging, stage_bytes))) break;
+        if ((rc = upload_q4(c, g, T("blk.%d.ffn_up.weight"), r0h, c->hid_l, 0, c->dim, RowMap{32, 64, 32}, W.w13, staging, stage_bytes))) break;
+        b = qmat_bytes(c->dim, c->hid_l);
+        if ((rc = dalloc(&W.w2, b, &c->weight_bytes))) break;
+        cudaMemset(W.w2, 0, b);
+        if ((rc = upload_q4(c, g, T("blk.%d.ffn_down.weight"), 0, c->dim, r0h / 32, c->hid_l, RowMap{c->dim, 0, 0}, W.w2, staging, stage_bytes))) break;
+        snprintf(nm, sizeof nm, "blk.%d.attn_norm.weight", l);
+        if ((rc = upload_f32(c, g, nm, &W.rms_att, c->dim))) break;
+        snprintf(nm, sizeof nm, "blk.%d.ffn_norm.weight", l);
+        if ((rc = upload_f32(c, g, nm, &W.rms_ffn, c->dim))) break;
+    }
+    if (!rc) {
+        const GTensor* te = g.find("token_embd.weight");
+        const GTensor* tl = g.find("output.weight");
+        if (!te || te->type != 2 || !tl || tl->type != 2) rc = fail(SD_ERR_FORMAT, "token_embd / output must be Q4_0");
+        if (!rc) {
+            size_t eb = (size_t)c->vocab * c->dim / 32 * 18;
+            if (!(rc = dalloc(&c->embd, eb, &c->weight_bytes)))
+                rc = ck(cudaMemcpy(c->embd, g.base + te->off, eb, cudaMemcpyHostToDevice), "embedding upload");
+        }
+        if (!rc) {
+            size_t b = qmat_bytes(c->vocab, c->dim);
+            if (!(rc = dalloc(&c->lm, b, &c->weight_bytes))) {
+                cudaMemset(c->lm, 0, b);
+                rc = upload_q4(c, g, tl, 0, c->vocab, 0, c->dim, RowMap{c->vocab, 0, 0}, c->lm, staging, stage_bytes);
+            }
+        }
+        if (!rc) rc = upload_f32(c, g, "output_norm.weight", &c->rms_final, c->dim);
+    }
+    cleanup_stage();
+    if (rc) return bail(rc);
+    // RoPE inverse frequencies on the host (mistral/mistral_model.h:69-74)
+    {
+        std::vector<float> th(c->hd / 2);
+        for (int i = 0; i < c->hd / 2; ++i) th[i] = 1.0f / powf(c->theta, (2.0f * (float)i) / (float)c->hd);
+        if ((rc = dalloc(&c->theta_inv, th.size()))) return bail(rc);
+        if ((rc = ck(cudaMemcpy(c->theta_inv, th.data(), th.size() * 4, cudaMemcpyHostToDevice), "theta"))) return bail(rc);
+    }
+    // ---- KV ring + buffers ----
+    const size_t kvn = (size_t)c->n_layers * c->max_seq * c->kv_rows;
+    if ((rc = dalloc(&c->kc, kvn, &c->kv_bytes)) || (rc = dalloc(&c->vc, kvn, &c->kv_bytes))) return bail(rc);
+    cudaMemset(c->kc, 0, kvn * 2);
+    cudaMemset(c->vc, 0, kvn * 2);
+    const int MB = c->MB;
+    const int amax = std::max(c->dim, c->q_rows);
+    c->max_chunks = (c->max_seq + c->attn_chunk - 1) / c->attn_chunk;
+    if ((rc = dalloc(&c->x, (size_t)MB * c->dim)) || (rc = dalloc(&c->y, (size_t)c->ypart_max * MB * c->dim)) ||
+        (rc = dalloc(&c->act.qs, (size_t)MB * amax)) || (rc = dalloc(&c->act.d, (size_t)MB * amax / 32)) ||
+        (rc = dalloc(&c->act.sum, (size_t)MB * amax / 32)) || (rc = dalloc(&c->hact.qs, (size_t)MB * c->hid_l)) ||
+        (rc = dalloc(&c->hact.d, (size_t)MB * c->hid_l / 32)) || (rc = dalloc(&c->hact.sum, (size_t)MB * c->hid_l / 32)) ||
+        (rc = dalloc(&c->q, (size_t)MB * c->q_rows)) ||
+        (rc = dalloc(&c->part_ml, (size_t)MB * c->nh_l * c->max_chunks)) ||
+        (rc = dalloc(&c->part_acc, (size_t)MB * c->nh_l * c->max_chunks * 128)) ||
+        (rc = dalloc(&c->logits, (size_t)MB * c->vocab)) || (rc = dalloc(&c->probs, (size_t)c->vocab)) ||
+        (rc = dalloc(&c->argmax, MB)) || (rc = dalloc(&c->ctrl, 1)) || (rc = dalloc(&c->dctrl, 1)) ||
+        (rc = dalloc(&c->err, 1)) || (rc = dalloc(&c->gs, 1)))
+        return bail(rc);
+    cudaMemset(c->err, 0, sizeof(int));
+    cudaMemset(c->x, 0, (size_t)MB * c->dim * 4);
+    cudaMemset(c->y, 0, (size_t)c->ypart_max * MB * c->dim * 4);
+    if ((rc = ck(cudaMallocHost(&c->ctrl_h, sizeof(DevCtrl)), "pinned")) ||
+        (rc = ck(cudaMallocHost(&c->tok_h, sizeof(int32_t) * 4096), "pinned")) ||
+        (rc = ck(cudaMallocHost(&c->gs_h, sizeof(GenState)), "pinned")))
+        return bail(rc);
+    if ((rc = ck(cudaDeviceSynchronize(), "context build"))) return bail(rc);
+    *out = c;
+    return SD_OK;
+}
+
+int sd_ctx_create(const void* gguf_base, size_t gguf_len, const sd_ctx_opts* opts, sd_ctx** out) {
+    return ctx_build(gguf_base, gguf_len, opts, out);
+}
+
+int sd_ctx_create_file(const char* path, const sd_ctx_opts* opts, sd_ctx** out) {
+    clear_error();
+    if (!path || !out) return fail(SD_ERR_INVALID, "null argument");
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(SD_ERR_INVALID, "cannot open %s", path);
+    struct stat stt;
+    if (fstat(fd, &stt) != 0) {
+        close(fd);
+        return fail(SD_ERR_INVALID, "cannot stat %s", path);
+    }
+    void* base = mmap(nullptr, stt.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (base == MAP_FAILED) return fail(SD_ERR_OOM, "mmap %s failed", path);
+    int rc = ctx_build(base, stt.st_size, opts, out);
+    munmap(base, stt.st_size);
+    return rc;
+}
+
+int sd_ctx_info(const sd_ctx* c, sd_model_info* o) {
+    if (!c || !o) return fail(SD_ERR_INVALID, "null argument");
+    o->dim = c->dim; o->hidden_dim = c->hidden; o->n_layers = c->n_layers; o->n_heads = c->n_heads;
+    o->n_kv_heads = c->n_kv; o->head_dim = c->hd; o->vocab_size = c->vocab; o->max_seq = c->max_seq;
+    o->rope_theta = c->theta; o->rms_eps = c->eps; o->bos_id = c->bos; o->eos_id = c->eos;
+    o->tp_rank = c->tp_rank; o->tp_size = c->tp_size; o->weight_bytes = c->weight_bytes; o->kv_bytes = c->kv_bytes;
+    return SD_OK;
+}
+
+int sd_ctx_device_error(sd_ctx* c) {
+    if (!c) return fail(SD_ERR_INVALID, "null context");
+    cudaSetDevice(c->dev);
+    int h = 0;
+    if (cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess)
+        return fail(SD_ERR_CUDA, "reading device error word");
+    cudaMemsetAsync(c->err, 0, sizeof(int), c->st);
+    cudaStreamSynchronize(c->st);
+    return h;
+}
+
+void* sd_ctx_stream(sd_ctx* c) { return c ? (void*)c->st : nullptr; }
+
+int sd_forward_dev(sd_ctx* c, const int32_t* tokens_dev, int S, int pos, float* logits_dev, int32_t* argmax_dev, void* stream) {
+    clear_error();
+    if (!c || !tokens_dev || S < 1 || S > c->MB || pos < 0) return fail(SD_ERR_INVALID, "sd_forward_dev: bad arguments");
+    if (pos + S > c->max_seq) return fail(SD_ERR_INVALID, "positions past the KV ring (%d)", c->max_seq);
+    cudaSetDevice(c->dev);
+    cudaEvent_t ev;
+    if (stream) {
+        // order after the caller's stream
+        CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event");
+        CK(cudaEventRecord(ev, (cudaStream_t)stream), "event");
+        CK(cudaStreamWaitEvent(c->st, ev, 0), "event");
+        cudaEventDestroy(ev);
+    }
+    int rc = set_ctrl(c, c->ctrl, tokens_dev, S, pos, false);
+    if (rc) return rc;
+    if ((rc = run_forward(c, S))) return rc;
+    if (logits_dev) CK(cudaMemcpyAsync(logits_dev, c->logits, (size_t)S * c->vocab * 4, cudaMemcpyDeviceToDevice, c->st), "logits");
+    if (argmax_dev) CK(cudaMemcpyAsync(argmax_dev, c->argmax, (size_t)S * 4, cudaMemcpyDeviceToDevice, c->st), "argmax");
+    if (stream) {
+        CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event");
+        CK(cudaEventRecord(ev, c->st), "event");
+        CK(cudaStreamWaitEvent((cudaStream_t)stream, ev, 0), "event");
+        cudaEventDestroy(ev);
+    }
+    return SD_OK;
+}
+
+int sd_forward(sd_ctx* c, const int32_t* tokens, int S, int pos, float* logits, int32_t* argmax) {
+    clear_error();
+    if (!c || !tokens || S < 1 || S > c->MB || pos < 0) return fail(SD_ERR_INVALID, "sd_forward: bad arguments");
+    if (pos + S > c->max_seq) return fail(SD_ERR_INVALID, "positions past the KV ring (%d)", c->max_seq);
+    int rc = check_tokens(c, tokens, S);
+    if (rc) return rc;
+    cudaSetDevice(c->dev);
+    if ((rc = set_ctrl(c, c->ctrl, tokens, S, pos, true))) return rc;
+    if ((rc = run_forward(c, S))) return rc;
+    if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)S * c->vocab * 4, cudaMemcpyDeviceToHost, c->st), "logits");
+    if (argmax) CK(cudaMemcpyAsync(argmax, c->argmax, (size_t)S * 4, cudaMemcpyDeviceToHost, c->st), "argmax");
+    return finish(c);
+}
+
+int sd_forward_layers(sd_ctx* c, int n_layers, const int32_t* tokens, int S, int pos, float* logits, int32_t* argmax) {
+    clear_error();
+    if (!c || !tokens || S < 1 || S > c->MB || pos < 0 || n_layers < 1 || n_layers > c->n_layers)
+        return fail(SD_ERR_INVALID, "sd_forward_layers: bad arguments");
+    if (pos + S > c->max_seq) return fail(SD_ERR_INVALID, "positions past the KV ring");
+    int rc = check_tokens(c, tokens, S);
+    if (rc) return rc;
+    cudaSetDevice(c->dev);
+    if ((rc = set_ctrl(c, c->ctrl, tokens, S, pos, true))) return rc;
+    if ((rc = enqueue_forward(c, S, n_layers, c->kc, c->vc, c->ctrl, true))) return rc;
+    if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)S * c->vocab * 4, cudaMemcpyDeviceToHost, c->st), "logits");
+    if (argmax) CK(cudaMemcpyAsync(argmax, c->argmax, (size_t)S * 4, cudaMemcpyDeviceToHost, c->st), "argmax");
+    return finish(c);
+}
+
+int sd_prefill(sd_ctx* c, const int32_t* tokens, int n, int start_pos) {
+    clear_error();
+    if (!c || !tokens || n < 0 || start_pos < 0) return fail(SD_ERR_INVALID, "sd_prefill: bad arguments");
+    if (start_pos + n > c->max_seq) return fail(SD_ERR_INVALID, "prompt past the KV ring");
+    int rc = check_tokens(c, tokens, n);
+    if (rc) return rc;
+    cudaSetDevice(c->dev);
+    for (int i = 0; i < n; i += c->MB) {
+        const int S = std::min(c->MB, n - i);
+        if ((rc = set_ctrl(c, c->ctrl, tokens + i, S, start_pos + i, true))) return rc;
+        if ((rc = run_forward(c, S))) return rc;
+        CK(cudaStreamSynchronize(c->st), "prefill");  // ctrl_h staging is reused
+    }
+    return finish(c);
+}
+
+int sd_kv_read(sd_ctx* c, int layer, int pos0, int n, uint16_t* k, uint16_t* v) {
+    clear_error();
+    if (!c || layer < 0 || layer >= c->n_layers || pos0 < 0 || n < 0 || pos0 + n > c->max_seq)
+        return fail(SD_ERR_INVALID, "sd_kv_read: bad arguments");
+    cudaSetDevice(c->dev);
+    const size_t off = ((size_t)layer * c->max_seq + pos0) * c->kv_rows;
+    if (k) CK(cudaMemcpyAsync(k, c->kc + off, (size_t)n * c->kv_rows * 2, cudaMemcpyDeviceToHost, c->st), "kv read");
+    if (v) CK(cudaMemcpyAsync(v, c->vc + off, (size_t)n * c->kv_rows * 2, cudaMemcpyDeviceToHost, c->st), "kv read");
+    return finish(c);
+}
+
+int sd_ngram_draft(const int32_t* history, int hlen, int ngram_n, int max_draft, int current, int32_t* draft_out, int* match_pos) {
+    clear_error();
+    if ((hlen > 0 && !history) || hlen < 0 || ngram_n < 1 || max_draft < 0 || (max_draft > 0 && !draft_out))
+        return fail(SD_ERR_INVALID, "sd_ngram_draft: bad arguments");
+    if (sd_device_count() == 0) return fail(SD_ERR_NO_DEVICE, "no CUDA device");
+    int* dh = nullptr;
+    int* dout = nullptr;
+    cudaStream_t st = nullptr;
+    int rc = SD_OK;
+    if ((rc = ck(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "stream"))) return rc;
+    if (!(rc = dalloc(&dh, (size_t)std::max(hlen, 1))) && !(rc = dalloc(&dout, (size_t)max_draft + 2))) {
+        if (hlen > 0) rc = ck(cudaMemcpyAsync(dh, history, (size_t)hlen * 4, cudaMemcpyHostToDevice, st), "upload");
+        if (!rc) rc = ck(launch_ngram_scan(dh, hlen, ngram_n, max_draft, current, dout, st), "ngram");
+        std::vector<int> h(max_draft + 2);
+        if (!rc) rc = ck(cudaMemcpyAsync(h.data(), dout, (max_draft + 2) * 4, cudaMemcpyDeviceToHost, st), "download");
+        if (!rc) rc = ck(cudaStreamSynchronize(st), "ngram");
+        if (!rc) {
+            for (int i = 0; i < h[0]; ++i) draft_out[i] = h[2 + i];
+            if (match_pos) *match_pos = h[1];
+            rc = h[0];
+        }
+    }
+    cudaFree(dh);
+    cudaFree(dout);
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+int sd_spec_accept(sd_ctx* c, const float* draft_probs, const float* logits, const int32_t* draft, int n_draft, float temp,
+                   int bonus_mode, uint64_t seed, uint64_t* counter, int32_t* accepted) {
+    clear_error();
+    if (!c || !logits || !draft || !accepted || n_draft < 1 || n_draft > kMaxS - 1 || (temp > 0 && !draft_probs))
+        return fail(SD_ERR_INVALID, "sd_spec_accept: bad arguments");
+    cudaSetDevice(c->dev);
+    int rc = check_tokens(c, draft, n_draft);
+    if (rc) return rc;
+    // scratch: logits rows in c->logits, probs in c->probs, small arrays in the tail of c->y
+    int* d_draft = reinterpret_cast<int*>(c->y);
+    float* d_dp = reinterpret_cast<float*>(c->y) + 16;
+    int* d_acc = reinterpret_cast<int*>(c->y) + 32;
+    int* d_n = reinterpret_cast<int*>(c->y) + 48;
+    unsigned long long* d_ctr = reinterpret_cast<unsigned long long*>(c->y + 64);
+    unsigned long long ctr = counter ? *counter : 0;
+    CK(cudaMemcpyAsync(c->logits, logits, (size_t)(n_draft + 1) * c->vocab * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    CK(cudaMemcpyAsync(d_draft, draft, n_draft * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    if (draft_probs) CK(cudaMemcpyAsync(d_dp, draft_probs, n_draft * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    else CK(cudaMemsetAsync(d_dp, 0, n_draft * 4, c->st), "memset");
+    CK(cudaMemcpyAsync(d_ctr, &ctr, 8, cudaMemcpyHostToDevice, c->st), "upload");
+    CK(launch_spec_accept(c->logits, c->probs, d_draft, d_dp, n_draft, c->vocab, temp, bonus_mode, seed, d_ctr, d_acc, d_n,
+                          c->st), "spec_accept");
+    int na = 0;
+    CK(cudaMemcpyAsync(&na, d_n, 4, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaMemcpyAsync(&ctr, d_ctr, 8, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaStreamSynchronize(c->st), "spec_accept");
+    if (na < 1 || na > n_draft + 1) return fail(SD_ERR_CUDA, "spec_accept returned %d", na);
+    CK(cudaMemcpy(accepted, d_acc, na * 4, cudaMemcpyDeviceToHost), "download");
+    if (counter) *counter = ctr;
+    return na;
+}
+
+void sd_gen_params_default(sd_gen_params* p) {
+    if (!p) return;
+    memset(p, 0, sizeof(*p));
+    // mistral/mistral_infer.m:396-410 defaults
+    p->mode = SD_GEN_GREEDY;
+    p->max_tokens = 128;
+    p->temp = 0.7f;
+    p->top_p = 0.9f;
+    p->top_k = 40;
+    p->rep_penalty = 1.1f;
+    p->rep_window = 64;
+    p->spec_k = 4;
+    p->ngram_n = 3;
+    p->draft_layers = 8;
+    p->history_has_current = 0;
+    p->bonus_mode = SD_BONUS_ARGMAX;
+    p->seed = 0;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Generation loops
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+int ensure_gen_buffers(sd_ctx* c, int cap) {
+    if (c->g_cap >= cap) return SD_OK;
+    cudaFree(c->g_out);
+    cudaFree(c->g_hist);
+    c->g_out = c->g_hist = nullptr;
+    c->g_cap = 0;
+    int rc = dalloc(&c->g_out, (size_t)cap);
+    if (!rc) rc = dalloc(&c->g_hist, (size_t)cap);
+    if (!rc) c->g_cap = cap;
+    return rc;
+}
+
+int ensure_draft_kv(sd_ctx* c, int layers) {
+    if (c->draft_layers_alloc >= layers) return SD_OK;
+    cudaFree(c->dkc);
+    cudaFree(c->dvc);
+    c->dkc = c->dvc = nullptr;
+    c->draft_layers_alloc = 0;
+    const size_t n = (size_t)layers * c->max_seq * c->kv_rows;
+    int rc = dalloc(&c->dkc, n);
+    if (!rc) rc = dalloc(&c->dvc, n);
+    if (rc) return rc;
+    cudaMemset(c->dkc, 0, n * 2);
+    cudaMemset(c->dvc, 0, n * 2);
+    c->draft_layers_alloc = layers;
+    return SD_OK;
+}
+
+// One decode iteration, enqueued on c->st (captured into c->iter_graph).
+int enqueue_iteration(sd_ctx* c, const GenParamsDev& p, int K, int draft_layers) {
+    int rc;
+    if (p.mode == SD_MODE_SELF) {
+        CK(launch_gen_self_begin(c->gs, c->dctrl, c->st), "self begin");
+        for (int k = 0; k < K; ++k) {
+            if ((rc = enqueue_forward(c, 1, draft_layers, c->dkc, c->dvc, c->dctrl, true))) return rc;
+            CK(launch_gen_draft_step(c->gs, c->dctrl, c->argmax, k, c->st), "draft step");
+        }
+        CK(launch_gen_self_verify(c->gs, c->ctrl, K, c->st), "self verify");
+        if ((rc = enqueue_forward(c, K + 1, c->n_layers, c->kc, c->vc, c->ctrl, true))) return rc;
+    } else {
+        const int S = p.mode == SD_MODE_NGRAM ? K + 1 : 1;
+        CK(launch_gen_prepare(c->gs, c->ctrl, p, c->st), "prepare");
+        if ((rc = enqueue_forward(c, S, c->n_layers, c->kc, c->vc, c->ctrl, true))) return rc;
+    }
+    CK(launch_gen_commit(c->gs, c->ctrl, c->logits, c->probs, c->argmax, p, c->vocab, c->st), "commit");
+    return SD_OK;
+}
+
+int iteration_graph(sd_ctx* c, const GenParamsDev& p, int K, int draft_layers) {
+    // key: mode, K, draft depth, and whether sampling parameters change kernel arguments (captured by value)
+    const int key[6] = {p.mode, K, draft_layers, (int)(p.temp * 1e4f), p.top_k, (int)(p.rep_penalty * 1e4f)};
+    bool same = c->iter_graph != nullptr;
+    for (int i = 0; i < 6; ++i) same = same && key[i] == c->iter_key[i];
+    // any other captured parameter change forces a rebuild
+    same = same && memcmp(&c->iter_p, &p, sizeof p) == 0;
+    if (same) return SD_OK;
+    if (c->iter_graph) {
+        cudaGraphExecDestroy(c->iter_graph);
+        c->iter_graph = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal), "capture");
+    int rc = enqueue_iteration(c, p, K, draft_layers);
+    cudaError_t e = cudaStreamEndCapture(c->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "end capture");
+    e = cudaGraphInstantiate(&c->iter_graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+    memcpy(c->iter_key, key, sizeof key);
+    c->iter_p = p;
+    return SD_OK;
+}
+
+double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+}  // namespace
+
+extern "C" {
+
+int sd_decode(sd_ctx* c, const sd_gen_params* gp, const int32_t* history, int n_hist, int first_token, int32_t* out_tokens,
+              int out_cap, sd_gen_stats* stats) {
+    clear_error();
+    if (!c || !gp || !history || n_hist < 1 || !out_tokens || out_cap < 1) return fail(SD_ERR_INVALID, "sd_decode: bad arguments");
+    if (first_token < 0 || first_token >= c->vocab) return fail(SD_ERR_INVALID, "bad first token");
+    int rc = check_tokens(c, history, n_hist);
+    if (rc) return rc;
+    const int mode = gp->mode == SD_GEN_NGRAM ? SD_MODE_NGRAM : gp->mode == SD_GEN_SELF_SPEC ? SD_MODE_SELF : SD_MODE_GREEDY;
+    int K = gp->spec_k < 1 ? 1 : gp->spec_k;
+    if (mode != SD_MODE_GREEDY && K + 1 > c->MB)
+        return fail(SD_ERR_UNSUPPORTED, "spec_k %d needs %d tokens per verify forward (max_batch %d)", K, K + 1, c->MB);
+    int dl = gp->draft_layers < 1 ? 1 : gp->draft_layers;
+    if (dl >= c->n_layers) dl = c->n_layers - 1;
+    if (mode == SD_MODE_SELF && dl < 1) return fail(SD_ERR_INVALID, "self-speculation needs >= 2 layers");
+    cudaSetDevice(c->dev);
+    const int cap = n_hist + gp->max_tokens + 2 * kMaxS + 16;
+    if ((rc = ensure_gen_buffers(c, cap))) return rc;
+    if (mode == SD_MODE_SELF && (rc = ensure_draft_kv(c, dl))) return rc;
+    // the first token counts as generated (printed before the loop, mistral_infer.m:615-621)
+    GenParamsDev p{};
+    p.mode = mode;
+    p.temp = gp->temp;
+    p.top_k = gp->top_k;
+    p.top_p = gp->top_p;
+    p.rep_penalty = gp->rep_penalty;
+    p.rep_window = gp->rep_window;
+    p.ignore_eos = gp->ignore_eos;
+    p.eos_id = c->eos;
+    p.spec_k = K;
+    p.ngram_n = gp->ngram_n < 1 ? 3 : gp->ngram_n;
+    p.history_has_current = gp->history_has_current;
+    p.bonus_mode = gp->bonus_mode == SD_BONUS_REFERENCE ? SD_BONUS_REF_UNIFORM : SD_BONUS_ARGMAX_FIXED;
+    // greedy loop runs max_tokens more tokens (mistral_infer.m:690-716); the speculative loops run
+    // until max_tokens - 1 (speculative.h:232, mistral_infer.m:652-654)
+    p.gen_limit = mode == SD_MODE_GREEDY ? gp->max_tokens : gp->max_tokens - 1;
+    p.max_seq = c->max_seq;
+    GenState h{};
+    h.cur = first_token;
+    h.pos = n_hist - 1;  // history = prompt + first token; the first token sits at position n_prompt
+    h.done = p.gen_limit <= 0 || (!p.ignore_eos && first_token == c->eos);
+    h.out_cap = cap;
+    h.out = c->g_out;
+    h.hist_cap = cap;
+    h.hist = c->g_hist;
+    h.hlen = n_hist;
+    h.seed = gp->seed;
+    h.rng_counter = c->rng_start;  // continues the Philox stream after the first-token sample
+    c->rng_start = 1ull << 20;
+    *c->gs_h = h;
+    CK(cudaMemcpyAsync(c->g_hist, history, (size_t)n_hist * 4, cudaMemcpyHostToDevice, c->st), "history");
+    CK(cudaMemcpyAsync(c->gs, c->gs_h, sizeof(GenState), cudaMemcpyHostToDevice, c->st), "state");
+    if (mode == SD_MODE_SELF) {
+        // drafter KV prefill through the first dl layers (mistral_infer.m:675-681)
+        for (int i = 0; i < n_hist - 1; i += c->MB) {
+            const int S = std::min(c->MB, n_hist - 1 - i);
+            if ((rc = set_ctrl(c, c->dctrl, history + i, S, i, true))) return rc;
+            if ((rc = enqueue_forward(c, S, dl, c->dkc, c->dvc, c->dctrl, false))) return rc;
+            CK(cudaStreamSynchronize(c->st), "draft prefill");
+        }
+    }
+    if ((rc = iteration_graph(c, p, K, dl))) return rc;
+    const double t0 = now_ms();
+    int generated = 0;
+    int guard = 0;
+    while (!c->gs_h->done) {
+        // launch at least as many iterations as tokens remaining / tokens per iteration (lower bound)
+        const int per = mode == SD_MODE_GREEDY ? 1 : K + 1;
+        int batch = std::max(1, (p.gen_limit - generated) / per);
+        if (batch > 64) batch = 64;
+        for (int i = 0; i < batch; ++i) CK(cudaGraphLaunch(c->iter_graph, c->st), "iteration");
+        CK(cudaMemcpyAsync(c->gs_h, c->gs, sizeof(GenState), cudaMemcpyDeviceToHost, c->st), "state");
+        CK(cudaStreamSynchronize(c->st), "decode");
+        generated = c->gs_h->generated;
+        if (++guard > 1000000) return fail(SD_ERR_TIMEOUT, "decode did not terminate");
+    }
+    const double t1 = now_ms();
+    if ((rc = check_device_error(c->err, c->st))) return rc;
+    GenState& s = *c->gs_h;
+    const int n = std::min(s.n_out, out_cap);
+    if (n > 0) CK(cudaMemcpy(out_tokens, c->g_out, (size_t)n * 4, cudaMemcpyDeviceToHost), "download");
+    if (stats) {
+        stats->n_generated = s.n_out;
+        stats->total_draft = s.total_draft;
+        stats->total_accepted = s.total_accepted;
+        stats->total_iterations = s.total_iterations;
+        stats->ms_decode = t1 - t0;
+    }
+    return n;
+}
+
+int sd_generate(sd_ctx* c, const sd_gen_params* gp, const int32_t* prompt, int n_prompt, int32_t* out_tokens, int out_cap,
+                sd_gen_stats* stats) {
+    clear_error();
+    if (!c || !gp || !prompt || n_prompt < 1 || !out_tokens || out_cap < 1) return fail(SD_ERR_INVALID, "sd_generate: bad arguments");
+    if (n_prompt + gp->max_tokens + kMaxS + 1 > c->max_seq) return fail(SD_ERR_INVALID, "prompt + tokens exceed the KV ring");
+    int rc = check_tokens(c, prompt, n_prompt);
+    if (rc) return rc;
+    cudaSetDevice(c->dev);
+    const double t0 = now_ms();
+    // prefill (W4A8 chunks of max_batch tokens); logits of the last prompt token
+    for (int i = 0; i < n_prompt; i += c->MB) {
+        const int S = std::min(c->MB, n_prompt - i);
+        if ((rc = set_ctrl(c, c->ctrl, prompt + i, S, i, true))) return rc;
+        if ((rc = run_forward(c, S))) return rc;
+        CK(cudaStreamSynchronize(c->st), "prefill");
+    }
+    const int last = (n_prompt - 1) % c->MB;
+    // first token: sample_token with repetition penalty over the prompt window (mistral_infer.m:610-621)
+    std::vector<int32_t> hist(prompt, prompt + n_prompt);
+    int first;
+    {
+        GenParamsDev p{};
+        p.mode = SD_MODE_GREEDY;
+        p.temp = gp->temp;
+        p.top_k = gp->top_k;
+        p.top_p = gp->top_p;
+        p.rep_penalty = gp->rep_penalty;
+        p.rep_window = gp->rep_window;
+        p.ignore_eos = 1;
+        p.eos_id = c->eos;
+        p.gen_limit = 1;
+        p.max_seq = c->max_seq;
+        const int cap = n_prompt + gp->max_tokens + 2 * kMaxS + 16;
+        if ((rc = ensure_gen_buffers(c, cap))) return rc;
+        GenState h{};
+        h.cur = 0;
+        h.pos = n_prompt;
+        h.out_cap = cap;
+        h.out = c->g_out;
+        h.hist_cap = cap;
+        h.hist = c->g_hist;
+        h.hlen = n_prompt;
+        h.seed = gp->seed;
+        h.rng_counter = 0;
+        h.n_draft = 0;
+        *c->gs_h = h;
+        CK(cudaMemcpyAsync(c->g_hist, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, c->st), "history");
+        CK(cudaMemcpyAsync(c->gs, c->gs_h, sizeof(GenState), cudaMemcpyHostToDevice, c->st), "state");
+        // commit samples from logits row 0: move the last prompt row there
+        if (last != 0)
+            CK(cudaMemcpyAsync(c->logits, c->logits + (size_t)last * c->vocab, (size_t)c->vocab * 4, cudaMemcpyDeviceToDevice, c->st), "logits");
+        CK(launch_gen_commit(c->gs, c->ctrl, c->logits, c->probs, c->argmax, p, c->vocab, c->st), "first token");
+        CK(cudaMemcpyAsync(c->gs_h, c->gs, sizeof(GenState), cudaMemcpyDeviceToHost, c->st), "state");
+        CK(cudaStreamSynchronize(c->st), "first token");
+        CK(cudaMemcpy(&first, c->g_out, 4, cudaMemcpyDeviceToHost), "first token");
+        c->rng_start = c->gs_h->rng_counter;
+    }
+    const double t1 = now_ms();
+    hist.push_back(first);
+    std::vector<int32_t> rest(std::max(out_cap, 1));
+    sd_gen_stats st2{};
+    int n = sd_decode(c, gp, hist.data(), (int)hist.size(), first, rest.data(), (int)rest.size(), &st2);
+    if (n < 0) return n;
+    out_tokens[0] = first;
+    const int m = std::min(n, out_cap - 1);
+    for (int i = 0; i < m; ++i) out_tokens[1 + i] = rest[i];
+    if (stats) {
+        *stats = st2;
+        stats->n_generated = 1 + st2.n_generated;
+        stats->ms_prefill = t1 - t0;
+    }
+    return 1 + m;
+}
+
+}  // extern "C"

@@ -403,14 +403,18 @@ int gemv_pick_stages(int Kp, int S, int chunk, int max_smem) {
     return 0;
 }
 
+// Allow the full opt-in shared memory for every matvec variant on the current device.  Called before
+// any launch (and before stream capture: it is not a stream operation but is kept out of captures).
+cudaError_t gemv_init_attrs(int max_smem) {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(k_gemv<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(k_gemv<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(k_gemv<EPI_SILU_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    return cudaFuncSetAttribute(k_gemv<EPI_BLOCKSUMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+}
+
 template <int EPI>
 static cudaError_t launch_t(const GemvArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemvThreads);
@@ -453,8 +457,9 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a, int grid, size_t smem, cudaS
 // One thread per (source row, quad, word t): writes the 16-byte nibble piece; t == 0 also writes
 // the row's 4 scales for that quad.
 // ---------------------------------------------------------------------------------------------
-__global__ void k_repack(const uint8_t* __restrict__ aos, int rows, int cols, RowMap map, uint8_t* __restrict__ dst) {
-    const int nq = cols / 128, bpr = cols / 32;
+__global__ void k_repack(const uint8_t* __restrict__ aos, int rows, int cols, size_t src_row_bytes, RowMap map,
+                         uint8_t* __restrict__ dst) {
+    const int nq = cols / 128;
     const long long n = (long long)rows * nq * 4;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const int t = (int)(i & 3);
@@ -468,7 +473,7 @@ __global__ void k_repack(const uint8_t* __restrict__ aos, int rows, int cols, Ro
         uint16_t sc[4];
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
-            const uint8_t* b = aos + ((size_t)r * bpr + q * 4 + blk) * 18;
+            const uint8_t* b = aos + (size_t)r * src_row_bytes + ((size_t)q * 4 + blk) * 18;
             words[blk] = (uint32_t)b[2 + 4 * t] | ((uint32_t)b[3 + 4 * t] << 8) | ((uint32_t)b[4 + 4 * t] << 16) |
                          ((uint32_t)b[5 + 4 * t] << 24);
             sc[blk] = (uint16_t)(b[0] | (b[1] << 8));
@@ -481,11 +486,14 @@ __global__ void k_repack(const uint8_t* __restrict__ aos, int rows, int cols, Ro
     }
 }
 
-cudaError_t launch_repack(const uint8_t* aos, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st) {
+// aos points at row 0, column block 0 of the (sub)matrix; consecutive rows are src_row_bytes apart
+// (a column slice of a wider matrix for tensor-parallel shards).
+cudaError_t launch_repack(const uint8_t* aos, int rows, int cols, size_t src_row_bytes, RowMap map, uint8_t* dst,
+                          cudaStream_t st) {
     long long n = (long long)rows * (cols / 128) * 4;
     int blocks = (int)((n + 255) / 256);
     if (blocks > 65535 * 8) blocks = 65535 * 8;
-    k_repack<<<blocks, 256, 0, st>>>(aos, rows, cols, map, dst);
+    k_repack<<<blocks, 256, 0, st>>>(aos, rows, cols, src_row_bytes, map, dst);
     return cudaGetLastError();
 }
 

@@ -14,6 +14,7 @@ int check_device_error(int* word, cudaStream_t st);
 int repack_matrix(const uint8_t* aos_dev, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st);
 // Plan + launch a matvec.  a.kparts <= 0 lets the planner choose; a.kparts == 1 forces one slice.
 // For EPI_STORE with a K split the partial outputs go to a.out + p*a.part_stride (the caller sums).
+int gemv_prepare_device(int dev);
 int gemv_plan(GemvArgs& a, int dev, int* grid, size_t* smem);
 int run_gemv(int epi, const GemvArgs& a, int dev, cudaStream_t st, bool pdl);
 }  // namespace sd

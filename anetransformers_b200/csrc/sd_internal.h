@@ -98,10 +98,12 @@ struct GemvArgs {
 size_t gemv_smem_bytes(int Kp, int S, int chunk, int nstage);
 int gemv_pick_stages(int Kp, int S, int chunk, int max_smem);
 inline int gemv_chunk(int nq_part) { return nq_part >= kConsumerWarps ? kConsumerWarps : nq_part; }
+cudaError_t gemv_init_attrs(int max_smem);
 cudaError_t launch_gemv(int epi, const GemvArgs& a, int grid, size_t smem, cudaStream_t st, bool pdl);
 cudaError_t launch_sum_parts(const float* parts, float* out, int n, int kparts, size_t stride, cudaStream_t st);
 
-cudaError_t launch_repack(const uint8_t* aos, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st);
+cudaError_t launch_repack(const uint8_t* aos, int rows, int cols, size_t src_row_bytes, RowMap map, uint8_t* dst,
+                          cudaStream_t st);
 cudaError_t launch_quantize(const float* x, Q8Planes out, int S, int n, cudaStream_t st);
 cudaError_t launch_q8_to_blocks(Q8Planes in, void* blocks, int S, int n, cudaStream_t st);
 cudaError_t launch_blocks_to_q8(const void* blocks, Q8Planes out, int S, int n, cudaStream_t st);
@@ -119,6 +121,8 @@ struct NormArgs {
     const DevCtrl* ctrl;
     const int* tokens;    // host-independent token ids (mode 0); defaults to ctrl->tokens
     float* xn_out;        // optional: normalised fp32 output [S][dim]
+    int yparts;           // mode 1: y holds yparts partial slices summed in order (K-split matvec)
+    size_t ystride;       // floats between slices
 };
 cudaError_t launch_norm_quant(int mode, const NormArgs& a, cudaStream_t st, bool pdl);
 

@@ -93,8 +93,21 @@ int check_device_error(int* word, cudaStream_t st) {
 
 // Repack AoS Q4_0 [rows][cols/32] (device) into the tile layout at dst (zero-filled padding rows).
 int repack_matrix(const uint8_t* aos_dev, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st) {
-    cudaError_t e = launch_repack(aos_dev, rows, cols, map, dst, st);
+    cudaError_t e = launch_repack(aos_dev, rows, cols, (size_t)cols / 32 * 18, map, dst, st);
     if (e != cudaSuccess) return cuda_fail(e, "repack");
+    return SD_OK;
+}
+
+// Once per device (current device): opt every matvec variant into the full shared memory.
+int gemv_prepare_device(int dev) {
+    static bool done[64] = {false};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) return fail(SD_ERR_INVALID, "bad device %d", dev);
+    if (done[dev]) return SD_OK;
+    cudaError_t e = gemv_init_attrs(device_max_smem(dev));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    done[dev] = true;
     return SD_OK;
 }
 
@@ -243,6 +256,8 @@ int sd_blocks_to_q8_dev(const sd_block_q8_0* in, sd_q8_dev out, int S, int n, vo
 static int matvec_common(int epi, const sd_qmat* W, sd_q8_dev x, float* y, int32_t* isum, int S, void* stream) {
     if (!W || !x.qs || !x.d || !x.sum) return fail(SD_ERR_INVALID, "matvec: null argument");
     int dev = W->device;
+    int prc = gemv_prepare_device(dev);
+    if (prc) return prc;
     cudaStream_t st = (cudaStream_t)stream;
     GemvArgs a = {};
     a.w = W->w;

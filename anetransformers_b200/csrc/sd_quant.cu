@@ -114,7 +114,10 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
         for (int b = warp; b < nb; b += kNormThreads / 32) {
             float v = x[b * 32 + lane];
             if constexpr (MODE == 1) {
-                v = v + a.y[(size_t)tok * a.dim + b * 32 + lane];
+                const size_t yi = (size_t)tok * a.dim + b * 32 + lane;
+                float yv = a.y[yi];
+                for (int p = 1; p < a.yparts; ++p) yv += a.y[(size_t)p * a.ystride + yi];
+                v = v + yv;
                 x[b * 32 + lane] = v;
             }
             ss = fmaf(v, v, ss);
