@@ -1,8 +1,8 @@
 """GPU parity of the model path (forward, KV ring, sampling, drafting, acceptance, decode loops) against
 the CPU oracle on small configs with the Mistral head geometry (head_dim 128, 4:1 GQA).
 
-Bars: logits within 1e-2 relative (max |diff| / max |logit|, north_star); KV ring fp16 values within
-2 ulp; n-gram drafts bit-exact; temp-0 speculative output token-identical to greedy decode; greedy
+Bars: logits within 1e-2 relative (max |diff| / max |logit|, north_star); KV ring values within 1e-2
+of each row's scale; n-gram drafts bit-exact; temp-0 speculative output token-identical to greedy decode; greedy
 tokens identical to the oracle except at steps whose oracle top-2 logit gap is below 1e-3 of the
 logit scale (fp32 re-association can only flip such near-ties).
 """
@@ -54,14 +54,17 @@ def test_forward_logits_match_oracle(ctx, omodel):
         gap = np.sort(ref)[-1] - np.sort(ref)[-2]
         if gap > 1e-3 * np.max(np.abs(ref)):
             assert am[0] == int(np.argmax(ref))
-    # K/V ring contents of layer 1 vs the oracle's fp16 ring
-    k, v = ctx.kv_read(1, 0, len(toks))
-    ok, ov = omodel.kv_arrays(kv, 1)
-    for a, b in ((k, ok[:len(toks)]), (v, ov[:len(toks)])):
-        fa = a.view(np.float16).astype(np.float64)
-        fb = b.view(np.float16).astype(np.float64)
-        ulp = np.abs(np.spacing(fb.astype(np.float16)).astype(np.float64))
-        assert np.all(np.abs(fa - fb) <= 2 * ulp + 1e-7)
+    # K/V ring contents vs the oracle's fp16 ring, per row relative to the row's scale.  A last-bit
+    # difference in an RMSNorm scale can move one Q8_0 code across a rounding boundary, which shifts
+    # every row of the following matvec by ~amax/127 * w, so the ring is held to the logits' bar.
+    for layer in range(omodel.cfg.n_layers):
+        k, v = ctx.kv_read(layer, 0, len(toks))
+        ok, ov = omodel.kv_arrays(kv, layer)
+        for a, b in ((k, ok[:len(toks)]), (v, ov[:len(toks)])):
+            fa = a.view(np.float16).astype(np.float64)
+            fb = b.view(np.float16).astype(np.float64)
+            scale = np.max(np.abs(fb), axis=1, keepdims=True)
+            assert np.all(np.abs(fa - fb) <= LOGIT_RTOL * scale), layer
     omodel.free_kv(kv)
 
 
@@ -77,8 +80,9 @@ def test_verify_batch_bitwise_equals_single_token_forwards(ctx):
         np.testing.assert_array_equal(batch[i].view(np.uint32), single[i].view(np.uint32))
 
 
-def _near_tie_ok(gpu, ref, omodel, prompt):
-    """Greedy sequences agree up to the first step where the oracle's top-2 gap is tiny."""
+def _near_tie_ok(gpu, ref, omodel, prompt, rep_penalty=1.0, rep_window=64):
+    """Greedy sequences agree up to the first step where the oracle's top-2 gap (after the repetition
+    penalty, mistral_model.h:1147-1158) is tiny."""
     n = min(len(gpu), len(ref))
     if gpu[:n] == ref[:n]:
         return True
@@ -88,6 +92,10 @@ def _near_tie_ok(gpu, ref, omodel, prompt):
     for p, t in enumerate(seq):
         lg = omodel.forward(kv, t, p)
     omodel.free_kv(kv)
+    lg = lg.astype(np.float32).copy()
+    if rep_penalty != 1.0:
+        for t in seq[-rep_window:]:
+            lg[t] = lg[t] / np.float32(rep_penalty) if lg[t] > 0 else lg[t] * np.float32(rep_penalty)
     s = np.sort(lg)
     return (s[-1] - s[-2]) <= 1e-3 * np.max(np.abs(lg))
 
@@ -107,7 +115,7 @@ def test_greedy_with_repetition_penalty_matches_oracle(ctx, omodel):
     gpu, _ = ctx.generate(prompt, mode="greedy", max_tokens=20, temp=0.0, rep_penalty=1.1, ignore_eos=True)
     ref, _ = omodel.generate("greedy", prompt, 20, temp=0.0, rep_penalty=1.1, ignore_eos=True)
     assert len(gpu) == len(ref)
-    assert _near_tie_ok(gpu, ref, omodel, prompt)
+    assert _near_tie_ok(gpu, ref, omodel, prompt, rep_penalty=1.1)
 
 
 @pytest.mark.parametrize("K", [1, 4, 7])
