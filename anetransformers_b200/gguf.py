@@ -214,6 +214,39 @@ def synthetic_gguf_bytes(cfg: ModelConfig, seed: int = 0) -> bytes:
     return b"".join(iter_synthetic_gguf(cfg, seed))
 
 
+def _write_tensor_job(args):
+    path, cfg, seed, idx, name, ttype, shape, abs_off = args
+    data = _tensor_data(cfg, seed, idx, name, ttype, shape)
+    fd = os.open(path, os.O_WRONLY)
+    try:
+        os.pwrite(fd, data.tobytes(), abs_off)
+    finally:
+        os.close(fd)
+    return idx
+
+
+def write_synthetic_gguf_parallel(path: str, cfg: ModelConfig = MISTRAL_7B, seed: int = 0,
+                                  workers: Optional[int] = None) -> str:
+    """Same bytes as write_synthetic_gguf, tensors generated by a spawn-started process pool and written
+    at their offsets (each tensor depends only on (seed, tensor index))."""
+    import concurrent.futures as cf
+    import multiprocessing as mp
+    head, table = _header(cfg)
+    last_name, last_type, last_shape, last_off = table[-1]
+    total = len(head) + last_off + tensor_nbytes(last_type, last_shape)
+    tmp = path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(head)
+        f.truncate(total)
+    jobs = [(tmp, cfg, seed, i, n, t, sh, len(head) + off) for i, (n, t, sh, off) in enumerate(table)]
+    jobs.sort(key=lambda j: -tensor_nbytes(j[5], j[6]))
+    workers = workers or max(1, min(16, os.cpu_count() or 1))
+    with cf.ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn")) as ex:
+        list(ex.map(_write_tensor_job, jobs, chunksize=1))
+    os.replace(tmp, path)
+    return path
+
+
 # ----------------------------------------------------------------------------------------------
 # Reader
 # ----------------------------------------------------------------------------------------------
