@@ -23,7 +23,7 @@ constexpr int kSub = 32;        // positions per sub-block (one per lane)
 constexpr int kAttnThreads = 128;
 
 __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const AttnArgs a) {
-    __shared__ float qs[kGQA * kMaxS][kHD];              // 16 KB: query rows (token-major, 4 heads)
+    __shared__ float qs[kMaxS * kGQA][kHD];              // 16 KB: query rows r = s*4 + hq
     __shared__ __half kt[kHD][kSub + 2];                 // K sub-block transposed [d][j] (padded)
     __shared__ __align__(16) __half vt[kSub][kHD];       // V sub-block [j][d]
     if (a.ctrl && a.ctrl->done) return;
@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const AttnArgs a)
     const int lo_min = max(0, pos + 1 - a.max_seq);
     const int c_first = lo_min / a.chunk, c_last = hi_max / a.chunk;
     const int n_items = (c_last - c_first + 1) * a.n_kvh;
+    const int hq = warp;                                 // warp w computes query head 4*kvh + w, all tokens
 
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const int kvh = item % a.n_kvh;
@@ -44,29 +45,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const AttnArgs a)
         const int p0 = max(c * a.chunk, lo_min);
         const int p1 = min((c + 1) * a.chunk, hi_max + 1);  // exclusive
         __syncthreads();
-        // query rows r = s*4 + hq  (head h = kvh*4 + hq)
-        for (int i = tid; i < kGQA * kMaxS * (kHD / 4); i += kAttnThreads) {
+        for (int i = tid; i < kMaxS * kGQA * (kHD / 4); i += kAttnThreads) {
             const int r = i / (kHD / 4), d4 = (i % (kHD / 4)) * 4;
-            const int s = r / kGQA, hq = r % kGQA;
+            const int s = r / kGQA, h = r % kGQA;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (s < nv)
-                v = *reinterpret_cast<const float4*>(a.q + (size_t)s * a.q_ld + (size_t)(kvh * kGQA + hq) * kHD + d4);
+                v = *reinterpret_cast<const float4*>(a.q + (size_t)s * a.q_ld + (size_t)(kvh * kGQA + h) * kHD + d4);
             *reinterpret_cast<float4*>(&qs[r][d4]) = v;
         }
-        // per-row running state: warp w owns rows 8w..8w+7 (tokens 2w, 2w+1); lane owns dims 4*lane..+3
-        float m[8], l[8], acc[8][4];
+        // per-token running state for this warp's head; lane owns dims 4*lane..4*lane+3
+        float m[kMaxS], l[kMaxS], acc[kMaxS][4];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            m[r] = -INFINITY;
-            l[r] = 0.f;
-            acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+        for (int s = 0; s < kMaxS; ++s) {
+            m[s] = -INFINITY;
+            l[s] = 0.f;
+            acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0.f;
         }
-        const int row0 = warp * 8;
-        const bool warp_active = (warp * 2) < nv;
-
         for (int sb = p0; sb < p1; sb += kSub) {
             __syncthreads();
-            // load K (transposed) and V for positions sb..sb+31 of this kv head
             for (int i = tid; i < kSub * (kHD / 8); i += kAttnThreads) {
                 const int j = i / (kHD / 8), d8 = (i % (kHD / 8)) * 8;
                 const int p = sb + j;
@@ -82,80 +78,79 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const AttnArgs a)
                 *reinterpret_cast<uint4*>(&vt[j][d8]) = vv4;
             }
             __syncthreads();
-            if (!warp_active) continue;
-            // scores for (row, position sb + lane)
-            float sc[8];
+            // scores of (token s, position sb + lane)
+            float sc[kMaxS];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) sc[r] = 0.f;
+            for (int s = 0; s < kMaxS; ++s) sc[s] = 0.f;
             for (int d = 0; d < kHD; d += 4) {
                 const float k0 = __half2float(kt[d][lane]), k1 = __half2float(kt[d + 1][lane]);
                 const float k2 = __half2float(kt[d + 2][lane]), k3 = __half2float(kt[d + 3][lane]);
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const float4 qv = *reinterpret_cast<const float4*>(&qs[row0 + r][d]);
-                    sc[r] = fmaf(qv.x, k0, sc[r]);
-                    sc[r] = fmaf(qv.y, k1, sc[r]);
-                    sc[r] = fmaf(qv.z, k2, sc[r]);
-                    sc[r] = fmaf(qv.w, k3, sc[r]);
+                for (int s = 0; s < kMaxS; ++s) {
+                    if (s < nv) {
+                        const float4 qv = *reinterpret_cast<const float4*>(&qs[s * kGQA + hq][d]);
+                        sc[s] = fmaf(qv.x, k0, sc[s]);
+                        sc[s] = fmaf(qv.y, k1, sc[s]);
+                        sc[s] = fmaf(qv.z, k2, sc[s]);
+                        sc[s] = fmaf(qv.w, k3, sc[s]);
+                    }
                 }
             }
             const int p = sb + lane;
-            float pr[8];
+            float pr[kMaxS];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const int s = (row0 + r) / kGQA;
+            for (int s = 0; s < kMaxS; ++s) {
+                pr[s] = 0.f;
+                if (s >= nv) continue;
                 const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
-                const bool ok = (s < nv) && p < p1 && p >= lo && p <= hi;
-                const float v = ok ? sc[r] : -INFINITY;
+                const bool ok = p < p1 && p >= lo && p <= hi;
+                const float v = ok ? sc[s] : -INFINITY;
                 const float mx = warp_max(v);
-                const float mn = fmaxf(m[r], mx);
-                // rows with nothing valid yet keep m = -inf and contribute nothing
-                const float e = (mn == -INFINITY) ? 0.f : (ok ? expf(v - mn) : 0.f);
-                const float corr = (mn == -INFINITY || m[r] == -INFINITY) ? 0.f : expf(m[r] - mn);
+                const float mn = fmaxf(m[s], mx);
+                // a token with nothing valid yet keeps m = -inf and contributes nothing
+                const float e = (mn == -INFINITY || !ok) ? 0.f : expf(v - mn);
+                const float corr = (mn == -INFINITY || m[s] == -INFINITY) ? 0.f : expf(m[s] - mn);
                 const float es = warp_sum(e);
-                l[r] = l[r] * corr + es;
-                acc[r][0] *= corr;
-                acc[r][1] *= corr;
-                acc[r][2] *= corr;
-                acc[r][3] *= corr;
-                m[r] = mn;
-                pr[r] = e;
+                l[s] = l[s] * corr + es;
+                acc[s][0] *= corr;
+                acc[s][1] *= corr;
+                acc[s][2] *= corr;
+                acc[s][3] *= corr;
+                m[s] = mn;
+                pr[s] = e;
             }
-            // acc[r][d] += sum_j pr[r](lane j) * V[j][d]
+            // acc[s][d] += sum_j pr[s](lane j) * V[j][d]
             for (int j = 0; j < kSub; ++j) {
                 const uint2 vraw = *reinterpret_cast<const uint2*>(&vt[j][lane * 4]);
-                const __half2 v01 = *reinterpret_cast<const __half2*>(&vraw.x);
-                const __half2 v23 = *reinterpret_cast<const __half2*>(&vraw.y);
-                const float2 f01 = __half22float2(v01), f23 = __half22float2(v23);
+                const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&vraw.x));
+                const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&vraw.y));
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const float w = __shfl_sync(0xffffffffu, pr[r], j);
-                    acc[r][0] = fmaf(w, f01.x, acc[r][0]);
-                    acc[r][1] = fmaf(w, f01.y, acc[r][1]);
-                    acc[r][2] = fmaf(w, f23.x, acc[r][2]);
-                    acc[r][3] = fmaf(w, f23.y, acc[r][3]);
+                for (int s = 0; s < kMaxS; ++s) {
+                    if (s < nv) {
+                        const float w = __shfl_sync(0xffffffffu, pr[s], j);
+                        acc[s][0] = fmaf(w, f01.x, acc[s][0]);
+                        acc[s][1] = fmaf(w, f01.y, acc[s][1]);
+                        acc[s][2] = fmaf(w, f23.x, acc[s][2]);
+                        acc[s][3] = fmaf(w, f23.y, acc[s][3]);
+                    }
                 }
             }
         }
-        // write partials
-        if (warp_active) {
+        const int h = kvh * kGQA + hq;
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const int row = row0 + r;
-                const int s = row / kGQA, hq = row % kGQA;
-                if (s >= nv) continue;
-                const int h = kvh * kGQA + hq;
-                const size_t pi = ((size_t)s * a.n_heads + h) * a.max_chunks + c;
-                if (lane == 0) a.part_ml[pi] = make_float2(m[r], l[r]);
-                *reinterpret_cast<float4*>(a.part_acc + pi * kHD + lane * 4) =
-                    make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-            }
+        for (int s = 0; s < kMaxS; ++s) {
+            if (s >= nv) continue;
+            const size_t pi = ((size_t)s * a.n_heads + h) * a.max_chunks + c;
+            if (lane == 0) a.part_ml[pi] = make_float2(m[s], l[s]);
+            *reinterpret_cast<float4*>(a.part_acc + pi * kHD + lane * 4) =
+                make_float4(acc[s][0], acc[s][1], acc[s][2], acc[s][3]);
         }
     }
 }
 
-// Merge chunk partials in chunk order; quantise each head's 128 outputs to 4 Q8_0 blocks.
-// One warp per (token, head); lane owns dims 4*lane..4*lane+3.
+// Merge chunk partials (fixed chunk order per lane group); quantise each head's 128 outputs to 4
+// Q8_0 blocks.  One warp per (token, head): the (max, sum) statistics are read lane-parallel over
+// chunks; the 128-wide accumulators with 8 independent loads in flight per lane.
 __global__ void k_attn_combine(const AttnArgs a) {
     if (a.ctrl && a.ctrl->done) return;
     pdl_trigger();
@@ -170,20 +165,42 @@ __global__ void k_attn_combine(const AttnArgs a) {
     const int c0 = lo / a.chunk, c1 = hi / a.chunk;
     const size_t base = ((size_t)s * a.n_heads + h) * a.max_chunks;
     float M = -INFINITY;
-    for (int c = c0; c <= c1; ++c) M = fmaxf(M, a.part_ml[base + c].x);
-    float L = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-    for (int c = c0; c <= c1; ++c) {
+    for (int c = c0 + lane; c <= c1; c += 32) M = fmaxf(M, a.part_ml[base + c].x);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int c = c0 + lane; c <= c1; c += 32) {
         const float2 ml = a.part_ml[base + c];
-        const float f = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M);
-        L = fmaf(ml.y, f, L);
-        const float4 ac = *reinterpret_cast<const float4*>(a.part_acc + (base + c) * kHD + lane * 4);
-        o0 = fmaf(ac.x, f, o0);
-        o1 = fmaf(ac.y, f, o1);
-        o2 = fmaf(ac.z, f, o2);
-        o3 = fmaf(ac.w, f, o3);
+        L += (ml.x == -INFINITY) ? 0.f : ml.y * expf(ml.x - M);
+    }
+    L = warp_sum(L);
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    constexpr int U = 8;
+    for (int cb = c0; cb <= c1; cb += U) {
+        float4 ac[U];
+        float f[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = cb + u;
+            if (c <= c1) {
+                const float mx = a.part_ml[base + c].x;
+                f[u] = (mx == -INFINITY) ? 0.f : expf(mx - M);
+                ac[u] = *reinterpret_cast<const float4*>(a.part_acc + (base + c) * kHD + lane * 4);
+            } else {
+                f[u] = 0.f;
+                ac[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            o[0] = fmaf(ac[u].x, f[u], o[0]);
+            o[1] = fmaf(ac[u].y, f[u], o[1]);
+            o[2] = fmaf(ac[u].z, f[u], o[2]);
+            o[3] = fmaf(ac[u].w, f[u], o[3]);
+        }
     }
     const float inv = 1.0f / L;
-    float o[4] = {o0 * inv, o1 * inv, o2 * inv, o3 * inv};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] *= inv;
     if (a.out_f32) {
         float* op = a.out_f32 + (size_t)s * a.n_heads * kHD + (size_t)h * kHD + lane * 4;
         *reinterpret_cast<float4*>(op) = make_float4(o[0], o[1], o[2], o[3]);

@@ -394,7 +394,7 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         aa.part_acc = c->part_acc;
         aa.out = c->act;
         aa.ctrl = ctrl;
-        CK(launch_attention(aa, 2 * device_sm_count(c->dev), c->st, pdl), "attention");
+        CK(launch_attention(aa, 4 * device_sm_count(c->dev), c->st, pdl), "attention");
         // o-proj (K-split partials summed by the next norm)
         Plan po;
         if ((rc = build_plan(c, po, EPI_STORE, W.wo, c->dim, c->q_rows, kRPW, S, 0))) return rc;
@@ -579,7 +579,7 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
     c->kv_rows = c->nkv_l * c->hd;
     c->qkv_rows = c->q_rows + 2 * c->kv_rows;
     c->hid_l = c->hidden / c->tp_size;
-    if (c->dim % 1024 || c->q_rows % 1024 || c->hid_l % 1024 || c->hid_l % 64)
+    if (c->dim % 1024 || c->dim > 4096 || c->q_rows % 1024 || c->hid_l % 1024 || c->hid_l % 64)
         return bail(fail(SD_ERR_UNSUPPORTED, "dims %d / %d / %d must be multiples of 1024", c->dim, c->q_rows, c->hid_l));
     if (cudaSetDevice(c->dev) != cudaSuccess) return bail(fail(SD_ERR_INVALID, "bad device %d", c->dev));
     if ((rc = ck(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking), "stream"))) return bail(rc);
@@ -661,6 +661,8 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
     cudaMemset(c->vc, 0, kvn * 2);
     const int MB = c->MB;
     const int amax = std::max(c->dim, c->q_rows);
+    // split-K chunk of the attention: short rings favour parallelism, long ones fewer partials
+    c->attn_chunk = c->max_seq <= 8192 ? 32 : (c->max_seq <= 32768 ? 64 : 128);
     c->max_chunks = (c->max_seq + c->attn_chunk - 1) / c->attn_chunk;
     if ((rc = dalloc(&c->x, (size_t)MB * c->dim)) || (rc = dalloc(&c->y, (size_t)c->ypart_max * MB * c->dim)) ||
         (rc = dalloc(&c->act.qs, (size_t)MB * amax)) || (rc = dalloc(&c->act.d, (size_t)MB * amax / 32)) ||

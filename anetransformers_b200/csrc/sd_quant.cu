@@ -77,16 +77,21 @@ cudaError_t launch_blocks_to_q8(const void* blocks, Q8Planes out, int S, int n, 
 }
 
 // ---------------------------------------------------------------------------------------------
-// Residual add / embed + RMSNorm + Q8_0 quantisation, one CTA (256 threads) per token.
-// Warp w owns blocks w, w+8, ...; lane j owns element j of each block, so the sum of squares is
+// Residual add / embed + RMSNorm + Q8_0 quantisation, one CTA (1024 threads) per token.
+// Warp w owns Q8_0 blocks w, w+32, ... (up to kNormMaxBPW of them); lane j owns element j of each
+// block.  Every global load of a thread is issued before any is consumed (x, all K-split partials of
+// y, the norm weight), so a token costs about one memory round trip.  The sum of squares is
 // accumulated in a fixed order per lane, reduced by a butterfly within the warp and then across the
-// 8 warps in order -- identical for every S (batch invariant).
+// 32 warps in order -- identical for every S (batch invariant).
 // ---------------------------------------------------------------------------------------------
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 1024;
+constexpr int kNormWarps = kNormThreads / 32;
+constexpr int kNormMaxBPW = 4;          // dim <= 32 * 32 * 4 = 4096
+constexpr int kNormMaxParts = 8;
 
 template <int MODE>
 __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
-    __shared__ float wsum[kNormThreads / 32];
+    __shared__ float wsum[kNormWarps];
     const int tok = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (a.ctrl && a.ctrl->done) return;
@@ -95,44 +100,66 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
     const int nv = a.ctrl ? min(a.ctrl->n_valid, a.S) : a.S;
     if (tok >= nv) return;
     const int nb = a.dim >> 5;
+    const int bpw = nb / kNormWarps;      // blocks per warp (dim % 1024 == 0)
     float* x = a.x + (size_t)tok * a.dim;
 
-    float ss = 0.f;
-    if constexpr (MODE == 0) {
-        const int token = a.tokens ? a.tokens[tok] : a.ctrl->tokens[tok];
-        const uint8_t* row = a.embd + (size_t)token * nb * 18;
-        for (int b = warp; b < nb; b += kNormThreads / 32) {
-            const uint8_t* blk = row + (size_t)b * 18;
-            const float dd = __half2float(__ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8))));
-            const uint8_t byte = blk[2 + (lane & 15)];
-            const int q = (lane < 16) ? (byte & 0x0F) : (byte >> 4);
-            const float v = dd * ((float)q - 8.0f);
-            x[b * 32 + lane] = v;
-            ss = fmaf(v, v, ss);
-        }
-    } else {
-        for (int b = warp; b < nb; b += kNormThreads / 32) {
-            float v = x[b * 32 + lane];
-            if constexpr (MODE == 1) {
-                const size_t yi = (size_t)tok * a.dim + b * 32 + lane;
-                float yv = a.y[yi];
-                for (int p = 1; p < a.yparts; ++p) yv += a.y[(size_t)p * a.ystride + yi];
-                v = v + yv;
-                x[b * 32 + lane] = v;
+    float v[kNormMaxBPW];
+    float wv[kNormMaxBPW];
+#pragma unroll
+    for (int k = 0; k < kNormMaxBPW; ++k) {
+        v[k] = 0.f;
+        wv[k] = 0.f;
+        if (k < bpw) {
+            const int e = (warp + kNormWarps * k) * 32 + lane;
+            wv[k] = a.w[e];
+            if constexpr (MODE == 0) {
+                const int token = a.tokens ? a.tokens[tok] : a.ctrl->tokens[tok];
+                const uint8_t* blk = a.embd + ((size_t)token * nb + (warp + kNormWarps * k)) * 18;
+                const float dd = __half2float(__ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8))));
+                const uint8_t byte = blk[2 + (lane & 15)];
+                const int q = (lane < 16) ? (byte & 0x0F) : (byte >> 4);
+                v[k] = dd * ((float)q - 8.0f);
+            } else {
+                v[k] = x[e];
             }
-            ss = fmaf(v, v, ss);
         }
     }
+    if constexpr (MODE == 1) {
+        float yv[kNormMaxBPW];
+#pragma unroll
+        for (int k = 0; k < kNormMaxBPW; ++k) yv[k] = 0.f;
+        // partial slices summed in slice order (K-split matvec outputs)
+#pragma unroll
+        for (int p = 0; p < kNormMaxParts; ++p) {
+            if (p < a.yparts) {
+#pragma unroll
+                for (int k = 0; k < kNormMaxBPW; ++k)
+                    if (k < bpw) yv[k] += a.y[(size_t)p * a.ystride + (size_t)tok * a.dim + (warp + kNormWarps * k) * 32 + lane];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kNormMaxBPW; ++k) v[k] = v[k] + yv[k];
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormMaxBPW; ++k)
+        if (k < bpw) {
+            ss = fmaf(v[k], v[k], ss);
+            if constexpr (MODE != 2) x[(warp + kNormWarps * k) * 32 + lane] = v[k];
+        }
     ss = warp_sum(ss);
     if (lane == 0) wsum[warp] = ss;
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
-    for (int w = 0; w < kNormThreads / 32; ++w) tot += wsum[w];
+    for (int w = 0; w < kNormWarps; ++w) tot += wsum[w];
     const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)a.dim) + a.eps));
 
-    for (int b = warp; b < nb; b += kNormThreads / 32) {
-        const float xn = (x[b * 32 + lane] * s) * a.w[b * 32 + lane];
+#pragma unroll
+    for (int k = 0; k < kNormMaxBPW; ++k) {
+        if (k >= bpw) continue;
+        const int b = warp + kNormWarps * k;
+        const float xn = (v[k] * s) * wv[k];
         if (a.xn_out) a.xn_out[(size_t)tok * a.dim + b * 32 + lane] = xn;
         float d;
         int sum;
