@@ -114,28 +114,27 @@ def measured_peaks():
         return {}
 
 
-def dominant_kernel_roofline(peaks):
-    """Time the dominant kernel -- the fused gate|up matvec (28672 x 4096 Q4_0, 66 MB) at the verify
-    shape S = K+1 = 5 -- live, with CUDA events over a captured loop of launches on rotating copies
-    (> L2).  Algorithmic bytes per launch = Q4_0 weights + Q8_0 activations + fp32 outputs."""
+def matvec_timing(rows, cols, S, n=64, copies=None, seed=7):
+    """Average device time (us) of the W4A8 matvec for a rows x cols Q4_0 matrix and S activation rows,
+    from CUDA events around a captured loop of n launches over rotating weight copies (> L2 in total),
+    plus the algorithmic bytes of one launch (Q4_0 weights + Q8_0 activations + fp32 outputs)."""
     import torch
     from anetransformers_b200 import dequant as dq
     from anetransformers_b200.gguf import random_q4_0
-    rows, cols, S = 28672, 4096, SPEC_K + 1
-    W = random_q4_0(np.random.default_rng(7), rows, cols)
-    mats = [dq.QMat(W, device=torch.cuda.current_device()) for _ in range(8)]
+    W = random_q4_0(np.random.default_rng(seed), rows, cols)
+    copies = copies or max(2, int(np.ceil(400e6 / W.nbytes)))
+    mats = [dq.QMat(W, device=torch.cuda.current_device()) for _ in range(copies)]
     x = torch.randn(S, cols, device="cuda")
     act = dq.quantize_dev(x)
     y = torch.empty(S, rows, device="cuda")
     for i in range(4):
-        dq.matvec_dev(mats[i % 8], act, y)
+        dq.matvec_dev(mats[i % copies], act, y)
     torch.cuda.synchronize()
-    n = 64
     s = torch.cuda.Stream()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
         for i in range(n):
-            dq.matvec_dev(mats[i % 8], act, y)
+            dq.matvec_dev(mats[i % copies], act, y)
     g.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -145,6 +144,15 @@ def dominant_kernel_roofline(peaks):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / n
     alg = W.nbytes + S * (cols + cols // 32 * 8) + S * rows * 4
+    del g, mats
+    return us, alg
+
+
+def dominant_kernel_roofline(peaks):
+    """The dominant kernel -- the fused gate|up matvec (28672 x 4096 Q4_0, 66 MB) at the verify shape
+    S = K+1 = 5 -- timed live with CUDA events (matvec_timing)."""
+    rows, cols, S = 28672, 4096, SPEC_K + 1
+    us, alg = matvec_timing(rows, cols, S)
     achieved = alg / (us * 1e-6) / 1e9
     peak = peaks.get("hbm_gbs", 6650.0)
     traffic = None
@@ -154,7 +162,6 @@ def dominant_kernel_roofline(peaks):
                 traffic = int(line.split(":")[1])
     except Exception:
         pass
-    del g, mats
     return {"bound": "hbm", "kernel": "k_gemv<EPI_STORE> 28672x4096 Q4_0, S=5", "achieved": round(achieved, 1),
             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic, "us_per_launch": round(us, 2),
@@ -208,6 +215,24 @@ def run_reference(args, rank, world, dist):
     print(json.dumps(line), flush=True)
 
 
+def run_gemv(args):
+    """single-op W4A8 matvec (Q4_0 4096 x 4096 by default, Q8_0 activations), S = 1 and
+    S = 5, in HBM GB/s of algorithmic bytes.  --shape / --S select other shapes (profiling runs)."""
+    import torch
+    rows, cols = (int(v) for v in args.shape.split("x"))
+    peaks = measured_peaks()
+    out = {}
+    for S in ([args.S] if args.S else [1, 5]):
+        us, alg = matvec_timing(rows, cols, S, n=args.steps * 8)
+        out[f"S{S}"] = {"us_per_launch": round(us, 3), "gbs": round(alg / (us * 1e-6) / 1e9, 1)}
+    best = max(v["gbs"] for v in out.values())
+    print(json.dumps({"metric": "W4A8 GEMV HBM GB/s", "value": best, "unit": "GB/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                      "config": {"workload": f"BASELINE config 1: Q4_0 {rows}x{cols} x Q8_0, rotating weight copies > L2"},
+                      "per_S": out, "peak": peaks.get("hbm_gbs"),
+                      "frac": round(best / peaks.get("hbm_gbs", 6650.0), 4)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -216,7 +241,13 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=GEN_TOKENS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="specdec", choices=["specdec", "gemv"])
+    ap.add_argument("--shape", default="4096x4096")
+    ap.add_argument("--S", type=int, default=0)
     args = ap.parse_args()
+    if args.workload == "gemv":
+        run_gemv(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

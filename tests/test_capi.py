@@ -41,3 +41,33 @@ def test_header_compiles_as_c():
     out = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", "-x", "c", HEADER],
                          capture_output=True, text=True)
     assert out.returncode == 0, out.stderr
+
+
+ROOT_LIB = os.path.join(ROOT, "anetransformers_b200")
+
+
+def build_compat_check(tmp_path):
+    exe = str(tmp_path / "compat_check")
+    cmd = ["gcc", "-std=gnu11", "-Wall", "-Wno-unused-function", "-I" + os.path.join(ROOT, "include"),
+           os.path.join(ROOT, "tests", "compat_check.c"), "-o", exe, "-L" + ROOT_LIB, "-lspecdec_b200",
+           "-Wl,-rpath," + ROOT_LIB, "-lm"]
+    out = subprocess.run(cmd, capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    return exe
+
+
+def test_compat_headers_compile_and_link(tmp_path):
+    exe = build_compat_check(tmp_path)
+    from tests.conftest import gpu_available
+    if not gpu_available():
+        out = subprocess.run([exe], capture_output=True, text=True)
+        assert out.returncode == 0 and "no-device" in out.stdout, out.stdout + out.stderr
+
+
+def test_cli_usage_and_errors():
+    cli = os.path.join(ROOT_LIB, "mistral")
+    assert os.path.exists(cli)
+    out = subprocess.run([cli], capture_output=True, text=True)
+    assert out.returncode == 1 and "--prompt-ids" in out.stderr
+    out = subprocess.run([cli, "--model", "/nonexistent", "--prompt", "hi"], capture_output=True, text=True)
+    assert out.returncode == 1 and "tokenizer" in out.stderr
