@@ -64,6 +64,7 @@ _SIGS = {
     "sd_blocks_to_q8_dev": (i32, [vp, Q8Dev, i32, i32, vp]),
     "sd_matvec_q4_0_q8_0_dev": (i32, [vp, Q8Dev, vp, i32, vp]),
     "sd_block_sums_dev": (i32, [vp, Q8Dev, vp, vp]),
+    "sd_matvec_q4_0_q8_0_noalloc_dev": (i32, [vp, Q8Dev, vp, i32, vp]),
     "sd_host_quantize_f32_to_q8_0": (None, [vp, vp, i32]),
     "sd_host_q4_0_q8_0_matvec": (None, [vp, vp, vp, i32, i32]),
     "sd_host_cache_clear": (None, []),

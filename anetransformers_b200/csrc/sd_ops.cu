@@ -419,3 +419,83 @@ void sd_host_cache_clear(void) {
 }
 
 }  // extern "C"
+
+// ------------------------------- allocation-free matvec --------------------------------------
+// Some callers cannot let a library allocate device memory at call time: a serving process that
+// hands all free HBM to its own pool at start-up (a late cudaMalloc fails there), or a latency loop
+// that cannot take the device-wide synchronisation of the cudaFree that sd_matvec_q4_0_q8_0_dev
+// performs when its partial-output workspace grows.  For them the K-split partial outputs live in a
+// fixed array below, which every GPU that loads this library holds until the process exits.
+namespace sd {
+
+static __device__ __align__(256) float g_noalloc_parts[SD_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+// Device address of g_noalloc_parts on `dev`, looked up once per device with that device current.
+// In host code the name g_noalloc_parts is only a host-side stand-in; kernels get this address.
+static int noalloc_scratch(int dev, float** out) {
+    static float* addr[64] = {nullptr};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) return fail(SD_ERR_INVALID, "no-alloc matvec: bad device %d", dev);
+    if (!addr[dev]) {
+        int prev = -1;
+        cudaError_t e = cudaGetDevice(&prev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+        if (prev != dev && (e = cudaSetDevice(dev)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+        float* p = nullptr;
+        e = cudaGetSymbolAddress((void**)&p, g_noalloc_parts);
+        if (prev != dev) cudaSetDevice(prev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (no-alloc matvec scratch)");
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return SD_OK;
+}
+
+}  // namespace sd
+
+extern "C" int sd_matvec_q4_0_q8_0_noalloc_dev(const sd_qmat* W, sd_q8_dev x, float* y, int S, void* stream) {
+    clear_error();
+    if (!W || !x.qs || !x.d || !x.sum || !y) return fail(SD_ERR_INVALID, "no-alloc matvec: null argument");
+    const int dev = W->device;
+    int rc = gemv_prepare_device(dev);
+    if (rc) return rc;
+    float* scratch = nullptr;
+    if ((rc = noalloc_scratch(dev, &scratch))) return rc;
+    GemvArgs a = {};
+    a.w = W->w;
+    a.n_rg = qmat_row_groups(W->rows);
+    a.nq = W->cols / 128;
+    a.K = W->cols;
+    a.rg_per_unit = kRPW;
+    a.n_units = a.n_rg / kRPW;
+    a.act = Q8Planes{x.qs, x.d, x.sum};
+    a.S = S;
+    a.ctrl = nullptr;
+    a.err = nullptr;  // no error word: it would need an allocation; the device waits stay bounded
+    a.out_ld = W->rows;
+    a.out_rows = W->rows;
+    a.kparts = 0;
+    int grid;
+    size_t smem;
+    if ((rc = gemv_plan(a, dev, &grid, &smem))) return rc;
+    const size_t n_out = (size_t)S * W->rows;
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (a.kparts > 1) {
+        const size_t need = n_out * a.kparts * sizeof(float);
+        if (need > SD_NOALLOC_SCRATCH_BYTES)
+            return fail(SD_ERR_INVALID,
+                        "no-alloc matvec: %d x %d at S=%d splits K into %d parts and needs %zu bytes of scratch; "
+                        "the limit is %zu bytes (use sd_matvec_q4_0_q8_0_dev)",
+                        W->rows, W->cols, S, a.kparts, need, (size_t)SD_NOALLOC_SCRATCH_BYTES);
+        // Every partial that k_sum_parts reads is written by this call's matvec first, so the array
+        // needs no clearing between calls.
+        a.out = scratch;
+        a.part_stride = n_out;
+    } else {
+        a.out = y;
+    }
+    cudaError_t e = launch_gemv(EPI_STORE, a, grid, smem, st, false);
+    if (e == cudaSuccess && a.kparts > 1) e = launch_sum_parts(scratch, y, (int)n_out, a.kparts, n_out, st);
+    return e == cudaSuccess ? SD_OK : cuda_fail(e, "no-alloc matvec launch");
+}

@@ -89,6 +89,19 @@ SD_API int sd_matvec_q4_0_q8_0_dev(const sd_qmat *W, sd_q8_dev x, float *y, int 
  * per-block SDOT result of mistral/dequant.h:1078-1083.  isum: device [rows][cols/32]. */
 SD_API int sd_block_sums_dev(const sd_qmat *W, sd_q8_dev x, int32_t *isum, void *stream);
 
+/* sd_matvec_q4_0_q8_0_dev for callers that cannot have device memory allocated on their behalf:
+ * a process that gives all free HBM to its own pool at start-up, or a latency loop that cannot take
+ * the device-wide synchronisation of a cudaFree.  It has no counterpart in the reference.
+ * Where the matvec splits K (long rows at larger S), the partial outputs go to a fixed array of
+ * SD_NOALLOC_SCRATCH_BYTES that the library keeps on every GPU that loads it, until exit; a shape
+ * whose partials do not fit is rejected with SD_ERR_INVALID.  The first call on a device looks up
+ * that array's address (and may load the library's device code): make it before any stream capture.
+ * All calls on one device share the array, so calls that overlap on the GPU (different streams, or
+ * different threads) race and give wrong results; serialise them.  Results equal those of
+ * sd_matvec_q4_0_q8_0_dev bit for bit.  Device waits that run out are not reported. */
+#define SD_NOALLOC_SCRATCH_BYTES (1u << 20)
+SD_API int sd_matvec_q4_0_q8_0_noalloc_dev(const sd_qmat *W, sd_q8_dev x, float *y, int S, void *stream);
+
 /* Host-pointer drop-ins with the reference signatures (mistral/dequant.h:545 and :1022).  They run
  * on the current device; the matvec uploads and repacks W on first use and caches it keyed by the
  * host address and shape (weights are immutable mmap'd tensors in the reference).  Errors are
