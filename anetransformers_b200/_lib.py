@@ -31,12 +31,14 @@ class ModelInfo(C.Structure):
     _fields_ = [("dim", C.c_int), ("hidden_dim", C.c_int), ("n_layers", C.c_int), ("n_heads", C.c_int),
                 ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("vocab_size", C.c_int), ("max_seq", C.c_int),
                 ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("bos_id", C.c_int), ("eos_id", C.c_int),
-                ("tp_rank", C.c_int), ("tp_size", C.c_int), ("weight_bytes", C.c_size_t), ("kv_bytes", C.c_size_t)]
+                ("tp_rank", C.c_int), ("tp_size", C.c_int), ("weight_bytes", C.c_size_t), ("kv_bytes", C.c_size_t),
+                ("forward_kernel", C.c_int)]
 
 
 class CtxOpts(C.Structure):
     _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("max_batch", C.c_int), ("tp_rank", C.c_int),
-                ("tp_size", C.c_int), ("nccl_comm", C.c_void_p), ("use_graphs", C.c_int), ("use_pdl", C.c_int)]
+                ("tp_size", C.c_int), ("nccl_comm", C.c_void_p), ("use_graphs", C.c_int), ("use_pdl", C.c_int),
+                ("forward_kernel", C.c_int)]
 
 
 class GenParams(C.Structure):

@@ -31,6 +31,7 @@
 #include <unistd.h>
 
 #include "sd_attn.h"
+#include "sd_fwd.h"
 #include "sd_common.cuh"
 #include "sd_host.h"
 #include "sd_spec.h"
@@ -273,6 +274,15 @@ struct sd_ctx {
     int iter_key[6] = {-1, -1, -1, -1, -1, -1};
     GenParamsDev iter_p{};
     unsigned long long rng_start = 1ull << 20;  // Philox counter the next decode loop starts from
+    // persistent forward kernel (forward_kernel = 1)
+    bool fused = false;
+    FwdLayer* d_layers = nullptr;  // device copy of the per-layer weight pointers
+    float* ssq = nullptr;          // [MB][dim/16] group sums of squares of x
+    Q8Planes unorm{};              // [MB][dim] Q8_0 of x * (next norm weight)
+    unsigned* fsync = nullptr;     // grid barrier + slice counters
+    MvPhase ph_qkv{}, ph_wo{}, ph_w13{}, ph_w2{}, ph_lm{};
+    int fwd_stages = 0, fwd_grid = 0;
+    size_t fwd_smem = 0;
     // TP
     void* nccl = nullptr;
 };
@@ -336,14 +346,128 @@ int build_plan(sd_ctx* c, Plan& p, int epi, const uint8_t* w, int rows, int K, i
     return gemv_plan(a, c->dev, &p.grid, &p.smem);
 }
 
+// K split of a matvec, fixed for every S: the split the planner picks at the largest S.  A split that
+// changed with S would change the summation order, and a token's result must not depend on how many
+// tokens share its forward (verify rows equal single-token decode rows bit for bit).
+int fixed_kparts(sd_ctx* c, int rows, int K, int* kparts) {
+    Plan p;
+    int rc = build_plan(c, p, EPI_STORE, nullptr, rows, K, kRPW, kMaxS, 0);
+    if (rc) return rc;
+    *kparts = p.a.kparts;
+    return SD_OK;
+}
+
 int launch_plan(sd_ctx* c, int epi, Plan& p) {
     cudaError_t e = launch_gemv(epi, p.a, p.grid, p.smem, c->st, c->use_pdl);
     return e == cudaSuccess ? SD_OK : cuda_fail(e, "matvec launch");
 }
 
+// Plan of one matvec phase of the persistent forward (the same K split and chunk as the per-op
+// path); false if the shape does not fit the kernel's activation buffer.
+bool fwd_phase(MvPhase& p, int rows, int K, int rpu, int kparts) {
+    const int n_rg = qmat_row_groups(rows);
+    if (n_rg % rpu || K % 128 || kparts < 1) return false;
+    p.n_units = n_rg / rpu;
+    p.rpu = rpu;
+    p.nq = K / 128;
+    p.kparts = kparts;
+    if (p.nq % kparts) return false;
+    const int nqp = p.nq / kparts;
+    p.chunk = gemv_chunk(nqp);
+    return nqp % p.chunk == 0 && nqp <= 32;
+}
+
+// Set up the persistent forward kernel; leaves c->fused false (per-op kernels) where it does not apply.
+int setup_fused(sd_ctx* c) {
+    int coop = 0;
+    CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->dev), "device attribute");
+    if (!coop || c->tp_size != 1) return SD_OK;
+    int kp_o = 0, kp_d = 0, rc;
+    if ((rc = fixed_kparts(c, c->dim, c->q_rows, &kp_o)) || (rc = fixed_kparts(c, c->dim, c->hid_l, &kp_d))) return rc;
+    if (kp_o > c->ypart_max || kp_d > c->ypart_max) return SD_OK;
+    if (!fwd_phase(c->ph_qkv, c->qkv_rows, c->dim, kRPW, 1) || !fwd_phase(c->ph_wo, c->dim, c->q_rows, kRPW, kp_o) ||
+        !fwd_phase(c->ph_w13, 2 * c->hid_l, c->dim, 2 * kRPW, 1) || !fwd_phase(c->ph_w2, c->dim, c->hid_l, kRPW, kp_d) ||
+        !fwd_phase(c->ph_lm, c->vocab, c->dim, kRPW, 1))
+        return SD_OK;
+    const int max_smem = device_max_smem(c->dev);
+    c->fwd_stages = fwd_pick_stages(max_smem);
+    if (c->fwd_stages < 3) return SD_OK;
+    c->fwd_smem = fwd_smem_bytes(c->fwd_stages);
+    CK(fwd_init_attrs(max_smem), "cudaFuncSetAttribute (forward)");
+    int per_sm = 0;
+    CK(fwd_blocks_per_sm(c->fwd_smem, &per_sm), "occupancy");
+    if (per_sm < 1) return SD_OK;
+    c->fwd_grid = device_sm_count(c->dev);
+    std::vector<FwdLayer> hl(c->n_layers);
+    for (int l = 0; l < c->n_layers; ++l)
+        hl[l] = FwdLayer{c->L[l].qkv, c->L[l].wo, c->L[l].w13, c->L[l].w2, c->L[l].rms_att, c->L[l].rms_ffn};
+    if ((rc = dalloc(&c->d_layers, hl.size())) || (rc = dalloc(&c->ssq, (size_t)c->MB * (c->dim / 16))) ||
+        (rc = dalloc(&c->fsync, fwd_sync_words(c->dim))) || (rc = dalloc(&c->unorm.qs, (size_t)c->MB * c->dim)) ||
+        (rc = dalloc(&c->unorm.d, (size_t)c->MB * c->dim / 32)) || (rc = dalloc(&c->unorm.sum, (size_t)c->MB * c->dim / 32)))
+        return rc;
+    CK(cudaMemcpy(c->d_layers, hl.data(), hl.size() * sizeof(FwdLayer), cudaMemcpyHostToDevice), "layer table");
+    CK(cudaMemset(c->fsync, 0, fwd_sync_words(c->dim) * sizeof(unsigned)), "memset");
+    c->fused = true;
+    return SD_OK;
+}
+
+// One forward as a single persistent kernel (then the argmax kernel when logits are wanted).
+int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
+    FwdArgs a{};
+    a.layers = c->d_layers;
+    a.n_layers = n_layers;
+    a.embd = c->embd;
+    a.rms_out = c->rms_final;
+    a.lm = logits_and_argmax ? c->lm : nullptr;
+    a.dim = c->dim;
+    a.hidden = c->hid_l;
+    a.q_rows = c->q_rows;
+    a.kv_rows = c->kv_rows;
+    a.vocab = c->vocab;
+    a.head_dim = c->hd;
+    a.n_heads = c->nh_l;
+    a.n_kvh = c->nkv_l;
+    a.S = S;
+    a.max_seq = c->max_seq;
+    a.eps = c->eps;
+    a.q_scale = 1.0f / sqrtf((float)c->hd);
+    a.theta_inv = c->theta_inv;
+    a.k_cache = k;
+    a.v_cache = v;
+    a.kv_layer = (size_t)c->max_seq * c->kv_rows;
+    a.qkv = c->ph_qkv;
+    a.wo = c->ph_wo;
+    a.w13 = c->ph_w13;
+    a.w2 = c->ph_w2;
+    a.lmp = c->ph_lm;
+    a.nstage = c->fwd_stages;
+    a.x = c->x;
+    a.ssq = c->ssq;
+    a.un = c->unorm;
+    a.q = c->q;
+    a.attn = c->act;
+    a.h = c->hact;
+    a.yparts = c->y;
+    a.ypart_stride = (size_t)c->MB * c->dim;
+    a.sync = c->fsync;
+    a.part_ml = c->part_ml;
+    a.part_acc = c->part_acc;
+    a.attn_chunk = c->attn_chunk;
+    a.max_chunks = c->max_chunks;
+    a.logits = c->logits;
+    a.tokens = nullptr;
+    a.ctrl = ctrl;
+    a.err = c->err;
+    CK(cudaMemsetAsync(c->fsync, 0, fwd_sync_words(c->dim) * sizeof(unsigned), c->st), "memset");
+    CK(launch_forward(a, c->fwd_grid, c->fwd_smem, c->st), "forward launch");
+    if (logits_and_argmax) CK(launch_argmax(c->logits, c->vocab, S, c->argmax, ctrl, c->st, false), "argmax");
+    return SD_OK;
+}
+
 // Enqueue one forward of S (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the
 // position, the tokens and how many of the S are valid.
 int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
+    if (c->fused) return enqueue_forward_fused(c, S, n_layers, k, v, ctrl, logits_and_argmax);
     const bool pdl = c->use_pdl;
     NormArgs na{};
     na.x = c->x;
@@ -397,7 +521,10 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         CK(launch_attention(aa, 4 * device_sm_count(c->dev), c->st, pdl), "attention");
         // o-proj (K-split partials summed by the next norm)
         Plan po;
-        if ((rc = build_plan(c, po, EPI_STORE, W.wo, c->dim, c->q_rows, kRPW, S, 0))) return rc;
+        int kp_o = 0, kp_d = 0;
+        if ((rc = fixed_kparts(c, c->dim, c->q_rows, &kp_o))) return rc;
+        if ((rc = fixed_kparts(c, c->dim, c->hid_l, &kp_d))) return rc;
+        if ((rc = build_plan(c, po, EPI_STORE, W.wo, c->dim, c->q_rows, kRPW, S, kp_o))) return rc;
         po.a.act = c->act;
         po.a.ctrl = ctrl;
         po.a.out = c->y;
@@ -419,7 +546,7 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         if ((rc = launch_plan(c, EPI_SILU_Q8, pg))) return rc;
         // down
         Plan pd;
-        if ((rc = build_plan(c, pd, EPI_STORE, W.w2, c->dim, c->hid_l, kRPW, S, 0))) return rc;
+        if ((rc = build_plan(c, pd, EPI_STORE, W.w2, c->dim, c->hid_l, kRPW, S, kp_d))) return rc;
         pd.a.act = c->hact;
         pd.a.ctrl = ctrl;
         pd.a.out = c->y;
@@ -517,6 +644,7 @@ void sd_ctx_opts_default(sd_ctx_opts* o) {
     o->tp_size = 1;
     o->use_graphs = 1;
     o->use_pdl = 1;
+    o->forward_kernel = 0;
 }
 
 void sd_ctx_free(sd_ctx* c) {
@@ -535,6 +663,8 @@ void sd_ctx_free(sd_ctx* c) {
     cudaFree(c->hact.qs); cudaFree(c->hact.d); cudaFree(c->hact.sum); cudaFree(c->q);
     cudaFree(c->part_ml); cudaFree(c->part_acc); cudaFree(c->logits); cudaFree(c->probs); cudaFree(c->argmax);
     cudaFree(c->ctrl); cudaFree(c->dctrl); cudaFree(c->err); cudaFree(c->gs); cudaFree(c->g_out); cudaFree(c->g_hist);
+    cudaFree(c->d_layers); cudaFree(c->ssq); cudaFree(c->fsync);
+    cudaFree(c->unorm.qs); cudaFree(c->unorm.d); cudaFree(c->unorm.sum);
     if (c->ctrl_h) cudaFreeHost(c->ctrl_h);
     if (c->tok_h) cudaFreeHost(c->tok_h);
     if (c->gs_h) cudaFreeHost(c->gs_h);
@@ -682,6 +812,7 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
         (rc = ck(cudaMallocHost(&c->tok_h, sizeof(int32_t) * 4096), "pinned")) ||
         (rc = ck(cudaMallocHost(&c->gs_h, sizeof(GenState)), "pinned")))
         return bail(rc);
+    if (o.forward_kernel && (rc = setup_fused(c))) return bail(rc);
     if ((rc = ck(cudaDeviceSynchronize(), "context build"))) return bail(rc);
     *out = c;
     return SD_OK;
@@ -715,6 +846,7 @@ int sd_ctx_info(const sd_ctx* c, sd_model_info* o) {
     o->n_kv_heads = c->n_kv; o->head_dim = c->hd; o->vocab_size = c->vocab; o->max_seq = c->max_seq;
     o->rope_theta = c->theta; o->rms_eps = c->eps; o->bos_id = c->bos; o->eos_id = c->eos;
     o->tp_rank = c->tp_rank; o->tp_size = c->tp_size; o->weight_bytes = c->weight_bytes; o->kv_bytes = c->kv_bytes;
+    o->forward_kernel = c->fused ? 1 : 0;
     return SD_OK;
 }
 

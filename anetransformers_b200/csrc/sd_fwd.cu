@@ -1,0 +1,649 @@
+// sd_fwd.cu -- the whole forward of S <= 8 tokens (decode step or S = K+1 verify) as one persistent
+// kernel: one CTA per SM, launched cooperatively so that every CTA is resident and grid-wide barriers
+// are safe.
+//
+// Replaces the per-layer kernel sequence of the reference's batched forward (mistral/mistral_infer.m:
+// 103-179 driving mistral/mistral_model.h:490-560): embedding, RMSNorm + Q8_0, fused QKV matvec with
+// RoPE and the KV-ring write, 4:1 GQA attention, o-proj + residual, RMSNorm + Q8_0, gate|up matvec with
+// SiLU and Q8_0, down projection + residual, final norm and LM head.
+//
+// Why one kernel: at S <= 8 every matvec streams its weights once and does little math, so a forward
+// is a ~3.9 GB weight stream interrupted by small latency-bound steps.  Here a producer warp per CTA
+// streams the weight tiles of every matvec of the forward, in order, through a shared-memory ring (1-D
+// bulk copies, no multicast); weights do not depend on activations, so the ring keeps filling with the
+// next matvec's tiles while the CTA waits in a grid barrier, runs attention or normalises.
+//
+// Warp roles (608 threads): warps 0-15 consume tiles (int8 MMA), 16-17 reduce the 16 partials of a
+// row-group and apply the epilogue, 18 is the producer.  Warps 0-17 also run the non-matvec phases.
+//
+// Phases of a layer, each ended by a grid barrier:
+//   QKV    norm of x staged in every CTA (group sums of squares come with x), matvec, RoPE, KV write
+//   ATTN   (kv head, chunk) partials, two 128-thread groups per CTA
+//   COMB   merge of the chunk partials and Q8_0 of the head outputs
+//   WO     matvec; epilogue x += y and the group sums of squares of the new x
+//   W13    norm of x, gate|up matvec, SiLU(gate)*up, Q8_0
+//   W2     K-split matvec; the last slice to finish a row-group adds the slices into x
+// The arithmetic (tile math, reduction orders, norms, attention) is the same device code as the
+// per-op kernels, so both paths give bit-identical logits.
+#include "sd_dev.cuh"
+#include "sd_fwd.h"
+
+namespace sd {
+
+namespace {
+
+constexpr int kComputeWarps = kConsumerWarps + kEpiWarps;   // 18
+constexpr int kComputeThreads = kComputeWarps * 32;         // 576
+constexpr int kConsumerThreads = kConsumerWarps * 32;       // 512
+constexpr int kProducerWarp = kComputeWarps;
+constexpr int kMaxChunk = 16;
+constexpr uint32_t kStageBytes = kRPW * kMaxChunk * kTileBytes;  // 36864
+constexpr int kActMaxNb = 128;                                   // K slice <= 4096 columns
+constexpr uint32_t kGridSpinLimit = 1u << 22;                    // polls of 64+ ns: > 0.25 s
+
+// named barrier ids: 0 = __syncthreads, 1 = compute warps, 2 = the two epilogue warps,
+// 3 = consumer warps (staging), 4.. = attention groups
+constexpr int kBarCompute = 1, kBarEpi = 2, kBarStage = 3, kBarAttn0 = 4;
+
+struct FwdSmem {
+    size_t ring, act, red, ubuf, misc, bars, total;
+};
+
+__host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline FwdSmem fwd_layout(int nstage) {
+    FwdSmem L{};
+    L.ring = 0;
+    L.act = L.ring + (size_t)nstage * kStageBytes;
+    const size_t act_bytes = act_smem_bytes(kActMaxNb, kMaxS);
+    const size_t red_bytes = (size_t)kRedSlots * kRPW * kConsumerWarps * 128 * 4;
+    L.red = L.act + align_up(act_bytes, 128);
+    L.ubuf = L.red + red_bytes;
+    size_t uni = (L.ubuf + 4 * 128 * 4) - L.act;
+    const size_t attn = (size_t)kFwdAttnGroups * attn_smem_bytes();
+    if (attn > uni) uni = attn;
+    L.misc = L.act + align_up(uni, 128);
+    L.bars = L.misc + 512;  // misc: scale[kMaxS], abort, producer issued/done, epilogue pair scratch
+    L.total = L.bars + (2 * kMaxStages + 2 * kRedSlots) * 8;
+    return L;
+}
+
+// Scratch the two epilogue warps share while finishing a pair of row-groups (one Q8_0 block of x).
+struct PairX {
+    float am[kEpiWarps][8];
+    int qs[kEpiWarps][8];
+    int ab[kEpiWarps];
+    int last;
+};
+
+struct Misc {
+    float scale[kMaxS];
+    int abort;
+    int grid_ok;
+    uint32_t issued;
+    int pdone;
+    PairX px;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Single-thread wait that also gives up as soon as another warp of the CTA has aborted.
+__device__ __forceinline__ bool wait_or_abort_1(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31) == 31 && *abort_flag) return false;
+    }
+    return false;
+}
+
+// Whole-warp form: every lane waits (each lane then sees the data the phase guards) and the result
+// is made warp-uniform, so the warp never diverges on a give-up.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+    const bool ok = wait_or_abort_1(bar, parity, abort_flag);
+    return __all_sync(0xffffffffu, ok);
+}
+
+struct Items {
+    int i0, i1;
+};
+
+__device__ __forceinline__ Items my_items(const MvPhase& p) {
+    const int n = p.n_units * p.kparts, G = gridDim.x, c = blockIdx.x;
+    return Items{(int)((long long)c * n / G), (int)((long long)(c + 1) * n / G)};
+}
+
+// Grid barrier of the compute warps (CTA-wide arrive by thread 0, as cooperative groups do).  A CTA
+// that has aborted stops synchronising; the others then run out their bounded wait and abort too.
+__device__ void grid_barrier(const FwdArgs& a, Misc* m, uint32_t& target) {
+    named_sync(kBarCompute, kComputeThreads);
+    if (threadIdx.x == 0) {
+        target += gridDim.x;
+        volatile int* ab = &m->abort;
+        if (!*ab) {
+            __threadfence();
+            atomicAdd(&a.sync[0], 1u);
+            uint32_t n = 0;
+            while (ld_acquire_u32(&a.sync[0]) < target) {
+                if (++n > kGridSpinLimit) {
+                    set_dev_error(a.err, DEV_ERR_PEER_WAIT);
+                    *ab = 1;
+                    break;
+                }
+                __nanosleep(64);
+            }
+            __threadfence();
+        }
+    }
+    named_sync(kBarCompute, kComputeThreads);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Activation staging (consumer warps only)
+// ---------------------------------------------------------------------------------------------
+
+// Normalised activations: the producing epilogue already wrote Q8_0 of u = x*w (codes, sums, block
+// scales d_u) and the 16-row sums of squares of x; here each token's RMSNorm scale s is formed from
+// those sums and the block scales become d_u * s while the planes are staged.
+__device__ void stage_norm(const FwdArgs& a, const ActSmem& A, Misc* m, int nb, int nv, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int ngroups = a.dim >> 4;
+    if (warp < nv) {
+        const float tot = row_sumsq(a.ssq + (size_t)warp * ngroups, ngroups, lane);
+        if (lane == 0) m->scale[warp] = rms_scale(tot, a.dim, a.eps);
+    }
+    named_sync(kBarStage, kConsumerThreads);
+    stage_act_from_planes(A, a.un, a.dim, 0, nb, a.S, nv, tid, kConsumerThreads, m->scale);
+}
+
+// Q8_0 of u = v*w for one 32-value block (thread-level; the arithmetic of q8_quant_lane).
+__device__ __forceinline__ void q8_block_thread(const float* u, int8_t* qs, float* d_out, int* sum_out) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(u[i]));
+    const float d = __fdiv_rn(am, 127.0f);
+    int sum = 0;
+    int q[32];
+    if (am != 0.0f) {
+        const float id = __fdiv_rn(1.0f, d);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int r = __float2int_rn(__fmul_rn(u[i], id));
+            q[i] = r > 127 ? 127 : (r < -128 ? -128 : r);
+            sum += q[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) q[i] = 0;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        const uint32_t w = (uint32_t)(q[i] & 0xFF) | ((uint32_t)(q[i + 1] & 0xFF) << 8) | ((uint32_t)(q[i + 2] & 0xFF) << 16) |
+                           ((uint32_t)(q[i + 3] & 0xFF) << 24);
+        *reinterpret_cast<uint32_t*>(qs + i) = w;
+    }
+    *d_out = d;
+    *sum_out = sum;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Phase kinds
+// ---------------------------------------------------------------------------------------------
+enum PhaseKind : int { PH_QKV = 0, PH_WO = 1, PH_W13 = 2, PH_W2 = 3, PH_LM = 4 };
+
+struct Ring {
+    uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* red_full;
+    uint64_t* red_empty;
+    float* red;
+    float* ubuf;
+    int nstage;
+};
+
+// Residual update of row-group rg (epilogue warp r of the pair): x[tok][row] += t (the slice partials
+// already summed in slice order, as the per-op norm kernel adds them); the group's sum of squares of
+// the new x; and Q8_0 of u = x*wn for the next RMSNorm (wn its weight), the block being the pair's 32
+// rows: the two warps exchange their block maxima and code sums through px.  Both epilogue warps call
+// this together.
+__device__ void resid_update(const FwdArgs& a, const float (&t)[4], int rg, int r, int lane, int nv, const float* wn,
+                             PairX* px) {
+    float xv[4], u[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
+        const int gr = rg * kTileRows + row;
+        xv[k] = 0.f;
+        if (tok < nv) {
+            float* xp = a.x + (size_t)tok * a.dim + gr;
+            xv[k] = *xp + t[k];
+            *xp = xv[k];
+        }
+        u[k] = xv[k] * wn[gr];
+    }
+    const float ss = group16_sumsq_epi(xv);
+    if (lane < nv) a.ssq[(size_t)lane * (a.dim >> 4) + rg] = ss;
+    float am = fmaxf(fmaxf(fabsf(u[0]), fabsf(u[1])), fmaxf(fabsf(u[2]), fabsf(u[3])));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 8));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 16));
+    if (lane < 8) px->am[r][lane] = am;
+    named_sync(kBarEpi, kEpiWarps * 32);
+    const float amax = fmaxf(px->am[0][lane & 7], px->am[1][lane & 7]);
+    const float d = __fdiv_rn(amax, 127.0f);
+    int q[4] = {0, 0, 0, 0};
+    if (amax != 0.0f) {
+        const float id = __fdiv_rn(1.0f, d);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int rr = __float2int_rn(__fmul_rn(u[k], id));
+            q[k] = rr > 127 ? 127 : (rr < -128 ? -128 : rr);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
+        if (tok < nv) a.un.qs[(size_t)tok * a.dim + rg * kTileRows + row] = (int8_t)q[k];
+    }
+    int qs = q[0] + q[1] + q[2] + q[3];
+    qs += __shfl_xor_sync(0xffffffffu, qs, 8);
+    qs += __shfl_xor_sync(0xffffffffu, qs, 16);
+    if (lane < 8) px->qs[r][lane] = qs;
+    named_sync(kBarEpi, kEpiWarps * 32);
+    if (r == 0 && lane < nv) {
+        const size_t bi = (size_t)lane * (a.dim >> 5) + (rg >> 1);
+        a.un.sum[bi] = px->qs[0][lane] + px->qs[1][lane];
+        a.un.d[bi] = d;
+    }
+    named_sync(kBarEpi, kEpiWarps * 32);  // px may be reused
+}
+
+// One matvec phase for the compute warps (consumer and epilogue roles).
+template <int KIND>
+__device__ void mv_phase(const FwdArgs& a, const MvPhase& p, int layer, const Ring& R, Misc* m, uint32_t& sidx,
+                         uint32_t& pidx, bool& ab, int nv, int pos, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const Items it = my_items(p);
+    const int nq_p = p.nq / p.kparts, cpr = nq_p / p.chunk, pairs = p.rpu / kRPW;
+    const int nb = nq_p * 4;
+    const uint32_t half = (uint32_t)p.chunk * kTileBytes;
+    const ActSmem A = act_smem_at(R.ring + (size_t)R.nstage * kStageBytes, nb, a.S);
+    const volatile int* abort_flag = &m->abort;
+
+    if (warp < kConsumerWarps) {
+        // ============================ consumers ============================
+        int cur_part = -1;
+        const bool has_tile = warp < p.chunk;
+        for (int i = it.i0; i < it.i1; ++i) {
+            const int part = i / p.n_units, unit = i % p.n_units;
+            if (part != cur_part) {
+                named_sync(kBarStage, kConsumerThreads);  // every consumer is done with the previous slice
+                if constexpr (KIND == PH_QKV || KIND == PH_W13 || KIND == PH_LM) {
+                    stage_norm(a, A, m, nb, nv, tid);
+                } else if constexpr (KIND == PH_WO) {
+                    stage_act_from_planes(A, a.attn, a.q_rows, part * nb, nb, a.S, nv, tid, kConsumerThreads);
+                } else {
+                    stage_act_from_planes(A, a.h, a.hidden, part * nb, nb, a.S, nv, tid, kConsumerThreads);
+                }
+                named_sync(kBarStage, kConsumerThreads);
+                cur_part = part;
+            }
+            float2 accL[kRPW], accH[kRPW];
+            for (int pr = 0; pr < pairs; ++pr) {
+                const int rg = unit * p.rpu + pr * kRPW;
+#pragma unroll
+                for (int r = 0; r < kRPW; ++r) accL[r] = accH[r] = make_float2(0.f, 0.f);
+                for (int ch = 0; ch < cpr; ++ch, ++sidx) {
+                    const int slot = sidx % R.nstage;
+                    if (!ab && !wait_or_abort(&R.full[slot], (sidx / R.nstage) & 1, abort_flag)) {
+                        set_dev_error(a.err, DEV_ERR_FULL_WAIT);
+                        ab = true;
+                        m->abort = 1;
+                    }
+                    if (ab) continue;  // an aborted warp releases nothing more (see the drain)
+                    if (has_tile) {
+                        TileRegs tr;
+                        load_tiles(R.ring + (size_t)slot * kStageBytes, half, warp, lane, tr);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&R.empty[slot]);
+                        consume_tiles<false>(tr, lane, A, a.S, (ch * p.chunk + warp) * 4, accL, accH, nullptr, rg, 0,
+                                             0, 0);
+                    } else {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&R.empty[slot]);
+                    }
+                }
+                const int rs = pidx % kRedSlots;
+                if (pidx >= kRedSlots && !ab &&
+                    !wait_or_abort(&R.red_empty[rs], ((pidx / kRedSlots) - 1) & 1, abort_flag)) {
+                    set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
+                    ab = true;
+                    m->abort = 1;
+                }
+                ++pidx;
+                if (ab) continue;
+                if (has_tile) write_partials(R.red + (size_t)rs * kRPW * kConsumerWarps * 128, warp, lane, accL, accH);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&R.red_full[rs]);
+            }
+        }
+        return;
+    }
+
+    // ============================ epilogue warps ============================
+    const int r = warp - kConsumerWarps;
+    for (int i = it.i0; i < it.i1; ++i) {
+        const int part = i / p.n_units, unit = i % p.n_units;
+        for (int pr = 0; pr < pairs; ++pr, ++pidx) {
+            const int slot = pidx % kRedSlots;
+            if (!ab && !wait_or_abort(&R.red_full[slot], (pidx / kRedSlots) & 1, abort_flag)) {
+                set_dev_error(a.err, DEV_ERR_FULL_WAIT);
+                ab = true;
+                m->abort = 1;
+            }
+            const int rg = unit * p.rpu + pr * kRPW + r;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (!ab) {
+                reduce_partials(R.red + ((size_t)slot * kRPW + r) * kConsumerWarps * 128, p.chunk, lane, v);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&R.red_empty[slot]);
+            }
+            if constexpr (KIND == PH_QKV) {
+                if (!ab)
+                    epi_qkv(v, rg, lane, nv, pos, a.q, a.k_cache + (size_t)layer * a.kv_layer,
+                            a.v_cache + (size_t)layer * a.kv_layer, a.q_rows, a.kv_rows, a.max_seq, a.head_dim,
+                            a.theta_inv, a.q_scale);
+            } else if constexpr (KIND == PH_LM) {
+                if (!ab) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
+                        const int gr = rg * kTileRows + row;
+                        if (gr < a.vocab && tok < nv) a.logits[(size_t)tok * a.vocab + gr] = v[k];
+                    }
+                }
+            } else if constexpr (KIND == PH_W13) {
+                // unit of 4 row-groups = 2 pairs: (gate lo, gate hi), (up lo, up hi)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) R.ubuf[(pr * 2 + r) * 128 + lane + 32 * k] = v[k];
+                if (pr == 1) {
+                    named_sync(kBarEpi, kEpiWarps * 32);
+                    if (!ab) epi_silu_q8(R.ubuf, r, lane, unit, nv, a.h, a.hidden);
+                    named_sync(kBarEpi, kEpiWarps * 32);
+                }
+            } else {
+                // PH_WO / PH_W2: residual add (through the slice counters when K is split) and the next
+                // norm's Q8_0 input.  Both epilogue warps take every step together.
+                const float* wn = KIND == PH_WO ? a.layers[layer].rms_ffn
+                                : (layer + 1 < a.n_layers ? a.layers[layer + 1].rms_att : a.rms_out);
+                PairX* px = &m->px;
+                if (p.kparts > 1 && !ab) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
+                        if (tok < nv)
+                            a.yparts[(size_t)part * a.ypart_stride + (size_t)tok * a.dim + rg * kTileRows + row] = v[k];
+                    }
+                }
+                if (p.kparts > 1) __threadfence();  // this warp's slice is visible before the counter moves
+                if (lane == 0) px->ab[r] = ab ? 1 : 0;
+                named_sync(kBarEpi, kEpiWarps * 32);
+                if (r == 0 && lane == 0) {
+                    int last = 0;
+                    if (!(px->ab[0] | px->ab[1]))
+                        last = p.kparts == 1 || atomicAdd(&a.sync[1 + unit], 1u) == (uint32_t)(p.kparts - 1);
+                    px->last = last;
+                }
+                named_sync(kBarEpi, kEpiWarps * 32);
+                if (px->last) {
+                    float t[4];
+                    if (p.kparts == 1) {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) t[k] = 0.f + v[k];
+                    } else {
+                        __threadfence();
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
+                            t[k] = 0.f;
+                            if (tok < nv)
+                                for (int q = 0; q < p.kparts; ++q)
+                                    t[k] += __ldcg(a.yparts + (size_t)q * a.ypart_stride + (size_t)tok * a.dim +
+                                                   rg * kTileRows + row);
+                        }
+                    }
+                    resid_update(a, t, rg, r, lane, nv, wn, px);
+                    if (p.kparts > 1 && r == 0 && lane == 0) a.sync[1 + unit] = 0;  // all slices arrived: reset
+                } else {
+                    named_sync(kBarEpi, kEpiWarps * 32);  // px->last read by both warps before it is rewritten
+                }
+            }
+        }
+    }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const FwdSmem L = fwd_layout(a.nstage);
+    Misc* m = reinterpret_cast<Misc*>(smem + L.misc);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+    uint64_t* empty = full + kMaxStages;
+    uint64_t* red_full = empty + kMaxStages;
+    uint64_t* red_empty = red_full + kRedSlots;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x;
+
+    if (a.ctrl && a.ctrl->done) return;  // uniform: nothing writes ctrl while the kernel runs
+    const int nv = a.ctrl ? min(a.ctrl->n_valid, a.S) : a.S;
+    const int pos = a.ctrl ? a.ctrl->pos : 0;
+
+    if (tid == 0) {
+        for (int i = 0; i < a.nstage; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kConsumerWarps);
+        }
+        for (int i = 0; i < kRedSlots; ++i) {
+            mbar_init(&red_full[i], kConsumerWarps);
+            mbar_init(&red_empty[i], kEpiWarps);
+        }
+        m->abort = 0;
+        m->issued = 0;
+        m->pdone = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    Ring R;
+    R.ring = smem + L.ring;
+    R.full = full;
+    R.empty = empty;
+    R.red_full = red_full;
+    R.red_empty = red_empty;
+    R.red = reinterpret_cast<float*>(smem + L.red);
+    R.ubuf = reinterpret_cast<float*>(smem + L.ubuf);
+    R.nstage = a.nstage;
+
+    if (warp == kProducerWarp) {
+        // ---------------- producer: every matvec tile of the forward, in consumption order ----------------
+        if (lane == 0) {
+            const volatile int* abort_flag = &m->abort;
+            uint32_t sidx = 0;
+            bool ok = true;
+            auto stream = [&](const MvPhase& p, const uint8_t* w) {
+                const Items it = my_items(p);
+                const int nq_p = p.nq / p.kparts, cpr = nq_p / p.chunk, pairs = p.rpu / kRPW;
+                const uint32_t half = (uint32_t)p.chunk * kTileBytes;
+                for (int i = it.i0; i < it.i1 && ok; ++i) {
+                    const int part = i / p.n_units, unit = i % p.n_units;
+                    for (int pr = 0; pr < pairs && ok; ++pr) {
+                        const int rg = unit * p.rpu + pr * kRPW;
+                        for (int ch = 0; ch < cpr; ++ch) {
+                            const int slot = sidx % a.nstage;
+                            if (sidx >= (uint32_t)a.nstage &&
+                                !wait_or_abort_1(&empty[slot], ((sidx / a.nstage) - 1) & 1, abort_flag)) {
+                                if (!*abort_flag) set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
+                                m->abort = 1;
+                                ok = false;
+                                break;
+                            }
+                            const uint8_t* src =
+                                w + ((size_t)rg * p.nq + (size_t)part * nq_p + (size_t)ch * p.chunk) * kTileBytes;
+                            uint8_t* dst = R.ring + (size_t)slot * kStageBytes;
+                            mbar_arrive_expect_tx(&full[slot], 2 * half);
+                            bulk_g2s(dst, src, half, &full[slot]);
+                            bulk_g2s(dst + half, src + (size_t)p.nq * kTileBytes, half, &full[slot]);
+                            ++sidx;
+                        }
+                    }
+                }
+            };
+            for (int l = 0; l < a.n_layers && ok; ++l) {
+                const FwdLayer& W = a.layers[l];
+                stream(a.qkv, W.qkv);
+                stream(a.wo, W.wo);
+                stream(a.w13, W.w13);
+                stream(a.w2, W.w2);
+            }
+            if (a.lm && ok) stream(a.lmp, a.lm);
+            reinterpret_cast<volatile uint32_t*>(&m->issued)[0] = sidx;
+            __threadfence_block();
+            reinterpret_cast<volatile int*>(&m->pdone)[0] = 1;
+        }
+        return;
+    }
+
+    // ---------------- compute warps ----------------
+    uint32_t target = 0, sidx = 0, pidx = 0;
+    bool ab = false;
+
+    // embedding: x rows, their 16-row sums of squares and Q8_0 of x * (layer 0 attention norm weight);
+    // one thread per (token, 32-value block)
+    {
+        const int nbd = a.dim >> 5, ngroups = a.dim >> 4;
+        const float* w0 = a.layers[0].rms_att;
+        for (int t = blockIdx.x * kComputeThreads + tid; t < nv * nbd; t += G * kComputeThreads) {
+            const int s = t / nbd, b = t % nbd;
+            const int token = a.tokens ? a.tokens[s] : a.ctrl->tokens[s];
+            const uint8_t* blk = a.embd + ((size_t)token * nbd + b) * 18;
+            float v[32], u[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                v[i] = q4_0_value(blk, i);
+                u[i] = v[i] * w0[b * 32 + i];
+            }
+            float* xp = a.x + (size_t)s * a.dim + b * 32;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(xp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            a.ssq[(size_t)s * ngroups + 2 * b] = group16_sumsq(v);
+            a.ssq[(size_t)s * ngroups + 2 * b + 1] = group16_sumsq(v + 16);
+            float d;
+            int sum;
+            q8_block_thread(u, a.un.qs + (size_t)s * a.dim + b * 32, &d, &sum);
+            a.un.d[(size_t)s * nbd + b] = d;
+            a.un.sum[(size_t)s * nbd + b] = sum;
+        }
+    }
+    grid_barrier(a, m, target);
+
+    uint8_t* uni = smem + L.act;
+    for (int l = 0; l < a.n_layers; ++l) {
+        mv_phase<PH_QKV>(a, a.qkv, l, R, m, sidx, pidx, ab, nv, pos, tid);
+        grid_barrier(a, m, target);
+
+        AttnArgs aa{};
+        aa.q = a.q;
+        aa.q_ld = a.q_rows;
+        aa.k = a.k_cache + (size_t)l * a.kv_layer;
+        aa.v = a.v_cache + (size_t)l * a.kv_layer;
+        aa.kv_ld = a.kv_rows;
+        aa.n_heads = a.n_heads;
+        aa.n_kvh = a.n_kvh;
+        aa.S = a.S;
+        aa.pos = pos;
+        aa.max_seq = a.max_seq;
+        aa.chunk = a.attn_chunk;
+        aa.max_chunks = a.max_chunks;
+        aa.part_ml = a.part_ml;
+        aa.part_acc = a.part_acc;
+        aa.out = a.attn;
+        aa.out_f32 = nullptr;
+        aa.ctrl = nullptr;
+        {
+            // attention partials: two 128-thread groups per CTA over the (kv head, chunk) items
+            const int grp = warp >> 2;
+            if (grp < kFwdAttnGroups && nv > 0) {
+                const int hi_max = pos + nv - 1, lo_min = max(0, pos + 1 - a.max_seq);
+                const int c_first = lo_min / aa.chunk, c_last = hi_max / aa.chunk;
+                const int n_items = (c_last - c_first + 1) * a.n_kvh;
+                const AttnSmem sm = attn_smem_at(uni + (size_t)grp * attn_smem_bytes());
+                const int bar_id = kBarAttn0 + grp;
+                for (int item = blockIdx.x * kFwdAttnGroups + grp; item < n_items; item += G * kFwdAttnGroups)
+                    attn_item<4>(aa, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, tid & 127,
+                              [bar_id] { named_sync(bar_id, kAttnThreads); });
+            }
+        }
+        grid_barrier(a, m, target);
+        for (int wt = blockIdx.x * kComputeWarps + warp; wt < nv * a.n_heads; wt += G * kComputeWarps)
+            attn_combine_row(aa, pos, wt / a.n_heads, wt % a.n_heads, lane);
+        grid_barrier(a, m, target);
+
+        mv_phase<PH_WO>(a, a.wo, l, R, m, sidx, pidx, ab, nv, pos, tid);
+        grid_barrier(a, m, target);
+        mv_phase<PH_W13>(a, a.w13, l, R, m, sidx, pidx, ab, nv, pos, tid);
+        grid_barrier(a, m, target);
+        mv_phase<PH_W2>(a, a.w2, l, R, m, sidx, pidx, ab, nv, pos, tid);
+        grid_barrier(a, m, target);
+    }
+    if (a.lm) mv_phase<PH_LM>(a, a.lmp, 0, R, m, sidx, pidx, ab, nv, pos, tid);
+
+    // Drain: no bulk copy may still be landing in shared memory when the CTA exits.  Only the last
+    // nstage issued stages can be in flight (a slot is reissued only after every consumer waited for it).
+    named_sync(kBarCompute, kComputeThreads);
+    if (tid == 0) {
+        const volatile int* pd = &m->pdone;
+        uint32_t n = 0;
+        while (!*pd && ++n < kSpinLimit) __nanosleep(32);
+        const uint32_t issued = reinterpret_cast<volatile uint32_t*>(&m->issued)[0];
+        const uint32_t first = issued > (uint32_t)a.nstage ? issued - a.nstage : 0;
+        for (uint32_t s = first; s < issued; ++s) mbar_wait(&full[s % a.nstage], (s / a.nstage) & 1);
+    }
+}
+
+size_t fwd_smem_bytes(int nstage) { return fwd_layout(nstage).total; }
+
+int fwd_pick_stages(int max_smem) {
+    for (int n = kMaxStages; n >= 2; --n)
+        if (fwd_layout(n).total <= (size_t)max_smem) return n;
+    return 0;
+}
+
+size_t fwd_sync_words(int dim) { return 1 + (size_t)(dim >> 4); }
+
+cudaError_t fwd_init_attrs(int max_smem) {
+    return cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+}
+
+cudaError_t fwd_blocks_per_sm(size_t smem, int* n) {
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(n, k_forward, kGemvThreads, smem);
+}
+
+cudaError_t launch_forward(const FwdArgs& a, int grid, size_t smem, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_forward, a);
+}
+
+}  // namespace sd

@@ -16,7 +16,7 @@
 // Determinism / batch invariance: every (row, token) value is accumulated in a fixed order (per warp
 // over its tiles, then warps 0..15), independent of S and of the other tokens, so a token's result in
 // an S=5 verify is bit-identical to its S=1 decode result.
-#include "sd_common.cuh"
+#include "sd_dev.cuh"
 
 namespace sd {
 
@@ -44,20 +44,6 @@ __host__ __device__ inline SmemLayout smem_layout(int Kp, int S, int chunk, int 
     return L;
 }
 
-__device__ __forceinline__ void named_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
-__device__ __forceinline__ float2 h2x2f(uint32_t w) {
-    return __half22float2(*reinterpret_cast<const __half2*>(&w));
-}
-
-// The MMA accumulator is initialised with -8*sum(codes) + kMagic: the result bits are then the fp32
-// value 1.5*2^23 + isum (exact for |isum| < 2^22; |isum| <= 32*8*128 here), so one exact FADD
-// recovers (float)isum without the quarter-rate I2F conversion.
-constexpr int kMagicI = 0x4B400000;
-constexpr float kMagicF = 12582912.0f;
-
 }  // namespace
 
 template <int EPI>
@@ -70,10 +56,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
     const int nb = Kp >> 5;                    // blocks of the slice
     const SmemLayout L = smem_layout(Kp, S, chunk, a.nstage);
     uint8_t* ring = smem + L.ring;
-    uint2* act_b = reinterpret_cast<uint2*>(smem + L.act_b);
-    uint2* act_zero = reinterpret_cast<uint2*>(smem + L.act_zero);
-    int4* act_c = reinterpret_cast<int4*>(smem + L.act_c);
-    float2* act_x = reinterpret_cast<float2*>(smem + L.act_x);
     float* red = reinterpret_cast<float*>(smem + L.red);
     float* ubuf = reinterpret_cast<float*>(smem + L.ubuf);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
@@ -82,7 +64,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
     uint64_t* red_empty = red_full + kRedSlots; // epilogue -> consumers (count: epilogue warps)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = lane >> 2, t = lane & 3;
     const int nstage = a.nstage;
     const uint32_t half_bytes = (uint32_t)chunk * kTileBytes;   // one row-group's share of a stage
     const uint32_t stage_bytes = kRPW * half_bytes;
@@ -148,41 +129,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
         pos = a.ctrl->pos;
     }
     const int nthr = (kConsumerWarps + kEpiWarps) * 32;
-    {
-        // B fragments: act_b[b*4S + 4s + tt] = (word tt of token s, word 4+tt of token s) of block b
-        const int n16 = S * nb * 2;
-        for (int i = tid; i < n16; i += nthr) {
-            const int s = i / (nb * 2), rem = i - s * (nb * 2);
-            const int b = rem >> 1, half = rem & 1;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (s < nv)
-                v = *reinterpret_cast<const uint4*>(a.act.qs + (size_t)s * a.K + (size_t)(kb0 + b) * 32 + half * 16);
-            uint32_t* base = reinterpret_cast<uint32_t*>(act_b + (size_t)b * 4 * S + 4 * s) + half;
-            base[0] = v.x;
-            base[2] = v.y;
-            base[4] = v.z;
-            base[6] = v.w;
-        }
-        for (int i = tid; i < 4 * 4 * S; i += nthr) act_zero[i] = make_uint2(0, 0);
-        // C quad (-8*sum + magic for tokens 2t, 2t+1, repeated for rows g+8) and scales (xd pair)
-        const int nbK = a.K >> 5;
-        for (int i = tid; i < nb * 4; i += nthr) {
-            const int b = i >> 2, tt = i & 3;
-            const int s0 = 2 * tt, s1 = 2 * tt + 1;
-            int c0 = kMagicI, c1 = kMagicI;
-            float x0 = 0.f, x1 = 0.f;
-            if (s0 < nv) {
-                c0 = kMagicI - 8 * a.act.sum[(size_t)s0 * nbK + kb0 + b];
-                x0 = a.act.d[(size_t)s0 * nbK + kb0 + b];
-            }
-            if (s1 < nv) {
-                c1 = kMagicI - 8 * a.act.sum[(size_t)s1 * nbK + kb0 + b];
-                x1 = a.act.d[(size_t)s1 * nbK + kb0 + b];
-            }
-            act_c[i] = make_int4(c0, c1, c0, c1);
-            act_x[i] = make_float2(x0, x1);
-        }
-    }
+    const ActSmem A = act_smem_at(smem + L.act_b, nb, S);
+    stage_act_from_planes(A, a.act, a.K, kb0, nb, S, nv, tid, nthr);
     named_sync(1, nthr);
 
     if (warp >= kConsumerWarps) {
@@ -199,12 +147,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
             const int rg = rg0 + pi * kRPW + r;
             const float* rr = red + ((size_t)slot * kRPW + r) * kConsumerWarps * 128;
             float v[4] = {0.f, 0.f, 0.f, 0.f};  // elements lane + 32*k: row = e>>3, tok = e&7
-            if (!ab) {
-                for (int w = 0; w < chunk; ++w) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) v[k] += rr[w * 128 + lane + 32 * k];
-                }
-            }
+            if (!ab) reduce_partials(rr, chunk, lane, v);
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_empty[slot]);
             if (ab) continue;
@@ -217,40 +160,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
                     if (gr < a.out_rows && tok < nv) out[(size_t)tok * a.out_ld + gr] = v[k];
                 }
             } else if constexpr (EPI == EPI_QKV) {
-                // element (row, tok) lives in lane (row*8 + tok) % 32, register (row*8 + tok) / 32;
-                // the partner row (row ^ 1) of a RoPE pair is the same register of lane ^ 8
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int e = lane + 32 * k;
-                    const int row = e >> 3, tok = e & 7;
-                    const float other = __shfl_xor_sync(0xffffffffu, v[k], 8);
-                    if ((row & 1) == 0 && tok < nv) {
-                        const float ve = v[k], vo = other;
-                        const int gr = rg * kTileRows + row;
-                        const int tpos = pos + tok;
-                        if (gr < a.q_rows + a.kv_rows) {
-                            // RoPE on q and k rows (mistral/mistral_model.h:79-122)
-                            const int i = (gr % a.head_dim) >> 1;
-                            const float ang = a.theta_inv[i] * (float)tpos;
-                            float sn, cs;
-                            sincosf(ang, &sn, &cs);
-                            const float e2 = fmaf(-vo, sn, ve * cs);
-                            const float o2 = fmaf(ve, sn, vo * cs);
-                            if (gr < a.q_rows) {
-                                a.q_out[(size_t)tok * a.q_rows + gr] = e2 * a.q_scale;
-                                a.q_out[(size_t)tok * a.q_rows + gr + 1] = o2 * a.q_scale;
-                            } else {
-                                const size_t sl = (size_t)(tpos % a.max_seq) * a.kv_rows + (gr - a.q_rows);
-                                a.k_cache[sl] = __float2half_rn(e2);
-                                a.k_cache[sl + 1] = __float2half_rn(o2);
-                            }
-                        } else if (gr < a.q_rows + 2 * a.kv_rows) {
-                            const size_t sl = (size_t)(tpos % a.max_seq) * a.kv_rows + (gr - a.q_rows - a.kv_rows);
-                            a.v_cache[sl] = __float2half_rn(ve);
-                            a.v_cache[sl + 1] = __float2half_rn(vo);
-                        }
-                    }
-                }
+                epi_qkv(v, rg, lane, nv, pos, a.q_out, a.k_cache, a.v_cache, a.q_rows, a.kv_rows, a.max_seq, a.head_dim,
+                        a.theta_inv, a.q_scale);
             } else if constexpr (EPI == EPI_SILU_Q8) {
                 // unit of 4 row-groups = 2 pairs: (gate lo, gate hi), (up lo, up hi)
                 const int pair_in_unit = ((rg0 / kRPW) + pi) & 1;
@@ -258,28 +169,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
                 for (int k = 0; k < 4; ++k) ubuf[(pair_in_unit * 2 + r) * 128 + lane + 32 * k] = v[k];
                 if (pair_in_unit == 1) {
                     named_sync(2, kEpiWarps * 32);
-                    const int unit = rg >> 2;
-                    const int nbh = a.hidden >> 5;
-                    for (int k = 0; k < 4; ++k) {
-                        const int tok = r * 4 + k;
-                        const int rr2 = lane & 15, hsel = lane >> 4;
-                        const float gv = ubuf[hsel * 128 + rr2 * 8 + tok];
-                        const float uv = ubuf[(2 + hsel) * 128 + rr2 * 8 + tok];
-                        // SiLU(g) * u (mistral/mistral_model.h:174-199)
-                        const float e = expf(-gv);
-                        const float sig = 1.0f / (1.0f + e);
-                        const float hv = (gv * sig) * uv;
-                        float dq;
-                        int sq;
-                        const int q = q8_quant_lane(hv, &dq, &sq);
-                        if (tok < nv) {
-                            a.h.qs[(size_t)tok * a.hidden + unit * 32 + lane] = (int8_t)q;
-                            if (lane == 0) {
-                                a.h.d[(size_t)tok * nbh + unit] = dq;
-                                a.h.sum[(size_t)tok * nbh + unit] = sq;
-                            }
-                        }
-                    }
+                    epi_silu_q8(ubuf, r, lane, rg >> 2, nv, a.h, a.hidden);
                     named_sync(2, kEpiWarps * 32);  // ubuf reused by the next unit
                 }
             }
@@ -292,8 +182,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
 #pragma unroll
     for (int r = 0; r < kRPW; ++r) accL[r] = accH[r] = make_float2(0.f, 0.f);
     const bool has_tile = warp < chunk;
-    const bool zero_lane = g >= S;             // token column g beyond the launch's S reads zeros
-    const uint2* bf_lane = zero_lane ? act_zero + t : act_b + lane;
     int sidx = 0;
     // A stage that never arrives (only possible if the producer gave up) marks the warp aborted: it
     // stops waiting and computing but keeps its place in every handshake, so no warp is left waiting
@@ -309,68 +197,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
                 aborted = true;
             }
             if (aborted) continue;
-            uint4 wl[kRPW], wh[kRPW];
-            uint2 sl[kRPW], sh[kRPW];
+            const uint8_t* slot_p = ring + (size_t)slot * stage_bytes;
             if (has_tile) {
-#pragma unroll
-                for (int r = 0; r < kRPW; ++r) {
-                    const uint8_t* tile = ring + (size_t)slot * stage_bytes + r * half_bytes + warp * kTileBytes;
-                    wl[r] = *reinterpret_cast<const uint4*>(tile + lane * 16);
-                    wh[r] = *reinterpret_cast<const uint4*>(tile + 512 + lane * 16);
-                    sl[r] = *reinterpret_cast<const uint2*>(tile + 1024 + g * 8);
-                    sh[r] = *reinterpret_cast<const uint2*>(tile + 1088 + g * 8);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            if (!has_tile) continue;
-
-            float2 dl[kRPW][2], dh[kRPW][2];
-#pragma unroll
-            for (int r = 0; r < kRPW; ++r) {
-                dl[r][0] = h2x2f(sl[r].x);
-                dl[r][1] = h2x2f(sl[r].y);
-                dh[r][0] = h2x2f(sh[r].x);
-                dh[r][1] = h2x2f(sh[r].y);
-            }
-            const int bbase = (ch * chunk + warp) * 4;   // block index within the slice
-            const uint2* bf_p = zero_lane ? bf_lane : bf_lane + (size_t)bbase * 4 * S;
-            const int4* c_p = act_c + bbase * 4 + t;
-            const float2* x_p = act_x + bbase * 4 + t;
-#pragma unroll
-            for (int blk = 0; blk < 4; ++blk) {
-                const uint2 bf = bf_p[blk * 4 * S];
-                const int4 cq = c_p[blk * 4];
-                const float2 xd = x_p[blk * 4];
-#pragma unroll
-                for (int r = 0; r < kRPW; ++r) {
-                    const uint32_t wlo = blk == 0 ? wl[r].x : blk == 1 ? wl[r].y : blk == 2 ? wl[r].z : wl[r].w;
-                    const uint32_t whi = blk == 0 ? wh[r].x : blk == 1 ? wh[r].y : blk == 2 ? wh[r].z : wh[r].w;
-                    const uint32_t a0 = wlo & 0x0F0F0F0Fu, a2 = (wlo >> 4) & 0x0F0F0F0Fu;
-                    const uint32_t a1 = whi & 0x0F0F0F0Fu, a3 = (whi >> 4) & 0x0F0F0F0Fu;
-                    int d[4];
-                    mma_u8s8(d, a0, a1, a2, a3, bf.x, bf.y, cq.x, cq.y, cq.z, cq.w);
-                    if constexpr (EPI == EPI_BLOCKSUMS) {
-                        if (t == 0 && (rg + r) * kTileRows < a.out_rows) {
-                            const int r0 = (rg + r) * kTileRows + g;
-                            const size_t nbK = (size_t)(a.K >> 5);
-                            a.isum[(size_t)r0 * nbK + kb0 + bbase + blk] = d[0] - kMagicI;
-                            a.isum[(size_t)(r0 + 8) * nbK + kb0 + bbase + blk] = d[2] - kMagicI;
-                        }
-                    } else {
-                        const float wdl = (blk & 1) ? dl[r][blk >> 1].y : dl[r][blk >> 1].x;
-                        const float wdh = (blk & 1) ? dh[r][blk >> 1].y : dh[r][blk >> 1].x;
-                        const float2 fL = __fadd2_rn(make_float2(__int_as_float(d[0]), __int_as_float(d[1])),
-                                                     make_float2(-kMagicF, -kMagicF));
-                        const float2 fH = __fadd2_rn(make_float2(__int_as_float(d[2]), __int_as_float(d[3])),
-                                                     make_float2(-kMagicF, -kMagicF));
-                        // (wd*xd) * (float)isum accumulated per block, as mistral/dequant.h:1085
-                        const float2 sL = __fmul2_rn(make_float2(wdl, wdl), xd);
-                        const float2 sH = __fmul2_rn(make_float2(wdh, wdh), xd);
-                        accL[r] = __ffma2_rn(sL, fL, accL[r]);
-                        accH[r] = __ffma2_rn(sH, fH, accH[r]);
-                    }
-                }
+                // tile registers are loaded before the slot is released
+                TileRegs tr;
+                load_tiles(slot_p, half_bytes, warp, lane, tr);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                consume_tiles<EPI == EPI_BLOCKSUMS>(tr, lane, A, S, (ch * chunk + warp) * 4, accL, accH, a.isum, rg,
+                                                    a.out_rows, (size_t)(a.K >> 5), kb0);
+            } else {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
             }
         }
         if constexpr (EPI == EPI_BLOCKSUMS) continue;
@@ -380,14 +218,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
             set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
             aborted = true;
         }
-        if (has_tile && !aborted) {
-#pragma unroll
-            for (int r = 0; r < kRPW; ++r) {
-                float* rr = red + (((size_t)rs * kRPW + r) * kConsumerWarps + warp) * 128;
-                *reinterpret_cast<float2*>(&rr[g * 8 + 2 * t]) = accL[r];
-                *reinterpret_cast<float2*>(&rr[(g + 8) * 8 + 2 * t]) = accH[r];
-            }
-        }
+        if (has_tile && !aborted) write_partials(red + (size_t)rs * kRPW * kConsumerWarps * 128, warp, lane, accL, accH);
 #pragma unroll
         for (int r = 0; r < kRPW; ++r) accL[r] = accH[r] = make_float2(0.f, 0.f);
         __syncwarp();

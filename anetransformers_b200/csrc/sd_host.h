@@ -16,5 +16,6 @@ int repack_matrix(const uint8_t* aos_dev, int rows, int cols, RowMap map, uint8_
 // For EPI_STORE with a K split the partial outputs go to a.out + p*a.part_stride (the caller sums).
 int gemv_prepare_device(int dev);
 int gemv_plan(GemvArgs& a, int dev, int* grid, size_t* smem);
+int gemv_plan_fixed(GemvArgs& a, int dev, int* grid, size_t* smem);
 int run_gemv(int epi, const GemvArgs& a, int dev, cudaStream_t st, bool pdl);
 }  // namespace sd

@@ -141,6 +141,21 @@ int gemv_plan(GemvArgs& a, int dev, int* grid_out, size_t* smem_out) {
     return SD_OK;
 }
 
+// gemv_plan with the K split fixed for every S (the split chosen at S = kMaxS), so that a row's
+// result does not depend on how many activation rows share the call.
+int gemv_plan_fixed(GemvArgs& a, int dev, int* grid_out, size_t* smem_out) {
+    if (a.kparts <= 0) {
+        GemvArgs probe = a;
+        probe.S = kMaxS;
+        int g;
+        size_t sm;
+        int rc = gemv_plan(probe, dev, &g, &sm);
+        if (rc) return rc;
+        a.kparts = probe.kparts;
+    }
+    return gemv_plan(a, dev, grid_out, smem_out);
+}
+
 int run_gemv(int epi, const GemvArgs& base, int dev, cudaStream_t st, bool pdl) {
     GemvArgs a = base;
     int grid;
@@ -276,7 +291,7 @@ static int matvec_common(int epi, const sd_qmat* W, sd_q8_dev x, float* y, int32
     a.kparts = 0;
     int grid;
     size_t smem;
-    int rc = gemv_plan(a, dev, &grid, &smem);
+    int rc = gemv_plan_fixed(a, dev, &grid, &smem);
     if (rc) return rc;
     const size_t n_out = (size_t)S * W->rows;
     float* parts = nullptr;
@@ -478,7 +493,7 @@ extern "C" int sd_matvec_q4_0_q8_0_noalloc_dev(const sd_qmat* W, sd_q8_dev x, fl
     a.kparts = 0;
     int grid;
     size_t smem;
-    if ((rc = gemv_plan(a, dev, &grid, &smem))) return rc;
+    if ((rc = gemv_plan_fixed(a, dev, &grid, &smem))) return rc;
     const size_t n_out = (size_t)S * W->rows;
     const cudaStream_t st = (cudaStream_t)stream;
     if (a.kparts > 1) {

@@ -5,7 +5,7 @@
 // Embedding: Q4_0 row dequant d*((q&15)-8), mistral/mistral_model.h:134-145 (exact).
 // Outputs are Q8 planes: codes [S][n], fp32 scales [S][n/32] and per-block code sums [S][n/32]
 // (the sum feeds the -8*sum accumulator init of the u8 x s8 MMA in the matvec).
-#include "sd_common.cuh"
+#include "sd_dev.cuh"
 
 namespace sd {
 
@@ -91,7 +91,9 @@ constexpr int kNormMaxParts = 8;
 
 template <int MODE>
 __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
-    __shared__ float wsum[kNormWarps];
+    __shared__ __align__(16) float vs[kNormWarps * 32 * kNormMaxBPW];
+    __shared__ float gss[kNormMaxBPW * kNormWarps * 32 / 16];
+    __shared__ float scale;
     const int tok = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (a.ctrl && a.ctrl->done) return;
@@ -114,11 +116,7 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
             wv[k] = a.w[e];
             if constexpr (MODE == 0) {
                 const int token = a.tokens ? a.tokens[tok] : a.ctrl->tokens[tok];
-                const uint8_t* blk = a.embd + ((size_t)token * nb + (warp + kNormWarps * k)) * 18;
-                const float dd = __half2float(__ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8))));
-                const uint8_t byte = blk[2 + (lane & 15)];
-                const int q = (lane < 16) ? (byte & 0x0F) : (byte >> 4);
-                v[k] = dd * ((float)q - 8.0f);
+                v[k] = q4_0_value(a.embd + ((size_t)token * nb + (warp + kNormWarps * k)) * 18, lane);
             } else {
                 v[k] = x[e];
             }
@@ -140,33 +138,39 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
 #pragma unroll
         for (int k = 0; k < kNormMaxBPW; ++k) v[k] = v[k] + yv[k];
     }
-    float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < kNormMaxBPW; ++k)
         if (k < bpw) {
-            ss = fmaf(v[k], v[k], ss);
-            if constexpr (MODE != 2) x[(warp + kNormWarps * k) * 32 + lane] = v[k];
+            const int e = (warp + kNormWarps * k) * 32 + lane;
+            vs[e] = v[k];
+            if constexpr (MODE != 2) x[e] = v[k];
         }
-    ss = warp_sum(ss);
-    if (lane == 0) wsum[warp] = ss;
     __syncthreads();
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < kNormWarps; ++w) tot += wsum[w];
-    const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)a.dim) + a.eps));
+    const int ngroups = a.dim >> 4;
+    if ((int)threadIdx.x < ngroups) gss[threadIdx.x] = group16_sumsq(&vs[threadIdx.x * 16]);
+    __syncthreads();
+    if (warp == 0) {
+        const float tot = row_sumsq(gss, ngroups, lane);
+        if (lane == 0) scale = rms_scale(tot, a.dim, a.eps);
+    }
+    __syncthreads();
+    const float s = scale;
 
 #pragma unroll
     for (int k = 0; k < kNormMaxBPW; ++k) {
         if (k >= bpw) continue;
         const int b = warp + kNormWarps * k;
-        const float xn = (v[k] * s) * wv[k];
-        if (a.xn_out) a.xn_out[(size_t)tok * a.dim + b * 32 + lane] = xn;
-        float d;
+        // Q8_0 of the normalised row (x*s)*w, taken as Q8_0 of u = x*w with the block scale times s:
+        // s > 0 is common to the block, so the codes do not depend on it and whichever kernel produces x
+        // can quantise u before s is known (the persistent forward does; this kernel matches it).
+        const float u = v[k] * wv[k];
+        if (a.xn_out) a.xn_out[(size_t)tok * a.dim + b * 32 + lane] = u * s;
+        float du;
         int sum;
-        const int q = q8_quant_lane(xn, &d, &sum);
+        const int q = q8_quant_lane(u, &du, &sum);
         a.out.qs[(size_t)tok * a.dim + b * 32 + lane] = (int8_t)q;
         if (lane == 0) {
-            a.out.d[(size_t)tok * nb + b] = d;
+            a.out.d[(size_t)tok * nb + b] = du * s;
             a.out.sum[(size_t)tok * nb + b] = sum;
         }
     }

@@ -242,6 +242,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=GEN_TOKENS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="specdec", choices=["specdec", "gemv"])
+    ap.add_argument("--forward-kernel", type=int, default=None, choices=[0, 1],
+                    help="1 = one persistent kernel per forward, 0 = one kernel per op (default: library default)")
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--S", type=int, default=0)
     args = ap.parse_args()
@@ -271,7 +273,7 @@ def main():
     torch.cuda.set_device(local)
     path = model_path(rank, world, dist)
     peaks = measured_peaks()
-    ctx = Context(path, device=local, max_seq=PROMPT_LEN + args.tokens + 64)
+    ctx = Context(path, device=local, max_seq=PROMPT_LEN + args.tokens + 64, forward_kernel=args.forward_kernel)
     prompt = config3_prompt()
     first, _ = ctx.generate(prompt, mode="greedy", max_tokens=1, temp=0.0, rep_penalty=1.0, ignore_eos=True)
     hist = prompt + [first[0]]

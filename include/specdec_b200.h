@@ -125,6 +125,7 @@ typedef struct {
     int tp_rank, tp_size;
     size_t weight_bytes;  /* device bytes of repacked weights held by this rank */
     size_t kv_bytes;      /* device bytes of this rank's KV ring */
+    int forward_kernel;   /* 1 if forwards run as one persistent kernel, 0 if one kernel per op */
 } sd_model_info;
 
 typedef struct {
@@ -135,6 +136,8 @@ typedef struct {
     void *nccl_comm;      /* ncclComm_t for tp_size > 1, created by the caller */
     int use_graphs;       /* capture per-S forwards in CUDA graphs (default 1) */
     int use_pdl;          /* programmatic dependent launch between kernels (default 1) */
+    int forward_kernel;   /* 1 = each forward is one persistent kernel (single GPU),
+                             0 = one kernel per op (default); both give bit-identical logits */
 } sd_ctx_opts;
 
 SD_API void sd_ctx_opts_default(sd_ctx_opts *o);

@@ -220,3 +220,35 @@ def test_bad_inputs_rejected(ctx):
     with pytest.raises(SpecDecError):
         ctx.forward([1], 1024)         # past the KV ring
     assert ctx.device_error() == 0
+
+
+@pytest.mark.parametrize("max_seq", [1024, 64])
+def test_persistent_forward_bitwise_equals_per_op_kernels(mini, max_seq):
+    """The one-kernel forward and the kernel-per-op forward give bit-identical logits and KV rows, for
+    every S, up to the last slot of a short ring."""
+    from anetransformers_b200.engine import Context
+    fused = Context(mini, max_seq=max_seq, forward_kernel=1)
+    perop = Context(mini, max_seq=max_seq, forward_kernel=0)
+    try:
+        assert fused.info.forward_kernel == 1
+        assert perop.info.forward_kernel == 0
+        rng = np.random.default_rng(7)
+        prompt = rng.integers(3, fused.vocab, 53).tolist()
+        for c in (fused, perop):
+            c.prefill(prompt[:45], 0)
+        pos = 45
+        for S in (1, 5, 8, 3):
+            toks = rng.integers(3, fused.vocab, S).tolist()
+            a, am_a = fused.forward(toks, pos)
+            b, am_b = perop.forward(toks, pos)
+            np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+            np.testing.assert_array_equal(am_a, am_b)
+            pos += S
+        for layer in (0, fused.info.n_layers - 1):
+            ka, va = fused.kv_read(layer, 0, pos)
+            kb, vb = perop.kv_read(layer, 0, pos)
+            np.testing.assert_array_equal(ka, kb)
+            np.testing.assert_array_equal(va, vb)
+    finally:
+        fused.close()
+        perop.close()

@@ -108,19 +108,21 @@ def test_matvec_matches_oracle(oracle, dq, rows, cols, S):
         assert np.all(np.abs(ref2 - ref) <= bound)
 
 
-def test_matvec_batch_invariant(oracle, dq):
-    """A token's result does not depend on the other tokens of the batch (S=1 vs S=5, bitwise)."""
+@pytest.mark.parametrize("rows,cols,S", [(4096, 4096, 5), (4096, 14336, 8), (1024, 14336, 5)])
+def test_matvec_batch_invariant(oracle, dq, rows, cols, S):
+    """A token's result does not depend on the other tokens of the batch (S=1 vs S, bitwise), also for
+    long rows whose K range is split across CTAs at the larger S."""
     import torch
-    rng = np.random.default_rng(42)
-    W = rand_q4(rng, 4096, 4096)
-    x = rng.standard_normal((5, 4096)).astype(np.float32)
+    rng = np.random.default_rng(42 + cols)
+    W = rand_q4(rng, rows, cols)
+    x = rng.standard_normal((S, cols)).astype(np.float32)
     qm = dq.QMat(W)
-    act5 = dq.quantize_dev(torch.from_numpy(x).cuda())
-    y5 = dq.matvec_dev(qm, act5).cpu().numpy()
-    for s in range(5):
+    actS = dq.quantize_dev(torch.from_numpy(x).cuda())
+    yS = dq.matvec_dev(qm, actS).cpu().numpy()
+    for s in range(S):
         act1 = dq.quantize_dev(torch.from_numpy(x[s:s + 1]).cuda())
         y1 = dq.matvec_dev(qm, act1).cpu().numpy()
-        np.testing.assert_array_equal(y1[0].view(np.uint32), y5[s].view(np.uint32))
+        np.testing.assert_array_equal(y1[0].view(np.uint32), yS[s].view(np.uint32))
 
 
 def test_host_matvec_dropin(oracle, dq):
