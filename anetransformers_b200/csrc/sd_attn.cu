@@ -30,21 +30,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const AttnArgs a)
     const int n_items = (c_last - c_first + 1) * a.n_kvh;
     const AttnSmem sm = attn_smem_at(smem);
     for (int item = blockIdx.x; item < n_items; item += gridDim.x)
-        attn_item<kMaxS>(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, threadIdx.x,
+        attn_item<4, kMaxS>(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, threadIdx.x,
                   [] { __syncthreads(); });
 }
 
-// Merge chunk partials (fixed chunk order per lane group); quantise each head's 128 outputs to 4
-// Q8_0 blocks.  One warp per (token, head).
-__global__ void k_attn_combine(const AttnArgs a) {
+// Merge chunk partials and quantise each head's 128 outputs to 4 Q8_0 blocks: one CTA of
+// kCombineWarps warps per (token, head).
+__global__ void __launch_bounds__(kCombineWarps * 32) k_attn_combine(const AttnArgs a) {
+    __shared__ __align__(16) float obuf[kCombineWarps * kHD];
     if (a.ctrl && a.ctrl->done) return;
     pdl_trigger();
     pdl_wait();
     const int nv = a.ctrl ? min(a.ctrl->n_valid, a.S) : a.S;
     const int pos = a.ctrl ? a.ctrl->pos : a.pos;
-    const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (wid >= nv * a.n_heads) return;
-    attn_combine_row(a, pos, wid / a.n_heads, wid % a.n_heads, threadIdx.x & 31);
+    const int row = blockIdx.x;
+    if (row >= nv * a.n_heads) return;
+    attn_combine_row(a, pos, row / a.n_heads, row % a.n_heads, threadIdx.x >> 5, threadIdx.x & 31, obuf,
+                     [] { __syncthreads(); });
 }
 
 static void fill_cfg(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* at, dim3 grid, dim3 block, cudaStream_t st, bool pdl) {
@@ -64,8 +66,7 @@ cudaError_t launch_attention(const AttnArgs& a, int grid_partial, cudaStream_t s
     fill_cfg(cfg, at, dim3(grid_partial), dim3(kAttnThreads), st, pdl);
     cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_partial, a);
     if (e != cudaSuccess) return e;
-    const int warps = a.S * a.n_heads;
-    fill_cfg(cfg, at, dim3((warps * 32 + 255) / 256), dim3(256), st, pdl);
+    fill_cfg(cfg, at, dim3(a.S * a.n_heads), dim3(kCombineWarps * 32), st, pdl);
     return cudaLaunchKernelEx(&cfg, k_attn_combine, a);
 }
 

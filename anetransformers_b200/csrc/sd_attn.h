@@ -18,6 +18,7 @@ struct AttnArgs {
     float2* part_ml;       // [S][n_heads][max_chunks] (running max, sum)
     float* part_acc;       // [S][n_heads][max_chunks][128]
     Q8Planes out;          // [S][n_heads*128] quantised head outputs (o-proj input)
+    ActImage img;          // if img.b is set: the head outputs go here instead, in the matvec fragment layout
     float* out_f32;        // optional fp32 copy of the head outputs
     const DevCtrl* ctrl;
 };

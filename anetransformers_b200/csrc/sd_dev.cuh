@@ -22,30 +22,65 @@ __device__ __forceinline__ float2 h2x2f(uint32_t w) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Matvec activation fragments in shared memory, for one K slice of nb Q8_0 blocks and S tokens:
-//   b[blk*4S + 4s + tt]  = (word tt, word 4+tt) of token s's codes in block blk  (MMA B fragment)
-//   zero[4 * 4S]         = zeros read by lanes whose token column g >= S
-//   c[blk*4 + t]         = C quad (-8*sum + magic for tokens 2t, 2t+1, repeated for rows g+8)
-//   x[blk*4 + t]         = (xd of token 2t, xd of token 2t+1)
+// Matvec activation fragments in shared memory, for one K slice of nb Q8_0 blocks.  Every block holds
+// all kMaxS token slots (tokens >= the valid count are zero), so a lane's fragment address does not
+// depend on S:
+//   b[blk*kActStride + 4s + tt] = (word tt, word 4+tt) of token s's codes in block blk  (MMA B fragment)
+//   c[blk*4 + t]                = C quad (-8*sum + magic for tokens 2t, 2t+1, repeated for rows g+8)
+//   x[blk*4 + t]                = (xd of token 2t, xd of token 2t+1)
 // ---------------------------------------------------------------------------------------------
+constexpr int kActStride = 4 * kMaxS;
+
 struct ActSmem {
     uint2* b;
-    uint2* zero;
     int4* c;
     float2* x;
 };
 
-__host__ __device__ inline size_t act_smem_bytes(int nb, int S) {
-    return (size_t)nb * 4 * S * 8 + (size_t)4 * 4 * S * 8 + (size_t)nb * 4 * 16 + (size_t)nb * 4 * 8;
+__host__ __device__ inline size_t act_smem_bytes(int nb) {
+    return (size_t)nb * kActStride * 8 + (size_t)nb * 4 * 16 + (size_t)nb * 4 * 8;
 }
 
-__device__ inline ActSmem act_smem_at(uint8_t* base, int nb, int S) {
+__device__ inline ActSmem act_smem_at(uint8_t* base, int nb) {
     ActSmem A;
     A.b = reinterpret_cast<uint2*>(base);
-    A.zero = reinterpret_cast<uint2*>(base + (size_t)nb * 4 * S * 8);
-    A.c = reinterpret_cast<int4*>(base + (size_t)nb * 4 * S * 8 + (size_t)4 * 4 * S * 8);
+    A.c = reinterpret_cast<int4*>(base + (size_t)nb * kActStride * 8);
     A.x = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(A.c) + (size_t)nb * 4 * 16);
     return A;
+}
+
+// The same fragment layout in global memory for a whole K range (nbK blocks): written by the phase that
+// produces the activations so that staging a K slice is three contiguous bulk copies.
+//   b: [nbK][kActStride] uint2, c: [nbK][4] int4, x: [nbK][4] float2 (scales before any norm scale)
+__host__ __device__ inline size_t act_image_bytes(int nbK) { return act_smem_bytes(nbK); }
+
+__host__ __device__ inline ActImage act_image_at(void* base, int nbK) {
+    ActImage im;
+    im.b = reinterpret_cast<uint2*>(base);
+    im.c = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(base) + (size_t)nbK * kActStride * 8);
+    im.x = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(im.c) + (size_t)nbK * 4 * 16);
+    return im;
+}
+
+// Code word w (elements 4w..4w+3, packed little-endian) of token s in block blk.
+__device__ __forceinline__ void image_put_word(const ActImage& im, int s, int blk, int w, uint32_t word) {
+    reinterpret_cast<uint32_t*>(im.b + (size_t)blk * kActStride + 4 * s + (w & 3))[w >> 2] = word;
+}
+
+// Codes of one block held one per lane (lane = element); the whole warp calls this.
+__device__ __forceinline__ void image_put_codes_lane(const ActImage& im, int s, int blk, int lane, int code) {
+    uint32_t v = (uint32_t)(code & 0xFF) << (8 * (lane & 3));
+    v |= __shfl_xor_sync(0xffffffffu, v, 1);
+    v |= __shfl_xor_sync(0xffffffffu, v, 2);
+    if ((lane & 3) == 0) image_put_word(im, s, blk, lane >> 2, v);
+}
+
+// Block scale d and code sum of token s in block blk.
+__device__ __forceinline__ void image_put_meta(const ActImage& im, int s, int blk, float d, int sum) {
+    int* cp = reinterpret_cast<int*>(im.c + (size_t)blk * 4 + (s >> 1));
+    cp[s & 1] = kMagicI - 8 * sum;
+    cp[(s & 1) + 2] = kMagicI - 8 * sum;
+    reinterpret_cast<float*>(im.x + (size_t)blk * 4 + (s >> 1))[s & 1] = d;
 }
 
 // Stage Q8 planes (global, row stride K) blocks [kb0, kb0 + nb) of tokens < nv into A.  Loads are
@@ -55,7 +90,7 @@ __device__ inline ActSmem act_smem_at(uint8_t* base, int nb, int S) {
 __device__ inline void stage_act_from_planes(const ActSmem& A, const Q8Planes& act, int K, int kb0, int nb, int S, int nv,
                                              int tid, int nthr, const float* tok_scale = nullptr) {
     constexpr int U = 4;
-    const int n16 = S * nb * 2;
+    const int n16 = kMaxS * nb * 2;  // every token slot; tokens >= nv are zero
     for (int i0 = tid; i0 < n16; i0 += U * nthr) {
         uint4 v[U];
 #pragma unroll
@@ -74,7 +109,7 @@ __device__ inline void stage_act_from_planes(const ActSmem& A, const Q8Planes& a
             const int i = i0 + u * nthr;
             if (i < n16) {
                 const int s = i / (nb * 2), rem = i - s * (nb * 2);
-                uint32_t* base = reinterpret_cast<uint32_t*>(A.b + (size_t)(rem >> 1) * 4 * S + 4 * s) + (rem & 1);
+                uint32_t* base = reinterpret_cast<uint32_t*>(A.b + (size_t)(rem >> 1) * kActStride + 4 * s) + (rem & 1);
                 base[0] = v[u].x;
                 base[2] = v[u].y;
                 base[4] = v[u].z;
@@ -82,7 +117,6 @@ __device__ inline void stage_act_from_planes(const ActSmem& A, const Q8Planes& a
             }
         }
     }
-    for (int i = tid; i < 4 * 4 * S; i += nthr) A.zero[i] = make_uint2(0, 0);
     const int nbK = K >> 5;
     for (int i0 = tid; i0 < nb * 4; i0 += 2 * nthr) {
         int sm[2][2];
@@ -117,40 +151,6 @@ __device__ inline void stage_act_from_planes(const ActSmem& A, const Q8Planes& a
                 A.x[i] = make_float2(d0, d1);
             }
         }
-    }
-}
-
-// Write one quantised block (lane j holds code q of element j, every lane holds d and sum) of token s
-// into A.  Called by one full warp.  Tokens s < S only; the C quad / scale slots of s are set here.
-__device__ inline void stage_act_block(const ActSmem& A, int s, int b, int S, int q, float d, int sum, int lane) {
-    // word w (0..7) = codes 4w..4w+3; lane w < 8 gathers its word
-    uint32_t word = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int v = __shfl_sync(0xffffffffu, q, (lane & 7) * 4 + k);
-        word |= (uint32_t)(v & 0xFF) << (8 * k);
-    }
-    if (lane < 8) {
-        uint32_t* base = reinterpret_cast<uint32_t*>(A.b + (size_t)b * 4 * S + 4 * s);
-        const int tt = lane & 3, half = lane >> 2;
-        base[tt * 2 + half] = word;
-    }
-    if (lane == 0) {
-        int* cp = reinterpret_cast<int*>(&A.c[b * 4 + (s >> 1)]);
-        cp[s & 1] = kMagicI - 8 * sum;
-        cp[(s & 1) + 2] = kMagicI - 8 * sum;
-        reinterpret_cast<float*>(&A.x[b * 4 + (s >> 1)])[s & 1] = d;
-    }
-}
-
-// Empty token slot s (s >= nv, s < the pair's 8-token width): C quad magic, scale 0, codes 0.
-__device__ inline void stage_act_empty(const ActSmem& A, int s, int b, int S, int lane) {
-    if (s < S && lane < 4) A.b[(size_t)b * 4 * S + 4 * s + lane] = make_uint2(0, 0);
-    if (lane == 0) {
-        int* cp = reinterpret_cast<int*>(&A.c[b * 4 + (s >> 1)]);
-        cp[s & 1] = kMagicI;
-        cp[(s & 1) + 2] = kMagicI;
-        reinterpret_cast<float*>(&A.x[b * 4 + (s >> 1)])[s & 1] = 0.f;
     }
 }
 
@@ -190,13 +190,12 @@ __device__ __forceinline__ void consume_tiles(const TileRegs& tr, int lane, cons
         dh[r][0] = h2x2f(tr.sh[r].x);
         dh[r][1] = h2x2f(tr.sh[r].y);
     }
-    const bool zero_lane = g >= S;  // token column g beyond S reads zeros
-    const uint2* bf_p = zero_lane ? A.zero + t : A.b + lane + (size_t)bbase * 4 * S;
+    const uint2* bf_p = A.b + (size_t)bbase * kActStride + lane;  // token slot g, word pair t
     const int4* c_p = A.c + bbase * 4 + t;
     const float2* x_p = A.x + bbase * 4 + t;
 #pragma unroll
     for (int blk = 0; blk < 4; ++blk) {
-        const uint2 bf = bf_p[zero_lane ? 0 : blk * 4 * S];
+        const uint2 bf = bf_p[blk * kActStride];
         const int4 cq = c_p[blk * 4];
         const float2 xd = x_p[blk * 4];
 #pragma unroll
@@ -295,7 +294,8 @@ __device__ __forceinline__ void epi_qkv(const float (&v)[4], int rg, int lane, i
 
 // SiLU(gate)*up + Q8_0 of one 32-unit block for tokens r*4 .. r*4+3 (epilogue warp r of 2).
 // ubuf: [4][128] = gate lo, gate hi, up lo, up hi (row*8 + tok).
-__device__ __forceinline__ void epi_silu_q8(const float* ubuf, int r, int lane, int unit, int nv, Q8Planes h, int hidden) {
+__device__ __forceinline__ void epi_silu_q8(const float* ubuf, int r, int lane, int unit, int nv, Q8Planes h, int hidden,
+                                            const ActImage* img = nullptr) {
     const int nbh = hidden >> 5;
     for (int k = 0; k < 4; ++k) {
         const int tok = r * 4 + k;
@@ -309,7 +309,12 @@ __device__ __forceinline__ void epi_silu_q8(const float* ubuf, int r, int lane, 
         float dq;
         int sq;
         const int q = q8_quant_lane(hv, &dq, &sq);
-        if (tok < nv) {
+        if (img) {
+            if (tok < nv) {
+                image_put_codes_lane(*img, tok, unit, lane, q);
+                if (lane == 0) image_put_meta(*img, tok, unit, dq, sq);
+            }
+        } else if (tok < nv) {
             h.qs[(size_t)tok * hidden + unit * 32 + lane] = (int8_t)q;
             if (lane == 0) {
                 h.d[(size_t)tok * nbh + unit] = dq;
@@ -403,13 +408,14 @@ __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
 // K/V sub-block of kSub positions: thread's 4 pieces (position j = i/16, dims 8*(i%16) .. +7) of
 // K and V, loaded into registers together.
 struct KvRegs {
-    uint4 k[4], v[4];
+    uint4 k[4], v[4];  // up to 4 pieces per thread (4-warp groups); 8-warp groups use 2
 };
 
+template <int NT>
 __device__ __forceinline__ void attn_load_kv(const AttnArgs& a, int kvh, int sb, int p1, int tid, KvRegs& r) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int i = tid + u * kAttnThreads;  // < kSub * kHD / 8 = 512
+    for (int u = 0; u < 512 / NT; ++u) {
+        const int i = tid + u * NT;  // < kSub * kHD / 8 = 512
         const int j = i >> 4, d8 = (i & 15) * 8;
         const int p = sb + j;
         r.k[u] = r.v[u] = make_uint4(0, 0, 0, 0);
@@ -421,10 +427,11 @@ __device__ __forceinline__ void attn_load_kv(const AttnArgs& a, int kvh, int sb,
     }
 }
 
+template <int NT>
 __device__ __forceinline__ void attn_store_kv(const AttnSmem& sm, int tid, const KvRegs& r) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int i = tid + u * kAttnThreads;
+    for (int u = 0; u < 512 / NT; ++u) {
+        const int i = tid + u * NT;
         const int j = i >> 4, d8 = (i & 15) * 8;
         const __half* kh = reinterpret_cast<const __half*>(&r.k[u]);
 #pragma unroll
@@ -433,39 +440,43 @@ __device__ __forceinline__ void attn_store_kv(const AttnSmem& sm, int tid, const
     }
 }
 
-// gsync(): a barrier over the 128 threads of the group.  The query rows and the first K/V sub-block are
-// loaded together, so an item of one sub-block costs about one memory round trip before its math.
-// Tokens are processed TG at a time (a register budget: TG = 4 in the persistent forward, 8 in the
-// attention kernel); each token's arithmetic is the same either way.
-template <int TG, class Sync>
+// One work item (kv head kvh, position chunk c) for a group of NW warps (NW = 4 or 8); gsync() is a
+// barrier over the group's NW*32 threads.  Warp w computes query head 4*kvh + w % 4 for tokens
+// [TG*(w/4), ...) in steps of TG*(NW/4).  The query rows and the first K/V sub-block are loaded
+// together, so an item of one sub-block costs about one memory round trip before its math.  Each
+// token's arithmetic is the same for every (NW, TG).
+template <int NW, int TG, class Sync>
 __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi_max, int kvh, int c, const AttnSmem& sm,
                           int tid, Sync gsync) {
+    constexpr int NT = NW * 32;
     const int warp = tid >> 5, lane = tid & 31;
-    const int hq = warp;  // warp w computes query head 4*kvh + w
+    const int hq = warp & 3;  // query head 4*kvh + hq
     const int p0 = max(c * a.chunk, lo_min);
     const int p1 = min((c + 1) * a.chunk, hi_max + 1);  // exclusive
     gsync();
     {
-        float4 qv[8];  // rows r = s*4 + h, 32 float4 per row: kMaxS * kGQA * 32 = 8 * 128
+        float4 qv[1024 / NT];  // rows r = s*4 + h, 32 float4 per row: kMaxS * kGQA * 32 = 1024
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = tid + u * kAttnThreads;
+        for (int u = 0; u < 1024 / NT; ++u) {
+            const int i = tid + u * NT;
             const int r = i >> 5, d4 = (i & 31) * 4;
             const int s = r / kGQA, h = r % kGQA;
             qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (s < nv) qv[u] = *reinterpret_cast<const float4*>(a.q + (size_t)s * a.q_ld + (size_t)(kvh * kGQA + h) * kHD + d4);
         }
         KvRegs kv;
-        attn_load_kv(a, kvh, p0, p1, tid, kv);
+        attn_load_kv<NT>(a, kvh, p0, p1, tid, kv);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = tid + u * kAttnThreads;
+        for (int u = 0; u < 1024 / NT; ++u) {
+            const int i = tid + u * NT;
             *reinterpret_cast<float4*>(&sm.qs[(i >> 5) * kHD + (i & 31) * 4]) = qv[u];
         }
-        attn_store_kv(sm, tid, kv);
+        attn_store_kv<NT>(sm, tid, kv);
     }
     int resident = p0;  // sub-block held in shared memory
-    for (int t0 = 0; t0 < nv; t0 += TG) {
+    // every warp runs the same number of token rounds (syncs inside stay matched)
+    for (int r0 = 0; r0 < nv; r0 += TG * (NW / 4)) {
+        const int t0 = r0 + TG * (warp >> 2);
         float m[TG], l[TG], acc[TG][4];
 #pragma unroll
         for (int j = 0; j < TG; ++j) {
@@ -476,9 +487,9 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
         for (int sb = p0; sb < p1; sb += kSub) {
             if (sb != resident) {
                 KvRegs kv;
-                attn_load_kv(a, kvh, sb, p1, tid, kv);
+                attn_load_kv<NT>(a, kvh, sb, p1, tid, kv);
                 gsync();  // every warp is done with the resident sub-block
-                attn_store_kv(sm, tid, kv);
+                attn_store_kv<NT>(sm, tid, kv);
                 resident = sb;
             }
             gsync();
@@ -552,84 +563,88 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
 }
 
 // Merge the chunk partials of (token s, head h) and quantise the 128 outputs to 4 Q8_0 blocks.
-// One warp; lane owns dims 4*lane..4*lane+3.  Chunks are taken in groups of 128: a group's
-// (max, sum) pairs are loaded lane-parallel in one go and its per-chunk factors broadcast by shuffle;
-// the accumulator rows are read in batches of 4 chunks, the next batch's loads in flight while the
-// current one is added.  Every sum runs in chunk order (per lane for L), so the result does not depend
-// on how the loads are batched.
-__device__ inline void attn_combine_row(const AttnArgs& a, int pos, int s, int h, int lane) {
+// NWC warps share the row (wi = this warp's index among them, lane owns dims 4*lane..4*lane+3):
+//   1. every warp reads all (max, sum) pairs lane-parallel (groups of 128 chunks) -> M; L (lane sums in
+//      chunk order, then the butterfly);
+//   2. warp wi adds acc_c * exp(m_c - M) over its contiguous quarter of the chunks, in chunk order, four
+//      chunks' loads in flight at a time;
+//   3. the partial vectors meet in obuf ([NWC][128], shared) behind rsync(); warp 0 adds them in warp
+//      order, scales by 1/L and quantises.
+// The result depends only on NWC, which both forward paths fix at kCombineWarps.
+constexpr int kCombineWarps = 4;
+
+template <class Sync>
+__device__ void attn_combine_row(const AttnArgs& a, int pos, int s, int h, int wi, int lane, float* obuf, Sync rsync) {
     const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
     const int c0 = lo / a.chunk, c1 = hi / a.chunk;
     const size_t base = ((size_t)s * a.n_heads + h) * a.max_chunks;
-    auto load_ml = [&](int g0, float2 (&ml)[4]) {
+    float M = -INFINITY;
+    for (int g0 = c0; g0 <= c1; g0 += 128) {
+        float mx[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int c = g0 + lane + 32 * u;
-            ml[u] = c <= c1 ? a.part_ml[base + c] : make_float2(-INFINITY, 0.f);
+            mx[u] = c <= c1 ? a.part_ml[base + c].x : -INFINITY;
         }
-    };
-    float2 ml0[4];
-    load_ml(c0, ml0);
-    float M = -INFINITY;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) M = fmaxf(M, ml0[u].x);
-    for (int g0 = c0 + 128; g0 <= c1; g0 += 128) {
-        float2 ml[4];
-        load_ml(g0, ml);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) M = fmaxf(M, ml[u].x);
+        for (int u = 0; u < 4; ++u) M = fmaxf(M, mx[u]);
     }
     M = warp_max(M);
     float L = 0.f;
+    if (wi == 0) {
+        for (int g0 = c0; g0 <= c1; g0 += 128) {
+            float2 ml[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int c = g0 + lane + 32 * u;
+                ml[u] = c <= c1 ? a.part_ml[base + c] : make_float2(-INFINITY, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (g0 + lane + 32 * u <= c1) L += (ml[u].x == -INFINITY) ? 0.f : ml[u].y * expf(ml[u].x - M);
+        }
+        L = warp_sum(L);
+    }
+    // this warp's chunk range
+    const int nc = c1 - c0 + 1, per = (nc + kCombineWarps - 1) / kCombineWarps;
+    const int ca = c0 + wi * per, cb = min(c1, ca + per - 1);
     float o[4] = {0.f, 0.f, 0.f, 0.f};
     constexpr int U = 4;
-    for (int g0 = c0; g0 <= c1; g0 += 128) {
-        float2 ml[4];
-        if (g0 == c0) {
+    for (int cc = ca; cc <= cb; cc += U) {
+        float4 ac[U];
+        float mx[U];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) ml[u] = ml0[u];
-        } else {
-            load_ml(g0, ml);
+        for (int u = 0; u < U; ++u) {
+            const int c = cc + u;
+            ac[u] = c <= cb ? *reinterpret_cast<const float4*>(a.part_acc + (base + c) * kHD + lane * 4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            mx[u] = c <= cb ? a.part_ml[base + c].x : -INFINITY;
         }
-        float f[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            f[u] = (ml[u].x == -INFINITY) ? 0.f : expf(ml[u].x - M);
-            if (g0 + lane + 32 * u <= c1) L += (ml[u].x == -INFINITY) ? 0.f : ml[u].y * f[u];
-        }
-        const int gend = min(c1, g0 + 127);
-        float4 b0[U], b1[U];
-        auto load_batch = [&](int cb, float4 (&dst)[U]) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int c = cb + u;
-                dst[u] = c <= gend ? *reinterpret_cast<const float4*>(a.part_acc + (base + c) * kHD + lane * 4)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        };
-        auto add_batch = [&](int cb, const float4 (&src)[U]) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int rel = cb + u - g0;  // factor of this chunk: lane rel % 32, slot rel / 32
-                const int sl = (rel >> 5) & 3;
-                const float fv =
-                    __shfl_sync(0xffffffffu, sl == 0 ? f[0] : sl == 1 ? f[1] : sl == 2 ? f[2] : f[3], rel & 31);
-                const float fu = cb + u <= gend ? fv : 0.f;
-                o[0] = fmaf(src[u].x, fu, o[0]);
-                o[1] = fmaf(src[u].y, fu, o[1]);
-                o[2] = fmaf(src[u].z, fu, o[2]);
-                o[3] = fmaf(src[u].w, fu, o[3]);
-            }
-        };
-        load_batch(g0, b0);
-        for (int cb = g0; cb <= gend; cb += 2 * U) {
-            if (cb + U <= gend) load_batch(cb + U, b1);
-            add_batch(cb, b0);
-            if (cb + 2 * U <= gend) load_batch(cb + 2 * U, b0);
-            if (cb + U <= gend) add_batch(cb + U, b1);
+        for (int u = 0; u < U; ++u) {
+            if (cc + u > cb) break;
+            const float f = (mx[u] == -INFINITY) ? 0.f : expf(mx[u] - M);
+            o[0] = fmaf(ac[u].x, f, o[0]);
+            o[1] = fmaf(ac[u].y, f, o[1]);
+            o[2] = fmaf(ac[u].z, f, o[2]);
+            o[3] = fmaf(ac[u].w, f, o[3]);
         }
     }
-    L = warp_sum(L);
+    *reinterpret_cast<float4*>(obuf + wi * kHD + lane * 4) = make_float4(o[0], o[1], o[2], o[3]);
+    rsync();
+    if (wi != 0) {
+        rsync();  // obuf is free again once warp 0 has read it
+        return;
+    }
+#pragma unroll
+    for (int w = 1; w < kCombineWarps; ++w) {
+        const float4 p = *reinterpret_cast<const float4*>(obuf + w * kHD + lane * 4);
+        o[0] += p.x;
+        o[1] += p.y;
+        o[2] += p.z;
+        o[3] += p.w;
+    }
+    rsync();
     const float inv = 1.0f / L;
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[e] *= inv;
@@ -657,6 +672,12 @@ __device__ inline void attn_combine_row(const AttnArgs& a, int pos, int s, int h
     const size_t row_off = (size_t)s * a.n_heads * kHD + (size_t)h * kHD;
     const uint32_t packed = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
                             ((uint32_t)(q[3] & 0xFF) << 24);
+    if (a.img.b) {
+        const int blk = h * (kHD / 32) + (lane >> 3);
+        image_put_word(a.img, s, blk, lane & 7, packed);
+        if ((lane & 7) == 0) image_put_meta(a.img, s, blk, d, qsum);
+        return;
+    }
     *reinterpret_cast<uint32_t*>(a.out.qs + row_off + lane * 4) = packed;
     if ((lane & 7) == 0) {
         const size_t bi = row_off / 32 + (lane >> 3);

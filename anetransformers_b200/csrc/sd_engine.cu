@@ -32,6 +32,7 @@
 
 #include "sd_attn.h"
 #include "sd_fwd.h"
+#include "sd_dev.cuh"
 #include "sd_common.cuh"
 #include "sd_host.h"
 #include "sd_spec.h"
@@ -278,7 +279,8 @@ struct sd_ctx {
     bool fused = false;
     FwdLayer* d_layers = nullptr;  // device copy of the per-layer weight pointers
     float* ssq = nullptr;          // [MB][dim/16] group sums of squares of x
-    Q8Planes unorm{};              // [MB][dim] Q8_0 of x * (next norm weight)
+    void* img_mem = nullptr;       // activation images (norm input, head outputs, SiLU output)
+    ActImage img_un{}, img_attn{}, img_h{};
     unsigned* fsync = nullptr;     // grid barrier + slice counters
     MvPhase ph_qkv{}, ph_wo{}, ph_w13{}, ph_w2{}, ph_lm{};
     int fwd_stages = 0, fwd_grid = 0;
@@ -402,9 +404,19 @@ int setup_fused(sd_ctx* c) {
     for (int l = 0; l < c->n_layers; ++l)
         hl[l] = FwdLayer{c->L[l].qkv, c->L[l].wo, c->L[l].w13, c->L[l].w2, c->L[l].rms_att, c->L[l].rms_ffn};
     if ((rc = dalloc(&c->d_layers, hl.size())) || (rc = dalloc(&c->ssq, (size_t)c->MB * (c->dim / 16))) ||
-        (rc = dalloc(&c->fsync, fwd_sync_words(c->dim))) || (rc = dalloc(&c->unorm.qs, (size_t)c->MB * c->dim)) ||
-        (rc = dalloc(&c->unorm.d, (size_t)c->MB * c->dim / 32)) || (rc = dalloc(&c->unorm.sum, (size_t)c->MB * c->dim / 32)))
+        (rc = dalloc(&c->fsync, fwd_sync_words(c->dim))))
         return rc;
+    {
+        const size_t bu = act_image_bytes(c->dim / 32), ba = act_image_bytes(c->q_rows / 32),
+                     bh = act_image_bytes(c->hid_l / 32);
+        uint8_t* p = nullptr;
+        if ((rc = dalloc(&p, bu + ba + bh))) return rc;
+        CK(cudaMemset(p, 0, bu + ba + bh), "memset");
+        c->img_mem = p;
+        c->img_un = act_image_at(p, c->dim / 32);
+        c->img_attn = act_image_at(p + bu, c->q_rows / 32);
+        c->img_h = act_image_at(p + bu + ba, c->hid_l / 32);
+    }
     CK(cudaMemcpy(c->d_layers, hl.data(), hl.size() * sizeof(FwdLayer), cudaMemcpyHostToDevice), "layer table");
     CK(cudaMemset(c->fsync, 0, fwd_sync_words(c->dim) * sizeof(unsigned)), "memset");
     c->fused = true;
@@ -443,7 +455,9 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     a.nstage = c->fwd_stages;
     a.x = c->x;
     a.ssq = c->ssq;
-    a.un = c->unorm;
+    a.un_img = c->img_un;
+    a.attn_img = c->img_attn;
+    a.h_img = c->img_h;
     a.q = c->q;
     a.attn = c->act;
     a.h = c->hact;
@@ -664,7 +678,7 @@ void sd_ctx_free(sd_ctx* c) {
     cudaFree(c->part_ml); cudaFree(c->part_acc); cudaFree(c->logits); cudaFree(c->probs); cudaFree(c->argmax);
     cudaFree(c->ctrl); cudaFree(c->dctrl); cudaFree(c->err); cudaFree(c->gs); cudaFree(c->g_out); cudaFree(c->g_hist);
     cudaFree(c->d_layers); cudaFree(c->ssq); cudaFree(c->fsync);
-    cudaFree(c->unorm.qs); cudaFree(c->unorm.d); cudaFree(c->unorm.sum);
+    cudaFree(c->img_mem);
     if (c->ctrl_h) cudaFreeHost(c->ctrl_h);
     if (c->tok_h) cudaFreeHost(c->tok_h);
     if (c->gs_h) cudaFreeHost(c->gs_h);

@@ -17,14 +17,20 @@
 // row-group and apply the epilogue, 18 is the producer.  Warps 0-17 also run the non-matvec phases.
 //
 // Phases of a layer, each ended by a grid barrier:
-//   QKV    norm of x staged in every CTA (group sums of squares come with x), matvec, RoPE, KV write
+//   QKV    Q8_0 planes of x*w (written by the phase that produced x) staged with the RMSNorm scale;
+//          matvec, RoPE, KV write
 //   ATTN   (kv head, chunk) partials, two 128-thread groups per CTA
 //   COMB   merge of the chunk partials and Q8_0 of the head outputs
-//   WO     matvec; epilogue x += y and the group sums of squares of the new x
-//   W13    norm of x, gate|up matvec, SiLU(gate)*up, Q8_0
-//   W2     K-split matvec; the last slice to finish a row-group adds the slices into x
-// The arithmetic (tile math, reduction orders, norms, attention) is the same device code as the
-// per-op kernels, so both paths give bit-identical logits.
+//   WO     matvec, outputs to slice buffers
+//   RED    warp per (token, 32-row block): x += slices, 16-row sums of squares, Q8_0 of x*w for the
+//          next norm
+//   W13    gate|up matvec, SiLU(gate)*up, Q8_0
+//   W2     K-split matvec, outputs to slice buffers
+//   RED    as above
+// then the LM head.  The kernel is driven by this phase table with one call site per phase kind, so
+// its code stays small enough for the instruction cache.  The arithmetic (tile math, reduction orders,
+// norms, attention) is the same device code as the per-op kernels, so both paths give bit-identical
+// logits.
 #include "sd_dev.cuh"
 #include "sd_fwd.h"
 
@@ -55,7 +61,7 @@ __host__ __device__ inline FwdSmem fwd_layout(int nstage) {
     FwdSmem L{};
     L.ring = 0;
     L.act = L.ring + (size_t)nstage * kStageBytes;
-    const size_t act_bytes = act_smem_bytes(kActMaxNb, kMaxS);
+    const size_t act_bytes = act_smem_bytes(kActMaxNb);
     const size_t red_bytes = (size_t)kRedSlots * kRPW * kConsumerWarps * 128 * 4;
     L.red = L.act + align_up(act_bytes, 128);
     L.ubuf = L.red + red_bytes;
@@ -63,18 +69,10 @@ __host__ __device__ inline FwdSmem fwd_layout(int nstage) {
     const size_t attn = (size_t)kFwdAttnGroups * attn_smem_bytes();
     if (attn > uni) uni = attn;
     L.misc = L.act + align_up(uni, 128);
-    L.bars = L.misc + 512;  // misc: scale[kMaxS], abort, producer issued/done, epilogue pair scratch
-    L.total = L.bars + (2 * kMaxStages + 2 * kRedSlots) * 8;
+    L.bars = L.misc + 128;  // misc: scale[kMaxS], abort, producer issued/done
+    L.total = L.bars + (2 * kMaxStages + 2 * kRedSlots + 1) * 8;
     return L;
 }
-
-// Scratch the two epilogue warps share while finishing a pair of row-groups (one Q8_0 block of x).
-struct PairX {
-    float am[kEpiWarps][8];
-    int qs[kEpiWarps][8];
-    int ab[kEpiWarps];
-    int last;
-};
 
 struct Misc {
     float scale[kMaxS];
@@ -82,7 +80,19 @@ struct Misc {
     int grid_ok;
     uint32_t issued;
     int pdone;
-    PairX px;
+    uint32_t act_issued;  // activation stagings issued (bulk copies completing on the act barrier)
+};
+
+struct Ring {
+    uint64_t* act_full;  // activation staging copies
+    uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* red_full;
+    uint64_t* red_empty;
+    float* red;
+    float* ubuf;
+    int nstage;
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
@@ -93,11 +103,12 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
 
 // Single-thread wait that also gives up as soon as another warp of the CTA has aborted.
 __device__ __forceinline__ bool wait_or_abort_1(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 31) == 31 && *abort_flag) return false;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait_sleep(bar, parity)) {
+        if (*abort_flag || global_ns() - t0 > kWaitLimitNs) return false;
     }
-    return false;
+    return true;
 }
 
 // Whole-warp form: every lane waits (each lane then sees the data the phase guards) and the result
@@ -145,132 +156,158 @@ __device__ void grid_barrier(const FwdArgs& a, Misc* m, uint32_t& target) {
 // Activation staging (consumer warps only)
 // ---------------------------------------------------------------------------------------------
 
-// Normalised activations: the producing epilogue already wrote Q8_0 of u = x*w (codes, sums, block
-// scales d_u) and the 16-row sums of squares of x; here each token's RMSNorm scale s is formed from
-// those sums and the block scales become d_u * s while the planes are staged.
-__device__ void stage_norm(const FwdArgs& a, const ActSmem& A, Misc* m, int nb, int nv, int tid) {
+// Stage blocks [kb0, kb0 + nb) of an activation image into A (consumer warps): three bulk copies on
+// the act barrier.  While they land, warps < nv form the RMSNorm scale s of their token from the 16-row
+// sums of squares (norm phases only: scale != null).  Then token slots >= nv are cleared (codes 0, C =
+// magic, scale 0) and, for norm phases, the block scales become d_u * s -- the same values the per-op
+// staging builds from Q8 planes.
+__device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem& A, const Ring& R, Misc* m, uint32_t& nstg,
+                            int kb0, int nb, int nv, bool norm, bool& ab, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int ngroups = a.dim >> 4;
-    if (warp < nv) {
+    if (tid == 0) {
+        const uint32_t bb = (uint32_t)nb * kActStride * 8, cb = (uint32_t)nb * 64, xb = (uint32_t)nb * 32;
+        mbar_arrive_expect_tx(R.act_full, bb + cb + xb);
+        bulk_g2s(A.b, im.b + (size_t)kb0 * kActStride, bb, R.act_full);
+        bulk_g2s(A.c, im.c + (size_t)kb0 * 4, cb, R.act_full);
+        bulk_g2s(A.x, im.x + (size_t)kb0 * 4, xb, R.act_full);
+        reinterpret_cast<volatile uint32_t*>(&m->act_issued)[0] = nstg + 1;
+    }
+    if (norm && warp < nv) {
+        const int ngroups = a.dim >> 4;
         const float tot = row_sumsq(a.ssq + (size_t)warp * ngroups, ngroups, lane);
         if (lane == 0) m->scale[warp] = rms_scale(tot, a.dim, a.eps);
     }
     named_sync(kBarStage, kConsumerThreads);
-    stage_act_from_planes(A, a.un, a.dim, 0, nb, a.S, nv, tid, kConsumerThreads, m->scale);
+    if (!ab && !wait_or_abort(R.act_full, nstg & 1, &m->abort)) {
+        set_dev_error(a.err, DEV_ERR_FULL_WAIT);
+        ab = true;
+        m->abort = 1;
+    }
+    ++nstg;
+    for (int i = tid; i < nb * 4; i += kConsumerThreads) {
+        int* cp = reinterpret_cast<int*>(&A.c[i]);
+        float* xp = reinterpret_cast<float*>(&A.x[i]);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int s = 2 * (i & 3) + hh;
+            if (s >= nv) {
+                cp[hh] = kMagicI;
+                cp[hh + 2] = kMagicI;
+                xp[hh] = 0.f;
+            } else if (norm) {
+                xp[hh] = xp[hh] * m->scale[s];
+            }
+        }
+    }
+    if (nv < kMaxS)
+        for (int i = tid; i < nb * kActStride; i += kConsumerThreads)
+            if (((i & (kActStride - 1)) >> 2) >= nv) A.b[i] = make_uint2(0, 0);
 }
 
-// Q8_0 of u = v*w for one 32-value block (thread-level; the arithmetic of q8_quant_lane).
-__device__ __forceinline__ void q8_block_thread(const float* u, int8_t* qs, float* d_out, int* sum_out) {
+// Q8_0 of u for one 32-value block of token s (thread-level; the arithmetic of q8_quant_lane), into the
+// activation image.
+__device__ __forceinline__ void q8_block_thread(const float* u, const ActImage& im, int s, int blk) {
     float am = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(u[i]));
     const float d = __fdiv_rn(am, 127.0f);
+    const float id = am != 0.0f ? __fdiv_rn(1.0f, d) : 0.f;
     int sum = 0;
-    int q[32];
-    if (am != 0.0f) {
-        const float id = __fdiv_rn(1.0f, d);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int r = __float2int_rn(__fmul_rn(u[i], id));
-            q[i] = r > 127 ? 127 : (r < -128 ? -128 : r);
-            sum += q[i];
+    for (int w = 0; w < 8; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            int q = 0;
+            if (am != 0.0f) {
+                const int r = __float2int_rn(__fmul_rn(u[4 * w + c], id));
+                q = r > 127 ? 127 : (r < -128 ? -128 : r);
+            }
+            sum += q;
+            word |= (uint32_t)(q & 0xFF) << (8 * c);
         }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) q[i] = 0;
+        image_put_word(im, s, blk, w, word);
     }
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-        const uint32_t w = (uint32_t)(q[i] & 0xFF) | ((uint32_t)(q[i + 1] & 0xFF) << 8) | ((uint32_t)(q[i + 2] & 0xFF) << 16) |
-                           ((uint32_t)(q[i + 3] & 0xFF) << 24);
-        *reinterpret_cast<uint32_t*>(qs + i) = w;
-    }
-    *d_out = d;
-    *sum_out = sum;
+    image_put_meta(im, s, blk, d, sum);
 }
 
 // ---------------------------------------------------------------------------------------------
 // Phase kinds
 // ---------------------------------------------------------------------------------------------
 enum PhaseKind : int { PH_QKV = 0, PH_WO = 1, PH_W13 = 2, PH_W2 = 3, PH_LM = 4 };
+constexpr int kMaxParts = 8;  // K slices of a matvec whose outputs a residual phase adds
 
-struct Ring {
-    uint8_t* ring;
-    uint64_t* full;
-    uint64_t* empty;
-    uint64_t* red_full;
-    uint64_t* red_empty;
-    float* red;
-    float* ubuf;
-    int nstage;
-};
 
-// Residual update of row-group rg (epilogue warp r of the pair): x[tok][row] += t (the slice partials
-// already summed in slice order, as the per-op norm kernel adds them); the group's sum of squares of
-// the new x; and Q8_0 of u = x*wn for the next RMSNorm (wn its weight), the block being the pair's 32
-// rows: the two warps exchange their block maxima and code sums through px.  Both epilogue warps call
-// this together.
-__device__ void resid_update(const FwdArgs& a, const float (&t)[4], int rg, int r, int lane, int nv, const float* wn,
-                             PairX* px) {
-    float xv[4], u[4];
+// Residual update of one (token, 32-row block), one warp, lane = row: x += the matvec's slice outputs
+// (added in slice order, as the per-op norm kernel adds them), the two 16-row sums of squares of the
+// new x, and Q8_0 of u = x*wn for the next RMSNorm (wn its weight; the norm scale is applied when the
+// planes are staged).
+__device__ void red_block(const FwdArgs& a, int s, int b, int kparts, const float* wn, int lane) {
+    const int row = b * 32 + lane;
+    float xv = a.x[(size_t)s * a.dim + row];
+    float yv[kMaxParts];
+#pragma unroll
+    for (int p = 0; p < kMaxParts; ++p)
+        yv[p] = p < kparts ? a.yparts[(size_t)p * a.ypart_stride + (size_t)s * a.dim + row] : 0.f;
+    const float w = wn[row];
+    float t = 0.f;
+#pragma unroll
+    for (int p = 0; p < kMaxParts; ++p)
+        if (p < kparts) t += yv[p];
+    xv = xv + t;
+    a.x[(size_t)s * a.dim + row] = xv;
+    // group sums (lanes 0-15: group 2b, 16-31: group 2b+1) in the canonical order of group16_sumsq
+    const int gb = lane & 16, j = lane & 3;
+    float q = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
-        const int gr = rg * kTileRows + row;
-        xv[k] = 0.f;
-        if (tok < nv) {
-            float* xp = a.x + (size_t)tok * a.dim + gr;
-            xv[k] = *xp + t[k];
-            *xp = xv[k];
-        }
-        u[k] = xv[k] * wn[gr];
+        const float e = __shfl_sync(0xffffffffu, xv, gb + 4 * k + j);
+        q = fmaf(e, e, q);
     }
-    const float ss = group16_sumsq_epi(xv);
-    if (lane < nv) a.ssq[(size_t)lane * (a.dim >> 4) + rg] = ss;
-    float am = fmaxf(fmaxf(fabsf(u[0]), fabsf(u[1])), fmaxf(fabsf(u[2]), fabsf(u[3])));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 8));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 16));
-    if (lane < 8) px->am[r][lane] = am;
-    named_sync(kBarEpi, kEpiWarps * 32);
-    const float amax = fmaxf(px->am[0][lane & 7], px->am[1][lane & 7]);
-    const float d = __fdiv_rn(amax, 127.0f);
-    int q[4] = {0, 0, 0, 0};
-    if (amax != 0.0f) {
-        const float id = __fdiv_rn(1.0f, d);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int rr = __float2int_rn(__fmul_rn(u[k], id));
-            q[k] = rr > 127 ? 127 : (rr < -128 ? -128 : rr);
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
-        if (tok < nv) a.un.qs[(size_t)tok * a.dim + rg * kTileRows + row] = (int8_t)q[k];
-    }
-    int qs = q[0] + q[1] + q[2] + q[3];
-    qs += __shfl_xor_sync(0xffffffffu, qs, 8);
-    qs += __shfl_xor_sync(0xffffffffu, qs, 16);
-    if (lane < 8) px->qs[r][lane] = qs;
-    named_sync(kBarEpi, kEpiWarps * 32);
-    if (r == 0 && lane < nv) {
-        const size_t bi = (size_t)lane * (a.dim >> 5) + (rg >> 1);
-        a.un.sum[bi] = px->qs[0][lane] + px->qs[1][lane];
-        a.un.d[bi] = d;
-    }
-    named_sync(kBarEpi, kEpiWarps * 32);  // px may be reused
+    q += __shfl_xor_sync(0xffffffffu, q, 1);
+    q += __shfl_xor_sync(0xffffffffu, q, 2);
+    if ((lane & 15) == 0) a.ssq[(size_t)s * (a.dim >> 4) + 2 * b + (lane >> 4)] = q;
+    float d;
+    int sum;
+    const int code = q8_quant_lane(xv * w, &d, &sum);
+    image_put_codes_lane(a.un_img, s, b, lane, code);
+    if (lane == 0) image_put_meta(a.un_img, s, b, d, sum);
 }
 
-// One matvec phase for the compute warps (consumer and epilogue roles).
-template <int KIND>
-__device__ void mv_phase(const FwdArgs& a, const MvPhase& p, int layer, const Ring& R, Misc* m, uint32_t& sidx,
-                         uint32_t& pidx, bool& ab, int nv, int pos, int tid) {
+__device__ __forceinline__ AttnArgs attn_args(const FwdArgs& a, int l, int pos) {
+    AttnArgs aa{};
+    aa.q = a.q;
+    aa.q_ld = a.q_rows;
+    aa.k = a.k_cache + (size_t)l * a.kv_layer;
+    aa.v = a.v_cache + (size_t)l * a.kv_layer;
+    aa.kv_ld = a.kv_rows;
+    aa.n_heads = a.n_heads;
+    aa.n_kvh = a.n_kvh;
+    aa.S = a.S;
+    aa.pos = pos;
+    aa.max_seq = a.max_seq;
+    aa.chunk = a.attn_chunk;
+    aa.max_chunks = a.max_chunks;
+    aa.part_ml = a.part_ml;
+    aa.part_acc = a.part_acc;
+    aa.out = a.attn;
+    aa.img = a.attn_img;
+    aa.out_f32 = nullptr;
+    aa.ctrl = nullptr;
+    return aa;
+}
+
+// One matvec phase for the compute warps (consumer and epilogue roles).  kind is a runtime value so that
+// the tile loop exists once in the kernel.
+__device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, const Ring& R, Misc* m, uint32_t& sidx,
+                                      uint32_t& pidx, uint32_t& nstg, bool& ab, int nv, int pos, int tid) {
+    const MvPhase& p = kind == PH_QKV ? a.qkv : kind == PH_WO ? a.wo : kind == PH_W13 ? a.w13 : kind == PH_W2 ? a.w2 : a.lmp;
     const int warp = tid >> 5, lane = tid & 31;
     const Items it = my_items(p);
     const int nq_p = p.nq / p.kparts, cpr = nq_p / p.chunk, pairs = p.rpu / kRPW;
     const int nb = nq_p * 4;
     const uint32_t half = (uint32_t)p.chunk * kTileBytes;
-    const ActSmem A = act_smem_at(R.ring + (size_t)R.nstage * kStageBytes, nb, a.S);
+    const ActSmem A = act_smem_at(R.ring + (size_t)R.nstage * kStageBytes, nb);
     const volatile int* abort_flag = &m->abort;
 
     if (warp < kConsumerWarps) {
@@ -281,13 +318,8 @@ __device__ void mv_phase(const FwdArgs& a, const MvPhase& p, int layer, const Ri
             const int part = i / p.n_units, unit = i % p.n_units;
             if (part != cur_part) {
                 named_sync(kBarStage, kConsumerThreads);  // every consumer is done with the previous slice
-                if constexpr (KIND == PH_QKV || KIND == PH_W13 || KIND == PH_LM) {
-                    stage_norm(a, A, m, nb, nv, tid);
-                } else if constexpr (KIND == PH_WO) {
-                    stage_act_from_planes(A, a.attn, a.q_rows, part * nb, nb, a.S, nv, tid, kConsumerThreads);
-                } else {
-                    stage_act_from_planes(A, a.h, a.hidden, part * nb, nb, a.S, nv, tid, kConsumerThreads);
-                }
+                const ActImage& im = kind == PH_WO ? a.attn_img : kind == PH_W2 ? a.h_img : a.un_img;
+                stage_image(a, im, A, R, m, nstg, part * nb, nb, nv, kind != PH_WO && kind != PH_W2, ab, tid);
                 named_sync(kBarStage, kConsumerThreads);
                 cur_part = part;
             }
@@ -351,77 +383,93 @@ __device__ void mv_phase(const FwdArgs& a, const MvPhase& p, int layer, const Ri
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&R.red_empty[slot]);
             }
-            if constexpr (KIND == PH_QKV) {
-                if (!ab)
-                    epi_qkv(v, rg, lane, nv, pos, a.q, a.k_cache + (size_t)layer * a.kv_layer,
-                            a.v_cache + (size_t)layer * a.kv_layer, a.q_rows, a.kv_rows, a.max_seq, a.head_dim,
-                            a.theta_inv, a.q_scale);
-            } else if constexpr (KIND == PH_LM) {
-                if (!ab) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
-                        const int gr = rg * kTileRows + row;
-                        if (gr < a.vocab && tok < nv) a.logits[(size_t)tok * a.vocab + gr] = v[k];
-                    }
-                }
-            } else if constexpr (KIND == PH_W13) {
+            if (kind == PH_W13) {
                 // unit of 4 row-groups = 2 pairs: (gate lo, gate hi), (up lo, up hi)
 #pragma unroll
                 for (int k = 0; k < 4; ++k) R.ubuf[(pr * 2 + r) * 128 + lane + 32 * k] = v[k];
                 if (pr == 1) {
                     named_sync(kBarEpi, kEpiWarps * 32);
-                    if (!ab) epi_silu_q8(R.ubuf, r, lane, unit, nv, a.h, a.hidden);
+                    if (!ab) epi_silu_q8(R.ubuf, r, lane, unit, nv, a.h, a.hidden, &a.h_img);
                     named_sync(kBarEpi, kEpiWarps * 32);
                 }
+            } else if (ab) {
+                continue;
+            } else if (kind == PH_QKV) {
+                epi_qkv(v, rg, lane, nv, pos, a.q, a.k_cache + (size_t)layer * a.kv_layer,
+                        a.v_cache + (size_t)layer * a.kv_layer, a.q_rows, a.kv_rows, a.max_seq, a.head_dim, a.theta_inv,
+                        a.q_scale);
             } else {
-                // PH_WO / PH_W2: residual add (through the slice counters when K is split) and the next
-                // norm's Q8_0 input.  Both epilogue warps take every step together.
-                const float* wn = KIND == PH_WO ? a.layers[layer].rms_ffn
-                                : (layer + 1 < a.n_layers ? a.layers[layer + 1].rms_att : a.rms_out);
-                PairX* px = &m->px;
-                if (p.kparts > 1 && !ab) {
+                // WO / W2: this slice's outputs (the residual add runs in the following phase); LM: logits
+                float* out = kind == PH_LM ? a.logits : a.yparts + (size_t)part * a.ypart_stride;
+                const int ld = kind == PH_LM ? a.vocab : a.dim;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
-                        if (tok < nv)
-                            a.yparts[(size_t)part * a.ypart_stride + (size_t)tok * a.dim + rg * kTileRows + row] = v[k];
-                    }
-                }
-                if (p.kparts > 1) __threadfence();  // this warp's slice is visible before the counter moves
-                if (lane == 0) px->ab[r] = ab ? 1 : 0;
-                named_sync(kBarEpi, kEpiWarps * 32);
-                if (r == 0 && lane == 0) {
-                    int last = 0;
-                    if (!(px->ab[0] | px->ab[1]))
-                        last = p.kparts == 1 || atomicAdd(&a.sync[1 + unit], 1u) == (uint32_t)(p.kparts - 1);
-                    px->last = last;
-                }
-                named_sync(kBarEpi, kEpiWarps * 32);
-                if (px->last) {
-                    float t[4];
-                    if (p.kparts == 1) {
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) t[k] = 0.f + v[k];
-                    } else {
-                        __threadfence();
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
-                            t[k] = 0.f;
-                            if (tok < nv)
-                                for (int q = 0; q < p.kparts; ++q)
-                                    t[k] += __ldcg(a.yparts + (size_t)q * a.ypart_stride + (size_t)tok * a.dim +
-                                                   rg * kTileRows + row);
-                        }
-                    }
-                    resid_update(a, t, rg, r, lane, nv, wn, px);
-                    if (p.kparts > 1 && r == 0 && lane == 0) a.sync[1 + unit] = 0;  // all slices arrived: reset
-                } else {
-                    named_sync(kBarEpi, kEpiWarps * 32);  // px->last read by both warps before it is rewritten
+                for (int k = 0; k < 4; ++k) {
+                    const int e = lane + 32 * k, row = e >> 3, tok = e & 7;
+                    const int gr = rg * kTileRows + row;
+                    if (gr < ld && tok < nv) out[(size_t)tok * ld + gr] = v[k];
                 }
             }
         }
+    }
+}
+
+__device__ __forceinline__ void attention_phase(const FwdArgs& a, int l, uint8_t* uni, int nv, int pos, int tid) {
+    const int warp = tid >> 5;
+    const int G = gridDim.x;
+    const AttnArgs aa = attn_args(a, l, pos);
+    const int grp = warp >> 3;  // two 8-warp groups per CTA over the (kv head, chunk) items
+    if (grp >= kFwdAttnGroups || nv <= 0) return;
+    const int hi_max = pos + nv - 1, lo_min = max(0, pos + 1 - a.max_seq);
+    const int c_first = lo_min / aa.chunk, c_last = hi_max / aa.chunk;
+    const int n_items = (c_last - c_first + 1) * a.n_kvh;
+    const AttnSmem sm = attn_smem_at(uni + (size_t)grp * attn_smem_bytes());
+    const int bar_id = kBarAttn0 + grp;
+    for (int item = blockIdx.x * kFwdAttnGroups + grp; item < n_items; item += G * kFwdAttnGroups)
+        attn_item<8, 4>(aa, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, tid & 255,
+                        [bar_id] { named_sync(bar_id, 256); });
+}
+
+// kCombineWarps warps per (token, head) row; warps 0-15 hold four rows at a time.
+__device__ __forceinline__ void combine_phase(const FwdArgs& a, int l, uint8_t* uni, int nv, int pos, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int slot = warp / kCombineWarps;  // 0..3 for warps 0-15
+    if (slot >= 4) return;
+    const AttnArgs aa = attn_args(a, l, pos);
+    float* obuf = reinterpret_cast<float*>(uni) + slot * kCombineWarps * kHD;
+    const int bar_id = kBarAttn0 + slot;
+    for (int row = blockIdx.x * 4 + slot; row < nv * a.n_heads; row += gridDim.x * 4)
+        attn_combine_row(aa, pos, row / a.n_heads, row % a.n_heads, warp % kCombineWarps, lane, obuf,
+                         [bar_id] { named_sync(bar_id, kCombineWarps * 32); });
+}
+
+__device__ __forceinline__ void red_phase(const FwdArgs& a, int kparts, const float* wn, int nv, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nbd = a.dim >> 5;
+    for (int wt = blockIdx.x * kComputeWarps + warp; wt < nv * nbd; wt += gridDim.x * kComputeWarps)
+        red_block(a, wt / nbd, wt % nbd, kparts, wn, lane);
+}
+
+// embedding: x rows, their 16-row sums of squares and Q8_0 of x * (layer 0 attention norm weight); one
+// thread per (token, 32-value block)
+__device__ __forceinline__ void embed_phase(const FwdArgs& a, int nv, int tid) {
+    const int nbd = a.dim >> 5, ngroups = a.dim >> 4;
+    const float* w0 = a.layers[0].rms_att;
+    for (int t = blockIdx.x * kComputeThreads + tid; t < nv * nbd; t += gridDim.x * kComputeThreads) {
+        const int s = t / nbd, b = t % nbd;
+        const int token = a.tokens ? a.tokens[s] : a.ctrl->tokens[s];
+        const uint8_t* blk = a.embd + ((size_t)token * nbd + b) * 18;
+        float v[32], u[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            v[i] = q4_0_value(blk, i);
+            u[i] = v[i] * w0[b * 32 + i];
+        }
+        float* xp = a.x + (size_t)s * a.dim + b * 32;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(xp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        a.ssq[(size_t)s * ngroups + 2 * b] = group16_sumsq(v);
+        a.ssq[(size_t)s * ngroups + 2 * b + 1] = group16_sumsq(v + 16);
+        q8_block_thread(u, a.un_img, s, b);
     }
 }
 
@@ -436,7 +484,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
     uint64_t* red_full = empty + kMaxStages;
     uint64_t* red_empty = red_full + kRedSlots;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = gridDim.x;
 
     if (a.ctrl && a.ctrl->done) return;  // uniform: nothing writes ctrl while the kernel runs
     const int nv = a.ctrl ? min(a.ctrl->n_valid, a.S) : a.S;
@@ -451,14 +498,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
             mbar_init(&red_full[i], kConsumerWarps);
             mbar_init(&red_empty[i], kEpiWarps);
         }
+        mbar_init(&red_empty[kRedSlots], 1);  // act barrier (after the red slots)
         m->abort = 0;
         m->issued = 0;
         m->pdone = 0;
+        m->act_issued = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
     Ring R;
+    R.act_full = &red_empty[kRedSlots];
     R.ring = smem + L.ring;
     R.full = full;
     R.empty = empty;
@@ -505,9 +555,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
             for (int l = 0; l < a.n_layers && ok; ++l) {
                 const FwdLayer& W = a.layers[l];
                 stream(a.qkv, W.qkv);
-                stream(a.wo, W.wo);
-                stream(a.w13, W.w13);
-                stream(a.w2, W.w2);
+                if (ok) stream(a.wo, W.wo);
+                if (ok) stream(a.w13, W.w13);
+                if (ok) stream(a.w2, W.w2);
             }
             if (a.lm && ok) stream(a.lmp, a.lm);
             reinterpret_cast<volatile uint32_t*>(&m->issued)[0] = sidx;
@@ -517,89 +567,29 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
         return;
     }
 
-    // ---------------- compute warps ----------------
-    uint32_t target = 0, sidx = 0, pidx = 0;
+    // ---------------- compute warps: the phase table ----------------
+    uint32_t target = 0, sidx = 0, pidx = 0, nstg = 0;
     bool ab = false;
-
-    // embedding: x rows, their 16-row sums of squares and Q8_0 of x * (layer 0 attention norm weight);
-    // one thread per (token, 32-value block)
-    {
-        const int nbd = a.dim >> 5, ngroups = a.dim >> 4;
-        const float* w0 = a.layers[0].rms_att;
-        for (int t = blockIdx.x * kComputeThreads + tid; t < nv * nbd; t += G * kComputeThreads) {
-            const int s = t / nbd, b = t % nbd;
-            const int token = a.tokens ? a.tokens[s] : a.ctrl->tokens[s];
-            const uint8_t* blk = a.embd + ((size_t)token * nbd + b) * 18;
-            float v[32], u[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                v[i] = q4_0_value(blk, i);
-                u[i] = v[i] * w0[b * 32 + i];
-            }
-            float* xp = a.x + (size_t)s * a.dim + b * 32;
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(xp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-            a.ssq[(size_t)s * ngroups + 2 * b] = group16_sumsq(v);
-            a.ssq[(size_t)s * ngroups + 2 * b + 1] = group16_sumsq(v + 16);
-            float d;
-            int sum;
-            q8_block_thread(u, a.un.qs + (size_t)s * a.dim + b * 32, &d, &sum);
-            a.un.d[(size_t)s * nbd + b] = d;
-            a.un.sum[(size_t)s * nbd + b] = sum;
-        }
-    }
+    embed_phase(a, nv, tid);
     grid_barrier(a, m, target);
-
     uint8_t* uni = smem + L.act;
-    for (int l = 0; l < a.n_layers; ++l) {
-        mv_phase<PH_QKV>(a, a.qkv, l, R, m, sidx, pidx, ab, nv, pos, tid);
-        grid_barrier(a, m, target);
-
-        AttnArgs aa{};
-        aa.q = a.q;
-        aa.q_ld = a.q_rows;
-        aa.k = a.k_cache + (size_t)l * a.kv_layer;
-        aa.v = a.v_cache + (size_t)l * a.kv_layer;
-        aa.kv_ld = a.kv_rows;
-        aa.n_heads = a.n_heads;
-        aa.n_kvh = a.n_kvh;
-        aa.S = a.S;
-        aa.pos = pos;
-        aa.max_seq = a.max_seq;
-        aa.chunk = a.attn_chunk;
-        aa.max_chunks = a.max_chunks;
-        aa.part_ml = a.part_ml;
-        aa.part_acc = a.part_acc;
-        aa.out = a.attn;
-        aa.out_f32 = nullptr;
-        aa.ctrl = nullptr;
-        {
-            // attention partials: two 128-thread groups per CTA over the (kv head, chunk) items
-            const int grp = warp >> 2;
-            if (grp < kFwdAttnGroups && nv > 0) {
-                const int hi_max = pos + nv - 1, lo_min = max(0, pos + 1 - a.max_seq);
-                const int c_first = lo_min / aa.chunk, c_last = hi_max / aa.chunk;
-                const int n_items = (c_last - c_first + 1) * a.n_kvh;
-                const AttnSmem sm = attn_smem_at(uni + (size_t)grp * attn_smem_bytes());
-                const int bar_id = kBarAttn0 + grp;
-                for (int item = blockIdx.x * kFwdAttnGroups + grp; item < n_items; item += G * kFwdAttnGroups)
-                    attn_item<4>(aa, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, tid & 127,
-                              [bar_id] { named_sync(bar_id, kAttnThreads); });
-            }
+    const int n_ph = 8 * a.n_layers + (a.lm ? 1 : 0);
+    for (int ph = 0; ph < n_ph; ++ph) {
+        const int l = ph >> 3, k = ph & 7;
+        if (k == 1 && l < a.n_layers) {
+            attention_phase(a, l, uni, nv, pos, tid);
+        } else if (k == 2) {
+            combine_phase(a, l, uni, nv, pos, tid);
+        } else if (k == 4 || k == 7) {
+            const int kp = k == 4 ? a.wo.kparts : a.w2.kparts;
+            const float* wn = k == 4 ? a.layers[l].rms_ffn : l + 1 < a.n_layers ? a.layers[l + 1].rms_att : a.rms_out;
+            red_phase(a, kp, wn, nv, tid);
+        } else {
+            const int kind = l == a.n_layers ? PH_LM : k == 0 ? PH_QKV : k == 3 ? PH_WO : k == 5 ? PH_W13 : PH_W2;
+            mv_phase(a, kind, l, R, m, sidx, pidx, nstg, ab, nv, pos, tid);
         }
-        grid_barrier(a, m, target);
-        for (int wt = blockIdx.x * kComputeWarps + warp; wt < nv * a.n_heads; wt += G * kComputeWarps)
-            attn_combine_row(aa, pos, wt / a.n_heads, wt % a.n_heads, lane);
-        grid_barrier(a, m, target);
-
-        mv_phase<PH_WO>(a, a.wo, l, R, m, sidx, pidx, ab, nv, pos, tid);
-        grid_barrier(a, m, target);
-        mv_phase<PH_W13>(a, a.w13, l, R, m, sidx, pidx, ab, nv, pos, tid);
-        grid_barrier(a, m, target);
-        mv_phase<PH_W2>(a, a.w2, l, R, m, sidx, pidx, ab, nv, pos, tid);
-        grid_barrier(a, m, target);
+        if (ph + 1 < n_ph) grid_barrier(a, m, target);
     }
-    if (a.lm) mv_phase<PH_LM>(a, a.lmp, 0, R, m, sidx, pidx, ab, nv, pos, tid);
 
     // Drain: no bulk copy may still be landing in shared memory when the CTA exits.  Only the last
     // nstage issued stages can be in flight (a slot is reissued only after every consumer waited for it).
@@ -611,6 +601,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
         const uint32_t issued = reinterpret_cast<volatile uint32_t*>(&m->issued)[0];
         const uint32_t first = issued > (uint32_t)a.nstage ? issued - a.nstage : 0;
         for (uint32_t s = first; s < issued; ++s) mbar_wait(&full[s % a.nstage], (s / a.nstage) & 1);
+        const uint32_t acts = reinterpret_cast<volatile uint32_t*>(&m->act_issued)[0];
+        if (acts > 0) mbar_wait(R.act_full, (acts - 1) & 1);
     }
 }
 
@@ -622,7 +614,7 @@ int fwd_pick_stages(int max_smem) {
     return 0;
 }
 
-size_t fwd_sync_words(int dim) { return 1 + (size_t)(dim >> 4); }
+size_t fwd_sync_words(int) { return 1; }  // the grid barrier counter
 
 cudaError_t fwd_init_attrs(int max_smem) {
     return cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);

@@ -35,13 +35,15 @@ struct FwdArgs {
     int nstage;                 // weight ring stages
     float* x;                   // [S][dim] residual stream
     float* ssq;                 // [S][dim/16] sums of squares of x per 16-row group
-    Q8Planes un;                // [S][dim] Q8_0 of x * (next RMSNorm weight), block scales before the norm scale
+    ActImage un_img;            // Q8_0 of x * (next RMSNorm weight), block scales before the norm scale
+    ActImage attn_img;          // Q8_0 head outputs (o-proj input)
+    ActImage h_img;             // Q8_0 SiLU(gate)*up (down-projection input)
     float* q;                   // [S][q_rows]
-    Q8Planes attn;              // [S][q_rows] quantised head outputs
-    Q8Planes h;                 // [S][hidden] quantised SiLU(gate)*up
+    Q8Planes attn;              // [S][q_rows] quantised head outputs (planes; unused when attn_img is set)
+    Q8Planes h;                 // [S][hidden] quantised SiLU(gate)*up (planes; unused when h_img is set)
     float* yparts;              // [kparts][S][dim] K-slice partials
     size_t ypart_stride;
-    unsigned* sync;             // [0] grid barrier, [1 + unit] slice counters; zero at launch
+    unsigned* sync;             // [0] grid barrier counter; zero at launch
     float2* part_ml;            // attention partials
     float* part_acc;
     int attn_chunk, max_chunks;

@@ -25,7 +25,7 @@ namespace {
 // Shared memory: weight ring | B fragments (+ zero pad) | C quads | activation scales |
 //                partial-sum slots | SiLU unit | mbarriers
 struct SmemLayout {
-    size_t ring, act_b, act_zero, act_c, act_x, red, ubuf, bars, total;
+    size_t ring, act, red, ubuf, bars, total;
 };
 
 // Kp = the K range one CTA covers (K / kparts).
@@ -33,11 +33,8 @@ __host__ __device__ inline SmemLayout smem_layout(int Kp, int S, int chunk, int 
     SmemLayout L;
     const size_t nb = (size_t)Kp / 32;
     L.ring = 0;
-    L.act_b = L.ring + (size_t)nstage * kRPW * chunk * kTileBytes;
-    L.act_zero = L.act_b + nb * (size_t)(4 * S) * 8;   // uint2 per (block, lane < 4S)
-    L.act_c = L.act_zero + (size_t)4 * (4 * S) * 8;    // zeros read by lanes whose token g >= S
-    L.act_x = L.act_c + nb * 4 * 16;                   // int4 C quad per (block, t)
-    L.red = L.act_x + nb * 4 * 8;                      // float2 scales per (block, t)
+    L.act = L.ring + (size_t)nstage * kRPW * chunk * kTileBytes;
+    L.red = L.act + act_smem_bytes((int)nb);  // B fragments, C quads, scales (sd_dev.cuh)
     L.ubuf = L.red + (size_t)kRedSlots * kRPW * kConsumerWarps * 128 * 4;
     L.bars = L.ubuf + 4 * 128 * 4;
     L.total = L.bars + (2 * kMaxStages + 2 * kRedSlots) * 8;
@@ -129,7 +126,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
         pos = a.ctrl->pos;
     }
     const int nthr = (kConsumerWarps + kEpiWarps) * 32;
-    const ActSmem A = act_smem_at(smem + L.act_b, nb, S);
+    const ActSmem A = act_smem_at(smem + L.act, nb);
     stage_act_from_planes(A, a.act, a.K, kb0, nb, S, nv, tid, nthr);
     named_sync(1, nthr);
 

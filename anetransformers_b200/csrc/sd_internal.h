@@ -42,6 +42,13 @@ struct RowMap {
     int unit, stride, offset;
 };
 
+// Activations in the matvec's shared-memory fragment layout, kept in global memory (sd_dev.cuh).
+struct ActImage {
+    uint2* b;
+    int4* c;
+    float2* x;
+};
+
 // Q8_0 activations on device as planes (codes, fp32 scale, per-block code sum).
 struct Q8Planes {
     int8_t* qs;     // [S][n]
