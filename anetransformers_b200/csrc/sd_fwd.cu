@@ -45,7 +45,6 @@ constexpr int kProducerWarp = kComputeWarps;
 constexpr int kMaxChunk = 16;
 constexpr uint32_t kStageBytes = kRPW * kMaxChunk * kTileBytes;  // 36864
 constexpr int kActMaxNb = 128;                                   // K slice <= 4096 columns
-constexpr uint32_t kGridSpinLimit = 1u << 22;                    // polls of 64+ ns: > 0.25 s
 
 // named barrier ids: 0 = __syncthreads, 1 = compute warps, 2 = the two epilogue warps,
 // 3 = consumer warps (staging), 4.. = attention groups
@@ -135,18 +134,19 @@ __device__ void grid_barrier(const FwdArgs& a, Misc* m, uint32_t& target) {
         target += gridDim.x;
         volatile int* ab = &m->abort;
         if (!*ab) {
-            __threadfence();
-            atomicAdd(&a.sync[0], 1u);
-            uint32_t n = 0;
-            while (ld_acquire_u32(&a.sync[0]) < target) {
-                if (++n > kGridSpinLimit) {
-                    set_dev_error(a.err, DEV_ERR_PEER_WAIT);
-                    *ab = 1;
-                    break;
+            // release: this CTA's writes (ordered before by the CTA barrier) are visible to a CTA that
+            // acquires the count; the acquiring load does the same for the others' writes
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&a.sync[0]) : "memory");
+            if (ld_acquire_u32(&a.sync[0]) < target) {
+                const uint64_t t0 = global_ns();
+                while (ld_acquire_u32(&a.sync[0]) < target) {
+                    if (global_ns() - t0 > kWaitLimitNs) {
+                        set_dev_error(a.err, DEV_ERR_PEER_WAIT);
+                        *ab = 1;
+                        break;
+                    }
                 }
-                __nanosleep(64);
             }
-            __threadfence();
         }
     }
     named_sync(kBarCompute, kComputeThreads);
@@ -204,33 +204,6 @@ __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem&
             if (((i & (kActStride - 1)) >> 2) >= nv) A.b[i] = make_uint2(0, 0);
 }
 
-// Q8_0 of u for one 32-value block of token s (thread-level; the arithmetic of q8_quant_lane), into the
-// activation image.
-__device__ __forceinline__ void q8_block_thread(const float* u, const ActImage& im, int s, int blk) {
-    float am = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(u[i]));
-    const float d = __fdiv_rn(am, 127.0f);
-    const float id = am != 0.0f ? __fdiv_rn(1.0f, d) : 0.f;
-    int sum = 0;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            int q = 0;
-            if (am != 0.0f) {
-                const int r = __float2int_rn(__fmul_rn(u[4 * w + c], id));
-                q = r > 127 ? 127 : (r < -128 ? -128 : r);
-            }
-            sum += q;
-            word |= (uint32_t)(q & 0xFF) << (8 * c);
-        }
-        image_put_word(im, s, blk, w, word);
-    }
-    image_put_meta(im, s, blk, d, sum);
-}
-
 // ---------------------------------------------------------------------------------------------
 // Phase kinds
 // ---------------------------------------------------------------------------------------------
@@ -238,25 +211,11 @@ enum PhaseKind : int { PH_QKV = 0, PH_WO = 1, PH_W13 = 2, PH_W2 = 3, PH_LM = 4 }
 constexpr int kMaxParts = 8;  // K slices of a matvec whose outputs a residual phase adds
 
 
-// Residual update of one (token, 32-row block), one warp, lane = row: x += the matvec's slice outputs
-// (added in slice order, as the per-op norm kernel adds them), the two 16-row sums of squares of the
-// new x, and Q8_0 of u = x*wn for the next RMSNorm (wn its weight; the norm scale is applied when the
-// planes are staged).
-__device__ void red_block(const FwdArgs& a, int s, int b, int kparts, const float* wn, int lane) {
-    const int row = b * 32 + lane;
-    float xv = a.x[(size_t)s * a.dim + row];
-    float yv[kMaxParts];
-#pragma unroll
-    for (int p = 0; p < kMaxParts; ++p)
-        yv[p] = p < kparts ? a.yparts[(size_t)p * a.ypart_stride + (size_t)s * a.dim + row] : 0.f;
-    const float w = wn[row];
-    float t = 0.f;
-#pragma unroll
-    for (int p = 0; p < kMaxParts; ++p)
-        if (p < kparts) t += yv[p];
-    xv = xv + t;
-    a.x[(size_t)s * a.dim + row] = xv;
-    // group sums (lanes 0-15: group 2b, 16-31: group 2b+1) in the canonical order of group16_sumsq
+// Finish one (token s, 32-row block b) of the residual stream, one warp, lane = row: store the new x
+// value xv, the block's two 16-row sums of squares (the canonical order of group16_sumsq), and Q8_0 of
+// u = x*wn for the next RMSNorm (wn its weight; the norm scale is applied when the image is staged).
+__device__ __forceinline__ void finish_block(const FwdArgs& a, int s, int b, float xv, float w, int lane) {
+    a.x[(size_t)s * a.dim + b * 32 + lane] = xv;
     const int gb = lane & 16, j = lane & 3;
     float q = 0.f;
 #pragma unroll
@@ -272,6 +231,23 @@ __device__ void red_block(const FwdArgs& a, int s, int b, int kparts, const floa
     const int code = q8_quant_lane(xv * w, &d, &sum);
     image_put_codes_lane(a.un_img, s, b, lane, code);
     if (lane == 0) image_put_meta(a.un_img, s, b, d, sum);
+}
+
+// Residual update of one (token, block): x += the matvec's slice outputs, added in slice order as the
+// per-op norm kernel adds them.
+__device__ void red_block(const FwdArgs& a, int s, int b, int kparts, const float* wn, int lane) {
+    const int row = b * 32 + lane;
+    float xv = a.x[(size_t)s * a.dim + row];
+    float yv[kMaxParts];
+#pragma unroll
+    for (int p = 0; p < kMaxParts; ++p)
+        yv[p] = p < kparts ? a.yparts[(size_t)p * a.ypart_stride + (size_t)s * a.dim + row] : 0.f;
+    const float w = wn[row];
+    float t = 0.f;
+#pragma unroll
+    for (int p = 0; p < kMaxParts; ++p)
+        if (p < kparts) t += yv[p];
+    finish_block(a, s, b, xv + t, w, lane);
 }
 
 __device__ __forceinline__ AttnArgs attn_args(const FwdArgs& a, int l, int pos) {
@@ -392,6 +368,30 @@ __device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, 
                     if (!ab) epi_silu_q8(R.ubuf, r, lane, unit, nv, a.h, a.hidden, &a.h_img);
                     named_sync(kBarEpi, kEpiWarps * 32);
                 }
+            } else if (kind == PH_WO && p.kparts == 1) {
+                // the pair is one 32-row block (unit): finish it here for every token, warp r taking
+                // tokens r, r + 2, ... (lane = row); x and the norm weight are loaded up front
+#pragma unroll
+                for (int k = 0; k < 4; ++k) R.ubuf[r * 128 + lane + 32 * k] = v[k];
+                const int row = unit * 32 + lane;
+                const float w = a.layers[layer].rms_ffn[row];
+                float xo[kMaxS / 2];
+#pragma unroll
+                for (int q = 0; q < kMaxS / 2; ++q) {
+                    const int s = r + 2 * q;
+                    xo[q] = s < nv ? a.x[(size_t)s * a.dim + row] : 0.f;
+                }
+                named_sync(kBarEpi, kEpiWarps * 32);
+                if (!ab) {
+#pragma unroll
+                    for (int q = 0; q < kMaxS / 2; ++q) {
+                        const int s = r + 2 * q;
+                        if (s >= nv) break;
+                        const float y = R.ubuf[(lane >> 4) * 128 + (lane & 15) * 8 + s];
+                        finish_block(a, s, unit, xo[q] + (0.f + y), w, lane);
+                    }
+                }
+                named_sync(kBarEpi, kEpiWarps * 32);  // ubuf free again
             } else if (ab) {
                 continue;
             } else if (kind == PH_QKV) {
@@ -450,26 +450,16 @@ __device__ __forceinline__ void red_phase(const FwdArgs& a, int kparts, const fl
 }
 
 // embedding: x rows, their 16-row sums of squares and Q8_0 of x * (layer 0 attention norm weight); one
-// thread per (token, 32-value block)
+// warp per (token, 32-value block)
 __device__ __forceinline__ void embed_phase(const FwdArgs& a, int nv, int tid) {
-    const int nbd = a.dim >> 5, ngroups = a.dim >> 4;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nbd = a.dim >> 5;
     const float* w0 = a.layers[0].rms_att;
-    for (int t = blockIdx.x * kComputeThreads + tid; t < nv * nbd; t += gridDim.x * kComputeThreads) {
-        const int s = t / nbd, b = t % nbd;
+    for (int wt = blockIdx.x * kComputeWarps + warp; wt < nv * nbd; wt += gridDim.x * kComputeWarps) {
+        const int s = wt / nbd, b = wt % nbd;
         const int token = a.tokens ? a.tokens[s] : a.ctrl->tokens[s];
-        const uint8_t* blk = a.embd + ((size_t)token * nbd + b) * 18;
-        float v[32], u[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            v[i] = q4_0_value(blk, i);
-            u[i] = v[i] * w0[b * 32 + i];
-        }
-        float* xp = a.x + (size_t)s * a.dim + b * 32;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(xp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-        a.ssq[(size_t)s * ngroups + 2 * b] = group16_sumsq(v);
-        a.ssq[(size_t)s * ngroups + 2 * b + 1] = group16_sumsq(v + 16);
-        q8_block_thread(u, a.un_img, s, b);
+        const float v = q4_0_value(a.embd + ((size_t)token * nbd + b) * 18, lane);
+        finish_block(a, s, b, v, w0[b * 32 + lane], lane);
     }
 }
 
@@ -580,6 +570,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
             attention_phase(a, l, uni, nv, pos, tid);
         } else if (k == 2) {
             combine_phase(a, l, uni, nv, pos, tid);
+        } else if (k == 4 && a.wo.kparts == 1) {
+            // done by the o-proj epilogue
         } else if (k == 4 || k == 7) {
             const int kp = k == 4 ? a.wo.kparts : a.w2.kparts;
             const float* wn = k == 4 ? a.layers[l].rms_ffn : l + 1 < a.n_layers ? a.layers[l + 1].rms_att : a.rms_out;
@@ -588,7 +580,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
             const int kind = l == a.n_layers ? PH_LM : k == 0 ? PH_QKV : k == 3 ? PH_WO : k == 5 ? PH_W13 : PH_W2;
             mv_phase(a, kind, l, R, m, sidx, pidx, nstg, ab, nv, pos, tid);
         }
-        if (ph + 1 < n_ph) grid_barrier(a, m, target);
+        if (ph + 1 < n_ph && !(k == 3 && a.wo.kparts == 1 && l < a.n_layers)) grid_barrier(a, m, target);
     }
 
     // Drain: no bulk copy may still be landing in shared memory when the CTA exits.  Only the last
