@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const AttnArgs a)
     const int n_items = (c_last - c_first + 1) * a.n_kvh;
     const AttnSmem sm = attn_smem_at(smem);
     for (int item = blockIdx.x; item < n_items; item += gridDim.x)
-        attn_item<4, kMaxS>(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, threadIdx.x,
+        attn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, threadIdx.x,
                   [] { __syncthreads(); });
 }
 

@@ -103,6 +103,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return true;
 }
 
+// Position in an n-slot mbarrier ring without per-step division: slot index and the phase parity of
+// the slot's current use.
+struct RingPos {
+    int slot = 0;
+    uint32_t phase = 0;
+    __device__ __forceinline__ void advance(int n) {
+        if (++slot == n) {
+            slot = 0;
+            phase ^= 1;
+        }
+    }
+};
+
 // ---------------------------------------------------------------------------------------------
 // 1-D bulk copy global -> shared through the TMA engine, completing on an mbarrier (transaction
 // bytes).  Both addresses 16-byte aligned, size a multiple of 16.  No multicast.

@@ -162,15 +162,27 @@ struct TileRegs {
     uint2 sl[kRPW], sh[kRPW];
 };
 
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+
 __device__ __forceinline__ void load_tiles(const uint8_t* slot, uint32_t half_bytes, int warp, int lane, TileRegs& tr) {
     const int g = lane >> 2;
+    const uint32_t base = smem_u32(slot) + warp * kTileBytes;
 #pragma unroll
     for (int r = 0; r < kRPW; ++r) {
-        const uint8_t* tile = slot + r * half_bytes + warp * kTileBytes;
-        tr.wl[r] = *reinterpret_cast<const uint4*>(tile + lane * 16);
-        tr.wh[r] = *reinterpret_cast<const uint4*>(tile + 512 + lane * 16);
-        tr.sl[r] = *reinterpret_cast<const uint2*>(tile + 1024 + g * 8);
-        tr.sh[r] = *reinterpret_cast<const uint2*>(tile + 1088 + g * 8);
+        const uint32_t tile = base + r * half_bytes;
+        tr.wl[r] = lds128(tile + lane * 16);
+        tr.wh[r] = lds128(tile + 512 + lane * 16);
+        tr.sl[r] = lds64(tile + 1024 + g * 8);
+        tr.sh[r] = lds64(tile + 1088 + g * 8);
     }
 }
 
@@ -190,14 +202,16 @@ __device__ __forceinline__ void consume_tiles(const TileRegs& tr, int lane, cons
         dh[r][0] = h2x2f(tr.sh[r].x);
         dh[r][1] = h2x2f(tr.sh[r].y);
     }
-    const uint2* bf_p = A.b + (size_t)bbase * kActStride + lane;  // token slot g, word pair t
-    const int4* c_p = A.c + bbase * 4 + t;
-    const float2* x_p = A.x + bbase * 4 + t;
+    const uint32_t bf_a = smem_u32(A.b) + (bbase * kActStride + lane) * 8;  // token slot g, word pair t
+    const uint32_t c_a = smem_u32(A.c) + (bbase * 4 + t) * 16;
+    const uint32_t x_a = smem_u32(A.x) + (bbase * 4 + t) * 8;
 #pragma unroll
     for (int blk = 0; blk < 4; ++blk) {
-        const uint2 bf = bf_p[blk * kActStride];
-        const int4 cq = c_p[blk * 4];
-        const float2 xd = x_p[blk * 4];
+        const uint2 bf = lds64(bf_a + blk * kActStride * 8);
+        const uint4 cu = lds128(c_a + blk * 64);
+        const int4 cq = make_int4((int)cu.x, (int)cu.y, (int)cu.z, (int)cu.w);
+        const uint2 xu = lds64(x_a + blk * 32);
+        const float2 xd = make_float2(__uint_as_float(xu.x), __uint_as_float(xu.y));
 #pragma unroll
         for (int r = 0; r < kRPW; ++r) {
             const uint32_t wlo = blk == 0 ? tr.wl[r].x : blk == 1 ? tr.wl[r].y : blk == 2 ? tr.wl[r].z : tr.wl[r].w;
@@ -380,185 +394,256 @@ __device__ __forceinline__ float q4_0_value(const uint8_t* blk, int e) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Attention work item (kv head, chunk) for one group of 4 warps (128 threads); see sd_attn.cu.
+// Attention work item (kv head, chunk) for a group of 8 warps (256 threads), on the tensor cores.
+//
+// Query rows r = 4*s + h (token s < 8, query head h of the kv head: 32 rows = two 16-row m-tiles) and
+// a sub-block of 32 positions.  Scores S = Q K^T and outputs O = P V use mma.m16n8k16 (f16 inputs,
+// f32 accumulate).  K and V are fp16 already; Q (fp32) and the probabilities P (fp32) are split into
+// a high and a low fp16 part and both are multiplied, so products keep ~22 bits (fp32-class results).
+// Warp w owns m-tile w/4 (tokens 4*(w/4) .. +3) and quarter w%4: score columns 8*(w%4) .. +7 of the
+// sub-block, output dims 32*(w%4) .. +31.  The online softmax (mistral/mistral_model.h:362-487
+// semantics, exp of score minus running max) runs per row between the two products.
 // ---------------------------------------------------------------------------------------------
 constexpr int kHD = 128;        // head_dim
 constexpr int kGQA = 4;         // query heads per kv head
-constexpr int kSub = 32;        // positions per sub-block (one per lane)
-constexpr int kAttnThreads = 128;
+constexpr int kSub = 32;        // positions per sub-block
+constexpr int kAttnThreads = 256;
+constexpr int kQRows = kMaxS * kGQA;  // 32
+constexpr int kQStride = kHD + 8;     // halves per Q / K row (bank-conflict-free fragment loads)
+constexpr int kVStride = kSub + 8;    // halves per transposed V row
+constexpr int kSStride = kSub + 4;    // floats per score row
 
 struct AttnSmem {
-    float* qs;      // [kMaxS * kGQA][kHD]
-    __half* kt;     // [kHD][kSub + 2]
-    __half* vt;     // [kSub][kHD]
+    __half* qh;     // [kQRows][kQStride] high part of q
+    __half* ql;     // [kQRows][kQStride] low part
+    __half* kk;     // [kSub][kQStride]  K sub-block (position-major)
+    __half* vt;     // [kHD][kVStride]   V sub-block transposed (dim-major)
+    float* st;      // [kQRows][kSStride] scores, then probabilities
+    float* rm;      // [kQRows] running max
+    float* rl;      // [kQRows] running sum
+    float* rc;      // [kQRows] correction of the last update
 };
 
 __host__ __device__ constexpr size_t attn_smem_bytes() {
-    return (size_t)kMaxS * kGQA * kHD * 4 + (size_t)kHD * (kSub + 2) * 2 + (size_t)kSub * kHD * 2;
+    return (size_t)2 * kQRows * kQStride * 2 + (size_t)kSub * kQStride * 2 + (size_t)kHD * kVStride * 2 +
+           (size_t)kQRows * kSStride * 4 + (size_t)3 * kQRows * 4;
 }
 
 __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
     AttnSmem s;
-    s.qs = reinterpret_cast<float*>(base);
-    s.kt = reinterpret_cast<__half*>(base + (size_t)kMaxS * kGQA * kHD * 4);
-    s.vt = reinterpret_cast<__half*>(base + (size_t)kMaxS * kGQA * kHD * 4 + (size_t)kHD * (kSub + 2) * 2);
+    s.qh = reinterpret_cast<__half*>(base);
+    s.ql = s.qh + kQRows * kQStride;
+    s.kk = s.ql + kQRows * kQStride;
+    s.vt = s.kk + kSub * kQStride;
+    s.st = reinterpret_cast<float*>(s.vt + kHD * kVStride);
+    s.rm = s.st + kQRows * kSStride;
+    s.rl = s.rm + kQRows;
+    s.rc = s.rl + kQRows;
     return s;
 }
 
-// K/V sub-block of kSub positions: thread's 4 pieces (position j = i/16, dims 8*(i%16) .. +7) of
-// K and V, loaded into registers together.
-struct KvRegs {
-    uint4 k[4], v[4];  // up to 4 pieces per thread (4-warp groups); 8-warp groups use 2
-};
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
-template <int NT>
-__device__ __forceinline__ void attn_load_kv(const AttnArgs& a, int kvh, int sb, int p1, int tid, KvRegs& r) {
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// (x, y) -> high and low fp16x2 parts: hi = fp16(x), lo = fp16(x - hi).
+__device__ __forceinline__ void split_f16x2(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    hi = h2u(h);
+    lo = h2u(__floats2half2_rn(x - hf.x, y - hf.y));
+}
+
+// Load one 32-position K/V sub-block: K position-major, V transposed.  8 dims per piece; 512 pieces.
+__device__ __forceinline__ void attn_load_kv(const AttnArgs& a, int kvh, int sb, int p1, int tid, uint4 (&kr)[2],
+                                             uint4 (&vr)[2]) {
 #pragma unroll
-    for (int u = 0; u < 512 / NT; ++u) {
-        const int i = tid + u * NT;  // < kSub * kHD / 8 = 512
+    for (int u = 0; u < 2; ++u) {
+        const int i = tid + u * kAttnThreads;
         const int j = i >> 4, d8 = (i & 15) * 8;
         const int p = sb + j;
-        r.k[u] = r.v[u] = make_uint4(0, 0, 0, 0);
+        kr[u] = vr[u] = make_uint4(0, 0, 0, 0);
         if (p < p1) {
             const size_t off = (size_t)(p % a.max_seq) * a.kv_ld + (size_t)kvh * kHD + d8;
-            r.k[u] = *reinterpret_cast<const uint4*>(a.k + off);
-            r.v[u] = *reinterpret_cast<const uint4*>(a.v + off);
+            kr[u] = *reinterpret_cast<const uint4*>(a.k + off);
+            vr[u] = *reinterpret_cast<const uint4*>(a.v + off);
         }
     }
 }
 
-template <int NT>
-__device__ __forceinline__ void attn_store_kv(const AttnSmem& sm, int tid, const KvRegs& r) {
+__device__ __forceinline__ void attn_store_kv(const AttnSmem& sm, int tid, const uint4 (&kr)[2], const uint4 (&vr)[2]) {
 #pragma unroll
-    for (int u = 0; u < 512 / NT; ++u) {
-        const int i = tid + u * NT;
+    for (int u = 0; u < 2; ++u) {
+        const int i = tid + u * kAttnThreads;
         const int j = i >> 4, d8 = (i & 15) * 8;
-        const __half* kh = reinterpret_cast<const __half*>(&r.k[u]);
+        *reinterpret_cast<uint4*>(sm.kk + j * kQStride + d8) = kr[u];
+        const __half* vh = reinterpret_cast<const __half*>(&vr[u]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) sm.kt[(d8 + e) * (kSub + 2) + j] = kh[e];
-        *reinterpret_cast<uint4*>(&sm.vt[j * kHD + d8]) = r.v[u];
+        for (int e = 0; e < 8; ++e) sm.vt[(d8 + e) * kVStride + j] = vh[e];
     }
 }
 
-// One work item (kv head kvh, position chunk c) for a group of NW warps (NW = 4 or 8); gsync() is a
-// barrier over the group's NW*32 threads.  Warp w computes query head 4*kvh + w % 4 for tokens
-// [TG*(w/4), ...) in steps of TG*(NW/4).  The query rows and the first K/V sub-block are loaded
-// together, so an item of one sub-block costs about one memory round trip before its math.  Each
-// token's arithmetic is the same for every (NW, TG).
-template <int NW, int TG, class Sync>
+// gsync(): a barrier over the group's 256 threads (tid = 0..255).
+template <class Sync>
 __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi_max, int kvh, int c, const AttnSmem& sm,
                           int tid, Sync gsync) {
-    constexpr int NT = NW * 32;
     const int warp = tid >> 5, lane = tid & 31;
-    const int hq = warp & 3;  // query head 4*kvh + hq
+    const int g = lane >> 2, t = lane & 3;
+    const int mt = warp >> 2, qw = warp & 3;
+    const bool active = mt * 4 < nv;  // this m-tile holds a valid token
     const int p0 = max(c * a.chunk, lo_min);
     const int p1 = min((c + 1) * a.chunk, hi_max + 1);  // exclusive
     gsync();
     {
-        float4 qv[1024 / NT];  // rows r = s*4 + h, 32 float4 per row: kMaxS * kGQA * 32 = 1024
+        // query rows -> fp16 high/low parts; first K/V sub-block; running statistics
+        float4 qv[4];
 #pragma unroll
-        for (int u = 0; u < 1024 / NT; ++u) {
-            const int i = tid + u * NT;
+        for (int u = 0; u < 4; ++u) {
+            const int i = tid + u * kAttnThreads;  // < 32 rows * 32 float4
             const int r = i >> 5, d4 = (i & 31) * 4;
-            const int s = r / kGQA, h = r % kGQA;
+            const int s = r >> 2, h = r & 3;
             qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (s < nv) qv[u] = *reinterpret_cast<const float4*>(a.q + (size_t)s * a.q_ld + (size_t)(kvh * kGQA + h) * kHD + d4);
         }
-        KvRegs kv;
-        attn_load_kv<NT>(a, kvh, p0, p1, tid, kv);
+        uint4 kr[2], vr[2];
+        attn_load_kv(a, kvh, p0, p1, tid, kr, vr);
 #pragma unroll
-        for (int u = 0; u < 1024 / NT; ++u) {
-            const int i = tid + u * NT;
-            *reinterpret_cast<float4*>(&sm.qs[(i >> 5) * kHD + (i & 31) * 4]) = qv[u];
+        for (int u = 0; u < 4; ++u) {
+            const int i = tid + u * kAttnThreads;
+            const int r = i >> 5, d4 = (i & 31) * 4;
+            uint32_t h0, l0, h1, l1;
+            split_f16x2(qv[u].x, qv[u].y, h0, l0);
+            split_f16x2(qv[u].z, qv[u].w, h1, l1);
+            *reinterpret_cast<uint2*>(sm.qh + r * kQStride + d4) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2*>(sm.ql + r * kQStride + d4) = make_uint2(l0, l1);
         }
-        attn_store_kv<NT>(sm, tid, kv);
+        attn_store_kv(sm, tid, kr, vr);
+        if (tid < kQRows) {
+            sm.rm[tid] = -INFINITY;
+            sm.rl[tid] = 0.f;
+        }
     }
-    int resident = p0;  // sub-block held in shared memory
-    // every warp runs the same number of token rounds (syncs inside stay matched)
-    for (int r0 = 0; r0 < nv; r0 += TG * (NW / 4)) {
-        const int t0 = r0 + TG * (warp >> 2);
-        float m[TG], l[TG], acc[TG][4];
+    float o[4][4];
 #pragma unroll
-        for (int j = 0; j < TG; ++j) {
-            m[j] = -INFINITY;
-            l[j] = 0.f;
-            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int sb = p0; sb < p1; sb += kSub) {
+        if (sb != p0) {
+            uint4 kr[2], vr[2];
+            attn_load_kv(a, kvh, sb, p1, tid, kr, vr);
+            gsync();  // everyone is done with the previous sub-block
+            attn_store_kv(sm, tid, kr, vr);
         }
-        for (int sb = p0; sb < p1; sb += kSub) {
-            if (sb != resident) {
-                KvRegs kv;
-                attn_load_kv<NT>(a, kvh, sb, p1, tid, kv);
-                gsync();  // every warp is done with the resident sub-block
-                attn_store_kv<NT>(sm, tid, kv);
-                resident = sb;
+        gsync();
+        // ---- scores of rows mt*16 .. +15, positions sb + 8*qw .. +7 ----
+        if (active) {
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            const __half* qh0 = sm.qh + (mt * 16 + g) * kQStride + 2 * t;
+            const __half* ql0 = sm.ql + (mt * 16 + g) * kQStride + 2 * t;
+            const __half* k0 = sm.kk + (qw * 8 + g) * kQStride + 2 * t;
+#pragma unroll
+            for (int ks = 0; ks < kHD / 16; ++ks) {
+                const int o16 = ks * 16;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(k0 + o16);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(k0 + o16 + 8);
+                mma_f16(sc, *reinterpret_cast<const uint32_t*>(qh0 + o16), *reinterpret_cast<const uint32_t*>(qh0 + 8 * kQStride + o16),
+                        *reinterpret_cast<const uint32_t*>(qh0 + o16 + 8), *reinterpret_cast<const uint32_t*>(qh0 + 8 * kQStride + o16 + 8),
+                        b0, b1);
+                mma_f16(sc, *reinterpret_cast<const uint32_t*>(ql0 + o16), *reinterpret_cast<const uint32_t*>(ql0 + 8 * kQStride + o16),
+                        *reinterpret_cast<const uint32_t*>(ql0 + o16 + 8), *reinterpret_cast<const uint32_t*>(ql0 + 8 * kQStride + o16 + 8),
+                        b0, b1);
             }
-            gsync();
-            float sc[TG];
+            // mask: row r -> token r/4; column -> position
 #pragma unroll
-            for (int j = 0; j < TG; ++j) sc[j] = 0.f;
-            for (int d = 0; d < kHD; d += 4) {
-                const float k0 = __half2float(sm.kt[d * (kSub + 2) + lane]), k1 = __half2float(sm.kt[(d + 1) * (kSub + 2) + lane]);
-                const float k2 = __half2float(sm.kt[(d + 2) * (kSub + 2) + lane]), k3 = __half2float(sm.kt[(d + 3) * (kSub + 2) + lane]);
-#pragma unroll
-                for (int j = 0; j < TG; ++j) {
-                    if (t0 + j < nv) {
-                        const float4 qv = *reinterpret_cast<const float4*>(&sm.qs[((t0 + j) * kGQA + hq) * kHD + d]);
-                        sc[j] = fmaf(qv.x, k0, sc[j]);
-                        sc[j] = fmaf(qv.y, k1, sc[j]);
-                        sc[j] = fmaf(qv.z, k2, sc[j]);
-                        sc[j] = fmaf(qv.w, k3, sc[j]);
-                    }
-                }
-            }
-            const int p = sb + lane;
-            float pr[TG];
-#pragma unroll
-            for (int j = 0; j < TG; ++j) {
-                pr[j] = 0.f;
-                if (t0 + j >= nv) continue;
-                const int hi = pos + t0 + j, lo = max(0, hi + 1 - a.max_seq);
-                const bool ok = p < p1 && p >= lo && p <= hi;
-                const float v = ok ? sc[j] : -INFINITY;
-                const float mx = warp_max(v);
-                const float mn = fmaxf(m[j], mx);
-                // a token with nothing valid yet keeps m = -inf and contributes nothing
-                const float e = (mn == -INFINITY || !ok) ? 0.f : expf(v - mn);
-                const float corr = (mn == -INFINITY || m[j] == -INFINITY) ? 0.f : expf(m[j] - mn);
-                const float es = warp_sum(e);
-                l[j] = l[j] * corr + es;
-                acc[j][0] *= corr;
-                acc[j][1] *= corr;
-                acc[j][2] *= corr;
-                acc[j][3] *= corr;
-                m[j] = mn;
-                pr[j] = e;
-            }
-            for (int jj = 0; jj < kSub; ++jj) {
-                const uint2 vraw = *reinterpret_cast<const uint2*>(&sm.vt[jj * kHD + lane * 4]);
-                const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&vraw.x));
-                const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&vraw.y));
-#pragma unroll
-                for (int j = 0; j < TG; ++j) {
-                    if (t0 + j < nv) {
-                        const float w = __shfl_sync(0xffffffffu, pr[j], jj);
-                        acc[j][0] = fmaf(w, f01.x, acc[j][0]);
-                        acc[j][1] = fmaf(w, f01.y, acc[j][1]);
-                        acc[j][2] = fmaf(w, f23.x, acc[j][2]);
-                        acc[j][3] = fmaf(w, f23.y, acc[j][3]);
-                    }
-                }
+            for (int e = 0; e < 4; ++e) {
+                const int r = mt * 16 + g + (e >> 1) * 8, s = r >> 2;
+                const int p = sb + qw * 8 + 2 * t + (e & 1);
+                const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
+                const bool ok = s < nv && p < p1 && p >= lo && p <= hi;
+                sm.st[r * kSStride + qw * 8 + 2 * t + (e & 1)] = ok ? sc[e] : -INFINITY;
             }
         }
-        const int h = kvh * kGQA + hq;
+        gsync();
+        // ---- online softmax: warp w updates rows 4w .. 4w+3, lane = position ----
 #pragma unroll
-        for (int j = 0; j < TG; ++j) {
-            const int s = t0 + j;
+        for (int k = 0; k < 4; ++k) {
+            const int r = warp * 4 + k;
+            if ((r >> 2) >= nv) {  // no token: zero probabilities and correction (rows stay unused)
+                sm.st[r * kSStride + lane] = 0.f;
+                if (lane == 0) sm.rc[r] = 0.f;
+                continue;
+            }
+            const float v = sm.st[r * kSStride + lane];
+            const float mo = sm.rm[r];
+            const float mx = warp_max(v);
+            const float mn = fmaxf(mo, mx);
+            // a row with nothing valid yet keeps m = -inf and contributes nothing
+            const float e = (mn == -INFINITY || v == -INFINITY) ? 0.f : expf(v - mn);
+            const float corr = (mn == -INFINITY || mo == -INFINITY) ? 0.f : expf(mo - mn);
+            const float es = warp_sum(e);
+            sm.st[r * kSStride + lane] = e;
+            if (lane == 0) {
+                sm.rl[r] = sm.rl[r] * corr + es;
+                sm.rm[r] = mn;
+                sm.rc[r] = corr;
+            }
+        }
+        gsync();
+        // ---- O (rows mt*16 .., dims 32*qw ..) = O * corr + P V ----
+        if (active) {
+            const float cl = sm.rc[mt * 16 + g], chh = sm.rc[mt * 16 + g + 8];
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+                o[n][0] *= cl;
+                o[n][1] *= cl;
+                o[n][2] *= chh;
+                o[n][3] *= chh;
+            }
+#pragma unroll
+            for (int ks = 0; ks < kSub / 16; ++ks) {
+                const float* p0r = sm.st + (mt * 16 + g) * kSStride + ks * 16 + 2 * t;
+                const float2 x0 = *reinterpret_cast<const float2*>(p0r);
+                const float2 x1 = *reinterpret_cast<const float2*>(p0r + 8 * kSStride);
+                const float2 x2 = *reinterpret_cast<const float2*>(p0r + 8);
+                const float2 x3 = *reinterpret_cast<const float2*>(p0r + 8 * kSStride + 8);
+                uint32_t ah[4], al[4];
+                split_f16x2(x0.x, x0.y, ah[0], al[0]);
+                split_f16x2(x1.x, x1.y, ah[1], al[1]);
+                split_f16x2(x2.x, x2.y, ah[2], al[2]);
+                split_f16x2(x3.x, x3.y, ah[3], al[3]);
+#pragma unroll
+                for (int n = 0; n < 4; ++n) {
+                    const __half* vp = sm.vt + (qw * 32 + n * 8 + g) * kVStride + ks * 16 + 2 * t;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(vp);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(vp + 8);
+                    mma_f16(o[n], ah[0], ah[1], ah[2], ah[3], b0, b1);
+                    mma_f16(o[n], al[0], al[1], al[2], al[3], b0, b1);
+                }
+            }
+        }
+    }
+    gsync();  // final statistics visible
+    // ---- partials of this chunk ----
+    if (active) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int r = mt * 16 + g + hh * 8, s = r >> 2, h = kvh * kGQA + (r & 3);
             if (s >= nv) continue;
             const size_t pi = ((size_t)s * a.n_heads + h) * a.max_chunks + c;
-            if (lane == 0) a.part_ml[pi] = make_float2(m[j], l[j]);
-            *reinterpret_cast<float4*>(a.part_acc + pi * kHD + lane * 4) =
-                make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+#pragma unroll
+            for (int n = 0; n < 4; ++n)
+                *reinterpret_cast<float2*>(a.part_acc + pi * kHD + qw * 32 + n * 8 + 2 * t) =
+                    make_float2(o[n][hh * 2], o[n][hh * 2 + 1]);
         }
+    }
+    if (tid < kQRows && (tid >> 2) < nv) {
+        const int s = tid >> 2, h = kvh * kGQA + (tid & 3);
+        a.part_ml[((size_t)s * a.n_heads + h) * a.max_chunks + c] = make_float2(sm.rm[tid], sm.rl[tid]);
     }
 }
 

@@ -275,7 +275,7 @@ __device__ __forceinline__ AttnArgs attn_args(const FwdArgs& a, int l, int pos) 
 
 // One matvec phase for the compute warps (consumer and epilogue roles).  kind is a runtime value so that
 // the tile loop exists once in the kernel.
-__device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, const Ring& R, Misc* m, uint32_t& sidx,
+__device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, const Ring& R, Misc* m, RingPos& rp,
                                       uint32_t& pidx, uint32_t& nstg, bool& ab, int nv, int pos, int tid) {
     const MvPhase& p = kind == PH_QKV ? a.qkv : kind == PH_WO ? a.wo : kind == PH_W13 ? a.w13 : kind == PH_W2 ? a.w2 : a.lmp;
     const int warp = tid >> 5, lane = tid & 31;
@@ -304,9 +304,9 @@ __device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, 
                 const int rg = unit * p.rpu + pr * kRPW;
 #pragma unroll
                 for (int r = 0; r < kRPW; ++r) accL[r] = accH[r] = make_float2(0.f, 0.f);
-                for (int ch = 0; ch < cpr; ++ch, ++sidx) {
-                    const int slot = sidx % R.nstage;
-                    if (!ab && !wait_or_abort(&R.full[slot], (sidx / R.nstage) & 1, abort_flag)) {
+                for (int ch = 0; ch < cpr; ++ch, rp.advance(R.nstage)) {
+                    const int slot = rp.slot;
+                    if (!ab && !wait_or_abort(&R.full[slot], rp.phase, abort_flag)) {
                         set_dev_error(a.err, DEV_ERR_FULL_WAIT);
                         ab = true;
                         m->abort = 1;
@@ -425,7 +425,7 @@ __device__ __forceinline__ void attention_phase(const FwdArgs& a, int l, uint8_t
     const AttnSmem sm = attn_smem_at(uni + (size_t)grp * attn_smem_bytes());
     const int bar_id = kBarAttn0 + grp;
     for (int item = blockIdx.x * kFwdAttnGroups + grp; item < n_items; item += G * kFwdAttnGroups)
-        attn_item<8, 4>(aa, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, tid & 255,
+        attn_item(aa, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, tid & 255,
                         [bar_id] { named_sync(bar_id, 256); });
 }
 
@@ -513,6 +513,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
         if (lane == 0) {
             const volatile int* abort_flag = &m->abort;
             uint32_t sidx = 0;
+            RingPos pp;
             bool ok = true;
             auto stream = [&](const MvPhase& p, const uint8_t* w) {
                 const Items it = my_items(p);
@@ -523,9 +524,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
                     for (int pr = 0; pr < pairs && ok; ++pr) {
                         const int rg = unit * p.rpu + pr * kRPW;
                         for (int ch = 0; ch < cpr; ++ch) {
-                            const int slot = sidx % a.nstage;
-                            if (sidx >= (uint32_t)a.nstage &&
-                                !wait_or_abort_1(&empty[slot], ((sidx / a.nstage) - 1) & 1, abort_flag)) {
+                            const int slot = pp.slot;
+                            if (sidx >= (uint32_t)a.nstage && !wait_or_abort_1(&empty[slot], pp.phase ^ 1, abort_flag)) {
                                 if (!*abort_flag) set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
                                 m->abort = 1;
                                 ok = false;
@@ -538,6 +538,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
                             bulk_g2s(dst, src, half, &full[slot]);
                             bulk_g2s(dst + half, src + (size_t)p.nq * kTileBytes, half, &full[slot]);
                             ++sidx;
+                            pp.advance(a.nstage);
                         }
                     }
                 }
@@ -558,7 +559,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
     }
 
     // ---------------- compute warps: the phase table ----------------
-    uint32_t target = 0, sidx = 0, pidx = 0, nstg = 0;
+    uint32_t target = 0, pidx = 0, nstg = 0;
+    RingPos rp;
     bool ab = false;
     embed_phase(a, nv, tid);
     grid_barrier(a, m, target);
@@ -578,7 +580,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
             red_phase(a, kp, wn, nv, tid);
         } else {
             const int kind = l == a.n_layers ? PH_LM : k == 0 ? PH_QKV : k == 3 ? PH_WO : k == 5 ? PH_W13 : PH_W2;
-            mv_phase(a, kind, l, R, m, sidx, pidx, nstg, ab, nv, pos, tid);
+            mv_phase(a, kind, l, R, m, rp, pidx, nstg, ab, nv, pos, tid);
         }
         if (ph + 1 < n_ph && !(k == 3 && a.wo.kparts == 1 && l < a.n_layers)) grid_barrier(a, m, target);
     }

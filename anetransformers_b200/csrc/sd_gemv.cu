@@ -99,9 +99,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
         // -------- producer: stream this CTA's row-group pairs through the ring (2 bulk copies/stage) --------
         // Weights do not depend on the previous kernel, so this runs before griddepcontrol.wait.
         if (lane == 0) {
-            for (int s = 0; s < n_stages_total; ++s) {
-                const int slot = s % nstage;
-                if (s >= nstage && !mbar_wait(&empty[slot], ((s / nstage) - 1) & 1)) {
+            RingPos rp;
+            for (int s = 0; s < n_stages_total; ++s, rp.advance(nstage)) {
+                const int slot = rp.slot;
+                if (s >= nstage && !mbar_wait(&empty[slot], rp.phase ^ 1)) {
                     set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
                     break;  // consumers give up on the stages never issued
                 }
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
 #pragma unroll
     for (int r = 0; r < kRPW; ++r) accL[r] = accH[r] = make_float2(0.f, 0.f);
     const bool has_tile = warp < chunk;
-    int sidx = 0;
+    RingPos rp;
     // A stage that never arrives (only possible if the producer gave up) marks the warp aborted: it
     // stops waiting and computing but keeps its place in every handshake, so no warp is left waiting
     // on one that returned.  Every stage issued before the give-up has been waited for, so no bulk
@@ -187,9 +188,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs a) {
     bool aborted = false;
     for (int pi = 0; pi < n_pairs; ++pi) {
         const int rg = rg0 + pi * kRPW;
-        for (int ch = 0; ch < cpr; ++ch, ++sidx) {
-            const int slot = sidx % nstage;
-            if (!aborted && !mbar_wait(&full[slot], (sidx / nstage) & 1)) {
+        for (int ch = 0; ch < cpr; ++ch, rp.advance(nstage)) {
+            const int slot = rp.slot;
+            if (!aborted && !mbar_wait(&full[slot], rp.phase)) {
                 set_dev_error(a.err, DEV_ERR_FULL_WAIT);
                 aborted = true;
             }
