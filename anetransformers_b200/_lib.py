@@ -71,6 +71,9 @@ _SIGS = {
     "sd_host_q4_0_q8_0_matvec": (None, [vp, vp, vp, i32, i32]),
     "sd_host_cache_clear": (None, []),
     "sd_ctx_opts_default": (None, [vp]),
+    "sd_nccl_unique_id": (i32, [vp]),
+    "sd_nccl_comm_create": (i32, [vp, i32, i32, i32, vp]),
+    "sd_nccl_comm_destroy": (None, [vp]),
     "sd_ctx_create": (i32, [vp, sz, vp, vp]),
     "sd_ctx_create_file": (i32, [C.c_char_p, vp, vp]),
     "sd_ctx_free": (None, [vp]),

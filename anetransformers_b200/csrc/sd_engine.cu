@@ -478,6 +478,16 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     return SD_OK;
 }
 
+// Tensor parallelism: this rank's o-proj / down-proj output is a partial sum over its input columns.
+// Add its K slices into slice 0, then sum slice 0 over the ranks; the norm then adds one slice.
+int tp_reduce(sd_ctx* c, int S, int* yparts) {
+    if (c->tp_size <= 1) return SD_OK;
+    const size_t n = (size_t)S * c->dim;
+    if (*yparts > 1) CK(launch_sum_parts(c->y, c->y, (int)n, *yparts, (size_t)c->MB * c->dim, c->st), "sum parts");
+    *yparts = 1;
+    return nccl_allreduce_sum(c->nccl, c->y, n, c->st);
+}
+
 // Enqueue one forward of S (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the
 // position, the tokens and how many of the S are valid.
 int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
@@ -546,9 +556,9 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         po.a.part_stride = (size_t)c->MB * c->dim;
         if (po.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "o-proj K split %d too wide", po.a.kparts);
         if ((rc = launch_plan(c, EPI_STORE, po))) return rc;
-        // TODO(tp): all-reduce of y across ranks goes here
         na.w = W.rms_ffn;
         na.yparts = po.a.kparts;
+        if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
         CK(launch_norm_quant(1, na, c->st, pdl), "norm");
         // gate/up + SiLU + Q8_0
         Plan pg;
@@ -570,6 +580,7 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         if ((rc = launch_plan(c, EPI_STORE, pd))) return rc;
         na.w = (l + 1 < n_layers) ? c->L[l + 1].rms_att : c->rms_final;
         na.yparts = pd.a.kparts;
+        if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
         CK(launch_norm_quant(1, na, c->st, pdl), "norm");
     }
     if (!logits_and_argmax) return SD_OK;
@@ -723,8 +734,9 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
     c->kv_rows = c->nkv_l * c->hd;
     c->qkv_rows = c->q_rows + 2 * c->kv_rows;
     c->hid_l = c->hidden / c->tp_size;
-    if (c->dim % 1024 || c->dim > 4096 || c->q_rows % 1024 || c->hid_l % 1024 || c->hid_l % 64)
-        return bail(fail(SD_ERR_UNSUPPORTED, "dims %d / %d / %d must be multiples of 1024", c->dim, c->q_rows, c->hid_l));
+    if (c->dim % 1024 || c->dim > 4096 || c->q_rows % 128 || c->hid_l % 128)
+        return bail(fail(SD_ERR_UNSUPPORTED, "dim %d must be a multiple of 1024 (<= 4096), local q rows %d and hidden %d of 128",
+                         c->dim, c->q_rows, c->hid_l));
     if (cudaSetDevice(c->dev) != cudaSuccess) return bail(fail(SD_ERR_INVALID, "bad device %d", c->dev));
     if ((rc = ck(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking), "stream"))) return bail(rc);
     if ((rc = gemv_prepare_device(c->dev))) return bail(rc);

@@ -165,6 +165,9 @@ __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem&
                             int kb0, int nb, int nv, bool norm, bool& ab, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
+        // the image was written by ordinary stores of other CTAs (ordered before us by a grid barrier);
+        // order those with this thread's async-proxy reads
+        asm volatile("fence.proxy.async.global;" ::: "memory");
         const uint32_t bb = (uint32_t)nb * kActStride * 8, cb = (uint32_t)nb * 64, xb = (uint32_t)nb * 32;
         mbar_arrive_expect_tx(R.act_full, bb + cb + xb);
         bulk_g2s(A.b, im.b + (size_t)kb0 * kActStride, bb, R.act_full);

@@ -18,4 +18,6 @@ int gemv_prepare_device(int dev);
 int gemv_plan(GemvArgs& a, int dev, int* grid, size_t* smem);
 int gemv_plan_fixed(GemvArgs& a, int dev, int* grid, size_t* smem);
 int run_gemv(int epi, const GemvArgs& a, int dev, cudaStream_t st, bool pdl);
+// Sum-all-reduce of n fp32 values in place over an NCCL communicator (sd_nccl.cu).
+int nccl_allreduce_sum(void* comm, float* buf, size_t n, cudaStream_t st);
 }  // namespace sd

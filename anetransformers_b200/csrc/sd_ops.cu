@@ -112,7 +112,7 @@ int gemv_prepare_device(int dev) {
 }
 
 int gemv_plan(GemvArgs& a, int dev, int* grid_out, size_t* smem_out) {
-    if (a.K % 1024 != 0 || a.K <= 0) return fail(SD_ERR_INVALID, "matvec: in_dim %d is not a multiple of 1024", a.K);
+    if (a.K % 128 != 0 || a.K <= 0) return fail(SD_ERR_INVALID, "matvec: in_dim %d is not a multiple of 128", a.K);
     if (a.S < 1 || a.S > kMaxS) return fail(SD_ERR_INVALID, "matvec: S=%d outside 1..%d", a.S, kMaxS);
     const int max_smem = device_max_smem(dev);
     const int sms = device_sm_count(dev);

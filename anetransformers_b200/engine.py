@@ -23,6 +23,36 @@ def _i32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
 
 
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """A new NCCL unique id (created by one rank, sent to the others)."""
+    buf = C.create_string_buffer(NCCL_ID_BYTES)
+    _lib.check(_lib.lib().sd_nccl_unique_id(buf), "sd_nccl_unique_id")
+    return buf.raw
+
+
+class NcclComm:
+    """One rank's NCCL communicator for tensor-parallel contexts (pass .handle as nccl_comm)."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int):
+        if len(unique_id) != NCCL_ID_BYTES:
+            raise ValueError("unique id must be %d bytes" % NCCL_ID_BYTES)
+        h = C.c_void_p()
+        _lib.check(_lib.lib().sd_nccl_comm_create(unique_id, nranks, rank, device, C.byref(h)), "sd_nccl_comm_create")
+        self.h = h
+
+    @property
+    def handle(self) -> int:
+        return self.h.value or 0
+
+    def close(self):
+        if getattr(self, "h", None):
+            _lib.lib().sd_nccl_comm_destroy(self.h)
+            self.h = None
+
+
 class Context:
     """A model on one GPU (or one tensor-parallel rank)."""
 

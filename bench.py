@@ -244,6 +244,9 @@ def main():
     ap.add_argument("--workload", default="specdec", choices=["specdec", "gemv"])
     ap.add_argument("--forward-kernel", type=int, default=None, choices=[0, 1],
                     help="1 = one persistent kernel per forward, 0 = one kernel per op (default: library default)")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
+                    help="with --gpus > 1: tp = one stream tensor-parallel over the GPUs (BASELINE config 3), "
+                         "dp = one independent stream per GPU")
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--S", type=int, default=0)
     args = ap.parse_args()
@@ -269,11 +272,21 @@ def main():
             dist.destroy_process_group()
         return
 
-    from anetransformers_b200.engine import Context
+    from anetransformers_b200.engine import Context, NcclComm, nccl_unique_id, NCCL_ID_BYTES
     torch.cuda.set_device(local)
     path = model_path(rank, world, dist)
     peaks = measured_peaks()
-    ctx = Context(path, device=local, max_seq=PROMPT_LEN + args.tokens + 64, forward_kernel=args.forward_kernel)
+    tp = world > 1 and args.parallel == "tp"
+    comm = None
+    if tp:
+        # one NCCL communicator for the model's all-reduces, from an id rank 0 creates
+        uid = torch.zeros(NCCL_ID_BYTES, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = NcclComm(bytes(uid.cpu().numpy().tobytes()), world, rank, local)
+    ctx = Context(path, device=local, max_seq=PROMPT_LEN + args.tokens + 64, forward_kernel=args.forward_kernel,
+                  tp_rank=rank if tp else 0, tp_size=world if tp else 1, nccl_comm=comm.handle if comm else 0)
     prompt = config3_prompt()
     first, _ = ctx.generate(prompt, mode="greedy", max_tokens=1, temp=0.0, rep_penalty=1.0, ignore_eos=True)
     hist = prompt + [first[0]]
@@ -308,7 +321,8 @@ def main():
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         sm = t.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms_max, tokens_all = float(mx[0]), float(sm[1])
+        # tp: every rank emits the same single stream; dp: the streams add up
+        ms_max, tokens_all = float(mx[0]), (float(tokens) if tp else float(sm[1]))
     else:
         ms_max, tokens_all = ms, float(tokens)
     value = tokens_all / (ms_max * 1e-3)
@@ -346,14 +360,15 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int4 -> int32 MMA, fp32 accumulate",
+                "scaling": "strong" if tp else "weak", "vs_baseline": None,
+                "dtype": "int8 x int4 -> int32 MMA, fp32 accumulate",
                 "data": "synthetic: seeded random-init Q4_0 weights of the Mistral-7B-v0.2 architecture, "
                         "seeded random token ids",
                 "config": {"workload": "BASELINE config 3: n-gram spec decode n=3 K=4, temp 0, 1024-token prompt "
                                        "(16 of 6 random 64-token segments), 512 generated tokens per step",
                            "model": "Mistral-7B-v0.2 (32 x 4096, FFN 14336, 32/8 heads, vocab 32000) Q4_0",
-                           "global_batch": world, "seq_len": PROMPT_LEN + args.tokens,
-                           "parallelism": f"dp{world}" if world > 1 else "single GPU",
+                           "global_batch": 1 if tp else world, "seq_len": PROMPT_LEN + args.tokens,
+                           "parallelism": (f"tp{world}" if tp else f"dp{world}") if world > 1 else "single GPU",
                            "l2": "no flush: each forward streams 4.0 GB of weights (> 126 MB L2)"},
                 "per_rank_tok_s": round(per_rank_tps, 2),
                 "acceptance_rate": round(stats["acceptance_rate"], 4) if stats else None,
@@ -362,7 +377,9 @@ def main():
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": int(iters * KERNELS_PER_ITER)}
         print(json.dumps(line), flush=True)
-    ctx.close()
+    ctx.close()  # releases the forward graphs (they hold NCCL calls) before the communicator
+    if comm:
+        comm.close()
     if dist:
         dist.destroy_process_group()
 

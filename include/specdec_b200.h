@@ -142,6 +142,17 @@ typedef struct {
 
 SD_API void sd_ctx_opts_default(sd_ctx_opts *o);
 
+/* Tensor parallelism within one node (one process per GPU): Wq/Wk/Wv/W1/W3 split by output rows,
+ * Wo/W2 by input columns, and a sum all-reduce of the S x dim partial outputs after o-proj and
+ * down-proj.  The reference runs on one device and has no counterpart; these only create the NCCL
+ * communicator that sd_ctx_opts.nccl_comm takes.  NCCL (libnccl.so.2) is loaded at run time.
+ * One rank calls sd_nccl_unique_id and sends the SD_NCCL_ID_BYTES bytes to the others; every rank then
+ * calls sd_nccl_comm_create with its rank and device. */
+#define SD_NCCL_ID_BYTES 128
+SD_API int sd_nccl_unique_id(void *id_out);
+SD_API int sd_nccl_comm_create(const void *id, int nranks, int rank, int device, void **comm_out);
+SD_API void sd_nccl_comm_destroy(void *comm);
+
 /* Replaces metal_context_init (mistral/metal_matvec.h:134-225) + mistral_load
  * (mistral/mistral_model.h:262-357): parses the GGUF v3 image at gguf_base (the mmap'd file, as
  * metal_context_init receives it), uploads every tensor and repacks the Q4_0 matrices in HBM,
