@@ -74,6 +74,8 @@ _SIGS = {
     "sd_nccl_unique_id": (i32, [vp]),
     "sd_nccl_comm_create": (i32, [vp, i32, i32, i32, vp]),
     "sd_nccl_comm_destroy": (None, [vp]),
+    "sd_ctx_tp_handle": (i32, [vp, vp]),
+    "sd_ctx_tp_connect": (i32, [vp, vp, i32]),
     "sd_ctx_create": (i32, [vp, sz, vp, vp]),
     "sd_ctx_create_file": (i32, [C.c_char_p, vp, vp]),
     "sd_ctx_free": (None, [vp]),

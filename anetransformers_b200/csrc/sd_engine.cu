@@ -287,6 +287,11 @@ struct sd_ctx {
     size_t fwd_smem = 0;
     // TP
     void* nccl = nullptr;
+    void* tp_mem = nullptr;                 // exchange region: [2][tp_buf] floats + kMaxTp flags
+    size_t tp_buf = 0;                      // floats per partial-output buffer
+    unsigned long long* tp_base = nullptr;  // reductions completed before the current forward
+    TpXchg tpx{};                           // peers connected: the norm kernels do the all-reduce
+    std::vector<void*> tp_opened;           // peer regions opened through CUDA IPC
 };
 
 namespace {
@@ -478,10 +483,24 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     return SD_OK;
 }
 
+// Output buffer of reduction idx (0-based within a forward) of this rank's o-proj / down-proj: with
+// peers connected, the exchange buffer of the reduction's parity (sequence numbers start at an even base
+// and grow by 2 * n_layers per forward), else the local partial-output buffer.
+float* tp_out(sd_ctx* c, int idx) {
+    if (c->tpx.n > 1) return c->tpx.y[c->tp_rank] + (size_t)((idx + 1) & 1) * c->tp_buf;
+    return c->y;
+}
+
+TpXchg tp_args(sd_ctx* c, int idx) {
+    TpXchg t = c->tpx;
+    t.idx = idx;
+    return t;
+}
+
 // Tensor parallelism: this rank's o-proj / down-proj output is a partial sum over its input columns.
 // Add its K slices into slice 0, then sum slice 0 over the ranks; the norm then adds one slice.
 int tp_reduce(sd_ctx* c, int S, int* yparts) {
-    if (c->tp_size <= 1) return SD_OK;
+    if (c->tp_size <= 1 || c->tpx.n > 1) return SD_OK;  // peer path: the next norm kernel reduces
     const size_t n = (size_t)S * c->dim;
     if (*yparts > 1) CK(launch_sum_parts(c->y, c->y, (int)n, *yparts, (size_t)c->MB * c->dim, c->st), "sum parts");
     *yparts = 1;
@@ -505,6 +524,7 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
     na.w = c->L[0].rms_att;
     na.yparts = 1;
     na.ystride = (size_t)c->MB * c->dim;
+    na.err = c->err;
     CK(launch_norm_quant(0, na, c->st, pdl), "embed");
     const size_t kv_layer = (size_t)c->max_seq * c->kv_rows;
     for (int l = 0; l < n_layers; ++l) {
@@ -551,7 +571,7 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         if ((rc = build_plan(c, po, EPI_STORE, W.wo, c->dim, c->q_rows, kRPW, S, kp_o))) return rc;
         po.a.act = c->act;
         po.a.ctrl = ctrl;
-        po.a.out = c->y;
+        po.a.out = tp_out(c, 2 * l);
         po.a.out_ld = c->dim;
         po.a.part_stride = (size_t)c->MB * c->dim;
         if (po.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "o-proj K split %d too wide", po.a.kparts);
@@ -559,6 +579,7 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         na.w = W.rms_ffn;
         na.yparts = po.a.kparts;
         if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
+        na.tp = tp_args(c, 2 * l);
         CK(launch_norm_quant(1, na, c->st, pdl), "norm");
         // gate/up + SiLU + Q8_0
         Plan pg;
@@ -573,7 +594,7 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         if ((rc = build_plan(c, pd, EPI_STORE, W.w2, c->dim, c->hid_l, kRPW, S, kp_d))) return rc;
         pd.a.act = c->hact;
         pd.a.ctrl = ctrl;
-        pd.a.out = c->y;
+        pd.a.out = tp_out(c, 2 * l + 1);
         pd.a.out_ld = c->dim;
         pd.a.part_stride = (size_t)c->MB * c->dim;
         if (pd.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "down K split %d too wide", pd.a.kparts);
@@ -581,8 +602,10 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
         na.w = (l + 1 < n_layers) ? c->L[l + 1].rms_att : c->rms_final;
         na.yparts = pd.a.kparts;
         if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
+        na.tp = tp_args(c, 2 * l + 1);
         CK(launch_norm_quant(1, na, c->st, pdl), "norm");
     }
+    if (c->tpx.n > 1) CK(launch_tp_advance(c->tp_base, 2 * n_layers, c->st), "tp advance");
     if (!logits_and_argmax) return SD_OK;
     Plan pl;
     int rc = build_plan(c, pl, EPI_STORE, c->lm, c->vocab, c->dim, kRPW, S, 1);
@@ -690,6 +713,9 @@ void sd_ctx_free(sd_ctx* c) {
     cudaFree(c->ctrl); cudaFree(c->dctrl); cudaFree(c->err); cudaFree(c->gs); cudaFree(c->g_out); cudaFree(c->g_hist);
     cudaFree(c->d_layers); cudaFree(c->ssq); cudaFree(c->fsync);
     cudaFree(c->img_mem);
+    for (void* p : c->tp_opened) cudaIpcCloseMemHandle(p);
+    cudaFree(c->tp_mem);
+    cudaFree(c->tp_base);
     if (c->ctrl_h) cudaFreeHost(c->ctrl_h);
     if (c->tok_h) cudaFreeHost(c->tok_h);
     if (c->gs_h) cudaFreeHost(c->gs_h);
@@ -838,6 +864,13 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
         (rc = ck(cudaMallocHost(&c->tok_h, sizeof(int32_t) * 4096), "pinned")) ||
         (rc = ck(cudaMallocHost(&c->gs_h, sizeof(GenState)), "pinned")))
         return bail(rc);
+    if (c->tp_size > 1) {
+        c->tp_buf = (size_t)c->ypart_max * MB * c->dim;
+        const size_t bytes = 2 * c->tp_buf * sizeof(float) + kMaxTp * sizeof(unsigned long long);
+        if ((rc = ck(cudaMalloc(&c->tp_mem, bytes), "cudaMalloc")) || (rc = ck(cudaMemset(c->tp_mem, 0, bytes), "memset")) ||
+            (rc = dalloc(&c->tp_base, 1)) || (rc = ck(cudaMemset(c->tp_base, 0, sizeof(unsigned long long)), "memset")))
+            return bail(rc);
+    }
     if (o.forward_kernel && (rc = setup_fused(c))) return bail(rc);
     if ((rc = ck(cudaDeviceSynchronize(), "context build"))) return bail(rc);
     *out = c;
@@ -889,6 +922,60 @@ int sd_ctx_device_error(sd_ctx* c) {
 }
 
 void* sd_ctx_stream(sd_ctx* c) { return c ? (void*)c->st : nullptr; }
+
+int sd_ctx_tp_handle(sd_ctx* c, void* out) {
+    clear_error();
+    if (!c || !out) return fail(SD_ERR_INVALID, "null argument");
+    if (c->tp_size <= 1 || !c->tp_mem) return fail(SD_ERR_INVALID, "not a tensor-parallel context");
+    cudaSetDevice(c->dev);
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, c->tp_mem), "cudaIpcGetMemHandle");
+    memcpy(out, &h, sizeof(h));
+    return SD_OK;
+}
+
+int sd_ctx_tp_connect(sd_ctx* c, const void* handles, int n) {
+    clear_error();
+    if (!c || !handles) return fail(SD_ERR_INVALID, "null argument");
+    if (c->tp_size <= 1 || n != c->tp_size || n > kMaxTp) return fail(SD_ERR_INVALID, "need %d handles", c->tp_size);
+    if (c->tpx.n > 1) return fail(SD_ERR_INVALID, "peers already connected");
+    cudaSetDevice(c->dev);
+    CK(cudaStreamSynchronize(c->st), "sync");
+    TpXchg t{};
+    t.n = n;
+    t.rank = c->tp_rank;
+    t.base = c->tp_base;
+    t.buf = c->tp_buf;
+    for (int r = 0; r < n; ++r) {
+        void* p = c->tp_mem;
+        if (r != c->tp_rank) {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+            cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                for (void* q : c->tp_opened) cudaIpcCloseMemHandle(q);
+                c->tp_opened.clear();
+                return cuda_fail(e, "cudaIpcOpenMemHandle");
+            }
+            c->tp_opened.push_back(p);
+        }
+        t.y[r] = static_cast<float*>(p);
+        t.flags[r] = reinterpret_cast<unsigned long long*>(static_cast<float*>(p) + 2 * c->tp_buf);
+    }
+    c->tpx = t;
+    // forwards captured for the NCCL path are rebuilt on next use
+    for (auto& g : c->fwd_graph)
+        if (g) {
+            cudaGraphExecDestroy(g);
+            g = nullptr;
+        }
+    if (c->iter_graph) {
+        cudaGraphExecDestroy(c->iter_graph);
+        c->iter_graph = nullptr;
+        for (int& k : c->iter_key) k = -1;
+    }
+    return SD_OK;
+}
 
 int sd_forward_dev(sd_ctx* c, const int32_t* tokens_dev, int S, int pos, float* logits_dev, int32_t* argmax_dev, void* stream) {
     clear_error();

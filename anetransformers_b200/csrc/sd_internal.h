@@ -117,6 +117,19 @@ cudaError_t launch_blocks_to_q8(const void* blocks, Q8Planes out, int S, int n, 
 
 // Residual add + RMSNorm + Q8_0 quantisation of S tokens (one CTA per token).
 //   mode 0: x = embed(tokens) (Q4_0 rows of tok_embd) ; 1: x += y ; 2: x unchanged
+// Tensor-parallel exchange over peer memory (CUDA IPC): every rank's o-proj / down-proj partial outputs
+// live in its own double-buffered region that the other ranks read over NVLink; flags[src] in each
+// rank's region holds the last reduction sequence number rank src has published.
+constexpr int kMaxTp = 8;
+struct TpXchg {
+    int n = 0, rank = 0;                       // n = 0: off
+    float* y[kMaxTp] = {};                     // each rank's buffers: [2][buf] floats
+    unsigned long long* flags[kMaxTp] = {};    // each rank's flags[kMaxTp]
+    const unsigned long long* base = nullptr;  // reductions done before this forward (this rank)
+    size_t buf = 0;                            // floats per buffer
+    int idx = 0;                               // this reduction's index within the forward
+};
+
 struct NormArgs {
     float* x;             // [S][dim] residual stream
     const float* y;       // [S][dim] to add (mode 1)
@@ -130,7 +143,10 @@ struct NormArgs {
     float* xn_out;        // optional: normalised fp32 output [S][dim]
     int yparts;           // mode 1: y holds yparts partial slices summed in order (K-split matvec)
     size_t ystride;       // floats between slices
+    TpXchg tp;            // mode 1 with tp.n > 1: y of every rank (read over NVLink), summed in rank order
+    int* err;             // device error word (a peer wait that runs out)
 };
+cudaError_t launch_tp_advance(unsigned long long* base, int n, cudaStream_t st);
 cudaError_t launch_norm_quant(int mode, const NormArgs& a, cudaStream_t st, bool pdl);
 
 }  // namespace sd

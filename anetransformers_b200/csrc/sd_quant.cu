@@ -126,13 +126,56 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
         float yv[kNormMaxBPW];
 #pragma unroll
         for (int k = 0; k < kNormMaxBPW; ++k) yv[k] = 0.f;
-        // partial slices summed in slice order (K-split matvec outputs)
+        if (a.tp.n > 1) {
+            // tensor parallel: every rank's partial outputs of this reduction, in rank order then slice
+            // order, read from the ranks' own memory once their flags show this sequence number
+            const unsigned long long seq = *a.tp.base + a.tp.idx + 1;
+            if (tok == 0 && threadIdx.x < a.tp.n) {
+                // this rank's slice is complete (previous kernel, stream order): publish it to every rank
+                __threadfence_system();
+                asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.tp.flags[threadIdx.x] + a.tp.rank), "l"(seq)
+                             : "memory");
+            }
+            if (threadIdx.x == 0) {
+                bool ok = true;
+                const uint64_t t0 = global_ns();
+                for (int r = 0; r < a.tp.n && ok; ++r) {
+                    const unsigned long long* f = a.tp.flags[a.tp.rank] + r;
+                    unsigned long long v;
+                    while (true) {
+                        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+                        if (v >= seq) break;
+                        if (global_ns() - t0 > kWaitLimitNs) {
+                            set_dev_error(a.err, DEV_ERR_PEER_WAIT);
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            const size_t boff = (size_t)(seq & 1) * a.tp.buf;
+            for (int r = 0; r < a.tp.n; ++r) {
 #pragma unroll
-        for (int p = 0; p < kNormMaxParts; ++p) {
-            if (p < a.yparts) {
+                for (int p = 0; p < kNormMaxParts; ++p) {
+                    if (p < a.yparts) {
 #pragma unroll
-                for (int k = 0; k < kNormMaxBPW; ++k)
-                    if (k < bpw) yv[k] += a.y[(size_t)p * a.ystride + (size_t)tok * a.dim + (warp + kNormWarps * k) * 32 + lane];
+                        for (int k = 0; k < kNormMaxBPW; ++k)
+                            if (k < bpw)
+                                yv[k] += __ldcg(a.tp.y[r] + boff + (size_t)p * a.ystride + (size_t)tok * a.dim +
+                                                (warp + kNormWarps * k) * 32 + lane);
+                    }
+                }
+            }
+        } else {
+            // partial slices summed in slice order (K-split matvec outputs)
+#pragma unroll
+            for (int p = 0; p < kNormMaxParts; ++p) {
+                if (p < a.yparts) {
+#pragma unroll
+                    for (int k = 0; k < kNormMaxBPW; ++k)
+                        if (k < bpw) yv[k] += a.y[(size_t)p * a.ystride + (size_t)tok * a.dim + (warp + kNormWarps * k) * 32 + lane];
+                }
             }
         }
 #pragma unroll
@@ -174,6 +217,13 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
             a.out.sum[(size_t)tok * nb + b] = sum;
         }
     }
+}
+
+__global__ void k_tp_advance(unsigned long long* base, int n) { *base += (unsigned long long)n; }
+
+cudaError_t launch_tp_advance(unsigned long long* base, int n, cudaStream_t st) {
+    k_tp_advance<<<1, 1, 0, st>>>(base, n);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_norm_quant(int mode, const NormArgs& a, cudaStream_t st, bool pdl) {

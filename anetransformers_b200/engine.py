@@ -82,6 +82,19 @@ class Context:
         self.vocab = info.vocab_size
         self.max_batch = max_batch if 0 < max_batch <= 8 else 8
 
+    # -- tensor parallel over peer memory -------------------------------------------------------------
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-region handle (CUDA IPC), to be sent to the other ranks."""
+        buf = C.create_string_buffer(64)
+        _lib.check(_lib.lib().sd_ctx_tp_handle(self.h, buf), "sd_ctx_tp_handle")
+        return buf.raw
+
+    def tp_connect(self, handles: Sequence[bytes]):
+        """Connect to every rank's exchange region (handles in rank order); the all-reduces then run
+        inside the norm kernels over NVLink instead of NCCL."""
+        blob = b"".join(handles)
+        _lib.check(_lib.lib().sd_ctx_tp_connect(self.h, blob, len(handles)), "sd_ctx_tp_connect")
+
     # -- lifetime --------------------------------------------------------------------------------
     def close(self):
         if getattr(self, "h", None):

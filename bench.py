@@ -247,6 +247,8 @@ def main():
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="with --gpus > 1: tp = one stream tensor-parallel over the GPUs (BASELINE config 3), "
                          "dp = one independent stream per GPU")
+    ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
+                    help="tp: all-reduce inside the norm kernels over peer memory, or by NCCL")
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--S", type=int, default=0)
     args = ap.parse_args()
@@ -287,6 +289,11 @@ def main():
         comm = NcclComm(bytes(uid.cpu().numpy().tobytes()), world, rank, local)
     ctx = Context(path, device=local, max_seq=PROMPT_LEN + args.tokens + 64, forward_kernel=args.forward_kernel,
                   tp_rank=rank if tp else 0, tp_size=world if tp else 1, nccl_comm=comm.handle if comm else 0)
+    if tp and args.tp_allreduce == "peer":
+        # all-reduces inside the norm kernels over NVLink (peer memory) instead of NCCL
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.tp_handle())
+        ctx.tp_connect(handles)
     prompt = config3_prompt()
     first, _ = ctx.generate(prompt, mode="greedy", max_tokens=1, temp=0.0, rep_penalty=1.0, ignore_eos=True)
     hist = prompt + [first[0]]
@@ -368,7 +375,8 @@ def main():
                                        "(16 of 6 random 64-token segments), 512 generated tokens per step",
                            "model": "Mistral-7B-v0.2 (32 x 4096, FFN 14336, 32/8 heads, vocab 32000) Q4_0",
                            "global_batch": 1 if tp else world, "seq_len": PROMPT_LEN + args.tokens,
-                           "parallelism": (f"tp{world}" if tp else f"dp{world}") if world > 1 else "single GPU",
+                           "parallelism": ((f"tp{world} ({args.tp_allreduce} all-reduce)" if tp else f"dp{world}")
+                                           if world > 1 else "single GPU"),
                            "l2": "no flush: each forward streams 4.0 GB of weights (> 126 MB L2)"},
                 "per_rank_tok_s": round(per_rank_tps, 2),
                 "acceptance_rate": round(stats["acceptance_rate"], 4) if stats else None,

@@ -152,6 +152,14 @@ SD_API void sd_ctx_opts_default(sd_ctx_opts *o);
 SD_API int sd_nccl_unique_id(void *id_out);
 SD_API int sd_nccl_comm_create(const void *id, int nranks, int rank, int device, void **comm_out);
 SD_API void sd_nccl_comm_destroy(void *comm);
+/* The same reduction without NCCL: each rank's o-proj / down-proj partial outputs stay in its own HBM
+ * and the following RMSNorm kernel of every rank reads all ranks' partials over NVLink (peer memory,
+ * CUDA IPC), adding them in rank order, after a flag handshake with bounded waits.  Every rank exports
+ * its SD_TP_HANDLE_BYTES handle, the handles are exchanged by the caller, and every rank connects
+ * with all of them in rank order; from then on no NCCL call is made.  No reference counterpart. */
+#define SD_TP_HANDLE_BYTES 64
+SD_API int sd_ctx_tp_handle(sd_ctx *ctx, void *handle_out);
+SD_API int sd_ctx_tp_connect(sd_ctx *ctx, const void *handles, int n_ranks);
 
 /* Replaces metal_context_init (mistral/metal_matvec.h:134-225) + mistral_load
  * (mistral/mistral_model.h:262-357): parses the GGUF v3 image at gguf_base (the mmap'd file, as

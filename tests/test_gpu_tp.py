@@ -1,5 +1,6 @@
-"""Tensor parallelism (Wq/Wk/Wv/W1/W3 by rows, Wo/W2 by columns, NCCL all-reduce after o-proj and
-down-proj) against the single-GPU context on the MINI model: both ranks agree bit for bit, logits stay
+"""Tensor parallelism (Wq/Wk/Wv/W1/W3 by rows, Wo/W2 by columns, an all-reduce after o-proj and
+down-proj -- by NCCL, or inside the norm kernels over peer memory) against the single-GPU context on the
+MINI model: both ranks agree bit for bit, logits stay
 within the 1e-2 relative bar (only the fp32 partial-sum order differs), and greedy tokens match up to a
 near-tie of the single-GPU logits.  Needs two GPUs; each rank is its own process, as in deployment.
 """
@@ -34,7 +35,7 @@ def _tokens():
     return rng.integers(3, 2048, 12).tolist()
 
 
-def _worker(rank, world, path, port, q):
+def _worker(rank, world, path, port, q, mode):
     import torch
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -47,6 +48,11 @@ def _worker(rank, world, path, port, q):
         dist.broadcast_object_list(obj, 0)
         comm = NcclComm(obj[0], world, rank, rank)
         ctx = Context(path, device=rank, max_seq=256, tp_rank=rank, tp_size=world, nccl_comm=comm.handle)
+        if mode == "peer":
+            # all-reduce inside the norm kernels over NVLink instead of NCCL
+            handles = [None] * world
+            dist.all_gather_object(handles, ctx.tp_handle())
+            ctx.tp_connect(handles)
         toks = _tokens()
         ctx.prefill(toks[:7], 0)
         lg, _ = ctx.forward(toks[7:], 7)
@@ -69,7 +75,8 @@ def mini(tmp_path_factory):
 
 
 @pytest.mark.skipif(gpu_available() and _n_gpus() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu(mini):
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_tp2_matches_single_gpu(mini, mode):
     import multiprocessing as mp
     from anetransformers_b200.engine import Context
 
@@ -82,7 +89,7 @@ def test_tp2_matches_single_gpu(mini):
     ctxm = mp.get_context("spawn")
     q = ctxm.Queue()
     port = _free_port()
-    procs = [ctxm.Process(target=_worker, args=(r, 2, mini, port, q), daemon=True) for r in range(2)]
+    procs = [ctxm.Process(target=_worker, args=(r, 2, mini, port, q, mode), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
