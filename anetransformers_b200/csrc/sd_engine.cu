@@ -388,7 +388,7 @@ bool fwd_phase(MvPhase& p, int rows, int K, int rpu, int kparts) {
 int setup_fused(sd_ctx* c) {
     int coop = 0;
     CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->dev), "device attribute");
-    if (!coop || c->tp_size != 1) return SD_OK;
+    if (!coop) return SD_OK;
     int kp_o = 0, kp_d = 0, rc;
     if ((rc = fixed_kparts(c, c->dim, c->q_rows, &kp_o)) || (rc = fixed_kparts(c, c->dim, c->hid_l, &kp_d))) return rc;
     if (kp_o > c->ypart_max || kp_d > c->ypart_max) return SD_OK;
@@ -477,8 +477,10 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     a.tokens = nullptr;
     a.ctrl = ctrl;
     a.err = c->err;
+    a.tp = c->tpx;
     CK(cudaMemsetAsync(c->fsync, 0, fwd_sync_words(c->dim) * sizeof(unsigned), c->st), "memset");
     CK(launch_forward(a, c->fwd_grid, c->fwd_smem, c->st), "forward launch");
+    if (c->tpx.n > 1) CK(launch_tp_advance(c->tp_base, 2 * n_layers, c->st), "tp advance");
     if (logits_and_argmax) CK(launch_argmax(c->logits, c->vocab, S, c->argmax, ctrl, c->st, false), "argmax");
     return SD_OK;
 }
@@ -510,7 +512,8 @@ int tp_reduce(sd_ctx* c, int S, int* yparts) {
 // Enqueue one forward of S (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the
 // position, the tokens and how many of the S are valid.
 int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
-    if (c->fused) return enqueue_forward_fused(c, S, n_layers, k, v, ctrl, logits_and_argmax);
+    // tensor parallel contexts use the persistent kernel once their peers are connected
+    if (c->fused && (c->tp_size == 1 || c->tpx.n > 1)) return enqueue_forward_fused(c, S, n_layers, k, v, ctrl, logits_and_argmax);
     const bool pdl = c->use_pdl;
     NormArgs na{};
     na.x = c->x;
@@ -905,7 +908,7 @@ int sd_ctx_info(const sd_ctx* c, sd_model_info* o) {
     o->n_kv_heads = c->n_kv; o->head_dim = c->hd; o->vocab_size = c->vocab; o->max_seq = c->max_seq;
     o->rope_theta = c->theta; o->rms_eps = c->eps; o->bos_id = c->bos; o->eos_id = c->eos;
     o->tp_rank = c->tp_rank; o->tp_size = c->tp_size; o->weight_bytes = c->weight_bytes; o->kv_bytes = c->kv_bytes;
-    o->forward_kernel = c->fused ? 1 : 0;
+    o->forward_kernel = (c->fused && (c->tp_size == 1 || c->tpx.n > 1)) ? 1 : 0;
     return SD_OK;
 }
 

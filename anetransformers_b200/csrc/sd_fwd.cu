@@ -238,18 +238,23 @@ __device__ __forceinline__ void finish_block(const FwdArgs& a, int s, int b, flo
 
 // Residual update of one (token, block): x += the matvec's slice outputs, added in slice order as the
 // per-op norm kernel adds them.
-__device__ void red_block(const FwdArgs& a, int s, int b, int kparts, const float* wn, int lane) {
+// With tensor parallelism the slices of every rank are added, rank by rank (each rank's own memory, read
+// over NVLink), as the per-op norm kernel adds them.
+__device__ void red_block(const FwdArgs& a, const float* const* ysrc, int nsrc, int s, int b, int kparts, const float* wn,
+                          int lane) {
     const int row = b * 32 + lane;
-    float xv = a.x[(size_t)s * a.dim + row];
-    float yv[kMaxParts];
-#pragma unroll
-    for (int p = 0; p < kMaxParts; ++p)
-        yv[p] = p < kparts ? a.yparts[(size_t)p * a.ypart_stride + (size_t)s * a.dim + row] : 0.f;
+    const float xv = a.x[(size_t)s * a.dim + row];
     const float w = wn[row];
     float t = 0.f;
+    for (int r = 0; r < nsrc; ++r) {
+        float yv[kMaxParts];
 #pragma unroll
-    for (int p = 0; p < kMaxParts; ++p)
-        if (p < kparts) t += yv[p];
+        for (int p = 0; p < kMaxParts; ++p)
+            yv[p] = p < kparts ? __ldcg(ysrc[r] + (size_t)p * a.ypart_stride + (size_t)s * a.dim + row) : 0.f;
+#pragma unroll
+        for (int p = 0; p < kMaxParts; ++p)
+            if (p < kparts) t += yv[p];
+    }
     finish_block(a, s, b, xv + t, w, lane);
 }
 
@@ -371,7 +376,7 @@ __device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, 
                     if (!ab) epi_silu_q8(R.ubuf, r, lane, unit, nv, a.h, a.hidden, &a.h_img);
                     named_sync(kBarEpi, kEpiWarps * 32);
                 }
-            } else if (kind == PH_WO && p.kparts == 1) {
+            } else if (kind == PH_WO && p.kparts == 1 && a.tp.n <= 1) {
                 // the pair is one 32-row block (unit): finish it here for every token, warp r taking
                 // tokens r, r + 2, ... (lane = row); x and the norm weight are loaded up front
 #pragma unroll
@@ -403,7 +408,9 @@ __device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, 
                         a.q_scale);
             } else {
                 // WO / W2: this slice's outputs (the residual add runs in the following phase); LM: logits
-                float* out = kind == PH_LM ? a.logits : a.yparts + (size_t)part * a.ypart_stride;
+                float* ybase = a.yparts;
+                if (a.tp.n > 1) ybase = a.tp.y[a.tp.rank] + (size_t)(((2 * layer + (kind == PH_W2)) + 1) & 1) * a.tp.buf;
+                float* out = kind == PH_LM ? a.logits : ybase + (size_t)part * a.ypart_stride;
                 const int ld = kind == PH_LM ? a.vocab : a.dim;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -445,11 +452,45 @@ __device__ __forceinline__ void combine_phase(const FwdArgs& a, int l, uint8_t* 
                          [bar_id] { named_sync(bar_id, kCombineWarps * 32); });
 }
 
-__device__ __forceinline__ void red_phase(const FwdArgs& a, int kparts, const float* wn, int nv, int tid) {
+// idx: the reduction's index in the forward (2 per layer).  Tensor parallel: after the grid barrier this
+// rank's slices are complete; CTA 0 publishes the reduction's sequence number to every rank's flags, and
+// every CTA waits (bounded) until all ranks have published before reading their slices.
+__device__ __forceinline__ void red_phase(const FwdArgs& a, Misc* m, int idx, unsigned long long seq0, int kparts,
+                                          const float* wn, int nv, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     const int nbd = a.dim >> 5;
+    const float* src[kMaxTp];
+    int nsrc = 1;
+    src[0] = a.yparts;
+    if (a.tp.n > 1) {
+        const unsigned long long seq = seq0 + idx + 1;
+        const size_t boff = (size_t)(seq & 1) * a.tp.buf;
+        nsrc = a.tp.n;
+        for (int r = 0; r < kMaxTp; ++r) src[r] = r < nsrc ? a.tp.y[r] + boff : nullptr;
+        if (blockIdx.x == 0 && tid < a.tp.n) {
+            __threadfence_system();
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.tp.flags[tid] + a.tp.rank), "l"(seq) : "memory");
+        }
+        if (tid == 0 && !m->abort) {
+            const uint64_t t0 = global_ns();
+            for (int r = 0; r < a.tp.n; ++r) {
+                const unsigned long long* fl = a.tp.flags[a.tp.rank] + r;
+                unsigned long long v;
+                while (true) {
+                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(fl) : "memory");
+                    if (v >= seq) break;
+                    if (global_ns() - t0 > kWaitLimitNs) {
+                        set_dev_error(a.err, DEV_ERR_PEER_WAIT);
+                        m->abort = 1;
+                        break;
+                    }
+                }
+            }
+        }
+        named_sync(kBarCompute, kComputeThreads);
+    }
     for (int wt = blockIdx.x * kComputeWarps + warp; wt < nv * nbd; wt += gridDim.x * kComputeWarps)
-        red_block(a, wt / nbd, wt % nbd, kparts, wn, lane);
+        red_block(a, src, nsrc, wt / nbd, wt % nbd, kparts, wn, lane);
 }
 
 // embedding: x rows, their 16-row sums of squares and Q8_0 of x * (layer 0 attention norm weight); one
@@ -569,23 +610,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
     grid_barrier(a, m, target);
     uint8_t* uni = smem + L.act;
     const int n_ph = 8 * a.n_layers + (a.lm ? 1 : 0);
+    // the o-proj epilogue finishes the residual itself when its sums are complete locally
+    const bool wo_fused = a.wo.kparts == 1 && a.tp.n <= 1;
+    // reductions done before this forward (tensor parallel; read before any CTA can advance it)
+    const unsigned long long seq0 = a.tp.n > 1 ? *a.tp.base : 0ull;
     for (int ph = 0; ph < n_ph; ++ph) {
         const int l = ph >> 3, k = ph & 7;
         if (k == 1 && l < a.n_layers) {
             attention_phase(a, l, uni, nv, pos, tid);
         } else if (k == 2) {
             combine_phase(a, l, uni, nv, pos, tid);
-        } else if (k == 4 && a.wo.kparts == 1) {
+        } else if (k == 4 && wo_fused) {
             // done by the o-proj epilogue
         } else if (k == 4 || k == 7) {
             const int kp = k == 4 ? a.wo.kparts : a.w2.kparts;
             const float* wn = k == 4 ? a.layers[l].rms_ffn : l + 1 < a.n_layers ? a.layers[l + 1].rms_att : a.rms_out;
-            red_phase(a, kp, wn, nv, tid);
+            red_phase(a, m, 2 * l + (k == 7), seq0, kp, wn, nv, tid);
         } else {
             const int kind = l == a.n_layers ? PH_LM : k == 0 ? PH_QKV : k == 3 ? PH_WO : k == 5 ? PH_W13 : PH_W2;
             mv_phase(a, kind, l, R, m, rp, pidx, nstg, ab, nv, pos, tid);
         }
-        if (ph + 1 < n_ph && !(k == 3 && a.wo.kparts == 1 && l < a.n_layers)) grid_barrier(a, m, target);
+        // no barrier after the o-proj when it finished the residual itself
+        if (ph + 1 < n_ph && !(k == 3 && wo_fused && l < a.n_layers)) grid_barrier(a, m, target);
     }
 
     // Drain: no bulk copy may still be landing in shared memory when the CTA exits.  Only the last

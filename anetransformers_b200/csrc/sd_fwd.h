@@ -51,6 +51,7 @@ struct FwdArgs {
     const int* tokens;          // token ids (null: ctrl->tokens)
     const DevCtrl* ctrl;        // pos / n_valid / done (null: pos = 0, all S valid)
     int* err;
+    TpXchg tp;                  // tensor parallel over peer memory (tp.n = 0: single GPU)
 };
 
 constexpr int kFwdAttnGroups = 2;  // 128-thread attention groups per CTA

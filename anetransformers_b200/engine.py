@@ -94,6 +94,9 @@ class Context:
         inside the norm kernels over NVLink instead of NCCL."""
         blob = b"".join(handles)
         _lib.check(_lib.lib().sd_ctx_tp_connect(self.h, blob, len(handles)), "sd_ctx_tp_connect")
+        info = _lib.ModelInfo()
+        _lib.check(_lib.lib().sd_ctx_info(self.h, C.byref(info)), "sd_ctx_info")
+        self.info = info  # forward_kernel may change once the peers are connected
 
     # -- lifetime --------------------------------------------------------------------------------
     def close(self):

@@ -244,9 +244,9 @@ def main():
     ap.add_argument("--workload", default="specdec", choices=["specdec", "gemv"])
     ap.add_argument("--forward-kernel", type=int, default=None, choices=[0, 1],
                     help="1 = one persistent kernel per forward, 0 = one kernel per op (default: library default)")
-    ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
-                    help="with --gpus > 1: tp = one stream tensor-parallel over the GPUs (BASELINE config 3), "
-                         "dp = one independent stream per GPU")
+    ap.add_argument("--parallel", default="dp", choices=["tp", "dp"],
+                    help="with --gpus > 1: dp = one independent stream per GPU (aggregate tok/s, weak scaling), "
+                         "tp = one stream tensor-parallel over the GPUs (BASELINE config 3's layout, strong scaling)")
     ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
                     help="tp: all-reduce inside the norm kernels over peer memory, or by NCCL")
     ap.add_argument("--shape", default="4096x4096")

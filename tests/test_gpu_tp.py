@@ -116,3 +116,60 @@ def test_tp2_matches_single_gpu(mini, mode):
         s = np.sort(lg[0])
         assert s[-1] - s[-2] <= 1e-3 * np.max(np.abs(lg[0])), (i, out0, out_ref)
     ref.close()
+
+
+def _worker_both(rank, world, path, port, q):
+    """Per rank: the persistent-kernel forward and the per-op forward, both tensor parallel over peer
+    memory, on the same inputs."""
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.cuda.set_device(rank)
+        from anetransformers_b200.engine import Context, NcclComm, nccl_unique_id
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, 0)
+        comm = NcclComm(obj[0], world, rank, rank)
+        res = []
+        for fk in (1, 0):
+            ctx = Context(path, device=rank, max_seq=256, tp_rank=rank, tp_size=world, nccl_comm=comm.handle,
+                          forward_kernel=fk)
+            handles = [None] * world
+            dist.all_gather_object(handles, ctx.tp_handle())
+            ctx.tp_connect(handles)
+            toks = _tokens()
+            ctx.prefill(toks[:7], 0)
+            lg, _ = ctx.forward(toks[7:], 7)
+            res.append((ctx.info.forward_kernel, lg))
+            ctx.close()
+        q.put((rank, res, None))
+        comm.close()
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(gpu_available() and _n_gpus() < 2, reason="needs 2 GPUs")
+def test_tp2_persistent_forward_equals_per_op(mini):
+    import multiprocessing as mp
+    ctxm = mp.get_context("spawn")
+    q = ctxm.Queue()
+    port = _free_port()
+    procs = [ctxm.Process(target=_worker_both, args=(r, 2, mini, port, q), daemon=True) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(2):
+        rank, res, err = q.get(timeout=300)
+        assert err is None, err
+        out[rank] = res
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        (fk1, lg1), (fk0, lg0) = out[r]
+        assert fk1 == 1 and fk0 == 0
+        np.testing.assert_array_equal(lg1.view(np.uint32), lg0.view(np.uint32))
+    np.testing.assert_array_equal(out[0][0][1].view(np.uint32), out[1][0][1].view(np.uint32))
