@@ -695,7 +695,7 @@ void sd_ctx_opts_default(sd_ctx_opts* o) {
     o->tp_size = 1;
     o->use_graphs = 1;
     o->use_pdl = 1;
-    o->forward_kernel = 0;
+    o->forward_kernel = 1;
 }
 
 void sd_ctx_free(sd_ctx* c) {

@@ -33,7 +33,16 @@ sys.path.insert(0, ROOT)
 METRIC = "Mistral-7B Q4_0 spec-decode tok/s @1/2/4/8 B200; W4A8 GEMV HBM GB/s"
 UNIT = "tok/s"
 PROMPT_LEN, GEN_TOKENS, NGRAM_N, SPEC_K = 1024, 512, 3, 4
-KERNELS_PER_ITER = 2 + 1 + 8 * 32 + 2     # prepare + commit, embed-norm, 8 per layer, LM head + argmax
+def kernels_per_iter(persistent: bool, tp_peer: bool = False, tp_nccl: bool = False, layers: int = 32) -> int:
+    """Our kernel launches per n-gram decode iteration: prepare + commit around one verify forward, which
+    is k_forward + argmax on the persistent path, or embed-norm, 8 per layer, LM head + argmax per op.
+    Tensor parallel adds the sequence-advance kernel (peer path) or the NCCL all-reduces."""
+    n = 2 + (2 if persistent else 1 + 8 * layers + 2)
+    if tp_peer:
+        n += 1
+    if tp_nccl:
+        n += 2 * layers
+    return n
 BYTES_PER_FORWARD = 32 * 122_683_392 + 73_728_000   # Q4_0 weights streamed per forward (3.9996 GB)
 KV_BYTES_PER_POS = 32 * 2 * 1024 * 2                # fp16 K+V of one position, all layers
 
@@ -383,7 +392,8 @@ def main():
                 "tokens_per_iteration": round(tokens / max(iters, 1), 3),
                 "step_roofline": step_roof,
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-                "gpu_launches": int(iters * KERNELS_PER_ITER)}
+                "gpu_launches": int(iters * kernels_per_iter(bool(ctx.info.forward_kernel), tp and args.tp_allreduce == "peer",
+                                                             tp and args.tp_allreduce == "nccl"))}
         print(json.dumps(line), flush=True)
     ctx.close()  # releases the forward graphs (they hold NCCL calls) before the communicator
     if comm:

@@ -136,8 +136,9 @@ typedef struct {
     void *nccl_comm;      /* ncclComm_t for tp_size > 1, created by the caller */
     int use_graphs;       /* capture per-S forwards in CUDA graphs (default 1) */
     int use_pdl;          /* programmatic dependent launch between kernels (default 1) */
-    int forward_kernel;   /* 1 = each forward is one persistent kernel (single GPU),
-                             0 = one kernel per op (default); both give bit-identical logits */
+    int forward_kernel;   /* 1 = each forward is one persistent kernel (default; tensor-parallel contexts
+                             once their peers are connected), 0 = one kernel per op; both give
+                             bit-identical logits */
 } sd_ctx_opts;
 
 SD_API void sd_ctx_opts_default(sd_ctx_opts *o);
