@@ -45,7 +45,8 @@ class GenParams(C.Structure):
     _fields_ = [("mode", C.c_int), ("max_tokens", C.c_int), ("temp", C.c_float), ("top_p", C.c_float),
                 ("top_k", C.c_int), ("rep_penalty", C.c_float), ("rep_window", C.c_int), ("ignore_eos", C.c_int),
                 ("spec_k", C.c_int), ("ngram_n", C.c_int), ("draft_layers", C.c_int),
-                ("history_has_current", C.c_int), ("bonus_mode", C.c_int), ("seed", C.c_uint64)]
+                ("history_has_current", C.c_int), ("bonus_mode", C.c_int), ("seed", C.c_uint64),
+                ("reuse_draft_kv", C.c_int)]
 
 
 class GenStats(C.Structure):

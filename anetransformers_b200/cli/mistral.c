@@ -29,7 +29,7 @@ static void usage(const char *argv0) {
     fprintf(stderr, "       [--context N] [--speculative] [--spec-k K] [--spec-layers N] [--metal]\n");
     fprintf(stderr, "       [--draft ngram|self] [--ngram-n N] [--ignore-eos] [--seed S] [--device D]\n");
     fprintf(stderr, "  --speculative    speculative decode (self-speculative; n-gram with --metal or --draft ngram)\n");
-    fprintf(stderr, "  --spec-k K       drafts per iteration (default 4, max 7)\n");
+    fprintf(stderr, "  --spec-k K       drafts per iteration (default 4, max 15)\n");
     fprintf(stderr, "  --spec-layers N  self-speculative draft depth (default 8)\n");
 }
 

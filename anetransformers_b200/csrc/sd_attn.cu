@@ -29,15 +29,17 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const AttnArgs a)
     const int c_first = lo_min / a.chunk, c_last = hi_max / a.chunk;
     const int n_items = (c_last - c_first + 1) * a.n_kvh;
     const AttnSmem sm = attn_smem_at(smem);
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x)
-        attn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, threadIdx.x,
-                  [] { __syncthreads(); });
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int nx = item + gridDim.x;  // this CTA's next item, prefetched into L2 during this one
+        attn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, nx % a.n_kvh,
+                  nx < n_items ? c_first + nx / a.n_kvh : -1, sm, threadIdx.x, [] { __syncthreads(); });
+    }
 }
 
 // Merge chunk partials and quantise each head's 128 outputs to 4 Q8_0 blocks: one CTA of
-// kCombineWarps warps per (token, head).
-__global__ void __launch_bounds__(kCombineWarps * 32) k_attn_combine(const AttnArgs a) {
-    __shared__ __align__(16) float obuf[kCombineWarps * kHD];
+// combine_warps(max_seq) warps per (token, head).
+__global__ void __launch_bounds__(kCombineWarpsMax * 32) k_attn_combine(const AttnArgs a) {
+    __shared__ __align__(16) float obuf[kCombineWarpsMax * kHD];
     if (a.ctrl && a.ctrl->done) return;
     pdl_trigger();
     pdl_wait();
@@ -45,8 +47,8 @@ __global__ void __launch_bounds__(kCombineWarps * 32) k_attn_combine(const AttnA
     const int pos = a.ctrl ? a.ctrl->pos : a.pos;
     const int row = blockIdx.x;
     if (row >= nv * a.n_heads) return;
-    attn_combine_row(a, pos, row / a.n_heads, row % a.n_heads, threadIdx.x >> 5, threadIdx.x & 31, obuf,
-                     [] { __syncthreads(); });
+    attn_combine_row(a, blockDim.x >> 5, pos, row / a.n_heads, row % a.n_heads, threadIdx.x >> 5, threadIdx.x & 31,
+                     obuf, [] { __syncthreads(); });
 }
 
 static void fill_cfg(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* at, dim3 grid, dim3 block, cudaStream_t st, bool pdl) {
@@ -66,7 +68,7 @@ cudaError_t launch_attention(const AttnArgs& a, int grid_partial, cudaStream_t s
     fill_cfg(cfg, at, dim3(grid_partial), dim3(kAttnThreads), st, pdl);
     cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_partial, a);
     if (e != cudaSuccess) return e;
-    fill_cfg(cfg, at, dim3(a.S * a.n_heads), dim3(kCombineWarps * 32), st, pdl);
+    fill_cfg(cfg, at, dim3(a.S * a.n_heads), dim3(combine_warps(a.max_seq) * 32), st, pdl);
     return cudaLaunchKernelEx(&cfg, k_attn_combine, a);
 }
 

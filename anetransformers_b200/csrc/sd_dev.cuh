@@ -409,15 +409,14 @@ constexpr int kGQA = 4;         // query heads per kv head
 constexpr int kSub = 32;        // positions per sub-block
 constexpr int kAttnThreads = 256;
 constexpr int kQRows = kMaxS * kGQA;  // 32
-constexpr int kQStride = kHD + 8;     // halves per Q / K row (bank-conflict-free fragment loads)
-constexpr int kVStride = kSub + 8;    // halves per transposed V row
+constexpr int kQStride = kHD + 8;     // halves per Q / K / V row (conflict-free ldmatrix rows)
 constexpr int kSStride = kSub + 4;    // floats per score row
 
 struct AttnSmem {
     __half* qh;     // [kQRows][kQStride] high part of q
     __half* ql;     // [kQRows][kQStride] low part
     __half* kk;     // [kSub][kQStride]  K sub-block (position-major)
-    __half* vt;     // [kHD][kVStride]   V sub-block transposed (dim-major)
+    __half* vv;     // [kSub][kQStride]  V sub-block (position-major; fragments by ldmatrix.trans)
     float* st;      // [kQRows][kSStride] scores, then probabilities
     float* rm;      // [kQRows] running max
     float* rl;      // [kQRows] running sum
@@ -425,8 +424,8 @@ struct AttnSmem {
 };
 
 __host__ __device__ constexpr size_t attn_smem_bytes() {
-    return (size_t)2 * kQRows * kQStride * 2 + (size_t)kSub * kQStride * 2 + (size_t)kHD * kVStride * 2 +
-           (size_t)kQRows * kSStride * 4 + (size_t)3 * kQRows * 4;
+    return (size_t)2 * kQRows * kQStride * 2 + (size_t)2 * kSub * kQStride * 2 + (size_t)kQRows * kSStride * 4 +
+           (size_t)3 * kQRows * 4;
 }
 
 __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
@@ -434,8 +433,8 @@ __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
     s.qh = reinterpret_cast<__half*>(base);
     s.ql = s.qh + kQRows * kQStride;
     s.kk = s.ql + kQRows * kQStride;
-    s.vt = s.kk + kSub * kQStride;
-    s.st = reinterpret_cast<float*>(s.vt + kHD * kVStride);
+    s.vv = s.kk + kSub * kQStride;
+    s.st = reinterpret_cast<float*>(s.vv + kSub * kQStride);
     s.rm = s.st + kQRows * kSStride;
     s.rl = s.rm + kQRows;
     s.rc = s.rl + kQRows;
@@ -450,6 +449,23 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Four 8x8 b16 matrices from shared memory; lanes 8i..8i+7 give the row addresses of matrix i.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// Start moving bytes (16-byte aligned, a multiple of 16) of global memory into L2; no completion.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 // (x, y) -> high and low fp16x2 parts: hi = fp16(x), lo = fp16(x - hi).
@@ -460,17 +476,36 @@ __device__ __forceinline__ void split_f16x2(float x, float y, uint32_t& hi, uint
     lo = h2u(__floats2half2_rn(x - hf.x, y - hf.y));
 }
 
-// Load one 32-position K/V sub-block: K position-major, V transposed.  8 dims per piece; 512 pieces.
-__device__ __forceinline__ void attn_load_kv(const AttnArgs& a, int kvh, int sb, int p1, int tid, uint4 (&kr)[2],
+// Ring slot of position p (0 <= p < 2 * max_seq).
+__device__ __forceinline__ int ring_slot(int p, int max_seq) { return p < max_seq ? p : p - max_seq; }
+
+// exp(x) as 2^(x log2 e) on the special-function unit (relative error ~1e-6 for the |x| of a softmax).
+__device__ __forceinline__ float exp_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.44269504088896341f));
+    return y;
+}
+
+// L2 prefetch of the K and V rows of kv head kvh at positions [p0, p1) (p1 - p0 <= 128): one 256-byte row
+// per thread, K by threads 0-127, V by 128-255.
+__device__ __forceinline__ void attn_prefetch(const AttnArgs& a, int kvh, int p0, int p1, int tid) {
+    const int p = p0 + (tid & 127);
+    if (p < p1) {
+        const size_t off = (size_t)ring_slot(p, a.max_seq) * a.kv_ld + (size_t)kvh * kHD;
+        prefetch_l2((tid < 128 ? a.k : a.v) + off, kHD * 2);
+    }
+}
+
+// Load one 32-position K/V sub-block into registers: this thread's pieces are positions sb + (tid >> 4) and
+// +16, dims 8 * (tid & 15) .. +7 of the kv head whose first dim is at column col = kvh * 128 + 8 * (tid & 15).
+__device__ __forceinline__ void attn_load_kv(const AttnArgs& a, uint32_t col, int sb, int p1, int tid, uint4 (&kr)[2],
                                              uint4 (&vr)[2]) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-        const int i = tid + u * kAttnThreads;
-        const int j = i >> 4, d8 = (i & 15) * 8;
-        const int p = sb + j;
+        const int p = sb + (tid >> 4) + 16 * u;
         kr[u] = vr[u] = make_uint4(0, 0, 0, 0);
         if (p < p1) {
-            const size_t off = (size_t)(p % a.max_seq) * a.kv_ld + (size_t)kvh * kHD + d8;
+            const size_t off = (size_t)ring_slot(p, a.max_seq) * a.kv_ld + col;
             kr[u] = *reinterpret_cast<const uint4*>(a.k + off);
             vr[u] = *reinterpret_cast<const uint4*>(a.v + off);
         }
@@ -483,36 +518,41 @@ __device__ __forceinline__ void attn_store_kv(const AttnSmem& sm, int tid, const
         const int i = tid + u * kAttnThreads;
         const int j = i >> 4, d8 = (i & 15) * 8;
         *reinterpret_cast<uint4*>(sm.kk + j * kQStride + d8) = kr[u];
-        const __half* vh = reinterpret_cast<const __half*>(&vr[u]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sm.vt[(d8 + e) * kVStride + j] = vh[e];
+        *reinterpret_cast<uint4*>(sm.vv + j * kQStride + d8) = vr[u];
     }
 }
 
+// One work item: every query row (4 heads x nv tokens) of kv head kvh over chunk c.  The chunk's K/V rows
+// (and those of the next item, nkvh / nc, if nc >= 0) are prefetched into L2 at the start; each sub-block's
+// loads are issued before the previous sub-block's math so that their latency overlaps it.
 // gsync(): a barrier over the group's 256 threads (tid = 0..255).
 template <class Sync>
-__device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi_max, int kvh, int c, const AttnSmem& sm,
-                          int tid, Sync gsync) {
+__device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi_max, int kvh, int c, int nkvh, int nc,
+                          const AttnSmem& sm, int tid, Sync gsync) {
     const int warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int mt = warp >> 2, qw = warp & 3;
     const bool active = mt * 4 < nv;  // this m-tile holds a valid token
     const int p0 = max(c * a.chunk, lo_min);
     const int p1 = min((c + 1) * a.chunk, hi_max + 1);  // exclusive
-    gsync();
+    const int lo_max = max(0, pos + nv - a.max_seq);      // window start of the last valid token
+    attn_prefetch(a, kvh, p0, p1, tid);
+    if (nc >= 0) attn_prefetch(a, nkvh, max(nc * a.chunk, lo_min), min((nc + 1) * a.chunk, hi_max + 1), tid);
+    uint4 kr[2], vr[2];
+    float4 qv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int i = tid + u * kAttnThreads;  // < 32 rows * 32 float4
+        const int r = i >> 5, d4 = (i & 31) * 4;
+        const int s = r >> 2, h = r & 3;
+        qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s < nv) qv[u] = *reinterpret_cast<const float4*>(a.q + (size_t)s * a.q_ld + (size_t)(kvh * kGQA + h) * kHD + d4);
+    }
+    const uint32_t col = (uint32_t)(kvh * kHD + (tid & 15) * 8);
+    attn_load_kv(a, col, p0, p1, tid, kr, vr);
+    gsync();  // the previous item is done with the shared buffers
     {
         // query rows -> fp16 high/low parts; first K/V sub-block; running statistics
-        float4 qv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = tid + u * kAttnThreads;  // < 32 rows * 32 float4
-            const int r = i >> 5, d4 = (i & 31) * 4;
-            const int s = r >> 2, h = r & 3;
-            qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (s < nv) qv[u] = *reinterpret_cast<const float4*>(a.q + (size_t)s * a.q_ld + (size_t)(kvh * kGQA + h) * kHD + d4);
-        }
-        uint4 kr[2], vr[2];
-        attn_load_kv(a, kvh, p0, p1, tid, kr, vr);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int i = tid + u * kAttnThreads;
@@ -529,68 +569,103 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
             sm.rl[tid] = 0.f;
         }
     }
+    // ldmatrix row addresses.  Q (A operand, rows mt*16..+15): lanes 0-7 rows 0-7 dims +0, 8-15 rows 8-15
+    // dims +0, 16-23 rows 0-7 dims +8, 24-31 rows 8-15 dims +8.  K (B operand of the scores, positions
+    // qw*8..+7): lanes 8i..8i+7 give position lane&7 at dims +8i (two k-steps per load).  V (B operand
+    // of P V, transposed load): lanes 0-7 positions 0-7, 8-15 positions 8-15 of the k-step at dims d0,
+    // 16-31 the same at dims d0+8.
+    const int lr = lane & 7, lq = lane >> 3;
+    const uint32_t qh_a = smem_u32(sm.qh + (mt * 16 + lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8);
+    const uint32_t ql_a = qh_a + (uint32_t)(kQRows * kQStride * 2);
+    const uint32_t k_a = smem_u32(sm.kk + (qw * 8 + lr) * kQStride + lq * 8);
+    const uint32_t v_a = smem_u32(sm.vv + (lr + (lq & 1) * 8) * kQStride + qw * 32 + (lq >> 1) * 8);
     float o[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     for (int sb = p0; sb < p1; sb += kSub) {
-        if (sb != p0) {
-            uint4 kr[2], vr[2];
-            attn_load_kv(a, kvh, sb, p1, tid, kr, vr);
-            gsync();  // everyone is done with the previous sub-block
-            attn_store_kv(sm, tid, kr, vr);
-        }
+        const bool more = sb + kSub < p1;
+        if (more) attn_load_kv(a, col, sb + kSub, p1, tid, kr, vr);  // lands while this sub-block is computed
+        // positions outside some valid row's window occur only in edge sub-blocks (rows of tokens >= nv are
+        // never read)
+        const bool edge = sb + kSub > p1 || sb + kSub - 1 > pos || sb < lo_max;
         gsync();
         // ---- scores of rows mt*16 .. +15, positions sb + 8*qw .. +7 ----
         if (active) {
-            float sc[4] = {0.f, 0.f, 0.f, 0.f};
-            const __half* qh0 = sm.qh + (mt * 16 + g) * kQStride + 2 * t;
-            const __half* ql0 = sm.ql + (mt * 16 + g) * kQStride + 2 * t;
-            const __half* k0 = sm.kk + (qw * 8 + g) * kQStride + 2 * t;
+            // high and low parts of q accumulate in separate chains, added at the end
+            float sc[4] = {0.f, 0.f, 0.f, 0.f}, sl[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int ks = 0; ks < kHD / 16; ++ks) {
-                const int o16 = ks * 16;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(k0 + o16);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(k0 + o16 + 8);
-                mma_f16(sc, *reinterpret_cast<const uint32_t*>(qh0 + o16), *reinterpret_cast<const uint32_t*>(qh0 + 8 * kQStride + o16),
-                        *reinterpret_cast<const uint32_t*>(qh0 + o16 + 8), *reinterpret_cast<const uint32_t*>(qh0 + 8 * kQStride + o16 + 8),
-                        b0, b1);
-                mma_f16(sc, *reinterpret_cast<const uint32_t*>(ql0 + o16), *reinterpret_cast<const uint32_t*>(ql0 + 8 * kQStride + o16),
-                        *reinterpret_cast<const uint32_t*>(ql0 + o16 + 8), *reinterpret_cast<const uint32_t*>(ql0 + 8 * kQStride + o16 + 8),
-                        b0, b1);
+            for (int k2 = 0; k2 < kHD / 32; ++k2) {
+                uint32_t b[4];
+                ldsm_x4(k_a + k2 * 64, b[0], b[1], b[2], b[3]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t off = (k2 * 2 + h) * 32;
+                    uint32_t q0, q1, q2, q3;
+                    ldsm_x4(qh_a + off, q0, q1, q2, q3);
+                    mma_f16(sc, q0, q1, q2, q3, b[2 * h], b[2 * h + 1]);
+                    ldsm_x4(ql_a + off, q0, q1, q2, q3);
+                    mma_f16(sl, q0, q1, q2, q3, b[2 * h], b[2 * h + 1]);
+                }
             }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[e] += sl[e];
             // mask: row r -> token r/4; column -> position
+            if (edge) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int r = mt * 16 + g + (e >> 1) * 8, s = r >> 2;
-                const int p = sb + qw * 8 + 2 * t + (e & 1);
-                const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
-                const bool ok = s < nv && p < p1 && p >= lo && p <= hi;
-                sm.st[r * kSStride + qw * 8 + 2 * t + (e & 1)] = ok ? sc[e] : -INFINITY;
+                for (int e = 0; e < 4; ++e) {
+                    const int r = mt * 16 + g + (e >> 1) * 8, s = r >> 2;
+                    const int p = sb + qw * 8 + 2 * t + (e & 1);
+                    const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
+                    const bool ok = s < nv && p < p1 && p >= lo && p <= hi;
+                    if (!ok) sc[e] = -INFINITY;
+                }
             }
+            float* sr = sm.st + (mt * 16 + g) * kSStride + qw * 8 + 2 * t;
+            *reinterpret_cast<float2*>(sr) = make_float2(sc[0], sc[1]);
+            *reinterpret_cast<float2*>(sr + 8 * kSStride) = make_float2(sc[2], sc[3]);
         }
         gsync();
-        // ---- online softmax: warp w updates rows 4w .. 4w+3, lane = position ----
+        // ---- online softmax: warp w updates rows 4w .. 4w+3 (all of token w), lane = position; the four
+        // rows' reductions are interleaved ----
+        if (warp >= nv) {  // no token: zero probabilities and correction (rows stay unused)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int r = warp * 4 + k;
-            if ((r >> 2) >= nv) {  // no token: zero probabilities and correction (rows stay unused)
-                sm.st[r * kSStride + lane] = 0.f;
-                if (lane == 0) sm.rc[r] = 0.f;
-                continue;
+            for (int k = 0; k < 4; ++k) sm.st[(warp * 4 + k) * kSStride + lane] = 0.f;
+            if (lane < 4) sm.rc[warp * 4 + lane] = 0.f;
+        } else {
+            float v[4], mo[4], mx[4], e[4], corr[4], es[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[k] = sm.st[(warp * 4 + k) * kSStride + lane];
+                mo[k] = sm.rm[warp * 4 + k];
+                mx[k] = v[k];
             }
-            const float v = sm.st[r * kSStride + lane];
-            const float mo = sm.rm[r];
-            const float mx = warp_max(v);
-            const float mn = fmaxf(mo, mx);
-            // a row with nothing valid yet keeps m = -inf and contributes nothing
-            const float e = (mn == -INFINITY || v == -INFINITY) ? 0.f : expf(v - mn);
-            const float corr = (mn == -INFINITY || mo == -INFINITY) ? 0.f : expf(mo - mn);
-            const float es = warp_sum(e);
-            sm.st[r * kSStride + lane] = e;
-            if (lane == 0) {
-                sm.rl[r] = sm.rl[r] * corr + es;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], o));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float mn = fmaxf(mo[k], mx[k]);
+                // a row with nothing valid yet keeps m = -inf and contributes nothing
+                e[k] = (mn == -INFINITY || v[k] == -INFINITY) ? 0.f : exp_fast(v[k] - mn);
+                corr[k] = (mn == -INFINITY || mo[k] == -INFINITY) ? 0.f : exp_fast(mo[k] - mn);
+                mx[k] = mn;
+                es[k] = e[k];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) es[k] += __shfl_xor_sync(0xffffffffu, es[k], o);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sm.st[(warp * 4 + k) * kSStride + lane] = e[k];
+            if (lane < 4) {
+                const int r = warp * 4 + lane;
+                const float c = lane == 0 ? corr[0] : lane == 1 ? corr[1] : lane == 2 ? corr[2] : corr[3];
+                const float sum = lane == 0 ? es[0] : lane == 1 ? es[1] : lane == 2 ? es[2] : es[3];
+                const float mn = lane == 0 ? mx[0] : lane == 1 ? mx[1] : lane == 2 ? mx[2] : mx[3];
+                sm.rl[r] = sm.rl[r] * c + sum;
                 sm.rm[r] = mn;
-                sm.rc[r] = corr;
+                sm.rc[r] = c;
             }
         }
         gsync();
@@ -617,14 +692,20 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
                 split_f16x2(x2.x, x2.y, ah[2], al[2]);
                 split_f16x2(x3.x, x3.y, ah[3], al[3]);
 #pragma unroll
-                for (int n = 0; n < 4; ++n) {
-                    const __half* vp = sm.vt + (qw * 32 + n * 8 + g) * kVStride + ks * 16 + 2 * t;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(vp);
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(vp + 8);
-                    mma_f16(o[n], ah[0], ah[1], ah[2], ah[3], b0, b1);
-                    mma_f16(o[n], al[0], al[1], al[2], al[3], b0, b1);
+                for (int n2 = 0; n2 < 2; ++n2) {
+                    uint32_t b[4];  // (b0, b1) of dims qw*32 + n2*16 .. +7, then of +8 .. +15
+                    ldsm_x4_t(v_a + (uint32_t)(ks * 16 * kQStride * 2 + n2 * 32), b[0], b[1], b[2], b[3]);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        mma_f16(o[2 * n2 + h], ah[0], ah[1], ah[2], ah[3], b[2 * h], b[2 * h + 1]);
+                        mma_f16(o[2 * n2 + h], al[0], al[1], al[2], al[3], b[2 * h], b[2 * h + 1]);
+                    }
                 }
             }
+        }
+        if (more) {
+            gsync();  // every warp is done with this sub-block's K and V
+            attn_store_kv(sm, tid, kr, vr);
         }
     }
     gsync();  // final statistics visible
@@ -648,53 +729,57 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
 }
 
 // Merge the chunk partials of (token s, head h) and quantise the 128 outputs to 4 Q8_0 blocks.
-// NWC warps share the row (wi = this warp's index among them, lane owns dims 4*lane..4*lane+3):
-//   1. every warp reads all (max, sum) pairs lane-parallel (groups of 128 chunks) -> M; L (lane sums in
-//      chunk order, then the butterfly);
-//   2. warp wi adds acc_c * exp(m_c - M) over its contiguous quarter of the chunks, in chunk order, four
+// nwc warps share the row (wi = this warp's index among them, lane owns dims 4*lane..4*lane+3):
+//   1. every warp reads all (max, sum) pairs lane-parallel (up to 512 chunks in one round trip) -> M;
+//      warp 0: L (lane sums in chunk order, then the butterfly);
+//   2. warp wi adds acc_c * exp(m_c - M) over its contiguous share of the chunks, in chunk order, eight
 //      chunks' loads in flight at a time;
-//   3. the partial vectors meet in obuf ([NWC][128], shared) behind rsync(); warp 0 adds them in warp
+//   3. the partial vectors meet in obuf ([nwc][128], shared) behind rsync(); warp 0 adds them in warp
 //      order, scales by 1/L and quantises.
-// The result depends only on NWC, which both forward paths fix at kCombineWarps.
-constexpr int kCombineWarps = 4;
+// The result depends only on nwc, which both forward paths take from combine_warps(max_seq).
+constexpr int kCombineWarpsMax = 16;
+// Warps per merged row: more for long rings, whose rows have many chunks.
+__host__ __device__ inline int combine_warps(int max_seq) { return max_seq <= 8192 ? 4 : 16; }
 
 template <class Sync>
-__device__ void attn_combine_row(const AttnArgs& a, int pos, int s, int h, int wi, int lane, float* obuf, Sync rsync) {
+__device__ void attn_combine_row(const AttnArgs& a, int nwc, int pos, int s, int h, int wi, int lane, float* obuf,
+                                 Sync rsync) {
     const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
     const int c0 = lo / a.chunk, c1 = hi / a.chunk;
     const size_t base = ((size_t)s * a.n_heads + h) * a.max_chunks;
+    constexpr int kMl = 16;  // (max, sum) pairs per lane per round trip
     float M = -INFINITY;
-    for (int g0 = c0; g0 <= c1; g0 += 128) {
-        float mx[4];
+    for (int g0 = c0; g0 <= c1; g0 += 32 * kMl) {
+        float mx[kMl];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kMl; ++u) {
             const int c = g0 + lane + 32 * u;
             mx[u] = c <= c1 ? a.part_ml[base + c].x : -INFINITY;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) M = fmaxf(M, mx[u]);
+        for (int u = 0; u < kMl; ++u) M = fmaxf(M, mx[u]);
     }
     M = warp_max(M);
     float L = 0.f;
     if (wi == 0) {
-        for (int g0 = c0; g0 <= c1; g0 += 128) {
-            float2 ml[4];
+        for (int g0 = c0; g0 <= c1; g0 += 32 * kMl) {
+            float2 ml[kMl];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < kMl; ++u) {
                 const int c = g0 + lane + 32 * u;
                 ml[u] = c <= c1 ? a.part_ml[base + c] : make_float2(-INFINITY, 0.f);
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < kMl; ++u)
                 if (g0 + lane + 32 * u <= c1) L += (ml[u].x == -INFINITY) ? 0.f : ml[u].y * expf(ml[u].x - M);
         }
         L = warp_sum(L);
     }
     // this warp's chunk range
-    const int nc = c1 - c0 + 1, per = (nc + kCombineWarps - 1) / kCombineWarps;
+    const int nc = c1 - c0 + 1, per = (nc + nwc - 1) / nwc;
     const int ca = c0 + wi * per, cb = min(c1, ca + per - 1);
     float o[4] = {0.f, 0.f, 0.f, 0.f};
-    constexpr int U = 4;
+    constexpr int U = 8;
     for (int cc = ca; cc <= cb; cc += U) {
         float4 ac[U];
         float mx[U];
@@ -721,8 +806,7 @@ __device__ void attn_combine_row(const AttnArgs& a, int pos, int s, int h, int w
         rsync();  // obuf is free again once warp 0 has read it
         return;
     }
-#pragma unroll
-    for (int w = 1; w < kCombineWarps; ++w) {
+    for (int w = 1; w < nwc; ++w) {
         const float4 p = *reinterpret_cast<const float4*>(obuf + w * kHD + lane * 4);
         o[0] += p.x;
         o[1] += p.y;

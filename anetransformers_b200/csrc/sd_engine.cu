@@ -40,6 +40,8 @@
 
 using namespace sd;
 
+static_assert(sd::kMaxVerify == SD_MAX_VERIFY, "verify width differs between the ABI and the kernels");
+
 namespace {
 
 // ---------------------------------------------------------------------------------------------
@@ -245,6 +247,7 @@ struct sd_ctx {
     __half *kc = nullptr, *vc = nullptr;      // [n_layers][max_seq][kv_rows]
     __half *dkc = nullptr, *dvc = nullptr;    // self-spec drafter KV [draft_layers][max_seq][kv_rows]
     int draft_layers_alloc = 0;
+    int draft_kv_hist = 0, draft_kv_layers = 0;  // drafter K/V prefilled for history[0 .. draft_kv_hist) at this depth
     size_t weight_bytes = 0, kv_bytes = 0;
     // buffers
     float* x = nullptr;        // [MB][dim]
@@ -255,9 +258,10 @@ struct sd_ctx {
     float2* part_ml = nullptr;
     float* part_acc = nullptr;
     int attn_chunk = 64, max_chunks = 0;
-    float* logits = nullptr;   // [MB][vocab]
+    float* logits = nullptr;   // [kMaxVerify][vocab]
     float* probs = nullptr;    // [vocab]
-    int* argmax = nullptr;     // [MB]
+    int* argmax = nullptr;     // [kMaxVerify]
+    DevCtrl* ctrl_sub = nullptr;  // [kMaxVerify] control blocks of the forwards a wide verify batch splits into
     DevCtrl* ctrl = nullptr;   // verify / decode forward
     DevCtrl* dctrl = nullptr;  // self-spec drafter chain
     DevCtrl* ctrl_h = nullptr; // pinned staging
@@ -270,7 +274,7 @@ struct sd_ctx {
     int* g_hist = nullptr;
     int g_cap = 0;
     // graphs
-    cudaGraphExec_t fwd_graph[kMaxS + 1] = {};
+    cudaGraphExec_t fwd_graph[kMaxVerify + 1] = {};
     cudaGraphExec_t iter_graph = nullptr;
     int iter_key[6] = {-1, -1, -1, -1, -1, -1};
     GenParamsDev iter_p{};
@@ -429,7 +433,8 @@ int setup_fused(sd_ctx* c) {
 }
 
 // One forward as a single persistent kernel (then the argmax kernel when logits are wanted).
-int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
+int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax,
+                          int row0) {
     FwdArgs a{};
     a.layers = c->d_layers;
     a.n_layers = n_layers;
@@ -473,7 +478,7 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     a.part_acc = c->part_acc;
     a.attn_chunk = c->attn_chunk;
     a.max_chunks = c->max_chunks;
-    a.logits = c->logits;
+    a.logits = c->logits + (size_t)row0 * c->vocab;
     a.tokens = nullptr;
     a.ctrl = ctrl;
     a.err = c->err;
@@ -481,7 +486,8 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     CK(cudaMemsetAsync(c->fsync, 0, fwd_sync_words(c->dim) * sizeof(unsigned), c->st), "memset");
     CK(launch_forward(a, c->fwd_grid, c->fwd_smem, c->st), "forward launch");
     if (c->tpx.n > 1) CK(launch_tp_advance(c->tp_base, 2 * n_layers, c->st), "tp advance");
-    if (logits_and_argmax) CK(launch_argmax(c->logits, c->vocab, S, c->argmax, ctrl, c->st, false), "argmax");
+    if (logits_and_argmax)
+        CK(launch_argmax(c->logits + (size_t)row0 * c->vocab, c->vocab, S, c->argmax + row0, ctrl, c->st, false), "argmax");
     return SD_OK;
 }
 
@@ -509,11 +515,13 @@ int tp_reduce(sd_ctx* c, int S, int* yparts) {
     return nccl_allreduce_sum(c->nccl, c->y, n, c->st);
 }
 
-// Enqueue one forward of S (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the
-// position, the tokens and how many of the S are valid.
-int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
+// One forward of S <= MB (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the position,
+// the tokens and how many of the S are valid.  Logits / argmax go to rows row0.. of c->logits / c->argmax.
+int enqueue_forward_one(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax,
+                        int row0) {
     // tensor parallel contexts use the persistent kernel once their peers are connected
-    if (c->fused && (c->tp_size == 1 || c->tpx.n > 1)) return enqueue_forward_fused(c, S, n_layers, k, v, ctrl, logits_and_argmax);
+    if (c->fused && (c->tp_size == 1 || c->tpx.n > 1))
+        return enqueue_forward_fused(c, S, n_layers, k, v, ctrl, logits_and_argmax, row0);
     const bool pdl = c->use_pdl;
     NormArgs na{};
     na.x = c->x;
@@ -528,7 +536,8 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
     na.yparts = 1;
     na.ystride = (size_t)c->MB * c->dim;
     na.err = c->err;
-    CK(launch_norm_quant(0, na, c->st, pdl), "embed");
+    // a slice's control block was just written by the previous kernel: launch after it in full order
+    CK(launch_norm_quant(0, na, c->st, pdl && row0 == 0), "embed");
     const size_t kv_layer = (size_t)c->max_seq * c->kv_rows;
     for (int l = 0; l < n_layers; ++l) {
         LayerW& W = c->L[l];
@@ -615,10 +624,27 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
     if (rc) return rc;
     pl.a.act = c->act;
     pl.a.ctrl = ctrl;
-    pl.a.out = c->logits;
+    pl.a.out = c->logits + (size_t)row0 * c->vocab;
     pl.a.out_ld = c->vocab;
     if ((rc = launch_plan(c, EPI_STORE, pl))) return rc;
-    CK(launch_argmax(c->logits, c->vocab, S, c->argmax, ctrl, c->st, pdl), "argmax");
+    CK(launch_argmax(c->logits + (size_t)row0 * c->vocab, c->vocab, S, c->argmax + row0, ctrl, c->st, pdl), "argmax");
+    return SD_OK;
+}
+
+// Enqueue the forward of S <= kMaxVerify tokens.  A batch wider than MB runs as consecutive forwards of
+// MB tokens, each attending to the K/V the previous ones wrote; every reduction is batch invariant, so
+// the logits equal those of one wide forward bit for bit.
+int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax) {
+    if (S <= c->MB) return enqueue_forward_one(c, S, n_layers, k, v, ctrl, logits_and_argmax, 0);
+    for (int off = 0; off < S; off += c->MB) {
+        DevCtrl* cj = ctrl;
+        if (off > 0) {
+            cj = c->ctrl_sub + off / c->MB;
+            CK(launch_ctrl_slice(ctrl, cj, off, c->st), "ctrl slice");
+        }
+        int rc = enqueue_forward_one(c, std::min(c->MB, S - off), n_layers, k, v, cj, logits_and_argmax, off);
+        if (rc) return rc;
+    }
     return SD_OK;
 }
 
@@ -713,7 +739,7 @@ void sd_ctx_free(sd_ctx* c) {
     cudaFree(c->x); cudaFree(c->y); cudaFree(c->act.qs); cudaFree(c->act.d); cudaFree(c->act.sum);
     cudaFree(c->hact.qs); cudaFree(c->hact.d); cudaFree(c->hact.sum); cudaFree(c->q);
     cudaFree(c->part_ml); cudaFree(c->part_acc); cudaFree(c->logits); cudaFree(c->probs); cudaFree(c->argmax);
-    cudaFree(c->ctrl); cudaFree(c->dctrl); cudaFree(c->err); cudaFree(c->gs); cudaFree(c->g_out); cudaFree(c->g_hist);
+    cudaFree(c->ctrl); cudaFree(c->dctrl); cudaFree(c->ctrl_sub); cudaFree(c->err); cudaFree(c->gs); cudaFree(c->g_out); cudaFree(c->g_hist);
     cudaFree(c->d_layers); cudaFree(c->ssq); cudaFree(c->fsync);
     cudaFree(c->img_mem);
     for (void* p : c->tp_opened) cudaIpcCloseMemHandle(p);
@@ -856,8 +882,8 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
         (rc = dalloc(&c->q, (size_t)MB * c->q_rows)) ||
         (rc = dalloc(&c->part_ml, (size_t)MB * c->nh_l * c->max_chunks)) ||
         (rc = dalloc(&c->part_acc, (size_t)MB * c->nh_l * c->max_chunks * 128)) ||
-        (rc = dalloc(&c->logits, (size_t)MB * c->vocab)) || (rc = dalloc(&c->probs, (size_t)c->vocab)) ||
-        (rc = dalloc(&c->argmax, MB)) || (rc = dalloc(&c->ctrl, 1)) || (rc = dalloc(&c->dctrl, 1)) ||
+        (rc = dalloc(&c->logits, (size_t)kMaxVerify * c->vocab)) || (rc = dalloc(&c->probs, (size_t)c->vocab)) ||
+        (rc = dalloc(&c->argmax, kMaxVerify)) || (rc = dalloc(&c->ctrl_sub, kMaxVerify)) || (rc = dalloc(&c->ctrl, 1)) || (rc = dalloc(&c->dctrl, 1)) ||
         (rc = dalloc(&c->err, 1)) || (rc = dalloc(&c->gs, 1)))
         return bail(rc);
     cudaMemset(c->err, 0, sizeof(int));
@@ -982,7 +1008,7 @@ int sd_ctx_tp_connect(sd_ctx* c, const void* handles, int n) {
 
 int sd_forward_dev(sd_ctx* c, const int32_t* tokens_dev, int S, int pos, float* logits_dev, int32_t* argmax_dev, void* stream) {
     clear_error();
-    if (!c || !tokens_dev || S < 1 || S > c->MB || pos < 0) return fail(SD_ERR_INVALID, "sd_forward_dev: bad arguments");
+    if (!c || !tokens_dev || S < 1 || S > kMaxVerify || pos < 0) return fail(SD_ERR_INVALID, "sd_forward_dev: bad arguments");
     if (pos + S > c->max_seq) return fail(SD_ERR_INVALID, "positions past the KV ring (%d)", c->max_seq);
     cudaSetDevice(c->dev);
     cudaEvent_t ev;
@@ -1009,7 +1035,7 @@ int sd_forward_dev(sd_ctx* c, const int32_t* tokens_dev, int S, int pos, float* 
 
 int sd_forward(sd_ctx* c, const int32_t* tokens, int S, int pos, float* logits, int32_t* argmax) {
     clear_error();
-    if (!c || !tokens || S < 1 || S > c->MB || pos < 0) return fail(SD_ERR_INVALID, "sd_forward: bad arguments");
+    if (!c || !tokens || S < 1 || S > kMaxVerify || pos < 0) return fail(SD_ERR_INVALID, "sd_forward: bad arguments");
     if (pos + S > c->max_seq) return fail(SD_ERR_INVALID, "positions past the KV ring (%d)", c->max_seq);
     int rc = check_tokens(c, tokens, S);
     if (rc) return rc;
@@ -1023,7 +1049,7 @@ int sd_forward(sd_ctx* c, const int32_t* tokens, int S, int pos, float* logits, 
 
 int sd_forward_layers(sd_ctx* c, int n_layers, const int32_t* tokens, int S, int pos, float* logits, int32_t* argmax) {
     clear_error();
-    if (!c || !tokens || S < 1 || S > c->MB || pos < 0 || n_layers < 1 || n_layers > c->n_layers)
+    if (!c || !tokens || S < 1 || S > kMaxVerify || pos < 0 || n_layers < 1 || n_layers > c->n_layers)
         return fail(SD_ERR_INVALID, "sd_forward_layers: bad arguments");
     if (pos + S > c->max_seq) return fail(SD_ERR_INVALID, "positions past the KV ring");
     int rc = check_tokens(c, tokens, S);
@@ -1094,7 +1120,7 @@ int sd_ngram_draft(const int32_t* history, int hlen, int ngram_n, int max_draft,
 int sd_spec_accept(sd_ctx* c, const float* draft_probs, const float* logits, const int32_t* draft, int n_draft, float temp,
                    int bonus_mode, uint64_t seed, uint64_t* counter, int32_t* accepted) {
     clear_error();
-    if (!c || !logits || !draft || !accepted || n_draft < 1 || n_draft > kMaxS - 1 || (temp > 0 && !draft_probs))
+    if (!c || !logits || !draft || !accepted || n_draft < 1 || n_draft > kMaxVerify - 1 || (temp > 0 && !draft_probs))
         return fail(SD_ERR_INVALID, "sd_spec_accept: bad arguments");
     cudaSetDevice(c->dev);
     int rc = check_tokens(c, draft, n_draft);
@@ -1167,6 +1193,7 @@ int ensure_draft_kv(sd_ctx* c, int layers) {
     cudaFree(c->dvc);
     c->dkc = c->dvc = nullptr;
     c->draft_layers_alloc = 0;
+    c->draft_kv_hist = c->draft_kv_layers = 0;
     const size_t n = (size_t)layers * c->max_seq * c->kv_rows;
     int rc = dalloc(&c->dkc, n);
     if (!rc) rc = dalloc(&c->dvc, n);
@@ -1243,13 +1270,13 @@ int sd_decode(sd_ctx* c, const sd_gen_params* gp, const int32_t* history, int n_
     if (rc) return rc;
     const int mode = gp->mode == SD_GEN_NGRAM ? SD_MODE_NGRAM : gp->mode == SD_GEN_SELF_SPEC ? SD_MODE_SELF : SD_MODE_GREEDY;
     int K = gp->spec_k < 1 ? 1 : gp->spec_k;
-    if (mode != SD_MODE_GREEDY && K + 1 > c->MB)
-        return fail(SD_ERR_UNSUPPORTED, "spec_k %d needs %d tokens per verify forward (max_batch %d)", K, K + 1, c->MB);
+    if (mode != SD_MODE_GREEDY && K + 1 > kMaxVerify)
+        return fail(SD_ERR_UNSUPPORTED, "spec_k %d needs %d tokens per verify (at most %d)", K, K + 1, kMaxVerify);
     int dl = gp->draft_layers < 1 ? 1 : gp->draft_layers;
     if (dl >= c->n_layers) dl = c->n_layers - 1;
     if (mode == SD_MODE_SELF && dl < 1) return fail(SD_ERR_INVALID, "self-speculation needs >= 2 layers");
     cudaSetDevice(c->dev);
-    const int cap = n_hist + gp->max_tokens + 2 * kMaxS + 16;
+    const int cap = n_hist + gp->max_tokens + 2 * kMaxVerify + 16;
     if ((rc = ensure_gen_buffers(c, cap))) return rc;
     if (mode == SD_MODE_SELF && (rc = ensure_draft_kv(c, dl))) return rc;
     // the first token counts as generated (printed before the loop, mistral_infer.m:615-621)
@@ -1285,14 +1312,17 @@ int sd_decode(sd_ctx* c, const sd_gen_params* gp, const int32_t* history, int n_
     *c->gs_h = h;
     CK(cudaMemcpyAsync(c->g_hist, history, (size_t)n_hist * 4, cudaMemcpyHostToDevice, c->st), "history");
     CK(cudaMemcpyAsync(c->gs, c->gs_h, sizeof(GenState), cudaMemcpyHostToDevice, c->st), "state");
-    if (mode == SD_MODE_SELF) {
+    if (mode == SD_MODE_SELF && !(gp->reuse_draft_kv && c->draft_kv_hist >= n_hist - 1 && c->draft_kv_layers == dl)) {
         // drafter KV prefill through the first dl layers (mistral_infer.m:675-681)
+        c->draft_kv_hist = 0;
         for (int i = 0; i < n_hist - 1; i += c->MB) {
             const int S = std::min(c->MB, n_hist - 1 - i);
             if ((rc = set_ctrl(c, c->dctrl, history + i, S, i, true))) return rc;
             if ((rc = enqueue_forward(c, S, dl, c->dkc, c->dvc, c->dctrl, false))) return rc;
             CK(cudaStreamSynchronize(c->st), "draft prefill");
         }
+        c->draft_kv_hist = n_hist - 1;
+        c->draft_kv_layers = dl;
     }
     if ((rc = iteration_graph(c, p, K, dl))) return rc;
     const double t0 = now_ms();
@@ -1328,7 +1358,9 @@ int sd_generate(sd_ctx* c, const sd_gen_params* gp, const int32_t* prompt, int n
                 sd_gen_stats* stats) {
     clear_error();
     if (!c || !gp || !prompt || n_prompt < 1 || !out_tokens || out_cap < 1) return fail(SD_ERR_INVALID, "sd_generate: bad arguments");
-    if (n_prompt + gp->max_tokens + kMaxS + 1 > c->max_seq) return fail(SD_ERR_INVALID, "prompt + tokens exceed the KV ring");
+    // room for the last verify batch (as the decode loop's stop rule)
+    const int vw = std::max(kMaxS, (gp->mode == SD_GEN_GREEDY ? 0 : std::max(gp->spec_k, 1)) + 1);
+    if (n_prompt + gp->max_tokens + vw + 1 > c->max_seq) return fail(SD_ERR_INVALID, "prompt + tokens exceed the KV ring");
     int rc = check_tokens(c, prompt, n_prompt);
     if (rc) return rc;
     cudaSetDevice(c->dev);
@@ -1356,7 +1388,7 @@ int sd_generate(sd_ctx* c, const sd_gen_params* gp, const int32_t* prompt, int n
         p.eos_id = c->eos;
         p.gen_limit = 1;
         p.max_seq = c->max_seq;
-        const int cap = n_prompt + gp->max_tokens + 2 * kMaxS + 16;
+        const int cap = n_prompt + gp->max_tokens + 2 * kMaxVerify + 16;
         if ((rc = ensure_gen_buffers(c, cap))) return rc;
         GenState h{};
         h.cur = 0;

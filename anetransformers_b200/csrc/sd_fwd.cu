@@ -434,22 +434,26 @@ __device__ __forceinline__ void attention_phase(const FwdArgs& a, int l, uint8_t
     const int n_items = (c_last - c_first + 1) * a.n_kvh;
     const AttnSmem sm = attn_smem_at(uni + (size_t)grp * attn_smem_bytes());
     const int bar_id = kBarAttn0 + grp;
-    for (int item = blockIdx.x * kFwdAttnGroups + grp; item < n_items; item += G * kFwdAttnGroups)
-        attn_item(aa, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, sm, tid & 255,
-                        [bar_id] { named_sync(bar_id, 256); });
+    for (int item = blockIdx.x * kFwdAttnGroups + grp; item < n_items; item += G * kFwdAttnGroups) {
+        const int nx = item + G * kFwdAttnGroups;  // this group's next item, prefetched into L2 during this one
+        attn_item(aa, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, nx % a.n_kvh,
+                  nx < n_items ? c_first + nx / a.n_kvh : -1, sm, tid & 255, [bar_id] { named_sync(bar_id, 256); });
+    }
 }
 
-// kCombineWarps warps per (token, head) row; warps 0-15 hold four rows at a time.
+// combine_warps(max_seq) warps per (token, head) row; warps 0-15 hold 16 / that many rows at a time.
 __device__ __forceinline__ void combine_phase(const FwdArgs& a, int l, uint8_t* uni, int nv, int pos, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int slot = warp / kCombineWarps;  // 0..3 for warps 0-15
-    if (slot >= 4) return;
+    const int nwc = combine_warps(a.max_seq), slots = 16 / nwc;
+    const int slot = warp / nwc;
+    if (slot >= slots) return;
     const AttnArgs aa = attn_args(a, l, pos);
-    float* obuf = reinterpret_cast<float*>(uni) + slot * kCombineWarps * kHD;
+    float* obuf = reinterpret_cast<float*>(uni) + slot * nwc * kHD;
     const int bar_id = kBarAttn0 + slot;
-    for (int row = blockIdx.x * 4 + slot; row < nv * a.n_heads; row += gridDim.x * 4)
-        attn_combine_row(aa, pos, row / a.n_heads, row % a.n_heads, warp % kCombineWarps, lane, obuf,
-                         [bar_id] { named_sync(bar_id, kCombineWarps * 32); });
+    const int nthr = nwc * 32;
+    for (int row = blockIdx.x * slots + slot; row < nv * a.n_heads; row += gridDim.x * slots)
+        attn_combine_row(aa, nwc, pos, row / a.n_heads, row % a.n_heads, warp % nwc, lane, obuf,
+                         [bar_id, nthr] { named_sync(bar_id, nthr); });
 }
 
 // idx: the reduction's index in the forward (2 per layer).  Tensor parallel: after the grid barrier this
@@ -522,6 +526,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
     if (a.ctrl && a.ctrl->done) return;  // uniform: nothing writes ctrl while the kernel runs
     const int nv = a.ctrl ? min(a.ctrl->n_valid, a.S) : a.S;
     const int pos = a.ctrl ? a.ctrl->pos : 0;
+    if (nv <= 0) return;  // a slice of a verify batch with no valid token (uniform, as above)
 
     if (tid == 0) {
         for (int i = 0; i < a.nstage; ++i) {

@@ -27,6 +27,9 @@ constexpr int kGemvThreads = (kConsumerWarps + kEpiWarps + 1) * 32;  // + 1 prod
 constexpr int kRedSlots = 2;                             // row-group pairs in flight to the epilogue
 constexpr int kMaxStages = 16;
 constexpr int kMaxS = 8;                                 // tokens per forward (n8 MMA tile)
+// Tokens per verify: a batch of more than kMaxS tokens runs as consecutive forwards of <= kMaxS tokens
+// (every reduction is batch invariant, so the logits equal those of one wide forward).
+constexpr int kMaxVerify = 16;
 constexpr int kRPW = 2;                                  // row-groups per warp per stage (share B fragments)
 
 // Row-groups are allocated in whole pairs (a zero row-group pads an odd count).
@@ -62,7 +65,7 @@ struct DevCtrl {
     int pos;          // position of token 0 of this forward
     int n_valid;      // tokens of this forward that are real (<= S of the launch)
     int done;         // generation finished: every kernel of an iteration returns immediately
-    int tokens[kMaxS];
+    int tokens[kMaxVerify];
 };
 
 enum GemvEpi : int {

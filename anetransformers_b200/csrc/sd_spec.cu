@@ -381,7 +381,7 @@ __global__ void k_gen_self_verify(GenState* g, DevCtrl* ctrl, int K) {
 // Accept / emit phase after the verify (or single) forward.  logits: [n_valid][vocab].
 __global__ void __launch_bounds__(kSampleThreads) k_gen_commit(GenState* g, DevCtrl* ctrl, float* logits, float* probs,
                                                                const int* argmax, GenParamsDev p, int vocab) {
-    __shared__ int acc[kMaxS + 1];
+    __shared__ int acc[kMaxVerify + 1];
     __shared__ int n_acc_s;
     if (g->done) return;
     const int nd = g->n_draft;
@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_gen_commit(GenState* g, DevC
         g->total_iterations++;
         g->pos += na;
         g->cur = acc[na - 1];
-        if (stop || g->generated >= p.gen_limit || g->pos + kMaxS >= p.max_seq) g->done = 1;
+        if (stop || g->generated >= p.gen_limit || g->pos + max(kMaxS, (p.mode == SD_MODE_GREEDY ? 0 : p.spec_k) + 1) >= p.max_seq) g->done = 1;
     }
 }
 
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_spec_accept(const float* log
                                                                 int bonus_mode, unsigned long long seed,
                                                                 unsigned long long* counter, int* accepted, int* n_acc) {
     __shared__ GenState g;
-    __shared__ int acc_s[kMaxS + 1];
+    __shared__ int acc_s[kMaxVerify + 1];
     __shared__ float r_s;
     __shared__ int res_s;
     if (threadIdx.x == 0) {
@@ -667,6 +667,24 @@ cudaError_t launch_gen_draft_step(GenState* g, DevCtrl* dctrl, const int* argmax
     k_gen_draft_step<<<1, 32, 0, st>>>(g, dctrl, argmax, k);
     return cudaGetLastError();
 }
+// Control block of the forward that carries tokens [off, off + kMaxS) of a verify batch.  done is copied
+// (it only ever goes 0 -> 1 within a generation, so kernels may read it before their grid dependency
+// wait); a slice with no valid token gets n_valid 0.
+__global__ void k_ctrl_slice(const DevCtrl* src, DevCtrl* dst, int off) {
+    const int i = threadIdx.x;
+    if (i < kMaxS) dst->tokens[i] = off + i < kMaxVerify ? src->tokens[off + i] : 0;
+    if (i == 0) {
+        dst->pos = src->pos + off;
+        dst->n_valid = max(src->n_valid - off, 0);
+        dst->done = src->done;
+    }
+}
+
+cudaError_t launch_ctrl_slice(const DevCtrl* src, DevCtrl* dst, int off, cudaStream_t st) {
+    k_ctrl_slice<<<1, 32, 0, st>>>(src, dst, off);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gen_self_verify(GenState* g, DevCtrl* ctrl, int K, cudaStream_t st) {
     k_gen_self_verify<<<1, 32, 0, st>>>(g, ctrl, K);
     return cudaGetLastError();

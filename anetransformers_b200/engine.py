@@ -17,6 +17,7 @@ from . import _lib
 GEN_GREEDY, GEN_NGRAM, GEN_SELF_SPEC = 0, 1, 2
 BONUS_ARGMAX, BONUS_REFERENCE = 0, 1
 _MODES = {"greedy": GEN_GREEDY, "ngram": GEN_NGRAM, "self": GEN_SELF_SPEC}
+MAX_VERIFY = 16  # SD_MAX_VERIFY: tokens per verify forward (current + up to 15 drafts)
 
 
 def _i32(a) -> np.ndarray:
@@ -125,8 +126,8 @@ class Context:
 
     # -- forward ---------------------------------------------------------------------------------
     def forward(self, tokens: Sequence[int], pos: int, want_logits: bool = True) -> Tuple[np.ndarray, np.ndarray]:
-        """Forward len(tokens) <= max_batch tokens at positions pos.. (writes their K/V); returns
-        (logits [S, vocab] or None, argmax [S])."""
+        """Forward len(tokens) <= MAX_VERIFY tokens at positions pos.. (writes their K/V; batches wider than
+        max_batch run as consecutive forwards); returns (logits [S, vocab] or None, argmax [S])."""
         t = _i32(tokens)
         S = t.size
         logits = np.empty((S, self.vocab), np.float32) if want_logits else None
@@ -166,7 +167,7 @@ class Context:
     @staticmethod
     def gen_params(mode="greedy", max_tokens=128, temp=0.7, top_p=0.9, top_k=40, rep_penalty=1.1, rep_window=64,
                    ignore_eos=False, spec_k=4, ngram_n=3, draft_layers=8, history_has_current=False,
-                   bonus_mode=BONUS_ARGMAX, seed=0) -> _lib.GenParams:
+                   bonus_mode=BONUS_ARGMAX, seed=0, reuse_draft_kv=False) -> _lib.GenParams:
         p = _lib.GenParams()
         _lib.lib().sd_gen_params_default(C.byref(p))
         p.mode = _MODES[mode] if isinstance(mode, str) else mode
@@ -174,13 +175,14 @@ class Context:
         p.rep_penalty, p.rep_window, p.ignore_eos = rep_penalty, rep_window, int(ignore_eos)
         p.spec_k, p.ngram_n, p.draft_layers = spec_k, ngram_n, draft_layers
         p.history_has_current, p.bonus_mode, p.seed = int(history_has_current), bonus_mode, seed
+        p.reuse_draft_kv = int(reuse_draft_kv)
         return p
 
     def generate(self, prompt: Sequence[int], **kw) -> Tuple[List[int], Dict]:
         """Prefill + first token + decode loop (mistral_infer.m main).  Returns (tokens, stats)."""
         p = self.gen_params(**kw)
         t = _i32(prompt)
-        out = np.empty(p.max_tokens + 2 * 8 + 4, np.int32)
+        out = np.empty(p.max_tokens + 2 * MAX_VERIFY + 4, np.int32)
         st = _lib.GenStats()
         n = _lib.lib().sd_generate(self.h, C.byref(p), t.ctypes.data, t.size, out.ctypes.data, out.size, C.byref(st))
         if n < 0:
@@ -191,7 +193,7 @@ class Context:
         """Decode loop only; positions [0, len(history)-1) must already hold the prompt's K/V."""
         p = self.gen_params(**kw)
         h = _i32(history)
-        out = np.empty(p.max_tokens + 2 * 8 + 4, np.int32)
+        out = np.empty(p.max_tokens + 2 * MAX_VERIFY + 4, np.int32)
         st = _lib.GenStats()
         n = _lib.lib().sd_decode(self.h, C.byref(p), h.ctypes.data, h.size, first_token, out.ctypes.data, out.size,
                                  C.byref(st))

@@ -33,6 +33,8 @@ sys.path.insert(0, ROOT)
 METRIC = "Mistral-7B Q4_0 spec-decode tok/s @1/2/4/8 B200; W4A8 GEMV HBM GB/s"
 UNIT = "tok/s"
 PROMPT_LEN, GEN_TOKENS, NGRAM_N, SPEC_K = 1024, 512, 3, 4
+# self-speculative decode, K = 8 drafts from the first 8 layers, 32768-position KV
+SELF_CTX, SELF_TOKENS, SELF_K, SELF_LAYERS = 32768, 256, 8, 8
 def kernels_per_iter(persistent: bool, tp_peer: bool = False, tp_nccl: bool = False, layers: int = 32) -> int:
     """Our kernel launches per n-gram decode iteration: prepare + commit around one verify forward, which
     is k_forward + argmax on the persistent path, or embed-norm, 8 per layer, LM head + argmax per op.
@@ -242,15 +244,101 @@ def run_gemv(args):
                       "frac": round(best / peaks.get("hbm_gbs", 6650.0), 4)}), flush=True)
 
 
+def run_selfspec(args, ctx, rank, world, local, dist, tp, peaks):
+    """self-speculative decode (K = 8 drafts through the first 8 layers and the LM head,
+    a 9-token verify), KV ring pre-filled to 32768 positions of uniform-random tokens by the device
+    prefill, temp 0.7 / top-k 40 / top-p 0.9 / repetition penalty 1.1, fixed seed, 256 tokens per step.
+    A step = one 256-token decode from the filled ring (the prefix K/V of target and drafter stay resident)."""
+    import torch
+    rng = np.random.default_rng(4321)
+    prompt = rng.integers(3, 32000, SELF_CTX).tolist()
+    t = time.perf_counter()
+    ctx.prefill(prompt[:-1], 0)
+    lg, am = ctx.forward([prompt[-1]], SELF_CTX - 1, want_logits=False)
+    t_prefill = time.perf_counter() - t
+    first = int(am[0])
+    hist = prompt + [first]
+    kw = dict(mode="self", max_tokens=args.tokens, temp=0.7, top_k=40, top_p=0.9, rep_penalty=1.1,
+              ignore_eos=True, spec_k=SELF_K, draft_layers=SELF_LAYERS, seed=99)
+    t = time.perf_counter()
+    ctx.decode(hist, first, **kw)             # warm-up 1 also fills the drafter's K/V for the prefix
+    t_draft_prefill = time.perf_counter() - t
+    kw["reuse_draft_kv"] = True
+    for _ in range(args.warmup - 1):
+        ctx.decode(hist, first, **kw)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    clocks = ClockSampler(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    tokens = iters = drafted = accepted = 0
+    for _ in range(args.steps):
+        out, st = ctx.decode(hist, first, **kw)
+        tokens += len(out)
+        iters += st["total_iterations"]
+        drafted += st["total_draft"]
+        accepted += st["total_accepted"]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        tt = torch.tensor([ms, float(tokens)], device="cuda", dtype=torch.float64)
+        mx = tt.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = tt.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_max, tokens_all = float(mx[0]), (float(tokens) if tp else float(sm[1]))
+    else:
+        ms_max, tokens_all = ms, float(tokens)
+    value = tokens_all / (ms_max * 1e-3)
+    # weight + KV bytes per iteration: K drafter passes (8 layers + LM head) and a 9-token verify that runs
+    # as an 8-token and a 1-token forward
+    layer_b = (BYTES_PER_FORWARD - 73_728_000) // 32
+    draft_b = SELF_LAYERS * layer_b + 73_728_000 + SELF_LAYERS * 2 * 1024 * 2 * SELF_CTX
+    verify_b = 2 * (BYTES_PER_FORWARD + KV_BYTES_PER_POS * SELF_CTX)
+    it_per_s = (iters / args.steps) / (ms / args.steps * 1e-3)
+    step_roof = {"bytes_per_iteration": SELF_K * draft_b + verify_b, "iterations_per_s": round(it_per_s, 2)}
+    step_roof["achieved_gbs"] = round(step_roof["bytes_per_iteration"] * it_per_s / 1e9, 1)
+    step_roof["frac_of_hbm"] = round(step_roof["achieved_gbs"] / peaks.get("hbm_gbs", 6650.0), 4)
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+                "scaling": "strong" if tp else "weak", "vs_baseline": None,
+                "dtype": "int8 x int4 -> int32 MMA, fp32 accumulate",
+                "data": "synthetic: seeded random-init Q4_0 weights of the Mistral-7B-v0.2 architecture, "
+                        "uniform-random token ids",
+                "config": {"workload": "BASELINE config 4: self-speculative decode K=8 (drafter = first 8 layers "
+                                       "+ LM head), KV pre-filled to 32768 positions, temp 0.7 top-k 40 top-p 0.9 "
+                                       "rep 1.1, seed 99, 256 generated tokens per step",
+                           "model": "Mistral-7B-v0.2 (32 x 4096, FFN 14336, 32/8 heads, vocab 32000) Q4_0",
+                           "global_batch": 1 if tp else world, "seq_len": SELF_CTX + args.tokens,
+                           "parallelism": ((f"tp{world} ({args.tp_allreduce} all-reduce)" if tp else f"dp{world}")
+                                           if world > 1 else "single GPU"),
+                           "l2": "no flush: each forward streams >= 1 GB of weights and K/V (> 126 MB L2)"},
+                "acceptance_rate": round((accepted - iters) / drafted, 4) if drafted else None,
+                "tokens_per_iteration": round(tokens / max(iters, 1), 3),
+                "step_roofline": step_roof, "clocks": clk,
+                "setup_s": {"prefill_32k": round(t_prefill, 2), "first_decode_with_drafter_prefill": round(t_draft_prefill, 2)},
+                "gpu_launches": int(iters * (SELF_K * 3 + 2 * 2 + 1 + 1 + 2))}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--tokens", type=int, default=GEN_TOKENS)
+    ap.add_argument("--tokens", type=int, default=None, help="generated tokens per step (default: the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="specdec", choices=["specdec", "gemv"])
+    ap.add_argument("--workload", default="specdec", choices=["specdec", "selfspec", "gemv"],
+                    help="specdec = BASELINE config 3 (the default line), selfspec = config 4, gemv = config 1")
     ap.add_argument("--forward-kernel", type=int, default=None, choices=[0, 1],
                     help="1 = one persistent kernel per forward, 0 = one kernel per op (default: library default)")
     ap.add_argument("--parallel", default="dp", choices=["tp", "dp"],
@@ -261,6 +349,8 @@ def main():
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--S", type=int, default=0)
     args = ap.parse_args()
+    if args.tokens is None:
+        args.tokens = SELF_TOKENS if args.workload == "selfspec" else GEN_TOKENS
     if args.workload == "gemv":
         run_gemv(args)
         return
@@ -296,13 +386,22 @@ def main():
             uid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         comm = NcclComm(bytes(uid.cpu().numpy().tobytes()), world, rank, local)
-    ctx = Context(path, device=local, max_seq=PROMPT_LEN + args.tokens + 64, forward_kernel=args.forward_kernel,
+    n_ctx = SELF_CTX if args.workload == "selfspec" else PROMPT_LEN
+    ctx = Context(path, device=local, max_seq=n_ctx + args.tokens + 64, forward_kernel=args.forward_kernel,
                   tp_rank=rank if tp else 0, tp_size=world if tp else 1, nccl_comm=comm.handle if comm else 0)
     if tp and args.tp_allreduce == "peer":
         # all-reduces inside the norm kernels over NVLink (peer memory) instead of NCCL
         handles = [None] * world
         dist.all_gather_object(handles, ctx.tp_handle())
         ctx.tp_connect(handles)
+    if args.workload == "selfspec":
+        run_selfspec(args, ctx, rank, world, local, dist, tp, peaks)
+        ctx.close()
+        if comm:
+            comm.close()
+        if dist:
+            dist.destroy_process_group()
+        return
     prompt = config3_prompt()
     first, _ = ctx.generate(prompt, mode="greedy", max_tokens=1, temp=0.0, rep_penalty=1.0, ignore_eos=True)
     hist = prompt + [first[0]]

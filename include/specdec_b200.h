@@ -24,6 +24,8 @@ extern "C" {
 #endif
 
 #define SD_ABI_VERSION 1
+/* Most tokens one verify forward carries (current token + up to 15 drafts). */
+#define SD_MAX_VERIFY 16
 
 #if defined(__GNUC__)
 #define SD_API __attribute__((visibility("default")))
@@ -182,7 +184,8 @@ SD_API void *sd_ctx_stream(sd_ctx *ctx);
  * and the LM head.  Replaces metal_forward (S=1, mistral/mistral_infer.m:31-92),
  * metal_forward_batch (S=K+1, :103-179) with the CPU logits of metal_spec_verify (:224-248), and
  * spec_verify (mistral/speculative.h:81-105).  logits: host [S][vocab] or NULL; argmax: host [S]
- * (first index on ties, mistral/mistral_model.h:1136-1143) or NULL.  S <= max_batch. */
+ * (first index on ties, mistral/mistral_model.h:1136-1143) or NULL.  S <= SD_MAX_VERIFY; a batch wider
+ * than max_batch runs as consecutive forwards, with logits identical to one wide forward. */
 SD_API int sd_forward(sd_ctx *ctx, const int32_t *tokens, int S, int pos, float *logits, int32_t *argmax);
 /* Same with device buffers, stream-ordered, no host synchronisation. */
 SD_API int sd_forward_dev(sd_ctx *ctx, const int32_t *tokens_dev, int S, int pos, float *logits_dev,
@@ -230,12 +233,14 @@ typedef struct {
     float rep_penalty;        /* --rep-penalty */
     int rep_window;           /* --rep-window */
     int ignore_eos;
-    int spec_k;               /* drafts per iteration (<= 7 with max_batch 8) */
+    int spec_k;               /* drafts per iteration, <= SD_MAX_VERIFY - 1 */
     int ngram_n;              /* n-gram order */
     int draft_layers;         /* self-speculative drafter depth */
     int history_has_current;  /* 1 = reference n-gram wiring (history ends with the current token) */
     int bonus_mode;           /* SD_BONUS_* */
     uint64_t seed;            /* Philox seed replacing arc4random */
+    int reuse_draft_kv;       /* sd_decode, self-speculative: the drafter's K/V of history[0 .. n_hist-2] is already
+                                 in place (an earlier sd_decode of the same history), skip its prefill */
 } sd_gen_params;
 
 typedef struct {

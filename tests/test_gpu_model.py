@@ -68,16 +68,19 @@ def test_forward_logits_match_oracle(ctx, omodel):
     omodel.free_kv(kv)
 
 
-def test_verify_batch_bitwise_equals_single_token_forwards(ctx):
-    """S=K+1 verify rows are bit-identical to S=1 decode rows (batch invariance)."""
-    rng = np.random.default_rng(1)
-    prompt = rng.integers(3, ctx.vocab, 9).tolist()
+@pytest.mark.parametrize("S", [5, 9, 12, 16])
+def test_verify_batch_bitwise_equals_single_token_forwards(ctx, S):
+    """S=K+1 verify rows are bit-identical to S=1 decode rows (batch invariance); batches wider than
+    one forward (S > 8) run as consecutive forwards and keep the property."""
+    rng = np.random.default_rng(1 + S)
+    prompt = rng.integers(3, ctx.vocab, 4 + S).tolist()
     ctx.prefill(prompt[:4], 0)
-    single = [ctx.forward([t], 4 + i)[0][0] for i, t in enumerate(prompt[4:])]
+    single = [ctx.forward([t], 4 + i) for i, t in enumerate(prompt[4:])]
     ctx.prefill(prompt[:4], 0)
-    batch, _ = ctx.forward(prompt[4:], 4)
-    for i in range(5):
-        np.testing.assert_array_equal(batch[i].view(np.uint32), single[i].view(np.uint32))
+    batch, am = ctx.forward(prompt[4:], 4)
+    for i in range(S):
+        np.testing.assert_array_equal(batch[i].view(np.uint32), single[i][0][0].view(np.uint32))
+        assert am[i] == single[i][1][0]
 
 
 def _near_tie_ok(gpu, ref, omodel, prompt, rep_penalty=1.0, rep_window=64):
@@ -118,7 +121,7 @@ def test_greedy_with_repetition_penalty_matches_oracle(ctx, omodel):
     assert _near_tie_ok(gpu, ref, omodel, prompt, rep_penalty=1.1)
 
 
-@pytest.mark.parametrize("K", [1, 4, 7])
+@pytest.mark.parametrize("K", [1, 4, 7, 8, 12])
 def test_ngram_spec_equals_greedy(ctx, K):
     """temp-0 n-gram speculative output is token-identical to greedy decode (same engine)."""
     rng = np.random.default_rng(10 + K)
@@ -132,15 +135,34 @@ def test_ngram_spec_equals_greedy(ctx, K):
     assert st["total_iterations"] > 0
 
 
-def test_self_spec_equals_greedy(ctx):
+@pytest.mark.parametrize("K", [4, 8])
+def test_self_spec_equals_greedy(ctx, K):
+    """K = 8 is the self-speculative configuration (a 9-token verify, two forwards)."""
     rng = np.random.default_rng(21)
     prompt = rng.integers(3, ctx.vocab, 24).tolist()
     greedy, _ = ctx.generate(prompt, mode="greedy", max_tokens=30, temp=0.0, rep_penalty=1.0, ignore_eos=True)
     spec, st = ctx.generate(prompt, mode="self", max_tokens=30, temp=0.0, rep_penalty=1.0, ignore_eos=True,
-                            spec_k=4, draft_layers=1)
+                            spec_k=K, draft_layers=1)
     n = min(len(greedy), len(spec))
     assert n >= 29 and spec[:n] == greedy[:n]
-    assert st["total_draft"] == 4 * st["total_iterations"]
+    assert st["total_draft"] == K * st["total_iterations"]
+
+
+def test_self_spec_k8_sampling_is_seeded(ctx):
+    """The self-speculative sampling configuration (K = 8, temp 0.7, top-k 40, top-p 0.9, repetition
+    penalty 1.1): the same seed gives the same tokens, and acceptance stays within its bounds."""
+    rng = np.random.default_rng(22)
+    prompt = rng.integers(3, ctx.vocab, 40).tolist()
+    kw = dict(mode="self", max_tokens=40, temp=0.7, top_k=40, top_p=0.9, rep_penalty=1.1, ignore_eos=True,
+              spec_k=8, draft_layers=1, seed=1234)
+    a, sa = ctx.generate(prompt, **kw)
+    b, sb = ctx.generate(prompt, **kw)
+    assert a == b
+    for k in ("n_generated", "total_draft", "total_accepted", "total_iterations"):
+        assert sa[k] == sb[k]
+    assert len(a) >= 40 and all(0 <= t < ctx.vocab for t in a)
+    assert sa["total_draft"] == 8 * sa["total_iterations"]
+    assert 0 <= sa["total_accepted"] - sa["total_iterations"] <= sa["total_draft"]
 
 
 def test_ngram_spec_matches_oracle_loop(ctx, omodel):
@@ -216,7 +238,7 @@ def test_bad_inputs_rejected(ctx):
     with pytest.raises(SpecDecError):
         ctx.forward([ctx.vocab + 5], 0)
     with pytest.raises(SpecDecError):
-        ctx.forward([1] * 9, 0)        # more than max_batch tokens
+        ctx.forward([1] * 17, 0)       # more than SD_MAX_VERIFY tokens
     with pytest.raises(SpecDecError):
         ctx.forward([1], 1024)         # past the KV ring
     assert ctx.device_error() == 0
@@ -233,11 +255,13 @@ def test_persistent_forward_bitwise_equals_per_op_kernels(mini, max_seq):
         assert fused.info.forward_kernel == 1
         assert perop.info.forward_kernel == 0
         rng = np.random.default_rng(7)
-        prompt = rng.integers(3, fused.vocab, 53).tolist()
+        sizes = (1, 5, 8, 3, 12)
+        n0 = min(45, max_seq - sum(sizes))   # the last forward ends at the ring's last slot when short
+        prompt = rng.integers(3, fused.vocab, n0).tolist()
         for c in (fused, perop):
-            c.prefill(prompt[:45], 0)
-        pos = 45
-        for S in (1, 5, 8, 3):
+            c.prefill(prompt, 0)
+        pos = n0
+        for S in sizes:
             toks = rng.integers(3, fused.vocab, S).tolist()
             a, am_a = fused.forward(toks, pos)
             b, am_b = perop.forward(toks, pos)
@@ -252,3 +276,35 @@ def test_persistent_forward_bitwise_equals_per_op_kernels(mini, max_seq):
     finally:
         fused.close()
         perop.close()
+
+
+def test_long_context_verify_matches_oracle(mini, oracle):
+    """A 9-token verify after a 33K-token prefill (attention chunks of 128 slots, as in the 32K-context
+    self-speculative configuration): the device's K/V ring is loaded into the oracle's ring, then each verify
+    token's logits are checked against the oracle's single-token forward at the same position."""
+    from anetransformers_b200 import gguf as G
+    from anetransformers_b200.engine import Context
+    n_ctx, S, max_seq = 33000, 9, 33024
+    rng = np.random.default_rng(41)
+    ctx = Context(mini, max_seq=max_seq)
+    om = oracle.OracleModel(G.GGUFFile(mini), max_seq=max_seq)
+    kv = om.new_kv()
+    try:
+        toks = rng.integers(3, ctx.vocab, n_ctx + S).tolist()
+        ctx.prefill(toks[:n_ctx], 0)
+        lg, am = ctx.forward(toks[n_ctx:], n_ctx)
+        for layer in range(om.cfg.n_layers):
+            k, v = ctx.kv_read(layer, 0, n_ctx)
+            ok, ov = om.kv_arrays(kv, layer)
+            ok[:n_ctx] = k
+            ov[:n_ctx] = v
+        for i in range(S):
+            ref = om.forward(kv, toks[n_ctx + i], n_ctx + i)
+            assert rel_err(lg[i], ref) < LOGIT_RTOL, i
+            s = np.sort(ref)
+            if s[-1] - s[-2] > 1e-3 * np.max(np.abs(ref)):
+                assert am[i] == int(np.argmax(ref)), i
+    finally:
+        om.free_kv(kv)
+        om.close()
+        ctx.close()
