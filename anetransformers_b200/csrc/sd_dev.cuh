@@ -396,13 +396,15 @@ __device__ __forceinline__ float q4_0_value(const uint8_t* blk, int e) {
 // ---------------------------------------------------------------------------------------------
 // Attention work item (kv head, chunk) for a group of 8 warps (256 threads), on the tensor cores.
 //
-// Query rows r = 4*s + h (token s < 8, query head h of the kv head: 32 rows = two 16-row m-tiles) and
-// a sub-block of 32 positions.  Scores S = Q K^T and outputs O = P V use mma.m16n8k16 (f16 inputs,
-// f32 accumulate).  K and V are fp16 already; Q (fp32) and the probabilities P (fp32) are split into
-// a high and a low fp16 part and both are multiplied, so products keep ~22 bits (fp32-class results).
-// Warp w owns m-tile w/4 (tokens 4*(w/4) .. +3) and quarter w%4: score columns 8*(w%4) .. +7 of the
-// sub-block, output dims 32*(w%4) .. +31.  The online softmax (mistral/mistral_model.h:362-487
-// semantics, exp of score minus running max) runs per row between the two products.
+// Query rows r = 4*s + h (token s < 8, query head h of the kv head: 32 rows = four 8-row n-tiles).
+// The products run transposed, positions x rows: scores S^T = K Q^T and outputs O^T = V^T P^T, with
+// mma.m16n8k16 (f16 inputs, f32 accumulate).  K and V are fp16 already; Q (fp32) and the probabilities
+// P (fp32) are split into a high and a low fp16 part and both are multiplied, so products keep ~22 bits
+// (fp32-class results).  Warp w owns n-tile w & 3 (tokens 2*(w&3), +1) and position half w >> 2 of each
+// 32-position sub-block (16 positions, one m-tile): it keeps its own online softmax (mistral/
+// mistral_model.h:362-487 semantics, exp of score minus running max) and all 128 output dims in
+// registers, so the warps meet only to stage K/V and, at the end of the item, to merge the two
+// position halves in a fixed order.
 // ---------------------------------------------------------------------------------------------
 constexpr int kHD = 128;        // head_dim
 constexpr int kGQA = 4;         // query heads per kv head
@@ -410,23 +412,21 @@ constexpr int kSub = 32;        // positions per sub-block
 constexpr int kAttnThreads = 256;
 constexpr int kQRows = kMaxS * kGQA;  // 32
 constexpr int kQStride = kHD + 8;     // halves per Q / K / V row (conflict-free ldmatrix rows)
-constexpr int kSStride = kSub + 4;    // floats per score row
+constexpr int kXStride = kHD + 4;     // floats per row of the merge buffer
 
 struct AttnSmem {
     __half* qh;     // [kQRows][kQStride] high part of q
     __half* ql;     // [kQRows][kQStride] low part
     __half* kk;     // [kSub][kQStride]  K sub-block (position-major)
     __half* vv;     // [kSub][kQStride]  V sub-block (position-major; fragments by ldmatrix.trans)
-    float* st;      // [kQRows][kSStride] scores, then probabilities
-    float* rm;      // [kQRows] running max
-    float* rl;      // [kQRows] running sum
-    float* rc;      // [kQRows] correction of the last update
+    float* xo;      // [kQRows][kXStride] + [kQRows][2]: second-half partials at the end of an item (over kk, vv)
 };
 
 __host__ __device__ constexpr size_t attn_smem_bytes() {
-    return (size_t)2 * kQRows * kQStride * 2 + (size_t)2 * kSub * kQStride * 2 + (size_t)kQRows * kSStride * 4 +
-           (size_t)3 * kQRows * 4;
+    return (size_t)2 * kQRows * kQStride * 2 + (size_t)2 * kSub * kQStride * 2;
 }
+static_assert((size_t)kQRows * kXStride * 4 + (size_t)kQRows * 2 * 4 <= (size_t)2 * kSub * kQStride * 2,
+              "merge buffer fits over the K/V sub-block");
 
 __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
     AttnSmem s;
@@ -434,10 +434,7 @@ __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
     s.ql = s.qh + kQRows * kQStride;
     s.kk = s.ql + kQRows * kQStride;
     s.vv = s.kk + kSub * kQStride;
-    s.st = reinterpret_cast<float*>(s.vv + kSub * kQStride);
-    s.rm = s.st + kQRows * kSStride;
-    s.rl = s.rm + kQRows;
-    s.rc = s.rl + kQRows;
+    s.xo = reinterpret_cast<float*>(s.kk);
     return s;
 }
 
@@ -459,6 +456,13 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
+}
+
+// Transpose of an 8x8 b16 matrix held one row pair per lane (lane 4g+t: row g, columns 2t, 2t+1).
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
 }
 
 // Start moving bytes (16-byte aligned, a multiple of 16) of global memory into L2; no completion.
@@ -531,8 +535,8 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
                           const AttnSmem& sm, int tid, Sync gsync) {
     const int warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int mt = warp >> 2, qw = warp & 3;
-    const bool active = mt * 4 < nv;  // this m-tile holds a valid token
+    const int nt = warp & 3, ph = warp >> 2;
+    const bool active = 2 * nt < nv;  // this n-tile holds a valid token
     const int p0 = max(c * a.chunk, lo_min);
     const int p1 = min((c + 1) * a.chunk, hi_max + 1);  // exclusive
     const int lo_max = max(0, pos + nv - a.max_seq);      // window start of the last valid token
@@ -551,156 +555,105 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
     const uint32_t col = (uint32_t)(kvh * kHD + (tid & 15) * 8);
     attn_load_kv(a, col, p0, p1, tid, kr, vr);
     gsync();  // the previous item is done with the shared buffers
-    {
-        // query rows -> fp16 high/low parts; first K/V sub-block; running statistics
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = tid + u * kAttnThreads;
-            const int r = i >> 5, d4 = (i & 31) * 4;
-            uint32_t h0, l0, h1, l1;
-            split_f16x2(qv[u].x, qv[u].y, h0, l0);
-            split_f16x2(qv[u].z, qv[u].w, h1, l1);
-            *reinterpret_cast<uint2*>(sm.qh + r * kQStride + d4) = make_uint2(h0, h1);
-            *reinterpret_cast<uint2*>(sm.ql + r * kQStride + d4) = make_uint2(l0, l1);
-        }
-        attn_store_kv(sm, tid, kr, vr);
-        if (tid < kQRows) {
-            sm.rm[tid] = -INFINITY;
-            sm.rl[tid] = 0.f;
-        }
+    for (int u = 0; u < 4; ++u) {
+        const int i = tid + u * kAttnThreads;
+        const int r = i >> 5, d4 = (i & 31) * 4;
+        uint32_t h0, l0, h1, l1;
+        split_f16x2(qv[u].x, qv[u].y, h0, l0);
+        split_f16x2(qv[u].z, qv[u].w, h1, l1);
+        *reinterpret_cast<uint2*>(sm.qh + r * kQStride + d4) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(sm.ql + r * kQStride + d4) = make_uint2(l0, l1);
     }
-    // ldmatrix row addresses.  Q (A operand, rows mt*16..+15): lanes 0-7 rows 0-7 dims +0, 8-15 rows 8-15
-    // dims +0, 16-23 rows 0-7 dims +8, 24-31 rows 8-15 dims +8.  K (B operand of the scores, positions
-    // qw*8..+7): lanes 8i..8i+7 give position lane&7 at dims +8i (two k-steps per load).  V (B operand
-    // of P V, transposed load): lanes 0-7 positions 0-7, 8-15 positions 8-15 of the k-step at dims d0,
-    // 16-31 the same at dims d0+8.
+    attn_store_kv(sm, tid, kr, vr);
+    // ldmatrix row addresses (lane = 8 * lq + lr gives a row of matrix lq).
+    //   K (A of S^T, positions x dims): matrices (pos +0, dims +0), (+8, +0), (+0, +8), (+8, +8).
+    //   Q (B of S^T, dims x rows = Q rows): matrices at dims +0, +8, +16, +24 (two k-steps per load).
+    //   V (A of O^T via .trans, dims x positions): matrices (pos +0, dims +0), (+0, +8), (+8, +0), (+8, +8).
     const int lr = lane & 7, lq = lane >> 3;
-    const uint32_t qh_a = smem_u32(sm.qh + (mt * 16 + lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8);
+    const uint32_t k_a = smem_u32(sm.kk + (ph * 16 + lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8);
+    const uint32_t qh_a = smem_u32(sm.qh + (nt * 8 + lr) * kQStride + lq * 8);
     const uint32_t ql_a = qh_a + (uint32_t)(kQRows * kQStride * 2);
-    const uint32_t k_a = smem_u32(sm.kk + (qw * 8 + lr) * kQStride + lq * 8);
-    const uint32_t v_a = smem_u32(sm.vv + (lr + (lq & 1) * 8) * kQStride + qw * 32 + (lq >> 1) * 8);
-    float o[4][4];
+    const uint32_t v_a = smem_u32(sm.vv + (ph * 16 + lr + (lq >> 1) * 8) * kQStride + (lq & 1) * 8);
+    // rows 2t, 2t+1 of the n-tile: running max, lane-partial sum (positions g, g+8), outputs O^T
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
 #pragma unroll
-    for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     for (int sb = p0; sb < p1; sb += kSub) {
         const bool more = sb + kSub < p1;
         if (more) attn_load_kv(a, col, sb + kSub, p1, tid, kr, vr);  // lands while this sub-block is computed
-        // positions outside some valid row's window occur only in edge sub-blocks (rows of tokens >= nv are
-        // never read)
-        const bool edge = sb + kSub > p1 || sb + kSub - 1 > pos || sb < lo_max;
         gsync();
-        // ---- scores of rows mt*16 .. +15, positions sb + 8*qw .. +7 ----
         if (active) {
-            // high and low parts of q accumulate in separate chains, added at the end
+            // ---- S^T: positions sb + 16 ph + (g, g+8) x rows 8 nt + (2t, 2t+1) ----
             float sc[4] = {0.f, 0.f, 0.f, 0.f}, sl[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int k2 = 0; k2 < kHD / 32; ++k2) {
-                uint32_t b[4];
-                ldsm_x4(k_a + k2 * 64, b[0], b[1], b[2], b[3]);
+                uint32_t bh[4], bl[4];
+                ldsm_x4(qh_a + k2 * 64, bh[0], bh[1], bh[2], bh[3]);
+                ldsm_x4(ql_a + k2 * 64, bl[0], bl[1], bl[2], bl[3]);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const uint32_t off = (k2 * 2 + h) * 32;
-                    uint32_t q0, q1, q2, q3;
-                    ldsm_x4(qh_a + off, q0, q1, q2, q3);
-                    mma_f16(sc, q0, q1, q2, q3, b[2 * h], b[2 * h + 1]);
-                    ldsm_x4(ql_a + off, q0, q1, q2, q3);
-                    mma_f16(sl, q0, q1, q2, q3, b[2 * h], b[2 * h + 1]);
+                    uint32_t k0, k1, k2r, k3;
+                    ldsm_x4(k_a + (k2 * 2 + h) * 32, k0, k1, k2r, k3);
+                    mma_f16(sc, k0, k1, k2r, k3, bh[2 * h], bh[2 * h + 1]);
+                    mma_f16(sl, k0, k1, k2r, k3, bl[2 * h], bl[2 * h + 1]);
                 }
             }
 #pragma unroll
             for (int e = 0; e < 4; ++e) sc[e] += sl[e];
-            // mask: row r -> token r/4; column -> position
-            if (edge) {
+            // positions outside some valid row's window occur only in edge sub-blocks
+            if (sb + kSub > p1 || sb + kSub - 1 > pos || sb < lo_max) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int r = mt * 16 + g + (e >> 1) * 8, s = r >> 2;
-                    const int p = sb + qw * 8 + 2 * t + (e & 1);
+                    const int p = sb + ph * 16 + g + (e >> 1) * 8;
+                    const int s = 2 * nt + (t >> 1);  // token of rows 2t, 2t+1
                     const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
-                    const bool ok = s < nv && p < p1 && p >= lo && p <= hi;
-                    if (!ok) sc[e] = -INFINITY;
+                    if (!(s < nv && p < p1 && p >= lo && p <= hi)) sc[e] = -INFINITY;
                 }
             }
-            float* sr = sm.st + (mt * 16 + g) * kSStride + qw * 8 + 2 * t;
-            *reinterpret_cast<float2*>(sr) = make_float2(sc[0], sc[1]);
-            *reinterpret_cast<float2*>(sr + 8 * kSStride) = make_float2(sc[2], sc[3]);
-        }
-        gsync();
-        // ---- online softmax: warp w updates rows 4w .. 4w+3 (all of token w), lane = position; the four
-        // rows' reductions are interleaved ----
-        if (warp >= nv) {  // no token: zero probabilities and correction (rows stay unused)
+            // ---- online softmax over this warp's positions: rows 2t (sc 0, 2), 2t+1 (sc 1, 3) ----
+            float x0 = fmaxf(sc[0], sc[2]), x1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) sm.st[(warp * 4 + k) * kSStride + lane] = 0.f;
-            if (lane < 4) sm.rc[warp * 4 + lane] = 0.f;
-        } else {
-            float v[4], mo[4], mx[4], e[4], corr[4], es[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                v[k] = sm.st[(warp * 4 + k) * kSStride + lane];
-                mo[k] = sm.rm[warp * 4 + k];
-                mx[k] = v[k];
+            for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
+                x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
             }
+            const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+            // a row with nothing valid yet keeps m = -inf and contributes nothing
+            const float c0 = (m0 == -INFINITY) ? 0.f : exp_fast(m0 - n0);
+            const float c1 = (m1 == -INFINITY) ? 0.f : exp_fast(m1 - n1);
+            float pr[4];
+            pr[0] = sc[0] == -INFINITY ? 0.f : exp_fast(sc[0] - n0);
+            pr[1] = sc[1] == -INFINITY ? 0.f : exp_fast(sc[1] - n1);
+            pr[2] = sc[2] == -INFINITY ? 0.f : exp_fast(sc[2] - n0);
+            pr[3] = sc[3] == -INFINITY ? 0.f : exp_fast(sc[3] - n1);
+            m0 = n0;
+            m1 = n1;
+            l0 = l0 * c0 + (pr[0] + pr[2]);
+            l1 = l1 * c1 + (pr[1] + pr[3]);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], o));
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float mn = fmaxf(mo[k], mx[k]);
-                // a row with nothing valid yet keeps m = -inf and contributes nothing
-                e[k] = (mn == -INFINITY || v[k] == -INFINITY) ? 0.f : exp_fast(v[k] - mn);
-                corr[k] = (mn == -INFINITY || mo[k] == -INFINITY) ? 0.f : exp_fast(mo[k] - mn);
-                mx[k] = mn;
-                es[k] = e[k];
+            for (int i = 0; i < 8; ++i) {
+                o[i][0] *= c0;
+                o[i][1] *= c1;
+                o[i][2] *= c0;
+                o[i][3] *= c1;
             }
+            // P^T (positions x rows) -> B fragments of O^T += V^T P^T: b0 from positions g, b1 from g + 8
+            uint32_t ph0, pl0, ph1, pl1;
+            split_f16x2(pr[0], pr[1], ph0, pl0);
+            split_f16x2(pr[2], pr[3], ph1, pl1);
+            ph0 = movm_t(ph0);
+            pl0 = movm_t(pl0);
+            ph1 = movm_t(ph1);
+            pl1 = movm_t(pl1);
+            // ---- O^T (dims 16 i + (g, g+8) x rows 2t, 2t+1) ----
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) es[k] += __shfl_xor_sync(0xffffffffu, es[k], o);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) sm.st[(warp * 4 + k) * kSStride + lane] = e[k];
-            if (lane < 4) {
-                const int r = warp * 4 + lane;
-                const float c = lane == 0 ? corr[0] : lane == 1 ? corr[1] : lane == 2 ? corr[2] : corr[3];
-                const float sum = lane == 0 ? es[0] : lane == 1 ? es[1] : lane == 2 ? es[2] : es[3];
-                const float mn = lane == 0 ? mx[0] : lane == 1 ? mx[1] : lane == 2 ? mx[2] : mx[3];
-                sm.rl[r] = sm.rl[r] * c + sum;
-                sm.rm[r] = mn;
-                sm.rc[r] = c;
-            }
-        }
-        gsync();
-        // ---- O (rows mt*16 .., dims 32*qw ..) = O * corr + P V ----
-        if (active) {
-            const float cl = sm.rc[mt * 16 + g], chh = sm.rc[mt * 16 + g + 8];
-#pragma unroll
-            for (int n = 0; n < 4; ++n) {
-                o[n][0] *= cl;
-                o[n][1] *= cl;
-                o[n][2] *= chh;
-                o[n][3] *= chh;
-            }
-#pragma unroll
-            for (int ks = 0; ks < kSub / 16; ++ks) {
-                const float* p0r = sm.st + (mt * 16 + g) * kSStride + ks * 16 + 2 * t;
-                const float2 x0 = *reinterpret_cast<const float2*>(p0r);
-                const float2 x1 = *reinterpret_cast<const float2*>(p0r + 8 * kSStride);
-                const float2 x2 = *reinterpret_cast<const float2*>(p0r + 8);
-                const float2 x3 = *reinterpret_cast<const float2*>(p0r + 8 * kSStride + 8);
-                uint32_t ah[4], al[4];
-                split_f16x2(x0.x, x0.y, ah[0], al[0]);
-                split_f16x2(x1.x, x1.y, ah[1], al[1]);
-                split_f16x2(x2.x, x2.y, ah[2], al[2]);
-                split_f16x2(x3.x, x3.y, ah[3], al[3]);
-#pragma unroll
-                for (int n2 = 0; n2 < 2; ++n2) {
-                    uint32_t b[4];  // (b0, b1) of dims qw*32 + n2*16 .. +7, then of +8 .. +15
-                    ldsm_x4_t(v_a + (uint32_t)(ks * 16 * kQStride * 2 + n2 * 32), b[0], b[1], b[2], b[3]);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        mma_f16(o[2 * n2 + h], ah[0], ah[1], ah[2], ah[3], b[2 * h], b[2 * h + 1]);
-                        mma_f16(o[2 * n2 + h], al[0], al[1], al[2], al[3], b[2 * h], b[2 * h + 1]);
-                    }
-                }
+            for (int i = 0; i < 8; ++i) {
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_t(v_a + i * 32, v0, v1, v2, v3);
+                mma_f16(o[i], v0, v1, v2, v3, ph0, ph1);
+                mma_f16(o[i], v0, v1, v2, v3, pl0, pl1);
             }
         }
         if (more) {
@@ -708,23 +661,55 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
             attn_store_kv(sm, tid, kr, vr);
         }
     }
-    gsync();  // final statistics visible
-    // ---- partials of this chunk ----
-    if (active) {
+    // ---- merge the two position halves (first + second, in that order) and write the chunk partials ----
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const int r = mt * 16 + g + hh * 8, s = r >> 2, h = kvh * kGQA + (r & 3);
-            if (s >= nv) continue;
-            const size_t pi = ((size_t)s * a.n_heads + h) * a.max_chunks + c;
+    for (int o2 = 4; o2 < 32; o2 <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
+    }
+    const int r0 = nt * 8 + 2 * t;  // this lane's rows r0, r0 + 1
+    float* xml = sm.xo + kQRows * kXStride;
+    gsync();  // every warp is done with the K/V buffers
+    if (active && ph == 1) {
 #pragma unroll
-            for (int n = 0; n < 4; ++n)
-                *reinterpret_cast<float2*>(a.part_acc + pi * kHD + qw * 32 + n * 8 + 2 * t) =
-                    make_float2(o[n][hh * 2], o[n][hh * 2 + 1]);
+        for (int i = 0; i < 8; ++i) {
+            const int d = 16 * i + g;
+            sm.xo[r0 * kXStride + d] = o[i][0];
+            sm.xo[(r0 + 1) * kXStride + d] = o[i][1];
+            sm.xo[r0 * kXStride + d + 8] = o[i][2];
+            sm.xo[(r0 + 1) * kXStride + d + 8] = o[i][3];
+        }
+        if (g == 0) {
+            xml[2 * r0] = m0;
+            xml[2 * r0 + 1] = l0;
+            xml[2 * r0 + 2] = m1;
+            xml[2 * r0 + 3] = l1;
         }
     }
-    if (tid < kQRows && (tid >> 2) < nv) {
-        const int s = tid >> 2, h = kvh * kGQA + (tid & 3);
-        a.part_ml[((size_t)s * a.n_heads + h) * a.max_chunks + c] = make_float2(sm.rm[tid], sm.rl[tid]);
+    gsync();
+    if (active && ph == 0) {
+        const float bm0 = xml[2 * r0], bl0 = xml[2 * r0 + 1], bm1 = xml[2 * r0 + 2], bl1 = xml[2 * r0 + 3];
+        const float M0 = fmaxf(m0, bm0), M1 = fmaxf(m1, bm1);
+        const float fa0 = m0 == -INFINITY ? 0.f : exp_fast(m0 - M0), fb0 = bm0 == -INFINITY ? 0.f : exp_fast(bm0 - M0);
+        const float fa1 = m1 == -INFINITY ? 0.f : exp_fast(m1 - M1), fb1 = bm1 == -INFINITY ? 0.f : exp_fast(bm1 - M1);
+        const int s = 2 * nt + (t >> 1);  // token of rows r0, r0 + 1 (heads r0 & 3, +1)
+        if (s < nv) {
+            const size_t pi = ((size_t)s * a.n_heads + kvh * kGQA + (r0 & 3)) * a.max_chunks + c;
+            float* acc0 = a.part_acc + pi * kHD;
+            float* acc1 = acc0 + (size_t)a.max_chunks * kHD;  // next head, same token and chunk
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int d = 16 * i + g;
+                acc0[d] = o[i][0] * fa0 + sm.xo[r0 * kXStride + d] * fb0;
+                acc1[d] = o[i][1] * fa1 + sm.xo[(r0 + 1) * kXStride + d] * fb1;
+                acc0[d + 8] = o[i][2] * fa0 + sm.xo[r0 * kXStride + d + 8] * fb0;
+                acc1[d + 8] = o[i][3] * fa1 + sm.xo[(r0 + 1) * kXStride + d + 8] * fb1;
+            }
+            if (g == 0) {
+                a.part_ml[pi] = make_float2(M0, l0 * fa0 + bl0 * fb0);
+                a.part_ml[pi + a.max_chunks] = make_float2(M1, l1 * fa1 + bl1 * fb1);
+            }
+        }
     }
 }
 
