@@ -452,6 +452,9 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
 __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -568,11 +571,11 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
     attn_store_kv(sm, tid, kr, vr);
     // ldmatrix row addresses (lane = 8 * lq + lr gives a row of matrix lq).
     //   K (A of S^T, positions x dims): matrices (pos +0, dims +0), (+8, +0), (+0, +8), (+8, +8).
-    //   Q (B of S^T, dims x rows = Q rows): matrices at dims +0, +8, +16, +24 (two k-steps per load).
+    //   Q (B of S^T, dims x rows = Q rows): matrices at dims +0, +8 of the k-step (lanes 16-31 repeat 0-15).
     //   V (A of O^T via .trans, dims x positions): matrices (pos +0, dims +0), (+0, +8), (+8, +0), (+8, +8).
     const int lr = lane & 7, lq = lane >> 3;
     const uint32_t k_a = smem_u32(sm.kk + (ph * 16 + lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8);
-    const uint32_t qh_a = smem_u32(sm.qh + (nt * 8 + lr) * kQStride + lq * 8);
+    const uint32_t qh_a = smem_u32(sm.qh + (nt * 8 + lr) * kQStride + (lq & 1) * 8);
     const uint32_t ql_a = qh_a + (uint32_t)(kQRows * kQStride * 2);
     const uint32_t v_a = smem_u32(sm.vv + (ph * 16 + lr + (lq >> 1) * 8) * kQStride + (lq & 1) * 8);
     // rows 2t, 2t+1 of the n-tile: running max, lane-partial sum (positions g, g+8), outputs O^T
@@ -586,22 +589,16 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
         gsync();
         if (active) {
             // ---- S^T: positions sb + 16 ph + (g, g+8) x rows 8 nt + (2t, 2t+1) ----
-            float sc[4] = {0.f, 0.f, 0.f, 0.f}, sl[4] = {0.f, 0.f, 0.f, 0.f};
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int k2 = 0; k2 < kHD / 32; ++k2) {
-                uint32_t bh[4], bl[4];
-                ldsm_x4(qh_a + k2 * 64, bh[0], bh[1], bh[2], bh[3]);
-                ldsm_x4(ql_a + k2 * 64, bl[0], bl[1], bl[2], bl[3]);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t k0, k1, k2r, k3;
-                    ldsm_x4(k_a + (k2 * 2 + h) * 32, k0, k1, k2r, k3);
-                    mma_f16(sc, k0, k1, k2r, k3, bh[2 * h], bh[2 * h + 1]);
-                    mma_f16(sl, k0, k1, k2r, k3, bl[2 * h], bl[2 * h + 1]);
-                }
+            for (int ks = 0; ks < kHD / 16; ++ks) {
+                uint32_t k0, k1, k2, k3, b0, b1;
+                ldsm_x4(k_a + ks * 32, k0, k1, k2, k3);
+                ldsm_x2(qh_a + ks * 32, b0, b1);
+                mma_f16(sc, k0, k1, k2, k3, b0, b1);
+                ldsm_x2(ql_a + ks * 32, b0, b1);
+                mma_f16(sc, k0, k1, k2, k3, b0, b1);
             }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sc[e] += sl[e];
             // positions outside some valid row's window occur only in edge sub-blocks
             if (sb + kSub > p1 || sb + kSub - 1 > pos || sb < lo_max) {
 #pragma unroll
