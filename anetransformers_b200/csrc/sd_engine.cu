@@ -264,9 +264,7 @@ struct sd_ctx {
     DevCtrl* ctrl_sub = nullptr;  // [kMaxVerify] control blocks of the forwards a wide verify batch splits into
     DevCtrl* ctrl = nullptr;   // verify / decode forward
     DevCtrl* dctrl = nullptr;  // self-spec drafter chain
-    DevCtrl* ctrl_h = nullptr; // pinned staging
     int* err = nullptr;
-    int32_t* tok_h = nullptr;  // pinned token staging
     // generation
     GenState* gs = nullptr;
     GenState* gs_h = nullptr;
@@ -688,10 +686,9 @@ int set_ctrl(sd_ctx* c, DevCtrl* dst, const int32_t* tokens, int S, int pos, boo
     h.done = 0;
     if (host_tokens)
         for (int i = 0; i < S; ++i) h.tokens[i] = tokens[i];
-    *c->ctrl_h = h;
-    CK(cudaMemcpyAsync(dst, c->ctrl_h, sizeof(DevCtrl), cudaMemcpyHostToDevice, c->st), "ctrl upload");
-    if (!host_tokens && tokens)
-        CK(cudaMemcpyAsync(&dst->tokens[0], tokens, S * sizeof(int), cudaMemcpyDeviceToDevice, c->st), "tokens");
+    // the block travels as a kernel argument (copied at launch), so back-to-back stream-ordered calls
+    // never share a host staging buffer
+    CK(launch_set_ctrl(dst, h, host_tokens ? nullptr : tokens, S, c->st), "ctrl upload");
     return SD_OK;
 }
 
@@ -745,8 +742,6 @@ void sd_ctx_free(sd_ctx* c) {
     for (void* p : c->tp_opened) cudaIpcCloseMemHandle(p);
     cudaFree(c->tp_mem);
     cudaFree(c->tp_base);
-    if (c->ctrl_h) cudaFreeHost(c->ctrl_h);
-    if (c->tok_h) cudaFreeHost(c->tok_h);
     if (c->gs_h) cudaFreeHost(c->gs_h);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
@@ -889,9 +884,7 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
     cudaMemset(c->err, 0, sizeof(int));
     cudaMemset(c->x, 0, (size_t)MB * c->dim * 4);
     cudaMemset(c->y, 0, (size_t)c->ypart_max * MB * c->dim * 4);
-    if ((rc = ck(cudaMallocHost(&c->ctrl_h, sizeof(DevCtrl)), "pinned")) ||
-        (rc = ck(cudaMallocHost(&c->tok_h, sizeof(int32_t) * 4096), "pinned")) ||
-        (rc = ck(cudaMallocHost(&c->gs_h, sizeof(GenState)), "pinned")))
+    if ((rc = ck(cudaMallocHost(&c->gs_h, sizeof(GenState)), "pinned")))
         return bail(rc);
     if (c->tp_size > 1) {
         c->tp_buf = (size_t)c->ypart_max * MB * c->dim;
@@ -1073,7 +1066,6 @@ int sd_prefill(sd_ctx* c, const int32_t* tokens, int n, int start_pos) {
         const int S = std::min(c->MB, n - i);
         if ((rc = set_ctrl(c, c->ctrl, tokens + i, S, start_pos + i, true))) return rc;
         if ((rc = run_forward(c, S))) return rc;
-        CK(cudaStreamSynchronize(c->st), "prefill");  // ctrl_h staging is reused
     }
     return finish(c);
 }
@@ -1319,7 +1311,6 @@ int sd_decode(sd_ctx* c, const sd_gen_params* gp, const int32_t* history, int n_
             const int S = std::min(c->MB, n_hist - 1 - i);
             if ((rc = set_ctrl(c, c->dctrl, history + i, S, i, true))) return rc;
             if ((rc = enqueue_forward(c, S, dl, c->dkc, c->dvc, c->dctrl, false))) return rc;
-            CK(cudaStreamSynchronize(c->st), "draft prefill");
         }
         c->draft_kv_hist = n_hist - 1;
         c->draft_kv_layers = dl;
@@ -1370,7 +1361,6 @@ int sd_generate(sd_ctx* c, const sd_gen_params* gp, const int32_t* prompt, int n
         const int S = std::min(c->MB, n_prompt - i);
         if ((rc = set_ctrl(c, c->ctrl, prompt + i, S, i, true))) return rc;
         if ((rc = run_forward(c, S))) return rc;
-        CK(cudaStreamSynchronize(c->st), "prefill");
     }
     const int last = (n_prompt - 1) % c->MB;
     // first token: sample_token with repetition penalty over the prompt window (mistral_infer.m:610-621)

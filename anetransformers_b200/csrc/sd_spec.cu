@@ -680,6 +680,22 @@ __global__ void k_ctrl_slice(const DevCtrl* src, DevCtrl* dst, int off) {
     }
 }
 
+// Write a control block given by value; tokens_dev (optional) supplies its S tokens from device memory.
+__global__ void k_set_ctrl(DevCtrl* dst, DevCtrl val, const int* tokens_dev, int S) {
+    const int i = threadIdx.x;
+    if (i < kMaxVerify) dst->tokens[i] = (tokens_dev && i < S) ? tokens_dev[i] : val.tokens[i];
+    if (i == 0) {
+        dst->pos = val.pos;
+        dst->n_valid = val.n_valid;
+        dst->done = val.done;
+    }
+}
+
+cudaError_t launch_set_ctrl(DevCtrl* dst, const DevCtrl& val, const int* tokens_dev, int S, cudaStream_t st) {
+    k_set_ctrl<<<1, 32, 0, st>>>(dst, val, tokens_dev, S);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_ctrl_slice(const DevCtrl* src, DevCtrl* dst, int off, cudaStream_t st) {
     k_ctrl_slice<<<1, 32, 0, st>>>(src, dst, off);
     return cudaGetLastError();

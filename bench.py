@@ -329,6 +329,45 @@ def run_selfspec(args, ctx, rank, world, local, dist, tp, peaks):
         print(json.dumps(line), flush=True)
 
 
+def run_forward(args):
+    """Single verify forwards of S tokens (default K+1 = 5) after a ctx-token prefill, on a Mistral-7B-shaped
+    synthetic model with --layers layers (a few layers keep ncu captures small while every matrix keeps its
+    7B shape and the weights still exceed L2).  CUDA events around --steps forwards."""
+    import dataclasses
+    import torch
+    from anetransformers_b200 import gguf as G
+    from anetransformers_b200.engine import Context
+    cfg = dataclasses.replace(G.MISTRAL_7B, n_layers=args.layers)
+    path = os.path.join(tempfile.gettempdir(), f"specdec_mistral7b_{args.layers}l_q4_0_seed0.gguf")
+    if not os.path.exists(path):
+        G.write_synthetic_gguf_parallel(path, cfg, seed=0)
+    S = args.S or SPEC_K + 1
+    ctx = Context(path, max_seq=args.ctx + S * (args.steps + args.warmup) + 64, forward_kernel=args.forward_kernel)
+    rng = np.random.default_rng(5)
+    ctx.prefill(rng.integers(3, 32000, args.ctx).tolist(), 0)
+    pos = args.ctx
+    toks = torch.tensor(rng.integers(3, 32000, S), dtype=torch.int32, device="cuda")
+    for _ in range(args.warmup):
+        ctx.forward_dev(toks, pos)
+        pos += S
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ctx.forward_dev(toks, pos)   # stream-ordered, no host synchronisation between forwards
+        pos += S
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    wbytes = args.layers * 122_683_392 + 73_728_000
+    kv = args.layers * 2 * 1024 * 2 * (args.ctx + S)
+    print(json.dumps({"workload": "forward", "layers": args.layers, "S": S, "ctx": args.ctx,
+                      "forward_kernel": ctx.info.forward_kernel, "us_per_forward": round(us, 2),
+                      "weight_plus_kv_gbs": round((wbytes + kv) / (us * 1e-6) / 1e9, 1)}), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -337,8 +376,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=None, help="generated tokens per step (default: the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="specdec", choices=["specdec", "selfspec", "gemv"],
-                    help="specdec = BASELINE config 3 (the default line), selfspec = config 4, gemv = config 1")
+    ap.add_argument("--workload", default="specdec", choices=["specdec", "selfspec", "gemv", "forward"],
+                    help="specdec = BASELINE config 3 (the default line), selfspec = config 4, gemv = config 1, "
+                         "forward = single verify forwards (profiling: --layers, --S, --ctx)")
+    ap.add_argument("--layers", type=int, default=32, help="forward workload: layers of the 7B-shaped model")
+    ap.add_argument("--ctx", type=int, default=1024, help="forward workload: context positions before the forward")
     ap.add_argument("--forward-kernel", type=int, default=None, choices=[0, 1],
                     help="1 = one persistent kernel per forward, 0 = one kernel per op (default: library default)")
     ap.add_argument("--parallel", default="dp", choices=["tp", "dp"],
@@ -353,6 +395,9 @@ def main():
         args.tokens = SELF_TOKENS if args.workload == "selfspec" else GEN_TOKENS
     if args.workload == "gemv":
         run_gemv(args)
+        return
+    if args.workload == "forward":
+        run_forward(args)
         return
     args.warmup = max(args.warmup, 3)
 

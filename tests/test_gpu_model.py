@@ -308,3 +308,22 @@ def test_long_context_verify_matches_oracle(mini, oracle):
         om.free_kv(kv)
         om.close()
         ctx.close()
+
+
+def test_stream_ordered_forwards_back_to_back(ctx):
+    """sd_forward_dev calls issued back to back (no host synchronisation in between) give the same logits as
+    synchronous sd_forward calls: each call's control block reaches the device on its own."""
+    import torch
+    rng = np.random.default_rng(51)
+    toks = rng.integers(3, ctx.vocab, 14).tolist()
+    ctx.prefill(toks[:8], 0)
+    ref = [ctx.forward([t], 8 + i)[0][0] for i, t in enumerate(toks[8:])]
+    ctx.prefill(toks[:8], 0)
+    dev_toks = [torch.tensor([t], dtype=torch.int32, device="cuda") for t in toks[8:]]
+    outs = [torch.empty(1, ctx.vocab, dtype=torch.float32, device="cuda") for _ in dev_toks]
+    torch.cuda.synchronize()
+    for i, (t, o) in enumerate(zip(dev_toks, outs)):
+        ctx.forward_dev(t, 8 + i, logits_dev=o)
+    torch.cuda.synchronize()
+    for i in range(len(outs)):
+        np.testing.assert_array_equal(outs[i].cpu().numpy()[0].view(np.uint32), ref[i].view(np.uint32))
