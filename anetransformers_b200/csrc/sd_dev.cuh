@@ -400,11 +400,11 @@ __device__ __forceinline__ float q4_0_value(const uint8_t* blk, int e) {
 // The products run transposed, positions x rows: scores S^T = K Q^T and outputs O^T = V^T P^T, with
 // mma.m16n8k16 (f16 inputs, f32 accumulate).  K and V are fp16 already; Q (fp32) and the probabilities
 // P (fp32) are split into a high and a low fp16 part and both are multiplied, so products keep ~22 bits
-// (fp32-class results).  Warp w owns n-tile w & 3 (tokens 2*(w&3), +1) and position half w >> 2 of each
-// 32-position sub-block (16 positions, one m-tile): it keeps its own online softmax (mistral/
-// mistral_model.h:362-487 semantics, exp of score minus running max) and all 128 output dims in
-// registers, so the warps meet only to stage K/V and, at the end of the item, to merge the two
-// position halves in a fixed order.
+// (fp32-class results).  Warp w owns n-tile w & 3 (tokens 2*(w&3), +1) and output dims 64*(w >> 2) .. +63:
+// it computes the scores of its rows over each whole 32-position sub-block (the two warps of an n-tile
+// compute the same scores and the same online softmax -- mistral/mistral_model.h:362-487 semantics, exp
+// of score minus running max -- identically), so each warp holds its state and its 64 output dims in
+// registers and the warps meet only to stage K/V.
 // ---------------------------------------------------------------------------------------------
 constexpr int kHD = 128;        // head_dim
 constexpr int kGQA = 4;         // query heads per kv head
@@ -412,21 +412,17 @@ constexpr int kSub = 32;        // positions per sub-block
 constexpr int kAttnThreads = 256;
 constexpr int kQRows = kMaxS * kGQA;  // 32
 constexpr int kQStride = kHD + 8;     // halves per Q / K / V row (conflict-free ldmatrix rows)
-constexpr int kXStride = kHD + 4;     // floats per row of the merge buffer
 
 struct AttnSmem {
     __half* qh;     // [kQRows][kQStride] high part of q
     __half* ql;     // [kQRows][kQStride] low part
     __half* kk;     // [kSub][kQStride]  K sub-block (position-major)
     __half* vv;     // [kSub][kQStride]  V sub-block (position-major; fragments by ldmatrix.trans)
-    float* xo;      // [kQRows][kXStride] + [kQRows][2]: second-half partials at the end of an item (over kk, vv)
 };
 
 __host__ __device__ constexpr size_t attn_smem_bytes() {
     return (size_t)2 * kQRows * kQStride * 2 + (size_t)2 * kSub * kQStride * 2;
 }
-static_assert((size_t)kQRows * kXStride * 4 + (size_t)kQRows * 2 * 4 <= (size_t)2 * kSub * kQStride * 2,
-              "merge buffer fits over the K/V sub-block");
 
 __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
     AttnSmem s;
@@ -434,7 +430,6 @@ __device__ inline AttnSmem attn_smem_at(uint8_t* base) {
     s.ql = s.qh + kQRows * kQStride;
     s.kk = s.ql + kQRows * kQStride;
     s.vv = s.kk + kSub * kQStride;
-    s.xo = reinterpret_cast<float*>(s.kk);
     return s;
 }
 
@@ -538,7 +533,7 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
                           const AttnSmem& sm, int tid, Sync gsync) {
     const int warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int nt = warp & 3, ph = warp >> 2;
+    const int nt = warp & 3, dh = warp >> 2;
     const bool active = 2 * nt < nv;  // this n-tile holds a valid token
     const int p0 = max(c * a.chunk, lo_min);
     const int p1 = min((c + 1) * a.chunk, hi_max + 1);  // exclusive
@@ -574,43 +569,50 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
     //   Q (B of S^T, dims x rows = Q rows): matrices at dims +0, +8 of the k-step (lanes 16-31 repeat 0-15).
     //   V (A of O^T via .trans, dims x positions): matrices (pos +0, dims +0), (+0, +8), (+8, +0), (+8, +8).
     const int lr = lane & 7, lq = lane >> 3;
-    const uint32_t k_a = smem_u32(sm.kk + (ph * 16 + lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8);
+    const uint32_t k_a = smem_u32(sm.kk + (lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8);
     const uint32_t qh_a = smem_u32(sm.qh + (nt * 8 + lr) * kQStride + (lq & 1) * 8);
     const uint32_t ql_a = qh_a + (uint32_t)(kQRows * kQStride * 2);
-    const uint32_t v_a = smem_u32(sm.vv + (ph * 16 + lr + (lq >> 1) * 8) * kQStride + (lq & 1) * 8);
-    // rows 2t, 2t+1 of the n-tile: running max, lane-partial sum (positions g, g+8), outputs O^T
+    const uint32_t v_a = smem_u32(sm.vv + (lr + (lq >> 1) * 8) * kQStride + dh * 64 + (lq & 1) * 8);
+    // rows 2t, 2t+1 of the n-tile: running max, lane-partial sum (this lane's positions), outputs O^T
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float o[8][4];
+    float o[4][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     for (int sb = p0; sb < p1; sb += kSub) {
         const bool more = sb + kSub < p1;
         if (more) attn_load_kv(a, col, sb + kSub, p1, tid, kr, vr);  // lands while this sub-block is computed
         gsync();
         if (active) {
-            // ---- S^T: positions sb + 16 ph + (g, g+8) x rows 8 nt + (2t, 2t+1) ----
-            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            // ---- S^T: positions sb + 16 mt + (g, g+8) x rows 8 nt + (2t, 2t+1), m-tiles mt = 0, 1 ----
+            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
             for (int ks = 0; ks < kHD / 16; ++ks) {
-                uint32_t k0, k1, k2, k3, b0, b1;
-                ldsm_x4(k_a + ks * 32, k0, k1, k2, k3);
-                ldsm_x2(qh_a + ks * 32, b0, b1);
-                mma_f16(sc, k0, k1, k2, k3, b0, b1);
-                ldsm_x2(ql_a + ks * 32, b0, b1);
-                mma_f16(sc, k0, k1, k2, k3, b0, b1);
+                uint32_t bh0, bh1, bl0, bl1;
+                ldsm_x2(qh_a + ks * 32, bh0, bh1);
+                ldsm_x2(ql_a + ks * 32, bl0, bl1);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    uint32_t k0, k1, k2, k3;
+                    ldsm_x4(k_a + (uint32_t)(mt * 16 * kQStride * 2) + ks * 32, k0, k1, k2, k3);
+                    mma_f16(sc[mt], k0, k1, k2, k3, bh0, bh1);
+                    mma_f16(sc[mt], k0, k1, k2, k3, bl0, bl1);
+                }
             }
             // positions outside some valid row's window occur only in edge sub-blocks
             if (sb + kSub > p1 || sb + kSub - 1 > pos || sb < lo_max) {
+                const int s = 2 * nt + (t >> 1);  // token of rows 2t, 2t+1
+                const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int p = sb + ph * 16 + g + (e >> 1) * 8;
-                    const int s = 2 * nt + (t >> 1);  // token of rows 2t, 2t+1
-                    const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
-                    if (!(s < nv && p < p1 && p >= lo && p <= hi)) sc[e] = -INFINITY;
-                }
+                for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int p = sb + mt * 16 + g + (e >> 1) * 8;
+                        if (!(s < nv && p < p1 && p >= lo && p <= hi)) sc[mt][e] = -INFINITY;
+                    }
             }
-            // ---- online softmax over this warp's positions: rows 2t (sc 0, 2), 2t+1 (sc 1, 3) ----
-            float x0 = fmaxf(sc[0], sc[2]), x1 = fmaxf(sc[1], sc[3]);
+            // ---- online softmax over the sub-block: rows 2t (elements 0, 2), 2t+1 (elements 1, 3) ----
+            float x0 = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
+            float x1 = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
 #pragma unroll
             for (int o2 = 4; o2 < 32; o2 <<= 1) {
                 x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
@@ -620,37 +622,42 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
             // a row with nothing valid yet keeps m = -inf and contributes nothing
             const float c0 = (m0 == -INFINITY) ? 0.f : exp_fast(m0 - n0);
             const float c1 = (m1 == -INFINITY) ? 0.f : exp_fast(m1 - n1);
-            float pr[4];
-            pr[0] = sc[0] == -INFINITY ? 0.f : exp_fast(sc[0] - n0);
-            pr[1] = sc[1] == -INFINITY ? 0.f : exp_fast(sc[1] - n1);
-            pr[2] = sc[2] == -INFINITY ? 0.f : exp_fast(sc[2] - n0);
-            pr[3] = sc[3] == -INFINITY ? 0.f : exp_fast(sc[3] - n1);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                sc[mt][0] = sc[mt][0] == -INFINITY ? 0.f : exp_fast(sc[mt][0] - n0);
+                sc[mt][1] = sc[mt][1] == -INFINITY ? 0.f : exp_fast(sc[mt][1] - n1);
+                sc[mt][2] = sc[mt][2] == -INFINITY ? 0.f : exp_fast(sc[mt][2] - n0);
+                sc[mt][3] = sc[mt][3] == -INFINITY ? 0.f : exp_fast(sc[mt][3] - n1);
+            }
             m0 = n0;
             m1 = n1;
-            l0 = l0 * c0 + (pr[0] + pr[2]);
-            l1 = l1 * c1 + (pr[1] + pr[3]);
+            l0 = l0 * c0 + ((sc[0][0] + sc[0][2]) + (sc[1][0] + sc[1][2]));
+            l1 = l1 * c1 + ((sc[0][1] + sc[0][3]) + (sc[1][1] + sc[1][3]));
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 4; ++i) {
                 o[i][0] *= c0;
                 o[i][1] *= c1;
                 o[i][2] *= c0;
                 o[i][3] *= c1;
             }
-            // P^T (positions x rows) -> B fragments of O^T += V^T P^T: b0 from positions g, b1 from g + 8
-            uint32_t ph0, pl0, ph1, pl1;
-            split_f16x2(pr[0], pr[1], ph0, pl0);
-            split_f16x2(pr[2], pr[3], ph1, pl1);
-            ph0 = movm_t(ph0);
-            pl0 = movm_t(pl0);
-            ph1 = movm_t(ph1);
-            pl1 = movm_t(pl1);
-            // ---- O^T (dims 16 i + (g, g+8) x rows 2t, 2t+1) ----
+            // ---- O^T (dims 64 dh + 16 i + (g, g+8) x rows 2t, 2t+1) += V^T P^T, k-step = m-tile mt ----
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                uint32_t v0, v1, v2, v3;
-                ldsm_x4_t(v_a + i * 32, v0, v1, v2, v3);
-                mma_f16(o[i], v0, v1, v2, v3, ph0, ph1);
-                mma_f16(o[i], v0, v1, v2, v3, pl0, pl1);
+            for (int mt = 0; mt < 2; ++mt) {
+                // P^T (positions x rows) -> B fragments: b0 from positions g, b1 from g + 8
+                uint32_t ph0, pl0, ph1, pl1;
+                split_f16x2(sc[mt][0], sc[mt][1], ph0, pl0);
+                split_f16x2(sc[mt][2], sc[mt][3], ph1, pl1);
+                ph0 = movm_t(ph0);
+                pl0 = movm_t(pl0);
+                ph1 = movm_t(ph1);
+                pl1 = movm_t(pl1);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    uint32_t v0, v1, v2, v3;
+                    ldsm_x4_t(v_a + (uint32_t)(mt * 16 * kQStride * 2) + i * 32, v0, v1, v2, v3);
+                    mma_f16(o[i], v0, v1, v2, v3, ph0, ph1);
+                    mma_f16(o[i], v0, v1, v2, v3, pl0, pl1);
+                }
             }
         }
         if (more) {
@@ -658,54 +665,29 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
             attn_store_kv(sm, tid, kr, vr);
         }
     }
-    // ---- merge the two position halves (first + second, in that order) and write the chunk partials ----
+    // ---- chunk partials: rows r0, r0 + 1 (token s, heads r0 & 3, +1), this warp's 64 dims ----
 #pragma unroll
     for (int o2 = 4; o2 < 32; o2 <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, o2);
         l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
     }
-    const int r0 = nt * 8 + 2 * t;  // this lane's rows r0, r0 + 1
-    float* xml = sm.xo + kQRows * kXStride;
-    gsync();  // every warp is done with the K/V buffers
-    if (active && ph == 1) {
+    const int r0 = nt * 8 + 2 * t;
+    const int s = 2 * nt + (t >> 1);
+    if (active && s < nv) {
+        const size_t pi = ((size_t)s * a.n_heads + kvh * kGQA + (r0 & 3)) * a.max_chunks + c;
+        float* acc0 = a.part_acc + pi * kHD + dh * 64;
+        float* acc1 = acc0 + (size_t)a.max_chunks * kHD;  // next head, same token and chunk
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
             const int d = 16 * i + g;
-            sm.xo[r0 * kXStride + d] = o[i][0];
-            sm.xo[(r0 + 1) * kXStride + d] = o[i][1];
-            sm.xo[r0 * kXStride + d + 8] = o[i][2];
-            sm.xo[(r0 + 1) * kXStride + d + 8] = o[i][3];
+            acc0[d] = o[i][0];
+            acc1[d] = o[i][1];
+            acc0[d + 8] = o[i][2];
+            acc1[d + 8] = o[i][3];
         }
-        if (g == 0) {
-            xml[2 * r0] = m0;
-            xml[2 * r0 + 1] = l0;
-            xml[2 * r0 + 2] = m1;
-            xml[2 * r0 + 3] = l1;
-        }
-    }
-    gsync();
-    if (active && ph == 0) {
-        const float bm0 = xml[2 * r0], bl0 = xml[2 * r0 + 1], bm1 = xml[2 * r0 + 2], bl1 = xml[2 * r0 + 3];
-        const float M0 = fmaxf(m0, bm0), M1 = fmaxf(m1, bm1);
-        const float fa0 = m0 == -INFINITY ? 0.f : exp_fast(m0 - M0), fb0 = bm0 == -INFINITY ? 0.f : exp_fast(bm0 - M0);
-        const float fa1 = m1 == -INFINITY ? 0.f : exp_fast(m1 - M1), fb1 = bm1 == -INFINITY ? 0.f : exp_fast(bm1 - M1);
-        const int s = 2 * nt + (t >> 1);  // token of rows r0, r0 + 1 (heads r0 & 3, +1)
-        if (s < nv) {
-            const size_t pi = ((size_t)s * a.n_heads + kvh * kGQA + (r0 & 3)) * a.max_chunks + c;
-            float* acc0 = a.part_acc + pi * kHD;
-            float* acc1 = acc0 + (size_t)a.max_chunks * kHD;  // next head, same token and chunk
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int d = 16 * i + g;
-                acc0[d] = o[i][0] * fa0 + sm.xo[r0 * kXStride + d] * fb0;
-                acc1[d] = o[i][1] * fa1 + sm.xo[(r0 + 1) * kXStride + d] * fb1;
-                acc0[d + 8] = o[i][2] * fa0 + sm.xo[r0 * kXStride + d + 8] * fb0;
-                acc1[d + 8] = o[i][3] * fa1 + sm.xo[(r0 + 1) * kXStride + d + 8] * fb1;
-            }
-            if (g == 0) {
-                a.part_ml[pi] = make_float2(M0, l0 * fa0 + bl0 * fb0);
-                a.part_ml[pi + a.max_chunks] = make_float2(M1, l1 * fa1 + bl1 * fb1);
-            }
+        if (dh == 0 && g == 0) {
+            a.part_ml[pi] = make_float2(m0, l0);
+            a.part_ml[pi + a.max_chunks] = make_float2(m1, l1);
         }
     }
 }
