@@ -273,6 +273,7 @@ struct sd_ctx {
     int g_cap = 0;
     // graphs
     cudaGraphExec_t fwd_graph[kMaxVerify + 1] = {};
+    cudaGraphExec_t fwd_graph_kv[kMaxVerify + 1] = {};  // prefill forwards: K/V only, no LM head
     cudaGraphExec_t iter_graph = nullptr;
     int iter_key[6] = {-1, -1, -1, -1, -1, -1};
     GenParamsDev iter_p{};
@@ -646,37 +647,39 @@ int enqueue_forward(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtr
     return SD_OK;
 }
 
-// Forward graph for S tokens (full depth, target KV, ctrl), built on first use.
-int forward_graph(sd_ctx* c, int S, cudaGraphExec_t* out) {
-    if (c->fwd_graph[S]) {
-        *out = c->fwd_graph[S];
+// Forward graph for S tokens (full depth, target KV, ctrl), built on first use; logits = false leaves out
+// the LM head and argmax (prefill chunks whose logits nobody reads).
+int forward_graph(sd_ctx* c, int S, bool logits, cudaGraphExec_t* out) {
+    cudaGraphExec_t& slot = logits ? c->fwd_graph[S] : c->fwd_graph_kv[S];
+    if (slot) {
+        *out = slot;
         return SD_OK;
     }
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal), "capture");
-    int rc = enqueue_forward(c, S, c->n_layers, c->kc, c->vc, c->ctrl, true);
+    int rc = enqueue_forward(c, S, c->n_layers, c->kc, c->vc, c->ctrl, logits);
     cudaError_t e = cudaStreamEndCapture(c->st, &g);
     if (rc) {
         if (g) cudaGraphDestroy(g);
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "end capture");
-    e = cudaGraphInstantiate(&c->fwd_graph[S], g, 0);
+    e = cudaGraphInstantiate(&slot, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
-    *out = c->fwd_graph[S];
+    *out = slot;
     return SD_OK;
 }
 
-int run_forward(sd_ctx* c, int S) {
+int run_forward(sd_ctx* c, int S, bool logits = true) {
     if (c->use_graphs) {
         cudaGraphExec_t ge;
-        int rc = forward_graph(c, S, &ge);
+        int rc = forward_graph(c, S, logits, &ge);
         if (rc) return rc;
         CK(cudaGraphLaunch(ge, c->st), "graph launch");
         return SD_OK;
     }
-    return enqueue_forward(c, S, c->n_layers, c->kc, c->vc, c->ctrl, true);
+    return enqueue_forward(c, S, c->n_layers, c->kc, c->vc, c->ctrl, logits);
 }
 
 int set_ctrl(sd_ctx* c, DevCtrl* dst, const int32_t* tokens, int S, int pos, bool host_tokens) {
@@ -726,6 +729,8 @@ void sd_ctx_free(sd_ctx* c) {
     cudaSetDevice(c->dev);
     if (c->st) cudaStreamSynchronize(c->st);
     for (auto& g : c->fwd_graph)
+        if (g) cudaGraphExecDestroy(g);
+    for (auto& g : c->fwd_graph_kv)
         if (g) cudaGraphExecDestroy(g);
     if (c->iter_graph) cudaGraphExecDestroy(c->iter_graph);
     for (auto& W : c->L) {
@@ -986,11 +991,12 @@ int sd_ctx_tp_connect(sd_ctx* c, const void* handles, int n) {
     }
     c->tpx = t;
     // forwards captured for the NCCL path are rebuilt on next use
-    for (auto& g : c->fwd_graph)
-        if (g) {
-            cudaGraphExecDestroy(g);
-            g = nullptr;
-        }
+    for (auto* gs : {c->fwd_graph, c->fwd_graph_kv})
+        for (int i = 0; i <= kMaxVerify; ++i)
+            if (gs[i]) {
+                cudaGraphExecDestroy(gs[i]);
+                gs[i] = nullptr;
+            }
     if (c->iter_graph) {
         cudaGraphExecDestroy(c->iter_graph);
         c->iter_graph = nullptr;
@@ -1065,7 +1071,7 @@ int sd_prefill(sd_ctx* c, const int32_t* tokens, int n, int start_pos) {
     for (int i = 0; i < n; i += c->MB) {
         const int S = std::min(c->MB, n - i);
         if ((rc = set_ctrl(c, c->ctrl, tokens + i, S, start_pos + i, true))) return rc;
-        if ((rc = run_forward(c, S))) return rc;
+        if ((rc = run_forward(c, S, false))) return rc;
     }
     return finish(c);
 }
@@ -1360,7 +1366,7 @@ int sd_generate(sd_ctx* c, const sd_gen_params* gp, const int32_t* prompt, int n
     for (int i = 0; i < n_prompt; i += c->MB) {
         const int S = std::min(c->MB, n_prompt - i);
         if ((rc = set_ctrl(c, c->ctrl, prompt + i, S, i, true))) return rc;
-        if ((rc = run_forward(c, S))) return rc;
+        if ((rc = run_forward(c, S, i + S >= n_prompt))) return rc;  // logits of the last chunk only
     }
     const int last = (n_prompt - 1) % c->MB;
     // first token: sample_token with repetition penalty over the prompt window (mistral_infer.m:610-621)
