@@ -7,9 +7,9 @@
 
 namespace sd {
 
-// The MMA accumulator is initialised with -8*sum(codes) + kMagic: the result bits are then the fp32
-// value 1.5*2^23 + isum (exact for |isum| < 2^22; |isum| <= 32*8*128 here), so one exact FADD
-// recovers (float)isum without the quarter-rate I2F conversion.
+// The MMA accumulator is initialised with the bits of kMagic = 1.5*2^23: the result bits are then the fp32
+// value kMagic + sum(q*x) (q the 0..15 nibbles; exact, |sum| < 2^16), and one exact FADD of
+// -(kMagic + 8*sum(x)) recovers (float)isum = sum((q-8)*x) without the quarter-rate I2F conversion.
 constexpr int kMagicI = 0x4B400000;
 constexpr float kMagicF = 12582912.0f;
 
@@ -26,39 +26,36 @@ __device__ __forceinline__ float2 h2x2f(uint32_t w) {
 // all kMaxS token slots (tokens >= the valid count are zero), so a lane's fragment address does not
 // depend on S:
 //   b[blk*kActStride + 4s + tt] = (word tt, word 4+tt) of token s's codes in block blk  (MMA B fragment)
-//   c[blk*4 + t]                = C quad (-8*sum + magic for tokens 2t, 2t+1, repeated for rows g+8)
-//   x[blk*4 + t]                = (xd of token 2t, xd of token 2t+1)
+//   m[blk*4 + t]                = (xd of token 2t, xd of token 2t+1, -(kMagic + 8*sum) of 2t, of 2t+1)
 // ---------------------------------------------------------------------------------------------
 constexpr int kActStride = 4 * kMaxS;
 
 struct ActSmem {
     uint2* b;
-    int4* c;
-    float2* x;
+    float4* m;
 };
 
-__host__ __device__ inline size_t act_smem_bytes(int nb) {
-    return (size_t)nb * kActStride * 8 + (size_t)nb * 4 * 16 + (size_t)nb * 4 * 8;
-}
+__host__ __device__ inline size_t act_smem_bytes(int nb) { return (size_t)nb * kActStride * 8 + (size_t)nb * 4 * 16; }
 
 __device__ inline ActSmem act_smem_at(uint8_t* base, int nb) {
     ActSmem A;
     A.b = reinterpret_cast<uint2*>(base);
-    A.c = reinterpret_cast<int4*>(base + (size_t)nb * kActStride * 8);
-    A.x = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(A.c) + (size_t)nb * 4 * 16);
+    A.m = reinterpret_cast<float4*>(base + (size_t)nb * kActStride * 8);
     return A;
 }
 
+// Offset term of a token's block with code sum `sum` (see kMagicI).
+__host__ __device__ inline float act_offset(int sum) { return -(kMagicF + 8.0f * (float)sum); }
+
 // The same fragment layout in global memory for a whole K range (nbK blocks): written by the phase that
 // produces the activations so that staging a K slice is three contiguous bulk copies.
-//   b: [nbK][kActStride] uint2, c: [nbK][4] int4, x: [nbK][4] float2 (scales before any norm scale)
+//   b: [nbK][kActStride] uint2, m: [nbK][4] float4 (scales before any norm scale, offsets)
 __host__ __device__ inline size_t act_image_bytes(int nbK) { return act_smem_bytes(nbK); }
 
 __host__ __device__ inline ActImage act_image_at(void* base, int nbK) {
     ActImage im;
     im.b = reinterpret_cast<uint2*>(base);
-    im.c = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(base) + (size_t)nbK * kActStride * 8);
-    im.x = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(im.c) + (size_t)nbK * 4 * 16);
+    im.m = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(base) + (size_t)nbK * kActStride * 8);
     return im;
 }
 
@@ -77,10 +74,9 @@ __device__ __forceinline__ void image_put_codes_lane(const ActImage& im, int s, 
 
 // Block scale d and code sum of token s in block blk.
 __device__ __forceinline__ void image_put_meta(const ActImage& im, int s, int blk, float d, int sum) {
-    int* cp = reinterpret_cast<int*>(im.c + (size_t)blk * 4 + (s >> 1));
-    cp[s & 1] = kMagicI - 8 * sum;
-    cp[(s & 1) + 2] = kMagicI - 8 * sum;
-    reinterpret_cast<float*>(im.x + (size_t)blk * 4 + (s >> 1))[s & 1] = d;
+    float* mp = reinterpret_cast<float*>(im.m + (size_t)blk * 4 + (s >> 1));
+    mp[s & 1] = d;
+    mp[(s & 1) + 2] = act_offset(sum);
 }
 
 // Stage Q8 planes (global, row stride K) blocks [kb0, kb0 + nb) of tokens < nv into A.  Loads are
@@ -140,15 +136,13 @@ __device__ inline void stage_act_from_planes(const ActSmem& A, const Q8Planes& a
         for (int u = 0; u < 2; ++u) {
             const int i = i0 + u * nthr;
             if (i < nb * 4) {
-                const int c0 = kMagicI - 8 * sm[u][0], c1 = kMagicI - 8 * sm[u][1];
-                A.c[i] = make_int4(c0, c1, c0, c1);
                 float d0 = dv[u][0], d1 = dv[u][1];
                 if (tok_scale) {
                     const int tt = i & 3;
                     if (2 * tt < nv) d0 = d0 * tok_scale[2 * tt];
                     if (2 * tt + 1 < nv) d1 = d1 * tok_scale[2 * tt + 1];
                 }
-                A.x[i] = make_float2(d0, d1);
+                A.m[i] = make_float4(d0, d1, act_offset(sm[u][0]), act_offset(sm[u][1]));
             }
         }
     }
@@ -203,15 +197,13 @@ __device__ __forceinline__ void consume_tiles(const TileRegs& tr, int lane, cons
         dh[r][1] = h2x2f(tr.sh[r].y);
     }
     const uint32_t bf_a = smem_u32(A.b) + (bbase * kActStride + lane) * 8;  // token slot g, word pair t
-    const uint32_t c_a = smem_u32(A.c) + (bbase * 4 + t) * 16;
-    const uint32_t x_a = smem_u32(A.x) + (bbase * 4 + t) * 8;
+    const uint32_t m_a = smem_u32(A.m) + (bbase * 4 + t) * 16;
 #pragma unroll
     for (int blk = 0; blk < 4; ++blk) {
         const uint2 bf = lds64(bf_a + blk * kActStride * 8);
-        const uint4 cu = lds128(c_a + blk * 64);
-        const int4 cq = make_int4((int)cu.x, (int)cu.y, (int)cu.z, (int)cu.w);
-        const uint2 xu = lds64(x_a + blk * 32);
-        const float2 xd = make_float2(__uint_as_float(xu.x), __uint_as_float(xu.y));
+        const uint4 mu = lds128(m_a + blk * 64);
+        const float2 xd = make_float2(__uint_as_float(mu.x), __uint_as_float(mu.y));
+        const float2 off = make_float2(__uint_as_float(mu.z), __uint_as_float(mu.w));
 #pragma unroll
         for (int r = 0; r < kRPW; ++r) {
             const uint32_t wlo = blk == 0 ? tr.wl[r].x : blk == 1 ? tr.wl[r].y : blk == 2 ? tr.wl[r].z : tr.wl[r].w;
@@ -219,20 +211,18 @@ __device__ __forceinline__ void consume_tiles(const TileRegs& tr, int lane, cons
             const uint32_t a0 = wlo & 0x0F0F0F0Fu, a2 = (wlo >> 4) & 0x0F0F0F0Fu;
             const uint32_t a1 = whi & 0x0F0F0F0Fu, a3 = (whi >> 4) & 0x0F0F0F0Fu;
             int d[4];
-            mma_u8s8(d, a0, a1, a2, a3, bf.x, bf.y, cq.x, cq.y, cq.z, cq.w);
+            mma_u8s8(d, a0, a1, a2, a3, bf.x, bf.y, kMagicI, kMagicI, kMagicI, kMagicI);
             if constexpr (BLOCKSUMS) {
                 if (t == 0 && (rg + r) * kTileRows < out_rows) {
                     const int r0 = (rg + r) * kTileRows + g;
-                    isum[(size_t)r0 * nbK + kb0 + bbase + blk] = d[0] - kMagicI;
-                    isum[(size_t)(r0 + 8) * nbK + kb0 + bbase + blk] = d[2] - kMagicI;
+                    isum[(size_t)r0 * nbK + kb0 + bbase + blk] = (int)(__int_as_float(d[0]) + off.x);
+                    isum[(size_t)(r0 + 8) * nbK + kb0 + bbase + blk] = (int)(__int_as_float(d[2]) + off.x);
                 }
             } else {
                 const float wdl = (blk & 1) ? dl[r][blk >> 1].y : dl[r][blk >> 1].x;
                 const float wdh = (blk & 1) ? dh[r][blk >> 1].y : dh[r][blk >> 1].x;
-                const float2 fL = __fadd2_rn(make_float2(__int_as_float(d[0]), __int_as_float(d[1])),
-                                             make_float2(-kMagicF, -kMagicF));
-                const float2 fH = __fadd2_rn(make_float2(__int_as_float(d[2]), __int_as_float(d[3])),
-                                             make_float2(-kMagicF, -kMagicF));
+                const float2 fL = __fadd2_rn(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), off);
+                const float2 fH = __fadd2_rn(make_float2(__int_as_float(d[2]), __int_as_float(d[3])), off);
                 // (wd*xd) * (float)isum accumulated per block, as mistral/dequant.h:1085
                 const float2 sL = __fmul2_rn(make_float2(wdl, wdl), xd);
                 const float2 sH = __fmul2_rn(make_float2(wdh, wdh), xd);

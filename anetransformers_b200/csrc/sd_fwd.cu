@@ -168,11 +168,10 @@ __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem&
         // the image was written by ordinary stores of other CTAs (ordered before us by a grid barrier);
         // order those with this thread's async-proxy reads
         asm volatile("fence.proxy.async.global;" ::: "memory");
-        const uint32_t bb = (uint32_t)nb * kActStride * 8, cb = (uint32_t)nb * 64, xb = (uint32_t)nb * 32;
-        mbar_arrive_expect_tx(R.act_full, bb + cb + xb);
+        const uint32_t bb = (uint32_t)nb * kActStride * 8, mb = (uint32_t)nb * 64;
+        mbar_arrive_expect_tx(R.act_full, bb + mb);
         bulk_g2s(A.b, im.b + (size_t)kb0 * kActStride, bb, R.act_full);
-        bulk_g2s(A.c, im.c + (size_t)kb0 * 4, cb, R.act_full);
-        bulk_g2s(A.x, im.x + (size_t)kb0 * 4, xb, R.act_full);
+        bulk_g2s(A.m, im.m + (size_t)kb0 * 4, mb, R.act_full);
         reinterpret_cast<volatile uint32_t*>(&m->act_issued)[0] = nstg + 1;
     }
     if (norm && warp < nv) {
@@ -188,17 +187,15 @@ __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem&
     }
     ++nstg;
     for (int i = tid; i < nb * 4; i += kConsumerThreads) {
-        int* cp = reinterpret_cast<int*>(&A.c[i]);
-        float* xp = reinterpret_cast<float*>(&A.x[i]);
+        float* mp = reinterpret_cast<float*>(&A.m[i]);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int s = 2 * (i & 3) + hh;
             if (s >= nv) {
-                cp[hh] = kMagicI;
-                cp[hh + 2] = kMagicI;
-                xp[hh] = 0.f;
+                mp[hh] = 0.f;
+                mp[hh + 2] = -kMagicF;
             } else if (norm) {
-                xp[hh] = xp[hh] * m->scale[s];
+                mp[hh] = mp[hh] * m->scale[s];
             }
         }
     }

@@ -48,8 +48,7 @@ struct RowMap {
 // Activations in the matvec's shared-memory fragment layout, kept in global memory (sd_dev.cuh).
 struct ActImage {
     uint2* b;
-    int4* c;
-    float2* x;
+    float4* m;
 };
 
 // Q8_0 activations on device as planes (codes, fp32 scale, per-block code sum).
