@@ -68,23 +68,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps in hardware until the
-// phase completes or about kWaitHintNs pass, instead of spinning on issue slots its CTA's working warps
-// need.
-constexpr uint32_t kWaitHintNs = 20000;
-
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n"
-        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
-        : "memory");
-    return ok != 0;
-}
-
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -94,11 +77,13 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Any legitimate wait in these kernels is far below this; a wait that reaches it gives up.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-// Bounded wait: returns false if the phase did not complete within kWaitLimitNs.
+// Bounded wait: returns false if the phase did not complete within kWaitLimitNs.  (A try_wait with a
+// suspend-time hint measured 1.6 % slower on the whole forward than polling: the waiting warps are the
+// ones that resume work first.)
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait_sleep(bar, parity))
+    while (!mbar_try_wait(bar, parity))
         if (global_ns() - t0 > kWaitLimitNs) return false;
     return true;
 }

@@ -102,9 +102,9 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
 
 // Single-thread wait that also gives up as soon as another warp of the CTA has aborted.
 __device__ __forceinline__ bool wait_or_abort_1(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
-    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait_sleep(bar, parity)) {
+    while (!mbar_try_wait(bar, parity)) {
         if (*abort_flag || global_ns() - t0 > kWaitLimitNs) return false;
     }
     return true;
