@@ -175,8 +175,9 @@ __device__ __forceinline__ void load_tiles(const uint8_t* slot, uint32_t half_by
         const uint32_t tile = base + r * half_bytes;
         tr.wl[r] = lds128(tile + lane * 16);
         tr.wh[r] = lds128(tile + 512 + lane * 16);
-        tr.sl[r] = lds64(tile + 1024 + g * 8);
-        tr.sh[r] = lds64(tile + 1088 + g * 8);
+        const uint4 sc = lds128(tile + 1024 + g * 16);
+        tr.sl[r] = make_uint2(sc.x, sc.y);
+        tr.sh[r] = make_uint2(sc.z, sc.w);
     }
 }
 

@@ -310,7 +310,7 @@ __global__ void k_repack(const uint8_t* __restrict__ aos, int rows, int cols, si
         *reinterpret_cast<uint4*>(tile + h * 512 + (4 * gg + t) * 16) = make_uint4(words[0], words[1], words[2], words[3]);
         if (t == 0) {
             uint2 s2 = make_uint2((uint32_t)sc[0] | ((uint32_t)sc[1] << 16), (uint32_t)sc[2] | ((uint32_t)sc[3] << 16));
-            *reinterpret_cast<uint2*>(tile + 1024 + (h * 8 + gg) * 8) = s2;
+            *reinterpret_cast<uint2*>(tile + 1024 + gg * 16 + h * 8) = s2;
         }
     }
 }

@@ -14,7 +14,8 @@ namespace sd {
 // as cols/128 tiles ("quads" of 4 consecutive blocks), each tile 1152 bytes:
 //   bytes [0, 1024): nibbles.  Half h (rows 8h..8h+7), lane L = 4*g + t (g = row in half, t = word):
 //                    16 bytes at h*512 + L*16 = word t (qs[4t..4t+3]) of blocks 4q..4q+3 of row 8h+g.
-//   bytes [1024, 1152): fp16 scales, [h][g][blk] -> 8 bytes per row.
+//   bytes [1024, 1152): fp16 scales, [g][h][blk]: rows g and 8+g side by side, so a lane reads the scales of
+//                    both its rows with one 16-byte load.
 // Each lane of a warp then reads its int8 MMA A-fragment for 4 blocks with two conflict-free 16-byte
 // loads, and one row-group's whole K range is contiguous (cols/128 * 1152 bytes), so a CTA's range of
 // row-groups is one contiguous stream for the bulk-copy engine.
