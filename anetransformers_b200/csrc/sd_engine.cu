@@ -485,8 +485,10 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     CK(cudaMemsetAsync(c->fsync, 0, fwd_sync_words(c->dim) * sizeof(unsigned), c->st), "memset");
     CK(launch_forward(a, c->fwd_grid, c->fwd_smem, c->st), "forward launch");
     if (c->tpx.n > 1) CK(launch_tp_advance(c->tp_base, 2 * n_layers, c->st), "tp advance");
+    // the LM head phase reduced the argmax keys (first index on ties) into the sync words
     if (logits_and_argmax)
-        CK(launch_argmax(c->logits + (size_t)row0 * c->vocab, c->vocab, S, c->argmax + row0, ctrl, c->st, false), "argmax");
+        CK(launch_argmax_keys(reinterpret_cast<const unsigned long long*>(c->fsync + 32), S, c->argmax + row0, ctrl, c->st),
+           "argmax");
     return SD_OK;
 }
 

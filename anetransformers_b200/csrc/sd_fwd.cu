@@ -68,7 +68,7 @@ __host__ __device__ inline FwdSmem fwd_layout(int nstage) {
     const size_t attn = (size_t)kFwdAttnGroups * attn_smem_bytes();
     if (attn > uni) uni = attn;
     L.misc = L.act + align_up(uni, 128);
-    L.bars = L.misc + 128;  // misc: scale[kMaxS], abort, producer issued/done
+    L.bars = L.misc + 128;  // misc: scale[kMaxS], abort, producer issued/done, argmax keys
     L.total = L.bars + (2 * kMaxStages + 2 * kRedSlots + 1) * 8;
     return L;
 }
@@ -80,7 +80,9 @@ struct Misc {
     uint32_t issued;
     int pdone;
     uint32_t act_issued;  // activation stagings issued (bulk copies completing on the act barrier)
+    unsigned long long best[kMaxS];  // LM head: this CTA's best (logit, row) key per token
 };
+static_assert(sizeof(Misc) <= 128, "Misc fits its 128-byte slot");
 
 struct Ring {
     uint64_t* act_full;  // activation staging copies
@@ -210,6 +212,14 @@ __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem&
 enum PhaseKind : int { PH_QKV = 0, PH_WO = 1, PH_W13 = 2, PH_W2 = 3, PH_LM = 4 };
 constexpr int kMaxParts = 8;  // K slices of a matvec whose outputs a residual phase adds
 
+
+// Argmax key of logit v at row `row`: larger keys for larger logits, and for equal logits for the smaller
+// row (first index on ties, mistral/mistral_model.h:1136-1143).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)row);
+}
 
 // Finish one (token s, 32-row block b) of the residual stream, one warp, lane = row: store the new x
 // value xv, the block's two 16-row sums of squares (the canonical order of group16_sumsq), and Q8_0 of
@@ -415,6 +425,19 @@ __device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, 
                     const int gr = rg * kTileRows + row;
                     if (gr < ld && tok < nv) out[(size_t)tok * ld + gr] = v[k];
                 }
+                if (kind == PH_LM) {
+                    // token lane & 7 of rows (lane >> 3) + 4k: best of the four, then of the four lanes of the
+                    // token, into this CTA's best
+                    unsigned long long key = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int gr = rg * kTileRows + (lane >> 3) + 4 * k;
+                        if (gr < ld) key = max(key, argmax_key(v[k], gr));
+                    }
+                    key = max(key, __shfl_xor_sync(0xffffffffu, key, 8));
+                    key = max(key, __shfl_xor_sync(0xffffffffu, key, 16));
+                    if (lane < 8 && lane < nv) atomicMax(&m->best[lane], key);
+                }
             }
         }
     }
@@ -539,6 +562,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
         m->issued = 0;
         m->pdone = 0;
         m->act_issued = 0;
+        for (int i = 0; i < kMaxS; ++i) m->best[i] = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -639,6 +663,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_forward(const FwdArgs a) {
     // Drain: no bulk copy may still be landing in shared memory when the CTA exits.  Only the last
     // nstage issued stages can be in flight (a slot is reissued only after every consumer waited for it).
     named_sync(kBarCompute, kComputeThreads);
+    // the LM head's argmax: this CTA's best key per token into the forward's keys
+    if (a.lm && tid < nv && m->best[tid]) atomicMax(reinterpret_cast<unsigned long long*>(a.sync + 32) + tid, m->best[tid]);
     if (tid == 0) {
         const volatile int* pd = &m->pdone;
         uint32_t n = 0;
@@ -659,7 +685,8 @@ int fwd_pick_stages(int max_smem) {
     return 0;
 }
 
-size_t fwd_sync_words(int) { return 1; }  // the grid barrier counter
+// word 0: the grid barrier counter; words 32..: the argmax keys (u64 per token)
+size_t fwd_sync_words(int) { return 32 + 2 * kMaxS; }
 
 cudaError_t fwd_init_attrs(int max_smem) {
     return cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);

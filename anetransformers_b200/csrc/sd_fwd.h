@@ -43,7 +43,7 @@ struct FwdArgs {
     Q8Planes h;                 // [S][hidden] quantised SiLU(gate)*up (planes; unused when h_img is set)
     float* yparts;              // [kparts][S][dim] K-slice partials
     size_t ypart_stride;
-    unsigned* sync;             // [0] grid barrier counter; zero at launch
+    unsigned* sync;             // [0] grid barrier counter; from word 32: argmax keys [kMaxS] u64; zero at launch
     float2* part_ml;            // attention partials
     float* part_acc;
     int attn_chunk, max_chunks;

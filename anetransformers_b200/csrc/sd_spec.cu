@@ -185,6 +185,19 @@ cudaError_t launch_argmax(const float* logits, int vocab, int S, int* out, const
     return cudaLaunchKernelEx(&cfg, k_argmax, logits, vocab, S, out, ctrl);
 }
 
+// Argmax from the (logit, row) keys the persistent forward's LM head reduces: row = ~low word.
+__global__ void k_argmax_keys(const unsigned long long* __restrict__ keys, int S, int* __restrict__ out, const DevCtrl* ctrl) {
+    if (ctrl && ctrl->done) return;
+    const int nv = ctrl ? min(ctrl->n_valid, S) : S;
+    const int s = threadIdx.x;
+    if (s < nv) out[s] = (int)(0xFFFFFFFFu - (uint32_t)(keys[s] & 0xFFFFFFFFull));
+}
+
+cudaError_t launch_argmax_keys(const unsigned long long* keys, int S, int* out, const DevCtrl* ctrl, cudaStream_t st) {
+    k_argmax_keys<<<1, 32, 0, st>>>(keys, S, out, ctrl);
+    return cudaGetLastError();
+}
+
 // sample_token on logits row `row` (modified in place: repetition penalty, top-k selection marks).
 // Thread 0 performs the sequential parts exactly as the reference orders them.
 __device__ int sample_token_dev(float* logits, int n, const GenParamsDev& p, const int* prev, int n_prev, GenState* g) {
