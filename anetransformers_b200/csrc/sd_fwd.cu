@@ -158,11 +158,12 @@ __device__ void grid_barrier(const FwdArgs& a, Misc* m, uint32_t& target) {
 // Activation staging (consumer warps only)
 // ---------------------------------------------------------------------------------------------
 
-// Stage blocks [kb0, kb0 + nb) of an activation image into A (consumer warps): three bulk copies on
-// the act barrier.  While they land, warps < nv form the RMSNorm scale s of their token from the 16-row
-// sums of squares (norm phases only: scale != null).  Then token slots >= nv are cleared (codes 0, C =
-// magic, scale 0) and, for norm phases, the block scales become d_u * s -- the same values the per-op
-// staging builds from Q8 planes.
+// Stage blocks [kb0, kb0 + nb) of an activation image into A (consumer warps): two bulk copies on the
+// act barrier.  While they land, warps < nv form the RMSNorm scale s of their token from the 16-row sums of
+// squares (norm phases only).  Then, for norm phases, the block scales of tokens < nv become d_u * s -- the
+// same values the per-op staging builds from Q8 planes.  Token slots >= nv keep whatever an earlier forward
+// left there: each MMA output column depends only on its own token's fragments, and no epilogue reads the
+// columns of tokens >= nv (clearing them cost 3 % of a forward).
 __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem& A, const Ring& R, Misc* m, uint32_t& nstg,
                             int kb0, int nb, int nv, bool norm, bool& ab, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
@@ -188,22 +189,15 @@ __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem&
         m->abort = 1;
     }
     ++nstg;
-    for (int i = tid; i < nb * 4; i += kConsumerThreads) {
-        float* mp = reinterpret_cast<float*>(&A.m[i]);
+    if (norm)
+        for (int i = tid; i < nb * 4; i += kConsumerThreads) {
+            float* mp = reinterpret_cast<float*>(&A.m[i]);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const int s = 2 * (i & 3) + hh;
-            if (s >= nv) {
-                mp[hh] = 0.f;
-                mp[hh + 2] = -kMagicF;
-            } else if (norm) {
-                mp[hh] = mp[hh] * m->scale[s];
+            for (int hh = 0; hh < 2; ++hh) {
+                const int s = 2 * (i & 3) + hh;
+                if (s < nv) mp[hh] = mp[hh] * m->scale[s];
             }
         }
-    }
-    if (nv < kMaxS)
-        for (int i = tid; i < nb * kActStride; i += kConsumerThreads)
-            if (((i & (kActStride - 1)) >> 2) >= nv) A.b[i] = make_uint2(0, 0);
 }
 
 // ---------------------------------------------------------------------------------------------
