@@ -297,13 +297,15 @@ __device__ __forceinline__ void epi_qkv(const float (&v)[4], int rg, int lane, i
     }
 }
 
-// SiLU(gate)*up + Q8_0 of one 32-unit block for tokens r*4 .. r*4+3 (epilogue warp r of 2).
+// SiLU(gate)*up + Q8_0 of one 32-unit block for the valid tokens r, r + 2, ... (epilogue warp r of 2; the
+// epilogue is on the gate|up matvec's critical path, so tokens >= nv are skipped and the two warps alternate).
 // ubuf: [4][128] = gate lo, gate hi, up lo, up hi (row*8 + tok).
 __device__ __forceinline__ void epi_silu_q8(const float* ubuf, int r, int lane, int unit, int nv, Q8Planes h, int hidden,
                                             const ActImage* img = nullptr) {
     const int nbh = hidden >> 5;
     for (int k = 0; k < 4; ++k) {
-        const int tok = r * 4 + k;
+        const int tok = r + 2 * k;  // tokens alternate between the two epilogue warps
+        if (tok >= nv) break;
         const int rr2 = lane & 15, hsel = lane >> 4;
         const float gv = ubuf[hsel * 128 + rr2 * 8 + tok];
         const float uv = ubuf[(2 + hsel) * 128 + rr2 * 8 + tok];
