@@ -55,7 +55,7 @@ static inline int metal_alloc_batch_buffers(MetalContext *ctx, int S, int dim, i
     (void)dim; (void)kv_dim; (void)hidden; (void)n_heads;
     sd_model_info in;
     if (!ctx || sd_ctx_info(ctx, &in) != SD_OK) return -1;
-    return (S >= 1 && S <= 8 && max_att_len <= in.max_seq) ? 0 : -1;
+    return (S >= 1 && S <= SD_MAX_VERIFY && max_att_len <= in.max_seq) ? 0 : -1;
 }
 
 /* The ring stays in device memory; host code may still read kv->len / kv->max_seq.  Pass the
