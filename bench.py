@@ -53,6 +53,21 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+def aggregate_ranks(dist, ms: float, tokens: float, tp: bool, device="cuda"):
+    """Whole-job time and tokens over the ranks: the slowest rank's time (max), and the tokens of one
+    stream under tensor parallelism (every rank emits the same tokens) or of all streams (data parallel:
+    the sum).  Every rank takes part (two all-reduces in the same order)."""
+    if dist is None:
+        return ms, float(tokens)
+    import torch
+    t = torch.tensor([ms, float(tokens)], device=device, dtype=torch.float64)
+    mx = t.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    sm = t.clone()
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    return float(mx[0]), (float(tokens) if tp else float(sm[1]))
+
+
 def config3_prompt(seed: int = 1234, vocab: int = 32000):
     rng = np.random.default_rng(seed)
     pool = [rng.integers(3, vocab, 64).tolist() for _ in range(6)]
@@ -287,15 +302,7 @@ def run_selfspec(args, ctx, rank, world, local, dist, tp, peaks):
         dist.barrier()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
-    if dist:
-        tt = torch.tensor([ms, float(tokens)], device="cuda", dtype=torch.float64)
-        mx = tt.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = tt.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms_max, tokens_all = float(mx[0]), (float(tokens) if tp else float(sm[1]))
-    else:
-        ms_max, tokens_all = ms, float(tokens)
+    ms_max, tokens_all = aggregate_ranks(dist, ms, tokens, tp)
     value = tokens_all / (ms_max * 1e-3)
     # weight + KV bytes per iteration: K drafter passes (8 layers + LM head) and a 9-token verify that runs
     # as an 8-token and a 1-token forward
@@ -475,16 +482,8 @@ def main():
         dist.barrier()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ms, float(tokens)], device="cuda", dtype=torch.float64)
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = t.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        # tp: every rank emits the same single stream; dp: the streams add up
-        ms_max, tokens_all = float(mx[0]), (float(tokens) if tp else float(sm[1]))
-    else:
-        ms_max, tokens_all = ms, float(tokens)
+    # tp: every rank emits the same single stream; dp: the streams add up
+    ms_max, tokens_all = aggregate_ranks(dist, ms, tokens, tp)
     value = tokens_all / (ms_max * 1e-3)
     per_rank_tps = tokens / (ms * 1e-3)
     fwd_per_s = (iters / args.steps) / (ms / args.steps * 1e-3)
@@ -509,13 +508,7 @@ def main():
         e2e_tok += len(out)
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
-    if dist:
-        tt = torch.tensor([e2e_s, float(e2e_tok)], device="cuda", dtype=torch.float64)
-        mx = tt.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = tt.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        e2e_s, e2e_tok = float(mx[0]), (float(e2e_tok) if tp else float(sm[1]))
+    e2e_s, e2e_tok = aggregate_ranks(dist, e2e_s, e2e_tok, tp)
     e2e = {"value": round(e2e_tok / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 4 * len(hist),
            "d2h_bytes_per_step": 4 * len(out),
            "what": "sd_decode per step: history (1024-token prompt + first token) from pinned host memory, "

@@ -143,7 +143,8 @@ def quantize_q8_0(x: np.ndarray, variant: int = QUANT_IEEE) -> np.ndarray:
 def block_sums(W: np.ndarray, xq: np.ndarray) -> np.ndarray:
     rows, bpr = W.shape
     out = np.zeros((rows, bpr), dtype=np.int32)
-    lib().or_q4q8_block_sums(_p(np.ascontiguousarray(W)), _p(np.ascontiguousarray(xq)), _p(out), rows, bpr * 32)
+    Wc, xc = np.ascontiguousarray(W), np.ascontiguousarray(xq)  # alive across the call
+    lib().or_q4q8_block_sums(_p(Wc), _p(xc), _p(out), rows, bpr * 32)
     return out
 
 
@@ -152,7 +153,8 @@ def matvec(W: np.ndarray, xq: np.ndarray, acc_mode: int = ACC_FMA) -> np.ndarray
     y = np.zeros(rows, dtype=np.float32)
     L = lib()
     L.or_set_acc_mode(acc_mode)
-    L.or_matvec_q4_0_q8_0(_p(np.ascontiguousarray(W)), _p(np.ascontiguousarray(xq)), _p(y), rows, bpr * 32)
+    Wc, xc = np.ascontiguousarray(W), np.ascontiguousarray(xq)
+    L.or_matvec_q4_0_q8_0(_p(Wc), _p(xc), _p(y), rows, bpr * 32)
     L.or_set_acc_mode(ACC_FMA)
     return y
 
@@ -182,13 +184,15 @@ def apply_rope(q: np.ndarray, k: np.ndarray, pos: int, theta_inv: np.ndarray, n_
                head_dim: int):
     q = np.array(q, np.float32, copy=True)
     k = np.array(k, np.float32, copy=True)
-    lib().or_apply_rope(_p(q), _p(k), pos, _p(np.ascontiguousarray(theta_inv, np.float32)), n_heads, n_kv, head_dim)
+    ti = np.ascontiguousarray(theta_inv, np.float32)
+    lib().or_apply_rope(_p(q), _p(k), pos, _p(ti), n_heads, n_kv, head_dim)
     return q, k
 
 
 def silu_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
     g = np.array(g, np.float32, copy=True)
-    lib().or_silu_mul(_p(g), _p(np.ascontiguousarray(u, np.float32)), g.size)
+    uc = np.ascontiguousarray(u, np.float32)
+    lib().or_silu_mul(_p(g), _p(uc), g.size)
     return g
 
 
@@ -204,7 +208,8 @@ def attention(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, n_heads: int, heads
     q = np.array(q, np.float32, copy=True)
     att = np.zeros(n_heads * max_seq, np.float32)
     out = np.zeros(n_heads * hd, np.float32)
-    lib().or_attention(_p(q), _p(att), _p(out), _p(np.ascontiguousarray(kc)), _p(np.ascontiguousarray(vc)),
+    kcc, vcc = np.ascontiguousarray(kc), np.ascontiguousarray(vc)
+    lib().or_attention(_p(q), _p(att), _p(out), _p(kcc), _p(vcc),
                        n_heads, heads_per_kv, hd, max_seq, pos)
     return out
 
@@ -214,7 +219,8 @@ def philox(seed: int, counter: int) -> int:
 
 
 def sample_argmax(logits: np.ndarray) -> int:
-    return lib().or_sample_argmax(_p(np.ascontiguousarray(logits, np.float32)), logits.size)
+    lc = np.ascontiguousarray(logits, np.float32)
+    return lib().or_sample_argmax(_p(lc), logits.size)
 
 
 def spec_accept(draft_probs, logits, draft_tokens, temp: float, seed: int = 0, counter: int = 0):
