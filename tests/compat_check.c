@@ -55,8 +55,8 @@ int main(int argc, char **argv) {
         MetalContext *mc = metal_context_init(buf, len, in.dim, in.n_kv_heads * in.head_dim, in.hidden_dim, in.vocab_size,
                                               in.n_heads, in.n_layers, 512);
         if (!mc) return 4;
-        printf("batch5=%d batch9=%d\n", metal_alloc_batch_buffers(mc, 5, 0, 0, 0, 0, 512),
-               metal_alloc_batch_buffers(mc, 9, 0, 0, 0, 0, 512));
+        printf("batch5=%d batch9=%d batch17=%d\n", metal_alloc_batch_buffers(mc, 5, 0, 0, 0, 0, 512),
+               metal_alloc_batch_buffers(mc, 9, 0, 0, 0, 0, 512), metal_alloc_batch_buffers(mc, 17, 0, 0, 0, 0, 512));
         int toks[5] = {5, 6, 7, 8, 9};
         float *lg = malloc(sizeof(float) * 5 * in.vocab_size);
         int rc = spec_verify(mc, NULL, toks, 5, 0, lg);

@@ -25,7 +25,7 @@ def test_compat_headers_run(tmp_path, mini_path):
     assert out.returncode == 0, out.stdout + out.stderr
     lines = out.stdout.splitlines()
     assert any(l.startswith("ngram n=1 first=4") or l.startswith("ngram n=") for l in lines)
-    assert "batch5=0 batch9=-1" in out.stdout
+    assert "batch5=0 batch9=0 batch17=-1" in out.stdout   # verify batches up to SD_MAX_VERIFY = 16
     assert "verify rc=0 accepted=5" in out.stdout      # drafts = argmax of each row -> all accepted + bonus
 
 
