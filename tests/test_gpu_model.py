@@ -278,13 +278,15 @@ def test_persistent_forward_bitwise_equals_per_op_kernels(mini, max_seq):
         perop.close()
 
 
-def test_long_context_verify_matches_oracle(mini, oracle):
-    """A 9-token verify after a 33K-token prefill (attention chunks of 128 slots, as in the 32K-context
-    self-speculative configuration): the device's K/V ring is loaded into the oracle's ring, then each verify
-    token's logits are checked against the oracle's single-token forward at the same position."""
+@pytest.mark.parametrize("n_ctx,max_seq", [(8500, 8704), (33000, 33024)])
+def test_long_context_verify_matches_oracle(mini, oracle, n_ctx, max_seq):
+    """A 9-token verify after a long prefill (attention chunks of 64 slots and 16 combine warps per row past an
+    8K ring, 128-slot chunks past a 32K ring, as in the 32K-context self-speculative configuration): the
+    device's K/V ring is loaded into the oracle's ring, then each verify token's logits are checked against
+    the oracle's single-token forward at the same position."""
     from anetransformers_b200 import gguf as G
     from anetransformers_b200.engine import Context
-    n_ctx, S, max_seq = 33000, 9, 33024
+    S = 9
     rng = np.random.default_rng(41)
     ctx = Context(mini, max_seq=max_seq)
     om = oracle.OracleModel(G.GGUFFile(mini), max_seq=max_seq)

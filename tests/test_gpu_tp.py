@@ -35,6 +35,11 @@ def _tokens():
     return rng.integers(3, 2048, 12).tolist()
 
 
+def _tokens12():
+    rng = np.random.default_rng(12)
+    return rng.integers(3, 2048, 12).tolist()
+
+
 def _worker(rank, world, path, port, q, mode):
     import torch
     import torch.distributed as dist
@@ -56,8 +61,11 @@ def _worker(rank, world, path, port, q, mode):
         toks = _tokens()
         ctx.prefill(toks[:7], 0)
         lg, _ = ctx.forward(toks[7:], 7)
+        # a 12-token verify (two consecutive forwards under tensor parallelism)
+        ctx.prefill(toks[:3], 0)
+        lg12, _ = ctx.forward(_tokens12(), 3)
         out, _ = ctx.generate(toks, mode="greedy", max_tokens=12, temp=0.0, rep_penalty=1.0, ignore_eos=True)
-        q.put((rank, lg, out, None))
+        q.put((rank, (lg, lg12), out, None))
         ctx.close()
         comm.close()
     except Exception as e:  # reported to the parent
@@ -82,6 +90,8 @@ def test_tp2_matches_single_gpu(mini, mode):
 
     ref = Context(mini, device=0, max_seq=256)
     toks = _tokens()
+    ref.prefill(toks[:3], 0)
+    lg12_ref, _ = ref.forward(_tokens12(), 3)
     ref.prefill(toks[:7], 0)
     lg_ref, _ = ref.forward(toks[7:], 7)
     out_ref, _ = ref.generate(toks, mode="greedy", max_tokens=12, temp=0.0, rep_penalty=1.0, ignore_eos=True)
@@ -100,13 +110,15 @@ def test_tp2_matches_single_gpu(mini, mode):
         p.join(timeout=60)
     for r in range(2):
         assert res[r][2] is None, res[r][2]
-    (lg0, out0, _), (lg1, out1, _) = res[0], res[1]
+    ((lg0, lg12_0), out0, _), ((lg1, lg12_1), out1, _) = res[0], res[1]
     # ranks agree bit for bit (the all-reduce hands every rank the same sums)
     np.testing.assert_array_equal(lg0.view(np.uint32), lg1.view(np.uint32))
+    np.testing.assert_array_equal(lg12_0.view(np.uint32), lg12_1.view(np.uint32))
     assert out0 == out1
     # vs one GPU: only the partial-sum order differs
-    err = np.max(np.abs(lg0.astype(np.float64) - lg_ref)) / np.max(np.abs(lg_ref))
-    assert err < LOGIT_RTOL, err
+    for a, b in ((lg0, lg_ref), (lg12_0, lg12_ref)):
+        err = np.max(np.abs(a.astype(np.float64) - b)) / np.max(np.abs(b))
+        assert err < LOGIT_RTOL, err
     if out0 != out_ref:
         i = next(j for j in range(min(len(out0), len(out_ref))) if out0[j] != out_ref[j])
         # the single-GPU logits that chose token i
