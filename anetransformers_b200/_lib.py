@@ -54,6 +54,14 @@ class GenStats(C.Structure):
                 ("total_iterations", C.c_int64), ("ms_prefill", C.c_double), ("ms_decode", C.c_double)]
 
 
+class BatchStats(C.Structure):
+    _fields_ = [("n_generated", C.c_int64), ("total_draft", C.c_int64), ("total_accepted", C.c_int64),
+                ("total_iterations", C.c_int64), ("verify_forwards", C.c_int64), ("ms_prefill", C.c_double),
+                ("ms_decode", C.c_double)]
+
+
+BATCH_MAX_WIDTH = 8
+
 vp, i32, f32, sz, u64 = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_uint64
 _SIGS = {
     "sd_last_error": (C.c_char_p, []),
@@ -93,6 +101,13 @@ _SIGS = {
     "sd_gen_params_default": (None, [vp]),
     "sd_generate": (i32, [vp, vp, vp, i32, vp, i32, vp]),
     "sd_decode": (i32, [vp, vp, vp, i32, i32, vp, i32, vp]),
+    "sd_batch_create": (i32, [vp, i32, i32, i32, vp]),
+    "sd_batch_free": (None, [vp]),
+    "sd_batch_stream": (vp, [vp]),
+    "sd_batch_forward": (i32, [vp, vp, i32, vp, vp]),
+    "sd_batch_prefill": (i32, [vp, vp, i32]),
+    "sd_batch_decode": (i32, [vp, vp, vp, i32, vp, vp, i32, vp, vp]),
+    "sd_batch_generate": (i32, [vp, vp, vp, i32, vp, i32, vp, vp]),
 }
 
 _lib = None

@@ -21,6 +21,9 @@ struct AttnArgs {
     ActImage img;          // if img.b is set: the head outputs go here instead, in the matvec fragment layout
     float* out_f32;        // optional fp32 copy of the head outputs
     const DevCtrl* ctrl;
+    // batched path: head outputs of token s go to token tok0 + s of this wide image (if wimg.p is set)
+    WImg wimg;
+    int tok0;
 };
 
 cudaError_t launch_attention(const AttnArgs& a, int grid_partial, cudaStream_t st, bool pdl);

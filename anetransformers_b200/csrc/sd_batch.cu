@@ -1,0 +1,875 @@
+// sd_batch.cu -- batched serving: n independent streams on one GPU, each with its own KV ring and
+// generation state, sharing one context's weights.
+//
+// The reference serves one stream per process (mistral/mistral_infer.m:252-391 per stream); here one
+// forward carries T tokens of every stream (T = spec_k + 1 for the verify, up to 8 for prefill chunks),
+// M = n_streams * T tokens in all, so every weight tile read from HBM feeds M tokens of int8 MMA work:
+//   embed + RMSNorm + Q8_0            k_bnorm<0>              (one CTA per token, wide-image output)
+//   per layer:
+//     QKV GEMM                        k_wgemm<WG_STORE>       (K-split partials)
+//     RoPE + KV write                 k_brope_kv              (each stream's own ring, position pos_s + j)
+//     GQA attention + Q8_0            k_battn_partial, k_battn_combine (items per stream x kv head x chunk)
+//     o-proj GEMM                     k_wgemm<WG_STORE>
+//     residual + RMSNorm + Q8_0       k_bnorm<1>
+//     gate|up GEMM + SiLU + Q8_0      k_wgemm<WG_SILU>
+//     down GEMM                       k_wgemm<WG_STORE>
+//     residual + next RMSNorm + Q8_0  k_bnorm<1>
+//   LM head                           k_wgemm<WG_STORE>, k_argmax
+// Per token the arithmetic is the single-stream forward's (sd_engine.cu): the same quantizer, per-block
+// W4A8 products, RoPE, attention item and combine, in orders that do not depend on the other streams, so
+// a stream's tokens do not depend on what the other streams hold.  Per stream, drafting, acceptance and
+// emission are the single-stream kernels (sd_spec.cu), one CTA per stream.  Tokens of a stream beyond its
+// valid count (fewer drafts than T - 1, or a finished stream) are computed with stale activations and
+// dropped: they write no K/V and no output.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "sd_dev.cuh"
+#include "sd_host.h"
+#include "sd_spec.h"
+#include "specdec_b200.h"
+
+using namespace sd;
+
+static_assert(sd::kMaxS == SD_BATCH_MAX_WIDTH, "batch width differs between the ABI and the kernels");
+
+namespace sd {
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// Per-token kernels.  Token m of a forward is token j = m % T of stream b = m / T.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ bool token_valid(const DevCtrl* ctrl, int m, int T, int* b_out, int* j_out) {
+    const int b = m / T, j = m - b * T;
+    *b_out = b;
+    *j_out = j;
+    const DevCtrl& c = ctrl[b];
+    return !c.done && j < c.n_valid;
+}
+
+constexpr int kBNormThreads = 1024;
+
+struct BNormArgs {
+    float* x;             // [M][dim] residual stream
+    const float* y;       // [yparts][M][dim] (MODE 1), slices summed in order
+    size_t ystride;
+    int yparts;
+    const uint8_t* embd;  // Q4_0 AoS [vocab][dim/32] (MODE 0)
+    const float* w;       // RMSNorm weight
+    WImg out;             // Q8_0 of the normalised row
+    int dim, T;
+    float eps;
+    const DevCtrl* ctrl;  // [n_streams]
+};
+
+// Residual add / embed + RMSNorm + Q8_0 of one token (the arithmetic of k_norm_quant, sd_quant.cu).
+template <int MODE>
+__global__ void __launch_bounds__(kBNormThreads) k_bnorm(const BNormArgs a) {
+    __shared__ __align__(16) float vs[4096];
+    __shared__ float gss[256];
+    __shared__ float scale;
+    int b, j;
+    const int m = blockIdx.x;
+    if (!token_valid(a.ctrl, m, a.T, &b, &j)) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = a.dim >> 5, bpw = nb >> 5;
+    float* x = a.x + (size_t)m * a.dim;
+    float v[4], wv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        v[k] = wv[k] = 0.f;
+        if (k < bpw) {
+            const int e = (warp + 32 * k) * 32 + lane;
+            wv[k] = a.w[e];
+            if constexpr (MODE == 0) {
+                const int token = a.ctrl[b].tokens[j];
+                v[k] = q4_0_value(a.embd + ((size_t)token * nb + (warp + 32 * k)) * 18, lane);
+            } else {
+                v[k] = x[e];
+            }
+        }
+    }
+    if constexpr (MODE == 1) {
+        float yv[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int p = 0; p < a.yparts; ++p) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (k < bpw) yv[k] += a.y[(size_t)p * a.ystride + (size_t)m * a.dim + (warp + 32 * k) * 32 + lane];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = v[k] + yv[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        if (k < bpw) {
+            const int e = (warp + 32 * k) * 32 + lane;
+            vs[e] = v[k];
+            x[e] = v[k];
+        }
+    __syncthreads();
+    const int ngroups = a.dim >> 4;
+    if ((int)threadIdx.x < ngroups) gss[threadIdx.x] = group16_sumsq(&vs[threadIdx.x * 16]);
+    __syncthreads();
+    if (warp == 0) {
+        const float tot = row_sumsq(gss, ngroups, lane);
+        if (lane == 0) scale = rms_scale(tot, a.dim, a.eps);
+    }
+    __syncthreads();
+    const float s = scale;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        if (k >= bpw) continue;
+        const int blk = warp + 32 * k;
+        // Q8_0 of u = x*w with the block scale times s (the codes do not depend on s > 0)
+        const float u = v[k] * wv[k];
+        float du;
+        int sum;
+        const int q = q8_quant_lane(u, &du, &sum);
+        uint32_t word = (uint32_t)(q & 0xFF) << (8 * (lane & 3));
+        word |= __shfl_xor_sync(0xffffffffu, word, 1);
+        word |= __shfl_xor_sync(0xffffffffu, word, 2);
+        if ((lane & 3) == 0) wimg_put_word(a.out, m, blk, lane >> 2, word);
+        if (lane == 0) wimg_put_meta(a.out, m, blk, du * s, sum);
+    }
+}
+
+struct BRopeArgs {
+    const float* qkv;     // [kparts][M][qkv_rows] GEMM partials
+    size_t pstride;
+    int kparts;
+    float* q;             // [M][q_rows]: RoPE'd, times q_scale
+    __half *k, *v;        // this layer's ring of stream 0: [max_seq][kv_rows]; stream b at + b * kv_stream
+    size_t kv_stream;
+    int q_rows, kv_rows, max_seq, head_dim, T;
+    const float* theta_inv;
+    float q_scale;
+    const DevCtrl* ctrl;
+};
+
+// RoPE of q and k (mistral/mistral_model.h:79-122, the matvec epilogue's arithmetic) and the fp16 K/V write
+// at slot (pos + j) % max_seq of the token's stream.
+__global__ void __launch_bounds__(256) k_brope_kv(const BRopeArgs a) {
+    int b, j;
+    const int m = blockIdx.x;
+    if (!token_valid(a.ctrl, m, a.T, &b, &j)) return;
+    const int tpos = a.ctrl[b].pos + j;
+    const int rows = a.q_rows + 2 * a.kv_rows;
+    const float* src = a.qkv + (size_t)m * rows;
+    const size_t ring = (size_t)b * a.kv_stream + (size_t)(tpos % a.max_seq) * a.kv_rows;
+    for (int pr = threadIdx.x; pr < rows / 2; pr += blockDim.x) {
+        const int gr = 2 * pr;
+        float ve = 0.f, vo = 0.f;
+        for (int p = 0; p < a.kparts; ++p) {
+            const float2 t2 = *reinterpret_cast<const float2*>(src + (size_t)p * a.pstride + gr);
+            ve += t2.x;
+            vo += t2.y;
+        }
+        if (gr < a.q_rows + a.kv_rows) {
+            const int i = (gr % a.head_dim) >> 1;
+            const float ang = a.theta_inv[i] * (float)tpos;
+            float sn, cs;
+            sincosf(ang, &sn, &cs);
+            const float e2 = fmaf(-vo, sn, ve * cs);
+            const float o2 = fmaf(ve, sn, vo * cs);
+            if (gr < a.q_rows) {
+                *reinterpret_cast<float2*>(a.q + (size_t)m * a.q_rows + gr) = make_float2(e2 * a.q_scale, o2 * a.q_scale);
+            } else {
+                *reinterpret_cast<__half2*>(a.k + ring + (gr - a.q_rows)) = __halves2half2(__float2half_rn(e2), __float2half_rn(o2));
+            }
+        } else {
+            *reinterpret_cast<__half2*>(a.v + ring + (gr - a.q_rows - a.kv_rows)) =
+                __halves2half2(__float2half_rn(ve), __float2half_rn(vo));
+        }
+    }
+}
+
+struct BAttnArgs {
+    AttnArgs a;        // stream 0's view (q, ring, partial buffers); a.S = T, a.wimg = o-proj input image
+    size_t kv_stream;  // halves between consecutive streams' rings
+    int T;
+    const DevCtrl* ctrl;
+};
+
+__device__ __forceinline__ AttnArgs stream_view(const BAttnArgs& ba, int b) {
+    AttnArgs v = ba.a;
+    v.q = ba.a.q + (size_t)b * ba.T * ba.a.q_ld;
+    v.k = ba.a.k + (size_t)b * ba.kv_stream;
+    v.v = ba.a.v + (size_t)b * ba.kv_stream;
+    const size_t rows = (size_t)b * ba.T * ba.a.n_heads * ba.a.max_chunks;
+    v.part_ml = ba.a.part_ml + rows;
+    v.part_acc = ba.a.part_acc + rows * kHD;
+    v.tok0 = b * ba.T;
+    v.ctrl = nullptr;
+    return v;
+}
+
+// Work items (kv head, chunk) of stream blockIdx.y, grid-strided over blockIdx.x (sd_attn.cu per stream).
+__global__ void __launch_bounds__(kAttnThreads) k_battn_partial(const BAttnArgs ba) {
+    __shared__ __align__(16) uint8_t smem[attn_smem_bytes()];
+    const int b = blockIdx.y;
+    const DevCtrl& c = ba.ctrl[b];
+    const int nv = c.done ? 0 : min(c.n_valid, ba.T);
+    if (nv <= 0) return;
+    const AttnArgs a = stream_view(ba, b);
+    const int pos = c.pos;
+    const int hi_max = pos + nv - 1;
+    const int lo_min = max(0, pos + 1 - a.max_seq);
+    const int c_first = lo_min / a.chunk, c_last = hi_max / a.chunk;
+    const int n_items = (c_last - c_first + 1) * a.n_kvh;
+    const AttnSmem sm = attn_smem_at(smem);
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int nx = item + gridDim.x;
+        attn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, nx % a.n_kvh,
+                  nx < n_items ? c_first + nx / a.n_kvh : -1, sm, threadIdx.x, [] { __syncthreads(); });
+    }
+}
+
+// Merge of one (token, head) row and its Q8_0 quantisation into the o-proj image.
+__global__ void __launch_bounds__(kCombineWarpsMax * 32) k_battn_combine(const BAttnArgs ba) {
+    __shared__ __align__(16) float obuf[kCombineWarpsMax * kHD];
+    const int row = blockIdx.x;
+    const int m = row / ba.a.n_heads, h = row - m * ba.a.n_heads;
+    int b, s;
+    if (!token_valid(ba.ctrl, m, ba.T, &b, &s)) return;
+    const AttnArgs a = stream_view(ba, b);
+    attn_combine_row(a, blockDim.x >> 5, ba.ctrl[b].pos, s, h, threadIdx.x >> 5, threadIdx.x & 31, obuf,
+                     [] { __syncthreads(); });
+}
+
+// Control blocks of a forward of T tokens per stream: tokens[b * stride + col0 + j], position pos[b] (or col0).
+__global__ void k_bset_ctrl(DevCtrl* ctrl, int n, const int* tokens, int stride, int col0, int T, const int* pos) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n) return;
+    DevCtrl& c = ctrl[b];
+    for (int j = 0; j < T; ++j) c.tokens[j] = tokens[(size_t)b * stride + col0 + j];
+    c.pos = pos ? pos[b] : col0;
+    c.n_valid = T;
+    c.done = 0;
+}
+
+// Generation state of stream b from host-chosen fields: history row b of hist_src (stride), current
+// token cur[b] (or 0), position pos (same for all streams).
+__global__ void k_binit_gen(GenState* gs, int n, GenState tmpl, int* out, int* hist, int cap, const int* hist_src,
+                            int hstride, int n_hist, const int* cur, unsigned long long seed) {
+    const int b = blockIdx.x;
+    if (b >= n) return;
+    for (int i = threadIdx.x; i < n_hist; i += blockDim.x) hist[(size_t)b * cap + i] = hist_src[(size_t)b * hstride + i];
+    if (threadIdx.x == 0) {
+        GenState g = tmpl;
+        g.out = out + (size_t)b * cap;
+        g.hist = hist + (size_t)b * cap;
+        g.cur = cur ? cur[b] : 0;
+        g.seed = seed + (unsigned long long)b;
+        gs[b] = g;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// GEMM planning: the unit shape (token tile, K split) with the least estimated time.
+// ---------------------------------------------------------------------------------------------
+struct WgPlan {
+    WGemmArgs a{};
+    int grid = 0;
+    size_t smem = 0;
+};
+
+// Cost model in ns: a quad (128 columns) of a unit costs (1 + n8 tiles per warp) x 126 ns (the A-fragment
+// work of a quad is worth about one n8 tile); a unit adds about one quad of fill / epilogue; K-split partial
+// slices are written and read back at ~6.5 TB/s.
+void wg_plan(WgPlan& p, int epi, int rows, int K, int M, int kp_lo, int kp_max, int sms, int max_smem) {
+    const int n_rg = qmat_row_groups(rows);
+    const int n_rt = (n_rg + kWgRG - 1) / kWgRG;
+    const int nq = K / 128;
+    const int NT = (M + 7) / 8;
+    double best = 1e300;
+    int bt = 4, bk = kp_lo;
+    for (int tt = 4; tt <= kWgMaxTT; tt += 4) {
+        if (tt > 4 && tt - 4 >= NT) break;  // wider tiles than the tokens add nothing
+        const int n_tt = (NT + tt - 1) / tt;
+        const int per = (std::min(tt, NT) + 3) / 4;
+        for (int kp = kp_lo; kp <= kp_max; ++kp) {
+            if (kp > kp_lo && nq / kp < 2) break;
+            const long long units = (long long)n_rt * kp * n_tt;
+            const long long waves = (units + sms - 1) / sms;
+            double t = (double)waves * ((double)nq / kp + 1.0) * (1.0 + per) * 126.0;
+            if (kp > 1) t += (double)kp * M * rows * 8.0 / 6500.0;
+            if (t < best * 0.999) {
+                best = t;
+                bt = tt;
+                bk = kp;
+            }
+        }
+    }
+    WGemmArgs& a = p.a;
+    a = WGemmArgs{};
+    a.n_rg = n_rg;
+    a.nq = nq;
+    a.NT = NT;
+    a.M = M;
+    a.n_rt = n_rt;
+    a.tt_n8 = bt;
+    a.n_tt = (NT + bt - 1) / bt;
+    a.kparts = epi == WG_SILU ? 1 : bk;
+    a.stage_bytes = kWgWStage + bt * kWSeg;
+    a.nstage = std::min(kWgMaxStages, (int)((max_smem - 2 * kWgMaxStages * 8) / a.stage_bytes));
+    const long long units = (long long)n_rt * a.kparts * a.n_tt;
+    p.grid = (int)std::min<long long>(units, sms);
+    p.smem = wgemm_smem_bytes(bt, a.nstage);
+}
+
+struct BPlans {
+    bool ready = false;
+    WgPlan qkv, wo, w13, w2, lm;
+};
+
+}  // namespace
+}  // namespace sd
+
+struct sd_batch {
+    sd_ctx* ctx = nullptr;
+    ModelView m{};
+    int dev = 0, sms = 0, max_smem = 0;
+    cudaStream_t st = nullptr;
+    int B = 0, W = 0, max_seq = 0, M_max = 0;
+    int chunk = 256, max_chunks = 0, kp_max = 8;
+    __half *kc = nullptr, *vc = nullptr;  // [n_layers][B][max_seq][kv_rows]
+    size_t kv_stream = 0, kv_layer = 0;
+    float *x = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr;
+    uint8_t *img_x = nullptr, *img_attn = nullptr, *img_h = nullptr;
+    float2* part_ml = nullptr;
+    float* part_acc = nullptr;
+    float* logits = nullptr;  // [M_max][vocab]
+    int* argmax = nullptr;    // [M_max]
+    float* probs = nullptr;   // [B][vocab]
+    DevCtrl* ctrl = nullptr;  // [B]
+    int* tok = nullptr;       // token staging (prefill / forward inputs)
+    size_t tok_cap = 0;
+    int* pos_dev = nullptr;   // [B]
+    GenState* gs = nullptr;   // [B]
+    GenState* gs_h = nullptr; // pinned [B]
+    int *g_out = nullptr, *g_hist = nullptr;
+    int g_cap = 0;
+    int* ndone = nullptr;     // [2]: streams done, most tokens a live stream still has to generate
+    int* ndone_h = nullptr;   // pinned copy
+    BPlans plans[SD_BATCH_MAX_WIDTH + 1];
+    cudaGraphExec_t fwd_graph[SD_BATCH_MAX_WIDTH + 1][2] = {};
+    cudaGraphExec_t iter_graph = nullptr;
+    int iter_T = -1;
+    GenParamsDev iter_p{};
+};
+
+namespace {
+
+int ck(cudaError_t e, const char* what) { return e == cudaSuccess ? SD_OK : cuda_fail(e, what); }
+
+#define CK(expr, what)                 \
+    do {                               \
+        int _rc = ck((expr), (what));  \
+        if (_rc) return _rc;           \
+    } while (0)
+
+template <class T>
+int dalloc(T** p, size_t n) {
+    cudaError_t e = cudaMalloc((void**)p, n * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    return SD_OK;
+}
+
+double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// Plans for T tokens per stream.  The K split of each matrix is the one chosen for the widest forward and is
+// kept for every T, so a token's sums (slice partials added in slice order) do not depend on T: a verify of
+// T = K+1 and a one-token decode give a stream bit-identical logits.  Only the token tiling follows T.
+BPlans& plans_for(sd_batch* b, int T) {
+    BPlans& P = b->plans[T];
+    if (P.ready) return P;
+    const ModelView& m = b->m;
+    const int M = b->B * T, Mw = b->B * b->W;
+    auto plan = [&](WgPlan& out, int epi, int rows, int K, int kp_max) {
+        WgPlan wide;
+        wg_plan(wide, epi, rows, K, Mw, 1, kp_max, b->sms, b->max_smem);
+        wg_plan(out, epi, rows, K, M, wide.a.kparts, wide.a.kparts, b->sms, b->max_smem);
+    };
+    plan(P.qkv, WG_STORE, m.qkv_rows, m.dim, b->kp_max);
+    plan(P.wo, WG_STORE, m.dim, m.q_rows, b->kp_max);
+    plan(P.w13, WG_SILU, 2 * m.hidden, m.dim, 1);
+    plan(P.w2, WG_STORE, m.dim, m.hidden, b->kp_max);
+    plan(P.lm, WG_STORE, m.vocab, m.dim, 1);
+    P.ready = true;
+    return P;
+}
+
+int run_wgemm(sd_batch* b, int epi, WgPlan p, const uint8_t* w, const uint8_t* act) {
+    p.a.w = w;
+    p.a.act = act;
+    p.a.err = b->m.err;
+    CK(launch_wgemm(epi, p.a, p.grid, p.smem, b->st), "wide gemm");
+    return SD_OK;
+}
+
+// One forward of T tokens per stream (positions and token ids from the control blocks).
+int enqueue_bforward(sd_batch* b, int T, bool logits) {
+    const ModelView& m = b->m;
+    const int M = b->B * T, NT = (M + 7) / 8;
+    BPlans& P = plans_for(b, T);
+    BNormArgs na{};
+    na.x = b->x;
+    na.y = b->y;
+    na.ystride = (size_t)b->M_max * m.dim;
+    na.embd = m.embd;
+    na.out = WImg{b->img_x, NT};
+    na.dim = m.dim;
+    na.T = T;
+    na.eps = m.eps;
+    na.ctrl = b->ctrl;
+    na.w = m.rms_att[0];
+    k_bnorm<0><<<M, kBNormThreads, 0, b->st>>>(na);
+    CK(cudaGetLastError(), "embed");
+    for (int l = 0; l < m.n_layers; ++l) {
+        int rc;
+        // QKV
+        WgPlan pq = P.qkv;
+        pq.a.out = b->qkv;
+        pq.a.ld = m.qkv_rows;
+        pq.a.out_rows = m.qkv_rows;
+        pq.a.part_stride = (size_t)b->M_max * m.qkv_rows;
+        if ((rc = run_wgemm(b, WG_STORE, pq, m.qkv[l], b->img_x))) return rc;
+        BRopeArgs ra{};
+        ra.qkv = b->qkv;
+        ra.pstride = pq.a.part_stride;
+        ra.kparts = pq.a.kparts;
+        ra.q = b->q;
+        ra.k = b->kc + (size_t)l * b->kv_layer;
+        ra.v = b->vc + (size_t)l * b->kv_layer;
+        ra.kv_stream = b->kv_stream;
+        ra.q_rows = m.q_rows;
+        ra.kv_rows = m.kv_rows;
+        ra.max_seq = b->max_seq;
+        ra.head_dim = m.hd;
+        ra.T = T;
+        ra.theta_inv = m.theta_inv;
+        ra.q_scale = 1.0f / sqrtf((float)m.hd);
+        ra.ctrl = b->ctrl;
+        k_brope_kv<<<M, 256, 0, b->st>>>(ra);
+        CK(cudaGetLastError(), "rope");
+        // attention
+        BAttnArgs ba{};
+        ba.a.q = b->q;
+        ba.a.q_ld = m.q_rows;
+        ba.a.k = ra.k;
+        ba.a.v = ra.v;
+        ba.a.kv_ld = m.kv_rows;
+        ba.a.n_heads = m.n_heads;
+        ba.a.n_kvh = m.n_kv;
+        ba.a.S = T;
+        ba.a.max_seq = b->max_seq;
+        ba.a.chunk = b->chunk;
+        ba.a.max_chunks = b->max_chunks;
+        ba.a.part_ml = b->part_ml;
+        ba.a.part_acc = b->part_acc;
+        ba.a.wimg = WImg{b->img_attn, NT};
+        ba.kv_stream = b->kv_stream;
+        ba.T = T;
+        ba.ctrl = b->ctrl;
+        const int per_stream = std::max(1, (4 * b->sms + b->B - 1) / b->B);
+        k_battn_partial<<<dim3(per_stream, b->B), kAttnThreads, 0, b->st>>>(ba);
+        CK(cudaGetLastError(), "attention");
+        k_battn_combine<<<M * m.n_heads, combine_warps(b->max_seq) * 32, 0, b->st>>>(ba);
+        CK(cudaGetLastError(), "combine");
+        // o-proj, residual + norm
+        WgPlan po = P.wo;
+        po.a.out = b->y;
+        po.a.ld = m.dim;
+        po.a.out_rows = m.dim;
+        po.a.part_stride = (size_t)b->M_max * m.dim;
+        if ((rc = run_wgemm(b, WG_STORE, po, m.wo[l], b->img_attn))) return rc;
+        na.w = m.rms_ffn[l];
+        na.yparts = po.a.kparts;
+        k_bnorm<1><<<M, kBNormThreads, 0, b->st>>>(na);
+        CK(cudaGetLastError(), "norm");
+        // gate|up + SiLU + Q8_0
+        WgPlan pg = P.w13;
+        pg.a.h = WImg{b->img_h, NT};
+        pg.a.hidden = m.hidden;
+        if ((rc = run_wgemm(b, WG_SILU, pg, m.w13[l], b->img_x))) return rc;
+        // down, residual + next norm
+        WgPlan pd = P.w2;
+        pd.a.out = b->y;
+        pd.a.ld = m.dim;
+        pd.a.out_rows = m.dim;
+        pd.a.part_stride = (size_t)b->M_max * m.dim;
+        if ((rc = run_wgemm(b, WG_STORE, pd, m.w2[l], b->img_h))) return rc;
+        na.w = (l + 1 < m.n_layers) ? m.rms_att[l + 1] : m.rms_final;
+        na.yparts = pd.a.kparts;
+        k_bnorm<1><<<M, kBNormThreads, 0, b->st>>>(na);
+        CK(cudaGetLastError(), "norm");
+    }
+    if (!logits) return SD_OK;
+    WgPlan pl = P.lm;
+    pl.a.out = b->logits;
+    pl.a.ld = m.vocab;
+    pl.a.out_rows = m.vocab;
+    int rc = run_wgemm(b, WG_STORE, pl, m.lm, b->img_x);
+    if (rc) return rc;
+    CK(launch_argmax(b->logits, m.vocab, M, b->argmax, nullptr, b->st, false), "argmax");
+    return SD_OK;
+}
+
+int run_bforward(sd_batch* b, int T, bool logits) {
+    cudaGraphExec_t& slot = b->fwd_graph[T][logits ? 1 : 0];
+    if (!slot) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal), "capture");
+        const int rc = enqueue_bforward(b, T, logits);
+        const cudaError_t e = cudaStreamEndCapture(b->st, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        CK(e, "capture end");
+        const cudaError_t ie = cudaGraphInstantiate(&slot, g, 0);
+        cudaGraphDestroy(g);
+        CK(ie, "graph instantiate");
+    }
+    CK(cudaGraphLaunch(slot, b->st), "graph launch");
+    return SD_OK;
+}
+
+int check_host_tokens(sd_batch* b, const int32_t* t, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (t[i] < 0 || t[i] >= b->m.vocab) return fail(SD_ERR_INVALID, "token %d out of range [0, %d)", t[i], b->m.vocab);
+    return SD_OK;
+}
+
+int ensure_tok(sd_batch* b, size_t n) {
+    if (b->tok_cap >= n) return SD_OK;
+    cudaFree(b->tok);
+    b->tok = nullptr;
+    b->tok_cap = 0;
+    int rc = dalloc(&b->tok, n);
+    if (!rc) b->tok_cap = n;
+    return rc;
+}
+
+int ensure_gen(sd_batch* b, int cap) {
+    if (b->g_cap >= cap) return SD_OK;
+    cudaFree(b->g_out);
+    cudaFree(b->g_hist);
+    b->g_out = b->g_hist = nullptr;
+    b->g_cap = 0;
+    int rc = dalloc(&b->g_out, (size_t)b->B * cap);
+    if (!rc) rc = dalloc(&b->g_hist, (size_t)b->B * cap);
+    if (!rc) b->g_cap = cap;
+    return rc;
+}
+
+int finish(sd_batch* b) {
+    CK(cudaStreamSynchronize(b->st), "stream sync");
+    return check_device_error(b->m.err, b->st);
+}
+
+// Prefill of positions [0, n) of every stream from the device tokens b->tok ([B][stride], columns [0, n));
+// the last chunk's logits are computed when last_logits is set.
+int prefill_dev(sd_batch* b, int n, int stride, bool last_logits) {
+    for (int i = 0; i < n; i += b->W) {
+        const int T = std::min(b->W, n - i);
+        k_bset_ctrl<<<(b->B + 127) / 128, 128, 0, b->st>>>(b->ctrl, b->B, b->tok, stride, i, T, nullptr);
+        CK(cudaGetLastError(), "ctrl");
+        int rc = run_bforward(b, T, last_logits && i + T >= n);
+        if (rc) return rc;
+    }
+    return SD_OK;
+}
+
+GenParamsDev gen_params_dev(sd_batch* b, const sd_gen_params* gp, int* K_out) {
+    GenParamsDev p{};
+    p.mode = gp->mode == SD_GEN_NGRAM ? SD_MODE_NGRAM : SD_MODE_GREEDY;
+    p.temp = gp->temp;
+    p.top_k = gp->top_k;
+    p.top_p = gp->top_p;
+    p.rep_penalty = gp->rep_penalty;
+    p.rep_window = gp->rep_window;
+    p.ignore_eos = gp->ignore_eos;
+    p.eos_id = b->m.eos;
+    const int K = gp->spec_k < 1 ? 1 : gp->spec_k;
+    p.spec_k = K;
+    p.ngram_n = gp->ngram_n < 1 ? 3 : gp->ngram_n;
+    p.history_has_current = gp->history_has_current;
+    p.bonus_mode = gp->bonus_mode == SD_BONUS_REFERENCE ? SD_BONUS_REF_UNIFORM : SD_BONUS_ARGMAX_FIXED;
+    p.gen_limit = p.mode == SD_MODE_GREEDY ? gp->max_tokens : gp->max_tokens - 1;
+    p.max_seq = b->max_seq;
+    *K_out = K;
+    return p;
+}
+
+int iteration_graph(sd_batch* b, const GenParamsDev& p, int T) {
+    if (b->iter_graph && b->iter_T == T && memcmp(&b->iter_p, &p, sizeof(p)) == 0) return SD_OK;
+    if (b->iter_graph) cudaGraphExecDestroy(b->iter_graph);
+    b->iter_graph = nullptr;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal), "capture");
+    int rc = ck(launch_bgen_prepare(b->gs, b->ctrl, b->B, p, b->st), "prepare");
+    if (!rc) rc = enqueue_bforward(b, T, true);
+    if (!rc) rc = ck(launch_bgen_commit(b->gs, b->ctrl, b->B, b->logits, b->probs, b->argmax, p, b->m.vocab, T, 0, b->st), "commit");
+    if (!rc) rc = ck(launch_bcount_done(b->gs, b->B, p.gen_limit, b->ndone, b->st), "count");
+    const cudaError_t e = cudaStreamEndCapture(b->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    CK(e, "capture end");
+    const cudaError_t ie = cudaGraphInstantiate(&b->iter_graph, g, 0);
+    cudaGraphDestroy(g);
+    CK(ie, "graph instantiate");
+    b->iter_T = T;
+    b->iter_p = p;
+    return SD_OK;
+}
+
+// Decode loop over every stream from the generation states already on the device.
+int decode_loop(sd_batch* b, const GenParamsDev& p, int K, int32_t* out, int out_cap, int32_t* n_out, sd_batch_stats* stats) {
+    const int T = p.mode == SD_MODE_GREEDY ? 1 : K + 1;
+    int rc = iteration_graph(b, p, T);
+    if (rc) return rc;
+    const double t0 = now_ms();
+    long long iters = 0;
+    CK(launch_bcount_done(b->gs, b->B, p.gen_limit, b->ndone, b->st), "count");
+    CK(cudaMemcpyAsync(b->ndone_h, b->ndone, 2 * sizeof(int), cudaMemcpyDeviceToHost, b->st), "count");
+    CK(cudaStreamSynchronize(b->st), "decode");
+    while (b->ndone_h[0] < b->B) {
+        // an iteration emits 1 .. T tokens per live stream: every stream is still live after
+        // ceil(most remaining / T) more iterations, so launch that many before looking again
+        const int batch = std::max(1, (b->ndone_h[1] + T - 1) / T);
+        for (int i = 0; i < batch; ++i) CK(cudaGraphLaunch(b->iter_graph, b->st), "iteration");
+        iters += batch;
+        CK(cudaMemcpyAsync(b->ndone_h, b->ndone, 2 * sizeof(int), cudaMemcpyDeviceToHost, b->st), "count");
+        CK(cudaStreamSynchronize(b->st), "decode");
+        if (iters > 4LL * (p.gen_limit + 4) + 64) return fail(SD_ERR_TIMEOUT, "batched decode did not terminate");
+    }
+    const double t1 = now_ms();
+    if ((rc = finish(b))) return rc;
+    CK(cudaMemcpy(b->gs_h, b->gs, sizeof(GenState) * b->B, cudaMemcpyDeviceToHost), "state");
+    sd_batch_stats s{};
+    for (int i = 0; i < b->B; ++i) {
+        const GenState& g = b->gs_h[i];
+        const int n = std::min(g.n_out, std::min(out_cap, b->g_cap));
+        if (n > 0) CK(cudaMemcpy(out + (size_t)i * out_cap, b->g_out + (size_t)i * b->g_cap, (size_t)n * 4, cudaMemcpyDeviceToHost), "download");
+        n_out[i] = n;
+        s.n_generated += g.n_out;
+        s.total_draft += g.total_draft;
+        s.total_accepted += g.total_accepted;
+        s.total_iterations += g.total_iterations;
+    }
+    s.verify_forwards = iters;
+    s.ms_decode = t1 - t0;
+    if (stats) {
+        const double pre = stats->ms_prefill;
+        *stats = s;
+        stats->ms_prefill = pre;
+    }
+    return SD_OK;
+}
+
+int check_gen(sd_batch* b, const sd_gen_params* gp, int n_hist) {
+    if (gp->mode == SD_GEN_SELF_SPEC) return fail(SD_ERR_UNSUPPORTED, "batched streams: greedy or n-gram drafting");
+    const int K = gp->spec_k < 1 ? 1 : gp->spec_k;
+    const int T = gp->mode == SD_GEN_GREEDY ? 1 : K + 1;
+    if (T > b->W) return fail(SD_ERR_UNSUPPORTED, "verify width %d above the batch width %d", T, b->W);
+    const int vw = std::max(kMaxS, T);
+    if (n_hist + gp->max_tokens + vw + 1 > b->max_seq) return fail(SD_ERR_INVALID, "history + tokens exceed the KV ring");
+    return SD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void sd_batch_free(sd_batch* b) {
+    if (!b) return;
+    cudaSetDevice(b->dev);
+    if (b->st) cudaStreamSynchronize(b->st);
+    for (auto& row : b->fwd_graph)
+        for (auto& g : row)
+            if (g) cudaGraphExecDestroy(g);
+    if (b->iter_graph) cudaGraphExecDestroy(b->iter_graph);
+    cudaFree(b->kc); cudaFree(b->vc); cudaFree(b->x); cudaFree(b->y); cudaFree(b->qkv); cudaFree(b->q);
+    cudaFree(b->img_x); cudaFree(b->img_attn); cudaFree(b->img_h); cudaFree(b->part_ml); cudaFree(b->part_acc);
+    cudaFree(b->logits); cudaFree(b->argmax); cudaFree(b->probs); cudaFree(b->ctrl); cudaFree(b->tok);
+    cudaFree(b->pos_dev); cudaFree(b->gs); cudaFree(b->g_out); cudaFree(b->g_hist); cudaFree(b->ndone);
+    if (b->gs_h) cudaFreeHost(b->gs_h);
+    if (b->ndone_h) cudaFreeHost(b->ndone_h);
+    if (b->st) cudaStreamDestroy(b->st);
+    delete b;
+}
+
+void* sd_batch_stream(sd_batch* b) { return b ? (void*)b->st : nullptr; }
+
+int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_batch** out) {
+    clear_error();
+    if (!ctx || !out || n_streams < 1 || max_seq < 16 || max_width < 1 || max_width > SD_BATCH_MAX_WIDTH)
+        return fail(SD_ERR_INVALID, "sd_batch_create: bad arguments");
+    *out = nullptr;
+    sd_batch* b = new sd_batch();
+    int rc = sd_ctx_model_view(ctx, &b->m);
+    auto bail = [&](int code) { sd_batch_free(b); return code; };
+    if (rc) return bail(rc);
+    const ModelView& m = b->m;
+    if (m.tp_size != 1) return bail(fail(SD_ERR_UNSUPPORTED, "batched streams run on single-GPU contexts"));
+    if (m.dim > 4096 || m.dim % 1024) return bail(fail(SD_ERR_UNSUPPORTED, "dim %d", m.dim));
+    b->ctx = ctx;
+    b->dev = m.dev;
+    b->B = n_streams;
+    b->W = max_width;
+    b->max_seq = max_seq;
+    b->M_max = n_streams * max_width;
+    b->sms = device_sm_count(b->dev);
+    b->max_smem = device_max_smem(b->dev);
+    b->max_chunks = (max_seq + b->chunk - 1) / b->chunk;
+    if (cudaSetDevice(b->dev) != cudaSuccess) return bail(fail(SD_ERR_INVALID, "bad device %d", b->dev));
+    if ((rc = ck(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking), "stream"))) return bail(rc);
+    if ((rc = ck(wgemm_init_attrs(b->max_smem), "gemm attributes"))) return bail(rc);
+    b->kv_stream = (size_t)max_seq * m.kv_rows;
+    b->kv_layer = (size_t)n_streams * b->kv_stream;
+    const size_t M = b->M_max;
+    const size_t parts = (size_t)M * m.n_heads * b->max_chunks;
+    if ((rc = dalloc(&b->kc, (size_t)m.n_layers * b->kv_layer)) || (rc = dalloc(&b->vc, (size_t)m.n_layers * b->kv_layer)) ||
+        (rc = dalloc(&b->x, M * m.dim)) || (rc = dalloc(&b->y, (size_t)b->kp_max * M * m.dim)) ||
+        (rc = dalloc(&b->qkv, (size_t)b->kp_max * M * m.qkv_rows)) || (rc = dalloc(&b->q, M * m.q_rows)) ||
+        (rc = dalloc(&b->img_x, wimg_bytes((int)M, m.dim))) || (rc = dalloc(&b->img_attn, wimg_bytes((int)M, m.q_rows))) ||
+        (rc = dalloc(&b->img_h, wimg_bytes((int)M, m.hidden))) || (rc = dalloc(&b->part_ml, parts)) ||
+        (rc = dalloc(&b->part_acc, parts * kHD)) || (rc = dalloc(&b->logits, M * m.vocab)) ||
+        (rc = dalloc(&b->argmax, M)) || (rc = dalloc(&b->probs, (size_t)n_streams * m.vocab)) ||
+        (rc = dalloc(&b->ctrl, (size_t)n_streams)) || (rc = dalloc(&b->pos_dev, (size_t)n_streams)) ||
+        (rc = dalloc(&b->gs, (size_t)n_streams)) || (rc = dalloc(&b->ndone, 2)))
+        return bail(rc);
+    if ((rc = ck(cudaMallocHost((void**)&b->gs_h, sizeof(GenState) * n_streams), "pinned state"))) return bail(rc);
+    if ((rc = ck(cudaMallocHost((void**)&b->ndone_h, 2 * sizeof(int)), "pinned counter"))) return bail(rc);
+    // images start zeroed: tokens past a forward's count read zeros, never uninitialised bytes
+    cudaMemsetAsync(b->img_x, 0, wimg_bytes((int)M, m.dim), b->st);
+    cudaMemsetAsync(b->img_attn, 0, wimg_bytes((int)M, m.q_rows), b->st);
+    cudaMemsetAsync(b->img_h, 0, wimg_bytes((int)M, m.hidden), b->st);
+    cudaMemsetAsync(b->x, 0, M * m.dim * sizeof(float), b->st);
+    cudaMemsetAsync(b->ctrl, 0, sizeof(DevCtrl) * n_streams, b->st);
+    cudaMemsetAsync(b->gs, 0, sizeof(GenState) * n_streams, b->st);
+    if ((rc = finish(b))) return bail(rc);
+    *out = b;
+    return SD_OK;
+}
+
+int sd_batch_forward(sd_batch* b, const int32_t* tokens, int T, const int32_t* pos, float* logits) {
+    clear_error();
+    if (!b || !tokens || !pos || T < 1 || T > b->W) return fail(SD_ERR_INVALID, "sd_batch_forward: bad arguments");
+    int rc = check_host_tokens(b, tokens, (size_t)b->B * T);
+    if (rc) return rc;
+    for (int i = 0; i < b->B; ++i)
+        if (pos[i] < 0 || pos[i] + T > b->max_seq) return fail(SD_ERR_INVALID, "stream %d: positions past the ring", i);
+    cudaSetDevice(b->dev);
+    if ((rc = ensure_tok(b, (size_t)b->B * T))) return rc;
+    CK(cudaMemcpyAsync(b->tok, tokens, (size_t)b->B * T * 4, cudaMemcpyHostToDevice, b->st), "tokens");
+    CK(cudaMemcpyAsync(b->pos_dev, pos, (size_t)b->B * 4, cudaMemcpyHostToDevice, b->st), "positions");
+    k_bset_ctrl<<<(b->B + 127) / 128, 128, 0, b->st>>>(b->ctrl, b->B, b->tok, T, 0, T, b->pos_dev);
+    CK(cudaGetLastError(), "ctrl");
+    if ((rc = run_bforward(b, T, logits != nullptr))) return rc;
+    if (logits)
+        CK(cudaMemcpyAsync(logits, b->logits, (size_t)b->B * T * b->m.vocab * 4, cudaMemcpyDeviceToHost, b->st), "logits");
+    return finish(b);
+}
+
+int sd_batch_prefill(sd_batch* b, const int32_t* tokens, int n) {
+    clear_error();
+    if (!b || !tokens || n < 1 || n > b->max_seq) return fail(SD_ERR_INVALID, "sd_batch_prefill: bad arguments");
+    int rc = check_host_tokens(b, tokens, (size_t)b->B * n);
+    if (rc) return rc;
+    cudaSetDevice(b->dev);
+    if ((rc = ensure_tok(b, (size_t)b->B * n))) return rc;
+    CK(cudaMemcpyAsync(b->tok, tokens, (size_t)b->B * n * 4, cudaMemcpyHostToDevice, b->st), "tokens");
+    if ((rc = prefill_dev(b, n, n, false))) return rc;
+    return finish(b);
+}
+
+int sd_batch_decode(sd_batch* b, const sd_gen_params* gp, const int32_t* history, int n_hist, const int32_t* first,
+                    int32_t* out, int out_cap, int32_t* n_out, sd_batch_stats* stats) {
+    clear_error();
+    if (!b || !gp || !history || n_hist < 1 || !first || !out || out_cap < 1 || !n_out)
+        return fail(SD_ERR_INVALID, "sd_batch_decode: bad arguments");
+    int rc = check_gen(b, gp, n_hist);
+    if (rc) return rc;
+    if ((rc = check_host_tokens(b, history, (size_t)b->B * n_hist)) || (rc = check_host_tokens(b, first, (size_t)b->B)))
+        return rc;
+    cudaSetDevice(b->dev);
+    const int cap = n_hist + gp->max_tokens + 2 * kMaxVerify + 16;
+    if ((rc = ensure_gen(b, cap)) || (rc = ensure_tok(b, (size_t)b->B * n_hist + b->B))) return rc;
+    int K = 1;
+    const GenParamsDev p = gen_params_dev(b, gp, &K);
+    CK(cudaMemcpyAsync(b->tok, history, (size_t)b->B * n_hist * 4, cudaMemcpyHostToDevice, b->st), "history");
+    int* cur = b->tok + (size_t)b->B * n_hist;
+    CK(cudaMemcpyAsync(cur, first, (size_t)b->B * 4, cudaMemcpyHostToDevice, b->st), "first");
+    GenState t{};
+    t.pos = n_hist;  // the fix-up below moves it to n_hist - 1, where the first token (history's last) sits
+    t.out_cap = cap;
+    t.hist_cap = cap;
+    t.hlen = n_hist;
+    t.rng_counter = 1ull << 20;
+    k_binit_gen<<<b->B, 256, 0, b->st>>>(b->gs, b->B, t, b->g_out, b->g_hist, cap, b->tok, n_hist, n_hist, cur, gp->seed);
+    CK(cudaGetLastError(), "state");
+    // the first token counts as generated but is not in the output (sd_decode semantics)
+    CK(launch_bgen_first_fixup(b->gs, b->B, p.gen_limit, p.ignore_eos, p.eos_id, b->st), "state");
+    if (stats) stats->ms_prefill = 0.0;
+    return decode_loop(b, p, K, out, out_cap, n_out, stats);
+}
+
+int sd_batch_generate(sd_batch* b, const sd_gen_params* gp, const int32_t* prompts, int n_prompt, int32_t* out,
+                      int out_cap, int32_t* n_out, sd_batch_stats* stats) {
+    clear_error();
+    if (!b || !gp || !prompts || n_prompt < 1 || !out || out_cap < 1 || !n_out)
+        return fail(SD_ERR_INVALID, "sd_batch_generate: bad arguments");
+    int rc = check_gen(b, gp, n_prompt);
+    if (rc) return rc;
+    if ((rc = check_host_tokens(b, prompts, (size_t)b->B * n_prompt))) return rc;
+    cudaSetDevice(b->dev);
+    const double t0 = now_ms();
+    const int cap = n_prompt + gp->max_tokens + 2 * kMaxVerify + 16;
+    if ((rc = ensure_gen(b, cap)) || (rc = ensure_tok(b, (size_t)b->B * n_prompt))) return rc;
+    CK(cudaMemcpyAsync(b->tok, prompts, (size_t)b->B * n_prompt * 4, cudaMemcpyHostToDevice, b->st), "prompts");
+    if ((rc = prefill_dev(b, n_prompt, n_prompt, true))) return rc;
+    const int Tl = n_prompt - (n_prompt - 1) / b->W * b->W;  // tokens in the last chunk
+    // first token: sample_token with the repetition penalty over the prompt window, from each stream's last
+    // prompt row (mistral/mistral_infer.m:610-621)
+    GenParamsDev p1{};
+    p1.mode = SD_MODE_GREEDY;
+    p1.temp = gp->temp;
+    p1.top_k = gp->top_k;
+    p1.top_p = gp->top_p;
+    p1.rep_penalty = gp->rep_penalty;
+    p1.rep_window = gp->rep_window;
+    p1.ignore_eos = 1;
+    p1.eos_id = b->m.eos;
+    p1.gen_limit = 1;
+    p1.max_seq = b->max_seq;
+    GenState t{};
+    t.pos = n_prompt;
+    t.out_cap = cap;
+    t.hist_cap = cap;
+    t.hlen = n_prompt;
+    k_binit_gen<<<b->B, 256, 0, b->st>>>(b->gs, b->B, t, b->g_out, b->g_hist, cap, b->tok, n_prompt, n_prompt, nullptr,
+                                         gp->seed);
+    CK(cudaGetLastError(), "state");
+    CK(launch_bgen_commit(b->gs, b->ctrl, b->B, b->logits, b->probs, b->argmax, p1, b->m.vocab, Tl, Tl - 1, b->st), "first token");
+    int K = 1;
+    const GenParamsDev p = gen_params_dev(b, gp, &K);
+    CK(launch_bgen_first_fixup(b->gs, b->B, p.gen_limit, p.ignore_eos, p.eos_id, b->st), "state");
+    if ((rc = finish(b))) return rc;
+    sd_batch_stats s{};
+    s.ms_prefill = now_ms() - t0;
+    rc = decode_loop(b, p, K, out, out_cap, n_out, &s);
+    if (rc) return rc;
+    if (stats) *stats = s;
+    return SD_OK;
+}
+
+}  // extern "C"

@@ -2,7 +2,7 @@
 // sd_quant.cu) and the persistent forward kernel (sd_fwd.cu).  Both paths run the same code in the same
 // reduction orders, so they produce bit-identical results.
 #pragma once
-#include "sd_attn.h"
+#include "sd_batch.h"
 #include "sd_common.cuh"
 
 namespace sd {
@@ -77,6 +77,19 @@ __device__ __forceinline__ void image_put_meta(const ActImage& im, int s, int bl
     float* mp = reinterpret_cast<float*>(im.m + (size_t)blk * 4 + (s >> 1));
     mp[s & 1] = d;
     mp[(s & 1) + 2] = act_offset(sum);
+}
+
+// The same writes into a wide image (sd_batch.h) for token m.
+__device__ __forceinline__ uint8_t* wimg_seg(const WImg& im, int m, int blk) {
+    return im.p + ((size_t)(blk >> 2) * im.NT + (m >> 3)) * kWSeg;
+}
+__device__ __forceinline__ void wimg_put_word(const WImg& im, int m, int blk, int w, uint32_t word) {
+    reinterpret_cast<uint32_t*>(wimg_seg(im, m, blk) + (blk & 3) * 256 + (4 * (m & 7) + (w & 3)) * 8)[w >> 2] = word;
+}
+__device__ __forceinline__ void wimg_put_meta(const WImg& im, int m, int blk, float d, int sum) {
+    float* mp = reinterpret_cast<float*>(wimg_seg(im, m, blk) + 1024 + (blk & 3) * 64 + ((m & 7) >> 1) * 16);
+    mp[m & 1] = d;
+    mp[(m & 1) + 2] = act_offset(sum);
 }
 
 // Stage Q8 planes (global, row stride K) blocks [kb0, kb0 + nb) of tokens < nv into A.  Loads are
@@ -481,11 +494,10 @@ __device__ __forceinline__ float exp_fast(float x) {
     return y;
 }
 
-// L2 prefetch of the K and V rows of kv head kvh at positions [p0, p1) (p1 - p0 <= 128): one 256-byte row
-// per thread, K by threads 0-127, V by 128-255.
+// L2 prefetch of the K and V rows of kv head kvh at positions [p0, p1): one 256-byte row per thread per
+// round of 128 positions, K by threads 0-127, V by 128-255.
 __device__ __forceinline__ void attn_prefetch(const AttnArgs& a, int kvh, int p0, int p1, int tid) {
-    const int p = p0 + (tid & 127);
-    if (p < p1) {
+    for (int p = p0 + (tid & 127); p < p1; p += 128) {
         const size_t off = (size_t)ring_slot(p, a.max_seq) * a.kv_ld + (size_t)kvh * kHD;
         prefetch_l2((tid < 128 ? a.k : a.v) + off, kHD * 2);
     }
@@ -532,7 +544,11 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
     const int p1 = min((c + 1) * a.chunk, hi_max + 1);  // exclusive
     const int lo_max = max(0, pos + nv - a.max_seq);      // window start of the last valid token
     attn_prefetch(a, kvh, p0, p1, tid);
-    if (nc >= 0) attn_prefetch(a, nkvh, max(nc * a.chunk, lo_min), min((nc + 1) * a.chunk, hi_max + 1), tid);
+    if (nc >= 0) {
+        // the next item's first 128 positions (its whole chunk when chunks are that short)
+        const int np0 = max(nc * a.chunk, lo_min);
+        attn_prefetch(a, nkvh, np0, min(min((nc + 1) * a.chunk, hi_max + 1), np0 + 128), tid);
+    }
     uint4 kr[2], vr[2];
     float4 qv[4];
 #pragma unroll
@@ -803,6 +819,12 @@ __device__ void attn_combine_row(const AttnArgs& a, int nwc, int pos, int s, int
         const int blk = h * (kHD / 32) + (lane >> 3);
         image_put_word(a.img, s, blk, lane & 7, packed);
         if ((lane & 7) == 0) image_put_meta(a.img, s, blk, d, qsum);
+        return;
+    }
+    if (a.wimg.p) {
+        const int blk = h * (kHD / 32) + (lane >> 3);
+        wimg_put_word(a.wimg, a.tok0 + s, blk, lane & 7, packed);
+        if ((lane & 7) == 0) wimg_put_meta(a.wimg, a.tok0 + s, blk, d, qsum);
         return;
     }
     *reinterpret_cast<uint32_t*>(a.out.qs + row_off + lane * 4) = packed;

@@ -1429,3 +1429,37 @@ int sd_generate(sd_ctx* c, const sd_gen_params* gp, const int32_t* prompt, int n
 }
 
 }  // extern "C"
+
+int sd_ctx_model_view(sd_ctx* c, ModelView* m) {
+    if (!c || !m) return fail(SD_ERR_INVALID, "model view: bad arguments");
+    if (c->n_layers > kMaxLayers) return fail(SD_ERR_UNSUPPORTED, "more than %d layers", kMaxLayers);
+    *m = ModelView{};
+    m->dev = c->dev;
+    m->tp_size = c->tp_size;
+    m->dim = c->dim;
+    m->hidden = c->hid_l;
+    m->n_layers = c->n_layers;
+    m->n_heads = c->nh_l;
+    m->n_kv = c->nkv_l;
+    m->hd = c->hd;
+    m->vocab = c->vocab;
+    m->eos = c->eos;
+    m->eps = c->eps;
+    m->q_rows = c->q_rows;
+    m->kv_rows = c->kv_rows;
+    m->qkv_rows = c->qkv_rows;
+    for (int l = 0; l < c->n_layers; ++l) {
+        m->qkv[l] = c->L[l].qkv;
+        m->wo[l] = c->L[l].wo;
+        m->w13[l] = c->L[l].w13;
+        m->w2[l] = c->L[l].w2;
+        m->rms_att[l] = c->L[l].rms_att;
+        m->rms_ffn[l] = c->L[l].rms_ffn;
+    }
+    m->embd = c->embd;
+    m->lm = c->lm;
+    m->rms_final = c->rms_final;
+    m->theta_inv = c->theta_inv;
+    m->err = c->err;
+    return SD_OK;
+}

@@ -20,4 +20,23 @@ int gemv_plan_fixed(GemvArgs& a, int dev, int* grid, size_t* smem);
 int run_gemv(int epi, const GemvArgs& a, int dev, cudaStream_t st, bool pdl);
 // Sum-all-reduce of n fp32 values in place over an NCCL communicator (sd_nccl.cu).
 int nccl_allreduce_sum(void* comm, float* buf, size_t n, cudaStream_t st);
+
+// A context's device-resident model, as the batched engine (sd_batch.cu) reads it.
+constexpr int kMaxLayers = 128;
+struct ModelView {
+    int dev, tp_size;
+    int dim, hidden, n_layers, n_heads, n_kv, hd, vocab, eos;
+    float eps;
+    int q_rows, kv_rows, qkv_rows;
+    const uint8_t *qkv[kMaxLayers], *wo[kMaxLayers], *w13[kMaxLayers], *w2[kMaxLayers];  // tile16x4
+    const float *rms_att[kMaxLayers], *rms_ffn[kMaxLayers];
+    const uint8_t* embd;  // Q4_0 AoS [vocab][dim/32]
+    const uint8_t* lm;    // tile16x4 [vocab][dim]
+    const float* rms_final;
+    const float* theta_inv;
+    int* err;             // the context's device error word
+};
 }  // namespace sd
+
+struct sd_ctx;
+int sd_ctx_model_view(sd_ctx* c, sd::ModelView* out);  // defined in sd_engine.cu

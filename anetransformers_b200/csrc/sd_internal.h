@@ -52,6 +52,25 @@ struct ActImage {
     float4* m;
 };
 
+// ---------------------------------------------------------------------------------------------
+// Wide activation image: Q8_0 activations of M tokens over K columns in the GEMM's fragment layout.
+// Tokens are grouped in n8 tiles (NT = ceil(M / 8)); for quad q (blocks 4q..4q+3) and n8 tile n the
+// segment at ((size_t)q * NT + n) * kWSeg bytes holds
+//   [0, 1024)    uint2 b[4][32]: entry 4s + tt of block bq = (word tt, word tt + 4) of token 8n + s's codes
+//                (the int8 MMA B fragment of lane 4s + tt)
+//   [1024, 1280) float4 m[4][4]: entry t of block bq = (xd(8n+2t), xd(8n+2t+1), off(8n+2t), off(8n+2t+1)),
+//                off = -(kMagic + 8 * code sum) (sd_dev.cuh)
+// so a CTA's stage (one quad of a range of n8 tiles) is one contiguous bulk copy.
+// ---------------------------------------------------------------------------------------------
+constexpr int kWSeg = 1280;
+
+struct WImg {
+    uint8_t* p;
+    int NT;
+};
+
+inline size_t wimg_bytes(int M, int K) { return (size_t)(K / 128) * ((M + 7) / 8) * kWSeg; }
+
 // Q8_0 activations on device as planes (codes, fp32 scale, per-block code sum).
 struct Q8Planes {
     int8_t* qs;     // [S][n]

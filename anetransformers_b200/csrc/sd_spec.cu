@@ -302,7 +302,7 @@ __device__ void emit(GenState* g, int tok) {
 // Draft phase.  NGRAM: prompt-lookup scan (speculative.h:425-464) over the history (excluding the
 // current token unless the reference wiring is requested); writes the verify batch
 // [current, drafts...] into ctrl.  GREEDY / no draft: batch = [current].
-__global__ void k_gen_prepare(GenState* g, DevCtrl* ctrl, GenParamsDev p) {
+__device__ void gen_prepare_body(GenState* g, DevCtrl* ctrl, const GenParamsDev& p) {
     __shared__ int best;
     if (g->done) {
         if (threadIdx.x == 0) {
@@ -346,6 +346,13 @@ __global__ void k_gen_prepare(GenState* g, DevCtrl* ctrl, GenParamsDev p) {
         g->n_draft = nd;
         for (int i = 0; i < nd; ++i) g->draft_probs[i] = 0.9f;   // n-gram "probability"
     }
+}
+
+__global__ void k_gen_prepare(GenState* g, DevCtrl* ctrl, GenParamsDev p) { gen_prepare_body(g, ctrl, p); }
+
+// Batched streams: CTA b prepares stream b.
+__global__ void k_bgen_prepare(GenState* gs, DevCtrl* ctrls, GenParamsDev p) {
+    gen_prepare_body(gs + blockIdx.x, ctrls + blockIdx.x, p);
 }
 
 // Self-speculative drafter step: after a draft-depth forward of token tokens[0] at pos + k, take the
@@ -392,8 +399,8 @@ __global__ void k_gen_self_verify(GenState* g, DevCtrl* ctrl, int K) {
 }
 
 // Accept / emit phase after the verify (or single) forward.  logits: [n_valid][vocab].
-__global__ void __launch_bounds__(kSampleThreads) k_gen_commit(GenState* g, DevCtrl* ctrl, float* logits, float* probs,
-                                                               const int* argmax, GenParamsDev p, int vocab) {
+__device__ void gen_commit_body(GenState* g, DevCtrl* ctrl, float* logits, float* probs, const int* argmax,
+                                const GenParamsDev& p, int vocab) {
     __shared__ int acc[kMaxVerify + 1];
     __shared__ int n_acc_s;
     if (g->done) return;
@@ -521,6 +528,68 @@ __global__ void __launch_bounds__(kSampleThreads) k_gen_commit(GenState* g, DevC
         g->cur = acc[na - 1];
         if (stop || g->generated >= p.gen_limit || g->pos + max(kMaxS, (p.mode == SD_MODE_GREEDY ? 0 : p.spec_k) + 1) >= p.max_seq) g->done = 1;
     }
+}
+
+__global__ void __launch_bounds__(kSampleThreads) k_gen_commit(GenState* g, DevCtrl* ctrl, float* logits, float* probs,
+                                                               const int* argmax, GenParamsDev p, int vocab) {
+    gen_commit_body(g, ctrl, logits, probs, argmax, p, vocab);
+}
+
+// Batched streams: CTA b commits stream b from its verify rows b*T + row0 .. of logits / argmax.
+__global__ void __launch_bounds__(kSampleThreads) k_bgen_commit(GenState* gs, DevCtrl* ctrls, float* logits, float* probs,
+                                                                const int* argmax, GenParamsDev p, int vocab, int T,
+                                                                int row0) {
+    const int b = blockIdx.x;
+    gen_commit_body(gs + b, ctrls + b, logits + ((size_t)b * T + row0) * vocab, probs + (size_t)b * vocab,
+                    argmax + (size_t)b * T + row0, p, vocab);
+}
+
+// After the first-token commit (one greedy sample from the last prompt row): the decode loop's state, as
+// the single-stream path sets it up (the first token sits at position n_prompt, not yet fed).
+__global__ void k_bgen_first_fixup(GenState* gs, int n, int gen_limit, int ignore_eos, int eos) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n) return;
+    GenState* g = gs + b;
+    g->pos -= 1;
+    g->generated = 0;
+    g->total_draft = g->total_accepted = g->total_iterations = 0;
+    g->done = (gen_limit <= 0 || (!ignore_eos && g->cur == eos)) ? 1 : 0;
+}
+
+// out[0] = streams done, out[1] = the most tokens a live stream still has to generate.
+__global__ void k_bcount_done(const GenState* gs, int n, int gen_limit, int* out) {
+    int c = 0, rem = 0;
+    for (int b = threadIdx.x; b < n; b += blockDim.x) {
+        c += gs[b].done ? 1 : 0;
+        if (!gs[b].done) rem = max(rem, gen_limit - gs[b].generated);
+    }
+    c = (int)block_sum((float)c);  // counts far below 2^24: exact
+    rem = (int)block_max((float)rem);
+    if (threadIdx.x == 0) {
+        out[0] = c;
+        out[1] = rem;
+    }
+}
+
+cudaError_t launch_bgen_prepare(GenState* gs, DevCtrl* ctrls, int n, const GenParamsDev& p, cudaStream_t st) {
+    k_bgen_prepare<<<n, 1024, 0, st>>>(gs, ctrls, p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bgen_commit(GenState* gs, DevCtrl* ctrls, int n, float* logits, float* probs, const int* argmax,
+                               const GenParamsDev& p, int vocab, int T, int row0, cudaStream_t st) {
+    k_bgen_commit<<<n, kSampleThreads, 0, st>>>(gs, ctrls, logits, probs, argmax, p, vocab, T, row0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bgen_first_fixup(GenState* gs, int n, int gen_limit, int ignore_eos, int eos, cudaStream_t st) {
+    k_bgen_first_fixup<<<(n + 127) / 128, 128, 0, st>>>(gs, n, gen_limit, ignore_eos, eos);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bcount_done(const GenState* gs, int n, int gen_limit, int* out, cudaStream_t st) {
+    k_bcount_done<<<1, 256, 0, st>>>(gs, n, gen_limit, out);
+    return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------------------------

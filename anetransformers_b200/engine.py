@@ -215,6 +215,80 @@ class Context:
         return acc[:n].tolist(), ctr.value
 
 
+class BatchContext:
+    """Many independent streams on one GPU sharing a Context's weights (sd_batch_* of the C ABI).  Every
+    stream has its own KV ring and generation state; one forward carries `width` tokens of every stream."""
+
+    def __init__(self, ctx: Context, n_streams: int, max_seq: int, width: int = _lib.BATCH_MAX_WIDTH):
+        self.ctx = ctx  # keeps the weights alive
+        self.n_streams, self.max_seq, self.width, self.vocab = n_streams, max_seq, width, ctx.vocab
+        h = C.c_void_p()
+        _lib.check(_lib.lib().sd_batch_create(ctx.h, n_streams, max_seq, width, C.byref(h)), "sd_batch_create")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            _lib.lib().sd_batch_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return _lib.lib().sd_batch_stream(self.h) or 0
+
+    def forward(self, tokens, pos, want_logits: bool = True) -> np.ndarray:
+        """tokens [n_streams, T] at positions pos[s] ..; returns logits [n_streams, T, vocab] (or None)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        assert t.ndim == 2 and t.shape[0] == self.n_streams
+        ps = _i32(pos)
+        lg = np.empty((t.shape[0], t.shape[1], self.vocab), np.float32) if want_logits else None
+        _lib.check(_lib.lib().sd_batch_forward(self.h, t.ctypes.data, t.shape[1], ps.ctypes.data,
+                                               lg.ctypes.data if want_logits else None), "sd_batch_forward")
+        return lg
+
+    def prefill(self, tokens):
+        t = np.ascontiguousarray(tokens, np.int32)
+        _lib.check(_lib.lib().sd_batch_prefill(self.h, t.ctypes.data, t.shape[1]), "sd_batch_prefill")
+
+    def _out(self, p):
+        return np.empty((self.n_streams, p.max_tokens + 2 * MAX_VERIFY + 4), np.int32), np.empty(self.n_streams, np.int32)
+
+    def generate(self, prompts, **kw) -> Tuple[List[List[int]], Dict]:
+        """Prefill + first token + decode of every stream (prompts [n_streams, n_prompt])."""
+        p = Context.gen_params(**kw)
+        t = np.ascontiguousarray(prompts, np.int32)
+        out, n = self._out(p)
+        st = _lib.BatchStats()
+        _lib.check(_lib.lib().sd_batch_generate(self.h, C.byref(p), t.ctypes.data, t.shape[1], out.ctypes.data,
+                                                out.shape[1], n.ctypes.data, C.byref(st)), "sd_batch_generate")
+        return [out[i, :n[i]].tolist() for i in range(self.n_streams)], _batch_stats(st)
+
+    def decode(self, history, first, **kw) -> Tuple[List[List[int]], Dict]:
+        """Decode only: history [n_streams, n_hist] (ends with first), K/V of positions < n_hist - 1 in place."""
+        p = Context.gen_params(**kw)
+        h = np.ascontiguousarray(history, np.int32)
+        f = _i32(first)
+        out, n = self._out(p)
+        st = _lib.BatchStats()
+        _lib.check(_lib.lib().sd_batch_decode(self.h, C.byref(p), h.ctypes.data, h.shape[1], f.ctypes.data,
+                                              out.ctypes.data, out.shape[1], n.ctypes.data, C.byref(st)),
+                   "sd_batch_decode")
+        return [out[i, :n[i]].tolist() for i in range(self.n_streams)], _batch_stats(st)
+
+
+def _batch_stats(st: _lib.BatchStats) -> Dict:
+    it = st.total_iterations
+    return {"n_generated": st.n_generated, "total_draft": st.total_draft, "total_accepted": st.total_accepted,
+            "total_iterations": it, "verify_forwards": st.verify_forwards, "ms_prefill": st.ms_prefill,
+            "ms_decode": st.ms_decode,
+            "acceptance_rate": ((st.total_accepted - it) / st.total_draft) if st.total_draft else 0.0}
+
+
 def _stats(st: _lib.GenStats) -> Dict:
     it = st.total_iterations
     return {"n_generated": st.n_generated, "total_draft": st.total_draft, "total_accepted": st.total_accepted,

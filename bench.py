@@ -336,6 +336,114 @@ def run_selfspec(args, ctx, rank, world, local, dist, tp, peaks):
         print(json.dumps(line), flush=True)
 
 
+# batched speculative serving, 64 streams per GPU, 4096-token random contexts, K = 4 n-gram drafts
+SERVE_STREAMS, SERVE_CTX, SERVE_TOKENS = 64, 4096, 256
+
+
+def run_serving(args, ctx_path, rank, world, local, dist, peaks):
+    """per GPU, 64 concurrent streams, each with a 4096-token uniform-random context (K/V
+    prefilled by the device), n-gram drafting n=3 K=4, temp 0, 256 generated tokens per stream; every verify
+    forward carries 64 x 5 = 320 tokens (M = 320 wide-token W4A8 GEMMs).  A step = one batched 256-token decode
+    of all streams from the prefilled contexts.  N GPUs = N data-parallel replicas (weak scaling)."""
+    import torch
+    from anetransformers_b200.engine import BatchContext, Context
+    B, n_ctx = args.streams, args.ctx_serve
+    ctx = Context(ctx_path, device=local, max_seq=64)
+    bc = BatchContext(ctx, B, max_seq=n_ctx + args.tokens + 64, width=8)
+    rng = np.random.default_rng(2024 + rank)
+    prompts = rng.integers(3, 32000, (B, n_ctx)).astype(np.int32)
+    t = time.perf_counter()
+    bc.prefill(prompts[:, :-1])
+    lg = bc.forward(prompts[:, -1:], np.full(B, n_ctx - 1, np.int32))
+    t_prefill = time.perf_counter() - t
+    first = lg[:, 0].argmax(axis=1).astype(np.int32)
+    hist = np.concatenate([prompts, first[:, None]], axis=1)
+    kw = dict(mode="ngram", max_tokens=args.tokens, temp=0.0, rep_penalty=1.0, ignore_eos=True, spec_k=SPEC_K,
+              ngram_n=NGRAM_N)
+    for _ in range(args.warmup):
+        bc.decode(hist, first, **kw)
+    stream = torch.cuda.ExternalStream(bc.stream)
+    clocks = ClockSampler(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    tokens = iters = drafted = accepted = fwds = 0
+    for _ in range(args.steps):
+        outs, st = bc.decode(hist, first, **kw)
+        tokens += sum(len(o) for o in outs)
+        iters += st["total_iterations"]
+        drafted += st["total_draft"]
+        accepted += st["total_accepted"]
+        fwds += st["verify_forwards"]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max, tokens_all = aggregate_ranks(dist, ms, tokens, False)
+    value = tokens_all / (ms_max * 1e-3)
+    # e2e: the same decode through the public API, history from pinned host memory, tokens back to the host
+    hist_pinned = torch.from_numpy(hist).pin_memory()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e_tok = 0
+    for _ in range(max(1, args.steps // 2)):
+        outs, _ = bc.decode(hist_pinned.numpy(), first, **kw)
+        e2e_tok += sum(len(o) for o in outs)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    e2e_s, e2e_tok = aggregate_ranks(dist, e2e_s, e2e_tok, False)
+    e2e = {"value": round(e2e_tok / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": int(hist.nbytes + first.nbytes),
+           "d2h_bytes_per_step": int(4 * tokens / max(args.steps, 1)),
+           "what": "sd_batch_decode per step: 64 histories (4096-token context + first token) from pinned host "
+                   "memory, 256-token n-gram spec decode of every stream, tokens back to host; wall clock"}
+    fwd_ms = ms / max(fwds, 1)
+    ctx_mid = n_ctx + args.tokens / 2
+    wbytes = BYTES_PER_FORWARD
+    kvbytes = B * KV_BYTES_PER_POS * ctx_mid
+    M = B * (SPEC_K + 1)
+    flops = 2 * M * (BYTES_PER_FORWARD / 18 * 32)  # 2 x tokens x weights (Q4_0: 32 weights per 18 bytes)
+    step_roof = {"verify_forward_ms": round(fwd_ms, 3), "M": M,
+                 "weight_plus_kv_bytes_per_forward": int(wbytes + kvbytes),
+                 "achieved_gbs": round((wbytes + kvbytes) / (fwd_ms * 1e-3) / 1e9, 1),
+                 "int8_tops": round(flops / (fwd_ms * 1e-3) / 1e12, 1),
+                 "hbm_time_floor_ms": round((wbytes + kvbytes) / (peaks.get("hbm_gbs", 6650.0) * 1e6), 3)}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        tps, dt = cpu_decode_sample(ctx_path, 4, threads)
+        cpu = {"value": round(tps, 4), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": "4 single-token W4A8 forwards of the 7B model (oracle restatement of the reference's CPU "
+                         "SDOT decode, all host threads); the reference serves one stream per process"}
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int4 -> int32 MMA, fp32 accumulate",
+                "data": "synthetic: seeded random-init Q4_0 weights of the Mistral-7B-v0.2 architecture, "
+                        "uniform-random token ids",
+                "config": {"workload": f"BASELINE config 5: batched serving, {B} streams per GPU, {n_ctx}-token "
+                                       f"random contexts, n-gram n=3 K=4 drafts (verify M = {M}), temp 0, "
+                                       f"{args.tokens} generated tokens per stream per step",
+                           "model": "Mistral-7B-v0.2 (32 x 4096, FFN 14336, 32/8 heads, vocab 32000) Q4_0",
+                           "global_batch": B * world, "seq_len": n_ctx + args.tokens,
+                           "parallelism": f"dp{world}" if world > 1 else "single GPU",
+                           "l2": "no flush: each forward streams 4.0 GB of weights and ~1 GB of K/V (> 126 MB L2)"},
+                "acceptance_rate": round((accepted - iters) / drafted, 4) if drafted else None,
+                "tokens_per_stream_iteration": round(tokens / max(iters, 1), 3),
+                "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "setup_s": {"prefill": round(t_prefill, 2)},
+                "gpu_launches": int(fwds * (4 + 32 * 10 + 2))}
+        print(json.dumps(line), flush=True)
+    bc.close()
+    ctx.close()
+
+
 def run_forward(args):
     """Single verify forwards of S tokens (default K+1 = 5) after a ctx-token prefill, on a Mistral-7B-shaped
     synthetic model with --layers layers (a few layers keep ncu captures small while every matrix keeps its
@@ -383,9 +491,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=None, help="generated tokens per step (default: the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="specdec", choices=["specdec", "selfspec", "gemv", "forward"],
+    ap.add_argument("--workload", default="specdec", choices=["specdec", "selfspec", "gemv", "forward", "serving"],
                     help="specdec = BASELINE config 3 (the default line), selfspec = config 4, gemv = config 1, "
-                         "forward = single verify forwards (profiling: --layers, --S, --ctx)")
+                         "serving = config 5 (batched streams), forward = single verify forwards (profiling: "
+                         "--layers, --S, --ctx)")
+    ap.add_argument("--streams", type=int, default=SERVE_STREAMS, help="serving: streams per GPU")
+    ap.add_argument("--ctx-serve", type=int, default=SERVE_CTX, help="serving: context tokens per stream")
     ap.add_argument("--layers", type=int, default=32, help="forward workload: layers of the 7B-shaped model")
     ap.add_argument("--ctx", type=int, default=1024, help="forward workload: context positions before the forward")
     ap.add_argument("--forward-kernel", type=int, default=None, choices=[0, 1],
@@ -399,7 +510,7 @@ def main():
     ap.add_argument("--S", type=int, default=0)
     args = ap.parse_args()
     if args.tokens is None:
-        args.tokens = SELF_TOKENS if args.workload == "selfspec" else GEN_TOKENS
+        args.tokens = {"selfspec": SELF_TOKENS, "serving": SERVE_TOKENS}.get(args.workload, GEN_TOKENS)
     if args.workload == "gemv":
         run_gemv(args)
         return
@@ -429,6 +540,11 @@ def main():
     torch.cuda.set_device(local)
     path = model_path(rank, world, dist)
     peaks = measured_peaks()
+    if args.workload == "serving":
+        run_serving(args, path, rank, world, local, dist, peaks)
+        if dist:
+            dist.destroy_process_group()
+        return
     tp = world > 1 and args.parallel == "tp"
     comm = None
     if tp:

@@ -261,6 +261,42 @@ SD_API int sd_generate(sd_ctx *ctx, const sd_gen_params *p, const int32_t *promp
 SD_API int sd_decode(sd_ctx *ctx, const sd_gen_params *p, const int32_t *history, int n_hist, int first_token,
               int32_t *out_tokens, int out_cap, sd_gen_stats *stats);
 
+/* ======================================================================================
+ * Batched serving: many independent streams on one GPU sharing a context's weights.  Every stream
+ * has its own KV ring and generation state; one forward processes T tokens of every stream with the
+ * wide-token W4A8 GEMM (M = n_streams * T rows of int8 MMA work per weight tile read).  Per stream
+ * the semantics are those of sd_generate / sd_decode (the reference runs one stream per process).
+ * Single-GPU contexts only (tp_size 1).
+ * ====================================================================================== */
+#define SD_BATCH_MAX_WIDTH 8
+typedef struct sd_batch sd_batch;
+
+typedef struct {
+    int64_t n_generated;                                   /* over all streams */
+    int64_t total_draft, total_accepted, total_iterations; /* decode loop, summed over streams */
+    int64_t verify_forwards;                               /* batched forwards of the decode loop */
+    double ms_prefill, ms_decode;
+} sd_batch_stats;
+
+/* n_streams >= 1; max_seq ring positions per stream; max_width tokens per stream per forward
+ * (1..SD_BATCH_MAX_WIDTH; the verify width spec_k + 1 and the prefill chunk). */
+SD_API int sd_batch_create(sd_ctx *ctx, int n_streams, int max_seq, int max_width, sd_batch **out);
+SD_API void sd_batch_free(sd_batch *b);
+/* The CUDA stream (cudaStream_t) every sd_batch_* call of this batch is ordered on. */
+SD_API void *sd_batch_stream(sd_batch *b);
+/* One forward of T <= max_width tokens per stream: tokens [n_streams][T] at positions pos[s] .. pos[s]+T-1
+ * (K/V written to each stream's ring); logits: host [n_streams][T][vocab] or NULL. */
+SD_API int sd_batch_forward(sd_batch *b, const int32_t *tokens, int T, const int32_t *pos, float *logits);
+/* K/V of positions [0, n) of every stream from tokens [n_streams][n] (chunks of max_width tokens). */
+SD_API int sd_batch_prefill(sd_batch *b, const int32_t *tokens, int n);
+/* Decode of every stream after a prefill of history[s][0 .. n_hist-1): starts from first[s] at position
+ * n_hist - 1 (sd_decode per stream).  out: [n_streams][out_cap]; n_out: [n_streams] tokens written. */
+SD_API int sd_batch_decode(sd_batch *b, const sd_gen_params *p, const int32_t *history, int n_hist, const int32_t *first,
+                           int32_t *out, int out_cap, int32_t *n_out, sd_batch_stats *stats);
+/* Prefill + first token + decode of every stream (sd_generate per stream): prompts [n_streams][n_prompt]. */
+SD_API int sd_batch_generate(sd_batch *b, const sd_gen_params *p, const int32_t *prompts, int n_prompt, int32_t *out,
+                             int out_cap, int32_t *n_out, sd_batch_stats *stats);
+
 #ifdef __cplusplus
 }
 #endif

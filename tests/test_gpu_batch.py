@@ -1,0 +1,155 @@
+"""GPU parity of batched serving (sd_batch_*: many streams, one wide-token W4A8 GEMM per matrix) on a small
+Mistral-geometry model.
+
+Bars: every stream's logits within 1e-2 relative of the CPU oracle's single-stream forward (north_star);
+a stream's logits do not depend on the other streams (bit-identical when they change); the K split of every
+matrix is fixed, so a stream's logits at verify width 5 equal its width-1 logits bit for bit; temp-0 n-gram
+speculative output token-identical to the batch's greedy decode, per stream.
+"""
+import numpy as np
+import pytest
+
+from tests.conftest import gpu_available
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not gpu_available(), reason="needs a CUDA GPU")]
+
+LOGIT_RTOL = 1e-2
+B = 3
+
+
+@pytest.fixture(scope="module")
+def mini(tmp_path_factory):
+    from anetransformers_b200 import gguf as G
+    path = str(tmp_path_factory.mktemp("b") / "mini.gguf")
+    G.write_synthetic_gguf(path, G.MINI, seed=3)
+    return path
+
+
+@pytest.fixture(scope="module")
+def ctx(mini):
+    from anetransformers_b200.engine import Context
+    c = Context(mini, max_seq=512)
+    yield c
+    c.close()
+
+
+def rel_err(a, b):
+    return float(np.max(np.abs(a.astype(np.float64) - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def _prompts(rng, vocab, n):
+    return rng.integers(3, vocab, (B, n)).astype(np.int32)
+
+
+def test_batch_forward_matches_oracle(mini, ctx, oracle):
+    """Prefill 20 tokens per stream, then a 5-token forward at a different position per stream (rolled
+    back, as after rejected drafts); every row against the oracle's single-stream forward."""
+    from anetransformers_b200 import gguf as G
+    from anetransformers_b200.engine import BatchContext
+    rng = np.random.default_rng(7)
+    n0, T = 20, 5
+    prom = _prompts(rng, ctx.vocab, n0)
+    nxt = _prompts(rng, ctx.vocab, T)
+    pos = np.array([n0, n0 - 3, n0 - 8], np.int32)
+    bc = BatchContext(ctx, B, max_seq=256, width=8)
+    try:
+        bc.prefill(prom)
+        lg = bc.forward(nxt, pos)
+    finally:
+        bc.close()
+    om = oracle.OracleModel(G.GGUFFile(mini), max_seq=256)
+    for s in range(B):
+        kv = om.new_kv()
+        for i in range(pos[s]):
+            om.forward(kv, int(prom[s, i]), i)
+        for j in range(T):
+            ref = om.forward(kv, int(nxt[s, j]), int(pos[s]) + j)
+            assert rel_err(lg[s, j], ref) < LOGIT_RTOL, (s, j)
+        om.free_kv(kv)
+
+
+def test_batch_streams_are_independent_and_width_invariant(ctx):
+    from anetransformers_b200.engine import BatchContext
+    rng = np.random.default_rng(8)
+    n0, T = 12, 5
+    prom = _prompts(rng, ctx.vocab, n0)
+    nxt = _prompts(rng, ctx.vocab, T)
+    pos = np.full(B, n0, np.int32)
+    bc = BatchContext(ctx, B, max_seq=256, width=8)
+    try:
+        bc.prefill(prom)
+        lg_a = bc.forward(nxt, pos)
+        # other streams' tokens and history change: stream 0's logits must not
+        prom2 = prom.copy()
+        prom2[1:] = _prompts(rng, ctx.vocab, n0)[1:]
+        nxt2 = nxt.copy()
+        nxt2[1:] = _prompts(rng, ctx.vocab, T)[1:]
+        bc.prefill(prom2)
+        lg_b = bc.forward(nxt2, pos)
+        np.testing.assert_array_equal(lg_a[0].view(np.uint32), lg_b[0].view(np.uint32))
+        # width 1, token by token, equals the width-5 rows (fixed K splits, chunking by absolute position)
+        bc.prefill(prom)
+        for j in range(T):
+            lg1 = bc.forward(nxt[:, j:j + 1], pos + j)
+            np.testing.assert_array_equal(lg1[:, 0].view(np.uint32), lg_a[:, j].view(np.uint32))
+    finally:
+        bc.close()
+
+
+def test_batch_forward_close_to_single_stream_engine(ctx):
+    """Same arithmetic per block as the single-stream path; only K-split association and attention chunking
+    differ (a last-bit change can still move one Q8_0 code), so the logits agree well inside the oracle bar."""
+    from anetransformers_b200.engine import BatchContext
+    rng = np.random.default_rng(9)
+    n0, T = 30, 5
+    prom = _prompts(rng, ctx.vocab, n0)
+    nxt = _prompts(rng, ctx.vocab, T)
+    bc = BatchContext(ctx, B, max_seq=256, width=8)
+    try:
+        bc.prefill(prom)
+        lg = bc.forward(nxt, np.full(B, n0, np.int32))
+    finally:
+        bc.close()
+    for s in range(B):
+        ctx.prefill(prom[s].tolist(), 0)
+        ref, _ = ctx.forward(nxt[s].tolist(), n0)
+        assert rel_err(lg[s], ref.astype(np.float64)) < 5e-3, s
+
+
+def test_batch_ngram_spec_equals_greedy(ctx):
+    """Temp-0 n-gram speculative decode (K = 4, verify width 5) of every stream is token-identical to the
+    batch's greedy decode; prompts repeat segments so the drafter finds matches."""
+    from anetransformers_b200.engine import BatchContext
+    rng = np.random.default_rng(10)
+    pool = rng.integers(3, ctx.vocab, (3, 16))
+    prompts = np.stack([np.concatenate([pool[(s + i) % 3] for i in range(5)]) for s in range(B)]).astype(np.int32)
+    kw = dict(max_tokens=40, temp=0.0, rep_penalty=1.0, ignore_eos=True)
+    bc = BatchContext(ctx, B, max_seq=256, width=8)
+    try:
+        greedy, gst = bc.generate(prompts, mode="greedy", **kw)
+        spec, sst = bc.generate(prompts, mode="ngram", spec_k=4, ngram_n=3, **kw)
+    finally:
+        bc.close()
+    for s in range(B):
+        assert len(spec[s]) >= 40 - 1
+        n = min(len(spec[s]), len(greedy[s]))
+        assert spec[s][:n] == greedy[s][:n], s
+    assert sst["total_draft"] > 0
+    assert sst["verify_forwards"] <= gst["verify_forwards"]
+
+
+def test_batch_bad_arguments(ctx):
+    from anetransformers_b200 import _lib
+    from anetransformers_b200.engine import BatchContext
+    with pytest.raises(_lib.SpecDecError):
+        BatchContext(ctx, B, max_seq=256, width=9)
+    bc = BatchContext(ctx, B, max_seq=64, width=8)
+    try:
+        with pytest.raises(_lib.SpecDecError):
+            bc.forward(np.full((B, 5), ctx.vocab, np.int32), np.zeros(B, np.int32))  # token out of range
+        with pytest.raises(_lib.SpecDecError):
+            bc.forward(np.ones((B, 5), np.int32), np.full(B, 62, np.int32))  # past the ring
+        with pytest.raises(_lib.SpecDecError):
+            bc.generate(np.ones((B, 40), np.int32), mode="ngram", spec_k=4, max_tokens=40)  # exceeds the ring
+    finally:
+        bc.close()
