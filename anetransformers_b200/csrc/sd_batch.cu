@@ -206,9 +206,182 @@ __device__ __forceinline__ AttnArgs stream_view(const BAttnArgs& ba, int b) {
     return v;
 }
 
-// Work items (kv head, chunk) of stream blockIdx.y, grid-strided over blockIdx.x (sd_attn.cu per stream).
-__global__ void __launch_bounds__(kAttnThreads) k_battn_partial(const BAttnArgs ba) {
-    __shared__ __align__(16) uint8_t smem[attn_smem_bytes()];
+// ---------------------------------------------------------------------------------------------
+// Batched attention item: every query row (4 heads x nv tokens) of one stream's kv head kvh over chunk c.
+// The layout and online softmax are those of attn_item (sd_dev.cuh), with two changes for throughput over
+// the many streams' rings (together ~1 GB of K/V per layer at 64 x 4096 positions): K/V sub-blocks stream
+// into a kBStages-deep shared-memory ring by cp.async (no register round trip, three sub-blocks in flight,
+// one barrier per sub-block), and Q and the probabilities P enter the fp16 MMAs as single fp16 values
+// (relative error ~5e-4 on the head outputs, which are then quantised to Q8_0 with steps of 1/254).
+// ---------------------------------------------------------------------------------------------
+constexpr int kBStages = 4;
+constexpr size_t kBStageHalves = (size_t)2 * kSub * kQStride;  // K then V of one sub-block
+constexpr size_t battn_smem_bytes() { return ((size_t)kQRows * kQStride + kBStages * kBStageHalves) * 2; }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_stages() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kBStages - 2) : "memory");
+}
+
+// Sub-block at positions [sb, sb + 32) of kv head column col0 into ring slot `slot` (zero past p1).
+__device__ __forceinline__ void battn_issue(const AttnArgs& a, __half* ring, int slot, int sb, int p1, int col0, int tid) {
+    __half* kk = ring + (size_t)slot * kBStageHalves;
+    __half* vv = kk + kSub * kQStride;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int i = tid + u * kAttnThreads;
+        const int j = i >> 4, d8 = (i & 15) * 8;
+        const int p = sb + j;
+        const bool ok = p < p1;
+        const size_t off = ok ? (size_t)ring_slot(p, a.max_seq) * a.kv_ld + col0 + d8 : 0;
+        cp_async16(smem_u32(kk + j * kQStride + d8), a.k + off, ok ? 16u : 0u);
+        cp_async16(smem_u32(vv + j * kQStride + d8), a.v + off, ok ? 16u : 0u);
+    }
+}
+
+__device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi_max, int kvh, int c, __half* qh,
+                           __half* ring, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int nt = warp & 3, dh = warp >> 2;
+    const bool active = 2 * nt < nv;
+    const int p0 = max(c * a.chunk, lo_min);
+    const int p1 = min((c + 1) * a.chunk, hi_max + 1);
+    const int lo_max = max(0, pos + nv - a.max_seq);
+    const int col0 = kvh * kHD;
+    const int nsb = (p1 - p0 + kSub - 1) / kSub;
+    __syncthreads();  // the previous item is done with Q and the ring
+#pragma unroll
+    for (int i = 0; i < kBStages - 1; ++i) {
+        if (i < nsb) battn_issue(a, ring, i, p0 + i * kSub, p1, col0, tid);
+        cp_async_commit();
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int i = tid + u * kAttnThreads;
+        const int r = i >> 5, d4 = (i & 31) * 4;
+        const int s = r >> 2, h = r & 3;
+        float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s < nv) qv = *reinterpret_cast<const float4*>(a.q + (size_t)s * a.q_ld + (size_t)(kvh * kGQA + h) * kHD + d4);
+        *reinterpret_cast<uint2*>(qh + r * kQStride + d4) =
+            make_uint2(h2u(__floats2half2_rn(qv.x, qv.y)), h2u(__floats2half2_rn(qv.z, qv.w)));
+    }
+    const int lr = lane & 7, lq = lane >> 3;
+    const uint32_t q_a = smem_u32(qh + (nt * 8 + lr) * kQStride + (lq & 1) * 8);
+    const uint32_t k_off = (uint32_t)(((lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8) * 2);
+    const uint32_t v_off = (uint32_t)(((kSub + lr + (lq >> 1) * 8) * kQStride + dh * 64 + (lq & 1) * 8) * 2);
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    for (int ib = 0; ib < nsb; ++ib) {
+        const int sb = p0 + ib * kSub;
+        cp_async_wait_stages();
+        __syncthreads();  // sub-block ib landed for every thread; slot of ib - 1 is free
+        if (ib + kBStages - 1 < nsb)
+            battn_issue(a, ring, (ib + kBStages - 1) % kBStages, sb + (kBStages - 1) * kSub, p1, col0, tid);
+        cp_async_commit();
+        if (!active) continue;
+        const uint32_t slot = smem_u32(ring + (size_t)(ib % kBStages) * kBStageHalves);
+        const uint32_t k_a = slot + k_off, v_a = slot + v_off;
+        // ---- S^T: positions sb + 16 mt + (g, g+8) x rows 8 nt + (2t, 2t+1) ----
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int ks = 0; ks < kHD / 16; ++ks) {
+            uint32_t b0, b1;
+            ldsm_x2(q_a + ks * 32, b0, b1);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                uint32_t k0, k1, k2, k3;
+                ldsm_x4(k_a + (uint32_t)(mt * 16 * kQStride * 2) + ks * 32, k0, k1, k2, k3);
+                mma_f16(sc[mt], k0, k1, k2, k3, b0, b1);
+            }
+        }
+        if (sb + kSub > p1 || sb + kSub - 1 > pos || sb < lo_max) {
+            const int s = 2 * nt + (t >> 1);
+            const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int p = sb + mt * 16 + g + (e >> 1) * 8;
+                    if (!(s < nv && p < p1 && p >= lo && p <= hi)) sc[mt][e] = -INFINITY;
+                }
+        }
+        float x0 = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
+        float x1 = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+#pragma unroll
+        for (int o2 = 4; o2 < 32; o2 <<= 1) {
+            x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
+            x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
+        }
+        const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+        const float c0 = (m0 == -INFINITY) ? 0.f : exp_fast(m0 - n0);
+        const float c1 = (m1 == -INFINITY) ? 0.f : exp_fast(m1 - n1);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+            sc[mt][0] = sc[mt][0] == -INFINITY ? 0.f : exp_fast(sc[mt][0] - n0);
+            sc[mt][1] = sc[mt][1] == -INFINITY ? 0.f : exp_fast(sc[mt][1] - n1);
+            sc[mt][2] = sc[mt][2] == -INFINITY ? 0.f : exp_fast(sc[mt][2] - n0);
+            sc[mt][3] = sc[mt][3] == -INFINITY ? 0.f : exp_fast(sc[mt][3] - n1);
+        }
+        m0 = n0;
+        m1 = n1;
+        l0 = l0 * c0 + ((sc[0][0] + sc[0][2]) + (sc[1][0] + sc[1][2]));
+        l1 = l1 * c1 + ((sc[0][1] + sc[0][3]) + (sc[1][1] + sc[1][3]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            o[i][0] *= c0;
+            o[i][1] *= c1;
+            o[i][2] *= c0;
+            o[i][3] *= c1;
+        }
+        // ---- O^T (dims 64 dh + 16 i + (g, g+8) x rows 2t, 2t+1) += V^T P^T ----
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+            const uint32_t ph0 = movm_t(h2u(__floats2half2_rn(sc[mt][0], sc[mt][1])));
+            const uint32_t ph1 = movm_t(h2u(__floats2half2_rn(sc[mt][2], sc[mt][3])));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_t(v_a + (uint32_t)(mt * 16 * kQStride * 2) + i * 32, v0, v1, v2, v3);
+                mma_f16(o[i], v0, v1, v2, v3, ph0, ph1);
+            }
+        }
+    }
+#pragma unroll
+    for (int o2 = 4; o2 < 32; o2 <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
+    }
+    const int r0 = nt * 8 + 2 * t;
+    const int s = 2 * nt + (t >> 1);
+    if (active && s < nv) {
+        const size_t pi = ((size_t)s * a.n_heads + kvh * kGQA + (r0 & 3)) * a.max_chunks + c;
+        float* acc0 = a.part_acc + pi * kHD + dh * 64;
+        float* acc1 = acc0 + (size_t)a.max_chunks * kHD;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = 16 * i + g;
+            acc0[d] = o[i][0];
+            acc1[d] = o[i][1];
+            acc0[d + 8] = o[i][2];
+            acc1[d + 8] = o[i][3];
+        }
+        if (dh == 0 && g == 0) {
+            a.part_ml[pi] = make_float2(m0, l0);
+            a.part_ml[pi + a.max_chunks] = make_float2(m1, l1);
+        }
+    }
+}
+
+// Work items (kv head, chunk) of stream blockIdx.y, grid-strided over blockIdx.x.
+__global__ void __launch_bounds__(kAttnThreads, 2) k_battn_partial(const BAttnArgs ba) {
+    extern __shared__ __align__(16) uint8_t dsm[];
     const int b = blockIdx.y;
     const DevCtrl& c = ba.ctrl[b];
     const int nv = c.done ? 0 : min(c.n_valid, ba.T);
@@ -219,12 +392,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_battn_partial(const BAttnArgs 
     const int lo_min = max(0, pos + 1 - a.max_seq);
     const int c_first = lo_min / a.chunk, c_last = hi_max / a.chunk;
     const int n_items = (c_last - c_first + 1) * a.n_kvh;
-    const AttnSmem sm = attn_smem_at(smem);
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int nx = item + gridDim.x;
-        attn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, nx % a.n_kvh,
-                  nx < n_items ? c_first + nx / a.n_kvh : -1, sm, threadIdx.x, [] { __syncthreads(); });
-    }
+    __half* qh = reinterpret_cast<__half*>(dsm);
+    __half* ring = qh + kQRows * kQStride;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x)
+        battn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, qh, ring, threadIdx.x);
+    cp_async_wait_all();
 }
 
 // Merge of one (token, head) row and its Q8_0 quantisation into the o-proj image.
@@ -276,25 +448,24 @@ struct WgPlan {
     size_t smem = 0;
 };
 
-// Cost model in ns: a quad (128 columns) of a unit costs (1 + n8 tiles per warp) x 126 ns (the A-fragment
-// work of a quad is worth about one n8 tile); a unit adds about one quad of fill / epilogue; K-split partial
+// Cost model in ns: a quad (128 columns) of a unit costs (0.8 + n8 tiles per warp) x 126 ns (the A-fragment
+// work of a quad is worth most of one n8 tile); a unit adds about one quad of fill / epilogue; K-split partial
 // slices are written and read back at ~6.5 TB/s.
 void wg_plan(WgPlan& p, int epi, int rows, int K, int M, int kp_lo, int kp_max, int sms, int max_smem) {
-    const int n_rg = qmat_row_groups(rows);
-    const int n_rt = (n_rg + kWgRG - 1) / kWgRG;
+    const int n_rt = wide_row_tiles(rows);
     const int nq = K / 128;
     const int NT = (M + 7) / 8;
     double best = 1e300;
-    int bt = 4, bk = kp_lo;
-    for (int tt = 4; tt <= kWgMaxTT; tt += 4) {
-        if (tt > 4 && tt - 4 >= NT) break;  // wider tiles than the tokens add nothing
+    int bt = kWgTokGroups, bk = kp_lo;
+    for (int tt = kWgTokGroups; tt <= kWgMaxTT; tt += kWgTokGroups) {
+        if (tt > kWgTokGroups && tt - kWgTokGroups >= NT) break;  // wider tiles than the tokens add nothing
         const int n_tt = (NT + tt - 1) / tt;
-        const int per = (std::min(tt, NT) + 3) / 4;
+        const int per = (std::min(tt, NT) + kWgTokGroups - 1) / kWgTokGroups;
         for (int kp = kp_lo; kp <= kp_max; ++kp) {
             if (kp > kp_lo && nq / kp < 2) break;
             const long long units = (long long)n_rt * kp * n_tt;
             const long long waves = (units + sms - 1) / sms;
-            double t = (double)waves * ((double)nq / kp + 1.0) * (1.0 + per) * 126.0;
+            double t = (double)waves * ((double)nq / kp + 1.0) * (0.8 + per) * 126.0;
             if (kp > 1) t += (double)kp * M * rows * 8.0 / 6500.0;
             if (t < best * 0.999) {
                 best = t;
@@ -305,11 +476,10 @@ void wg_plan(WgPlan& p, int epi, int rows, int K, int M, int kp_lo, int kp_max, 
     }
     WGemmArgs& a = p.a;
     a = WGemmArgs{};
-    a.n_rg = n_rg;
+    a.n_rt = n_rt;
     a.nq = nq;
     a.NT = NT;
     a.M = M;
-    a.n_rt = n_rt;
     a.tt_n8 = bt;
     a.n_tt = (NT + bt - 1) / bt;
     a.kparts = epi == WG_SILU ? 1 : bk;
@@ -331,6 +501,9 @@ struct BPlans {
 struct sd_batch {
     sd_ctx* ctx = nullptr;
     ModelView m{};
+    // the context's matrices repacked into the wide GEMM layout (sd_batch.h)
+    std::vector<uint8_t*> wqkv, wwo, ww13, ww2;
+    uint8_t* wlm = nullptr;
     int dev = 0, sms = 0, max_smem = 0;
     cudaStream_t st = nullptr;
     int B = 0, W = 0, max_seq = 0, M_max = 0;
@@ -438,7 +611,7 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         pq.a.ld = m.qkv_rows;
         pq.a.out_rows = m.qkv_rows;
         pq.a.part_stride = (size_t)b->M_max * m.qkv_rows;
-        if ((rc = run_wgemm(b, WG_STORE, pq, m.qkv[l], b->img_x))) return rc;
+        if ((rc = run_wgemm(b, WG_STORE, pq, b->wqkv[l], b->img_x))) return rc;
         BRopeArgs ra{};
         ra.qkv = b->qkv;
         ra.pstride = pq.a.part_stride;
@@ -476,8 +649,8 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         ba.kv_stream = b->kv_stream;
         ba.T = T;
         ba.ctrl = b->ctrl;
-        const int per_stream = std::max(1, (4 * b->sms + b->B - 1) / b->B);
-        k_battn_partial<<<dim3(per_stream, b->B), kAttnThreads, 0, b->st>>>(ba);
+        const int per_stream = std::max(1, (2 * b->sms + b->B - 1) / b->B);
+        k_battn_partial<<<dim3(per_stream, b->B), kAttnThreads, battn_smem_bytes(), b->st>>>(ba);
         CK(cudaGetLastError(), "attention");
         k_battn_combine<<<M * m.n_heads, combine_warps(b->max_seq) * 32, 0, b->st>>>(ba);
         CK(cudaGetLastError(), "combine");
@@ -487,7 +660,7 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         po.a.ld = m.dim;
         po.a.out_rows = m.dim;
         po.a.part_stride = (size_t)b->M_max * m.dim;
-        if ((rc = run_wgemm(b, WG_STORE, po, m.wo[l], b->img_attn))) return rc;
+        if ((rc = run_wgemm(b, WG_STORE, po, b->wwo[l], b->img_attn))) return rc;
         na.w = m.rms_ffn[l];
         na.yparts = po.a.kparts;
         k_bnorm<1><<<M, kBNormThreads, 0, b->st>>>(na);
@@ -496,14 +669,14 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         WgPlan pg = P.w13;
         pg.a.h = WImg{b->img_h, NT};
         pg.a.hidden = m.hidden;
-        if ((rc = run_wgemm(b, WG_SILU, pg, m.w13[l], b->img_x))) return rc;
+        if ((rc = run_wgemm(b, WG_SILU, pg, b->ww13[l], b->img_x))) return rc;
         // down, residual + next norm
         WgPlan pd = P.w2;
         pd.a.out = b->y;
         pd.a.ld = m.dim;
         pd.a.out_rows = m.dim;
         pd.a.part_stride = (size_t)b->M_max * m.dim;
-        if ((rc = run_wgemm(b, WG_STORE, pd, m.w2[l], b->img_h))) return rc;
+        if ((rc = run_wgemm(b, WG_STORE, pd, b->ww2[l], b->img_h))) return rc;
         na.w = (l + 1 < m.n_layers) ? m.rms_att[l + 1] : m.rms_final;
         na.yparts = pd.a.kparts;
         k_bnorm<1><<<M, kBNormThreads, 0, b->st>>>(na);
@@ -514,7 +687,7 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
     pl.a.out = b->logits;
     pl.a.ld = m.vocab;
     pl.a.out_rows = m.vocab;
-    int rc = run_wgemm(b, WG_STORE, pl, m.lm, b->img_x);
+    int rc = run_wgemm(b, WG_STORE, pl, b->wlm, b->img_x);
     if (rc) return rc;
     CK(launch_argmax(b->logits, m.vocab, M, b->argmax, nullptr, b->st, false), "argmax");
     return SD_OK;
@@ -697,6 +870,9 @@ void sd_batch_free(sd_batch* b) {
         for (auto& g : row)
             if (g) cudaGraphExecDestroy(g);
     if (b->iter_graph) cudaGraphExecDestroy(b->iter_graph);
+    for (auto* v : {&b->wqkv, &b->wwo, &b->ww13, &b->ww2})
+        for (uint8_t* p : *v) cudaFree(p);
+    cudaFree(b->wlm);
     cudaFree(b->kc); cudaFree(b->vc); cudaFree(b->x); cudaFree(b->y); cudaFree(b->qkv); cudaFree(b->q);
     cudaFree(b->img_x); cudaFree(b->img_attn); cudaFree(b->img_h); cudaFree(b->part_ml); cudaFree(b->part_acc);
     cudaFree(b->logits); cudaFree(b->argmax); cudaFree(b->probs); cudaFree(b->ctrl); cudaFree(b->tok);
@@ -728,11 +904,14 @@ int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_b
     b->max_seq = max_seq;
     b->M_max = n_streams * max_width;
     b->sms = device_sm_count(b->dev);
-    b->max_smem = device_max_smem(b->dev);
+    b->max_smem = device_max_smem(b->dev) - 1024;  // room for the GEMM's static shared memory
     b->max_chunks = (max_seq + b->chunk - 1) / b->chunk;
     if (cudaSetDevice(b->dev) != cudaSuccess) return bail(fail(SD_ERR_INVALID, "bad device %d", b->dev));
     if ((rc = ck(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking), "stream"))) return bail(rc);
     if ((rc = ck(wgemm_init_attrs(b->max_smem), "gemm attributes"))) return bail(rc);
+    if ((rc = ck(cudaFuncSetAttribute(k_battn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)battn_smem_bytes()),
+                 "attention attributes")))
+        return bail(rc);
     b->kv_stream = (size_t)max_seq * m.kv_rows;
     b->kv_layer = (size_t)n_streams * b->kv_stream;
     const size_t M = b->M_max;
@@ -747,6 +926,21 @@ int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_b
         (rc = dalloc(&b->ctrl, (size_t)n_streams)) || (rc = dalloc(&b->pos_dev, (size_t)n_streams)) ||
         (rc = dalloc(&b->gs, (size_t)n_streams)) || (rc = dalloc(&b->ndone, 2)))
         return bail(rc);
+    // weights in the wide GEMM layout (the context keeps its tile16x4 copies for the single-stream path)
+    auto wide = [&](const uint8_t* tiles, int rows, int cols, uint8_t** out_w) {
+        int r = dalloc(out_w, wide_bytes(rows, cols));
+        if (!r) r = ck(launch_wide_repack(tiles, qmat_row_groups(rows), cols / 128, *out_w, b->st), "wide repack");
+        return r;
+    };
+    b->wqkv.assign(m.n_layers, nullptr);
+    b->wwo.assign(m.n_layers, nullptr);
+    b->ww13.assign(m.n_layers, nullptr);
+    b->ww2.assign(m.n_layers, nullptr);
+    for (int l = 0; l < m.n_layers; ++l)
+        if ((rc = wide(m.qkv[l], m.qkv_rows, m.dim, &b->wqkv[l])) || (rc = wide(m.wo[l], m.dim, m.q_rows, &b->wwo[l])) ||
+            (rc = wide(m.w13[l], 2 * m.hidden, m.dim, &b->ww13[l])) || (rc = wide(m.w2[l], m.dim, m.hidden, &b->ww2[l])))
+            return bail(rc);
+    if ((rc = wide(m.lm, m.vocab, m.dim, &b->wlm))) return bail(rc);
     if ((rc = ck(cudaMallocHost((void**)&b->gs_h, sizeof(GenState) * n_streams), "pinned state"))) return bail(rc);
     if ((rc = ck(cudaMallocHost((void**)&b->ndone_h, 2 * sizeof(int)), "pinned counter"))) return bail(rc);
     // images start zeroed: tokens past a forward's count read zeros, never uninitialised bytes

@@ -8,14 +8,14 @@
 // per token tile of up to 160 tokens, which turns the M = (streams x verify width) contraction of batched
 // serving from weight-bandwidth bound into a dense int8 contraction.
 //
-// CTA = 8 consumer warps + 1 producer warp, one CTA per SM, persistent over units.  Unit = (row tile of 128
-// rows, K slice, token tile of tt_n8 n8 tiles); units that share weights are adjacent so their weight reads
-// meet in L2.  Per quad (128 columns) a ring stage holds the row tile's 8 weight tiles (1152-byte tile16x4
-// tiles, one bulk copy each) and the token tile's activation segments (one bulk copy; sd_internal.h wide
-// image).  Consumer warp (wr, wt) owns rows 64 wr .. +63 (row-groups 4wr .. 4wr+3) and n8 tiles
-// [wt * per, wt * per + per) of the token tile: per block it unpacks the A fragments of its 4 row-groups once
-// and uses each B fragment for 4 MMAs (m16n8k32, u8 nibbles x s8 codes, accumulator started at the bits of
-// kMagic so one FADD recovers the exact block sum).
+// CTA = 16 warps, one CTA per SM, persistent over units.  Unit = (row tile of 128 rows, K slice, token tile
+// of tt_n8 n8 tiles); units that share weights are adjacent so their weight reads meet in L2.  Per quad (128
+// columns) a ring stage holds the row tile's weights in the wide layout (sd_batch.h; one bulk copy) and the
+// token tile's activation segments (one bulk copy; sd_internal.h wide image); lane 0 of warp 0 keeps the ring
+// filled ahead of the stage it consumes.  Warp (wr, wt) owns rows 64 wr .. +63 (row-groups 4wr .. 4wr+3) and
+// n8 tiles [wt * per, wt * per + per) of the token tile: per block it loads its B fragments once and the A
+// words of its four row-groups with two conflict-free 16-byte loads, and runs 4 x per MMAs (m16n8k32, u8
+// nibbles x s8 codes, accumulator started at the bits of kMagic so one FADD recovers the exact block sum).
 #include "sd_dev.cuh"
 
 namespace sd {
@@ -24,10 +24,18 @@ size_t wgemm_smem_bytes(int tt_n8, int nstage) {
     return (size_t)nstage * (kWgWStage + (size_t)tt_n8 * kWSeg) + 2 * kWgMaxStages * 8;
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
+// The int8 MMA as a pure register operation (no volatile): the compiler may interleave it with the shared
+// loads and the fp32 epilogue of other fragments.
+__device__ __forceinline__ void mma_u8s8_pure(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicI));
+}
+
+__device__ __forceinline__ uint32_t pick4(const uint4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
 // Unit u -> (row tile, K slice, token tile); quads [q0, q1) of the slice.
@@ -46,6 +54,51 @@ __device__ __forceinline__ WgUnit wg_unit(const WGemmArgs& a, int u) {
     w.q1 = (int)((long long)(w.kp + 1) * a.nq / a.kparts);
     return w;
 }
+
+// The ring's producer (lane 0 of warp 0): walks the same (unit, quad) sequence as the consumers.
+struct WgProducer {
+    int u, q, q1, s;  // next unit / quad to issue, its slice end, stages issued
+    const uint8_t* wsrc;
+    const uint8_t* asrc;
+    uint32_t bytes, abytes;
+    RingPos rp;
+    bool live;
+
+    __device__ __forceinline__ void start_unit(const WGemmArgs& a, int n_units) {
+        live = u < n_units;
+        if (!live) return;
+        const WgUnit w = wg_unit(a, u);
+        q = w.q0;
+        q1 = w.q1;
+        const int n0 = w.tt * a.tt_n8, nn = min(a.tt_n8, a.NT - n0);
+        abytes = (uint32_t)(nn * kWSeg);
+        bytes = (uint32_t)kWgWStage + abytes;
+        wsrc = a.w + (size_t)w.rt * a.nq * kWgWStage;
+        asrc = a.act + (size_t)n0 * kWSeg;
+    }
+
+    // Issue stages while fewer than `limit` have been issued; false if a wait for a free slot ran out.
+    __device__ __forceinline__ bool fill(const WGemmArgs& a, int n_units, int limit, uint8_t* smem, uint32_t SB,
+                                         uint64_t* full, uint64_t* empty, int nstage) {
+        while (live && s < limit) {
+            if (s >= nstage && !mbar_wait(&empty[rp.slot], rp.phase ^ 1)) {
+                live = false;
+                return false;
+            }
+            uint8_t* dst = smem + (size_t)rp.slot * SB;
+            mbar_arrive_expect_tx(&full[rp.slot], bytes);
+            bulk_g2s(dst, wsrc + (size_t)q * kWgWStage, kWgWStage, &full[rp.slot]);
+            bulk_g2s(dst + kWgWStage, asrc + (size_t)q * a.NT * kWSeg, abytes, &full[rp.slot]);
+            ++s;
+            rp.advance(nstage);
+            if (++q == q1) {
+                u += gridDim.x;
+                start_unit(a, n_units);
+            }
+        }
+        return true;
+    }
+};
 
 template <int EPI>
 __global__ void __launch_bounds__(kWgThreads, 1) k_wgemm(const WGemmArgs a) {
@@ -68,39 +121,22 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgemm(const WGemmArgs a) {
     pdl_trigger();
     pdl_wait();
 
-    if (warp == kWgWarps) {
-        // ---------------- producer: one weight copy per row-group and one activation copy per stage ----------------
-        if (lane == 0) {
-            RingPos rp;
-            int s = 0;
-            for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-                const WgUnit w = wg_unit(a, u);
-                const int nrg = min(kWgRG, a.n_rg - w.rt * kWgRG);
-                const int n0 = w.tt * a.tt_n8, nn = min(a.tt_n8, a.NT - n0);
-                const uint32_t bytes = (uint32_t)(nrg * kTileBytes + nn * kWSeg);
-                const uint8_t* wsrc = a.w + (size_t)w.rt * kWgRG * a.nq * kTileBytes;
-                for (int q = w.q0; q < w.q1; ++q, ++s, rp.advance(nstage)) {
-                    if (s >= nstage && !mbar_wait(&empty[rp.slot], rp.phase ^ 1)) {
-                        set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
-                        return;  // the consumers run out their bounded waits on the stages never issued
-                    }
-                    uint8_t* dst = smem + (size_t)rp.slot * SB;
-                    mbar_arrive_expect_tx(&full[rp.slot], bytes);
-                    for (int r = 0; r < nrg; ++r)
-                        bulk_g2s(dst + r * kTileBytes, wsrc + ((size_t)r * a.nq + q) * kTileBytes, kTileBytes, &full[rp.slot]);
-                    bulk_g2s(dst + kWgWStage, a.act + ((size_t)q * a.NT + n0) * kWSeg, (uint32_t)(nn * kWSeg),
-                             &full[rp.slot]);
-                }
-            }
-        }
-        return;
+    // the producer's cursor lives in shared memory: registers are the scarce resource of the consumer loop
+    __shared__ WgProducer P;
+    const bool producer = tid == 0;
+    if (producer) {
+        P.u = blockIdx.x;
+        P.s = 0;
+        P.rp = RingPos{};
+        P.start_unit(a, n_units);
+        if (!P.fill(a, n_units, nstage, smem, SB, full, empty, nstage)) set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
     }
 
-    // ---------------- consumers ----------------
-    const int wr = warp >> 2, wt = warp & 3;
+    const int wr = warp >> 3, wt = warp & 7;
     const int g = lane >> 2, t = lane & 3;
-    const int per = (a.tt_n8 + 3) >> 2;  // n8 tiles per warp
+    const int per = (a.tt_n8 + kWgTokGroups - 1) / kWgTokGroups;  // n8 tiles per warp
     RingPos rp;
+    int s = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
         const WgUnit w = wg_unit(a, u);
         const int n0 = w.tt * a.tt_n8, nn = min(a.tt_n8, a.NT - n0);
@@ -111,38 +147,36 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgemm(const WGemmArgs a) {
         for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int n = 0; n < kWgMaxN8; ++n) accL[r][n] = accH[r][n] = make_float2(0.f, 0.f);
-        for (int q = w.q0; q < w.q1; ++q, rp.advance(nstage)) {
+        for (int q = w.q0; q < w.q1; ++q, ++s, rp.advance(nstage)) {
+            // keep nstage - 1 stages in flight beyond this one (waits for the slot of stage s - 1 to drain)
+            if (producer && !P.fill(a, n_units, s + nstage, smem, SB, full, empty, nstage))
+                set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
+            __syncwarp();
             if (!mbar_wait(&full[rp.slot], rp.phase)) {
                 set_dev_error(a.err, DEV_ERR_FULL_WAIT);
                 return;
             }
             const uint32_t st = smem_u32(smem + (size_t)rp.slot * SB);
             if (nw > 0) {
-                // scales once per quad; nibble words per block (fewer live registers: 9 warps share the
-                // 4 x 16K-register scheduler partitions, 3 on one, so a thread has at most 168)
-                uint4 sc[4];
-                const uint32_t tile0 = st + 4 * wr * kTileBytes + lane * 16;
-#pragma unroll
-                for (int r = 0; r < 4; ++r) sc[r] = lds128(st + (4 * wr + r) * kTileBytes + 1024 + g * 16);
                 const uint32_t ab = st + kWgWStage + nb0 * kWSeg + lane * 8;
                 const uint32_t mb = st + kWgWStage + nb0 * kWSeg + 1024 + t * 16;
 #pragma unroll
                 for (int blk = 0; blk < 4; ++blk) {
+                    // A fragments and scales of the four row-groups, unpacked once per block
+                    const uint32_t seg = st + (wr * 4 + blk) * kTileBytes;
+                    const uint4 lo = lds128(seg + lane * 16);
+                    const uint4 hi = lds128(seg + 512 + lane * 16);
+                    const uint4 sc = lds128(seg + 1024 + g * 16);
                     uint32_t A[4][4];
-                    float wdl[4], wdh[4];
+                    float2 wd[4];  // (row g, row g + 8) of row-group r
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const uint32_t wlo = lds32(tile0 + r * kTileBytes + blk * 4);
-                        const uint32_t whi = lds32(tile0 + r * kTileBytes + 512 + blk * 4);
+                        const uint32_t wlo = pick4(lo, r), whi = pick4(hi, r);
                         A[r][0] = wlo & 0x0F0F0F0Fu;
                         A[r][1] = whi & 0x0F0F0F0Fu;
                         A[r][2] = (wlo >> 4) & 0x0F0F0F0Fu;
                         A[r][3] = (whi >> 4) & 0x0F0F0F0Fu;
-                        // scales [g][h][blk]: x = row g blocks 0,1; y = row g blocks 2,3; z, w = row g + 8
-                        const float2 dl = h2x2f(blk < 2 ? sc[r].x : sc[r].y);
-                        const float2 dh = h2x2f(blk < 2 ? sc[r].z : sc[r].w);
-                        wdl[r] = (blk & 1) ? dl.y : dl.x;
-                        wdh[r] = (blk & 1) ? dh.y : dh.x;
+                        wd[r] = h2x2f(pick4(sc, r));
                     }
 #pragma unroll
                     for (int n = 0; n < kWgMaxN8; ++n) {
@@ -154,12 +188,12 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgemm(const WGemmArgs a) {
 #pragma unroll
                             for (int r = 0; r < 4; ++r) {
                                 int d[4];
-                                mma_u8s8(d, A[r][0], A[r][1], A[r][2], A[r][3], bf.x, bf.y, kMagicI, kMagicI, kMagicI, kMagicI);
+                                mma_u8s8_pure(d, A[r][0], A[r][1], A[r][2], A[r][3], bf.x, bf.y);
                                 const float2 fL = __fadd2_rn(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), off);
                                 const float2 fH = __fadd2_rn(make_float2(__int_as_float(d[2]), __int_as_float(d[3])), off);
                                 // (wd*xd) * (float)isum accumulated per block, as mistral/dequant.h:1085
-                                const float2 sL = __fmul2_rn(make_float2(wdl[r], wdl[r]), xd);
-                                const float2 sH = __fmul2_rn(make_float2(wdh[r], wdh[r]), xd);
+                                const float2 sL = __fmul2_rn(make_float2(wd[r].x, wd[r].x), xd);
+                                const float2 sH = __fmul2_rn(make_float2(wd[r].y, wd[r].y), xd);
                                 accL[r][n] = __ffma2_rn(sL, fL, accL[r][n]);
                                 accH[r][n] = __ffma2_rn(sH, fH, accH[r][n]);
                             }
@@ -256,6 +290,49 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgemm(const WGemmArgs a) {
             }
         }
     }
+}
+
+// One thread per 4-byte word of the wide layout.
+__global__ void k_wide_repack(const uint8_t* __restrict__ tiles, int n_rg, int nq, uint8_t* __restrict__ wide,
+                              long long n_words) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_words;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long byte = i * 4;
+        const long long seg_i = byte / kTileBytes;  // ((rt * nq + q) * 2 + hh) * 4 + bq
+        const int off = (int)(byte - seg_i * kTileBytes);
+        const int bq = (int)(seg_i & 3), hh = (int)((seg_i >> 2) & 1);
+        const long long rq = seg_i >> 3;
+        const int q = (int)(rq % nq);
+        const long long rt = rq / nq;
+        uint32_t v = 0;
+        if (off < 1024) {
+            // lane L's 16 bytes: word bq of row-groups 4hh .. 4hh+3 (tile16x4: half h, lane L at h*512 + L*16)
+            const int h = off >> 9, L = (off & 511) >> 4, r = (off >> 2) & 3;
+            const long long rg = rt * kWgRG + hh * 4 + r;
+            if (rg < n_rg)
+                v = *reinterpret_cast<const uint32_t*>(tiles + ((size_t)rg * nq + q) * kTileBytes + h * 512 + L * 16 + bq * 4);
+        } else {
+            // g's 16 bytes: (wd row g, wd row g + 8) of block bq for row-groups 4hh .. 4hh+3
+            const int gg = (off - 1024) >> 4, r = ((off - 1024) >> 2) & 3;
+            const long long rg = rt * kWgRG + hh * 4 + r;
+            if (rg < n_rg) {
+                const uint8_t* sc = tiles + ((size_t)rg * nq + q) * kTileBytes + 1024 + gg * 16;  // [g][h][blk] fp16
+                const uint32_t lo = *reinterpret_cast<const uint16_t*>(sc + bq * 2);
+                const uint32_t hi = *reinterpret_cast<const uint16_t*>(sc + 8 + bq * 2);
+                v = lo | (hi << 16);
+            }
+        }
+        reinterpret_cast<uint32_t*>(wide)[i] = v;
+    }
+}
+
+cudaError_t launch_wide_repack(const uint8_t* tiles, int n_rg, int nq, uint8_t* wide, cudaStream_t st) {
+    const long long n_rt = (n_rg + kWgRG - 1) / kWgRG;
+    const long long n_words = n_rt * nq * kWgWStage / 4;
+    long long grid = (n_words + 255) / 256;
+    if (grid > 65536) grid = 65536;
+    k_wide_repack<<<(int)grid, 256, 0, st>>>(tiles, n_rg, nq, wide, n_words);
+    return cudaGetLastError();
 }
 
 cudaError_t wgemm_init_attrs(int max_smem) {
