@@ -214,7 +214,8 @@ __device__ __forceinline__ AttnArgs stream_view(const BAttnArgs& ba, int b) {
 // one barrier per sub-block), and Q and the probabilities P enter the fp16 MMAs as single fp16 values
 // (relative error ~5e-4 on the head outputs, which are then quantised to Q8_0 with steps of 1/254).
 // ---------------------------------------------------------------------------------------------
-constexpr int kBStages = 4;
+constexpr int kBPair = 2;    // sub-blocks per barrier
+constexpr int kBStages = 6;  // ring slots: three pairs (one computed, two in flight)
 constexpr size_t kBStageHalves = (size_t)2 * kSub * kQStride;  // K then V of one sub-block
 constexpr size_t battn_smem_bytes() { return ((size_t)kQRows * kQStride + kBStages * kBStageHalves) * 2; }
 
@@ -223,9 +224,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_stages() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(kBStages - 2) : "memory");
-}
+__device__ __forceinline__ void cp_async_wait_pair() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // Sub-block at positions [sb, sb + 32) of kv head column col0 into ring slot `slot` (zero past p1).
 __device__ __forceinline__ void battn_issue(const AttnArgs& a, __half* ring, int slot, int sb, int p1, int col0, int tid) {
@@ -254,10 +253,16 @@ __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int h
     const int lo_max = max(0, pos + nv - a.max_seq);
     const int col0 = kvh * kHD;
     const int nsb = (p1 - p0 + kSub - 1) / kSub;
+    const int npair = (nsb + kBPair - 1) / kBPair;
     __syncthreads();  // the previous item is done with Q and the ring
+    // pairs 0 and 1 in flight (one commit group per pair); sub-block ib lives in slot ib % kBStages
 #pragma unroll
-    for (int i = 0; i < kBStages - 1; ++i) {
-        if (i < nsb) battn_issue(a, ring, i, p0 + i * kSub, p1, col0, tid);
+    for (int jp = 0; jp < 2; ++jp) {
+#pragma unroll
+        for (int h = 0; h < kBPair; ++h) {
+            const int ib = jp * kBPair + h;
+            if (ib < nsb) battn_issue(a, ring, ib, p0 + ib * kSub, p1, col0, tid);
+        }
         cp_async_commit();
     }
 #pragma unroll
@@ -278,14 +283,21 @@ __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int h
     float o[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    for (int ib = 0; ib < nsb; ++ib) {
-        const int sb = p0 + ib * kSub;
-        cp_async_wait_stages();
-        __syncthreads();  // sub-block ib landed for every thread; slot of ib - 1 is free
-        if (ib + kBStages - 1 < nsb)
-            battn_issue(a, ring, (ib + kBStages - 1) % kBStages, sb + (kBStages - 1) * kSub, p1, col0, tid);
+    for (int jp = 0; jp < npair; ++jp) {
+        cp_async_wait_pair();
+        __syncthreads();  // pair jp landed for every thread; the slots of pair jp - 1 are free
+#pragma unroll
+        for (int h = 0; h < kBPair; ++h) {
+            const int ib = (jp + 2) * kBPair + h;
+            if (ib < nsb) battn_issue(a, ring, ib % kBStages, p0 + ib * kSub, p1, col0, tid);
+        }
         cp_async_commit();
         if (!active) continue;
+#pragma unroll 1
+        for (int h = 0; h < kBPair; ++h) {
+        const int ib = jp * kBPair + h;
+        if (ib >= nsb) break;
+        const int sb = p0 + ib * kSub;
         const uint32_t slot = smem_u32(ring + (size_t)(ib % kBStages) * kBStageHalves);
         const uint32_t k_a = slot + k_off, v_a = slot + v_off;
         // ---- S^T: positions sb + 16 mt + (g, g+8) x rows 8 nt + (2t, 2t+1) ----
@@ -351,6 +363,7 @@ __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int h
                 ldsm_x4_t(v_a + (uint32_t)(mt * 16 * kQStride * 2) + i * 32, v0, v1, v2, v3);
                 mma_f16(o[i], v0, v1, v2, v3, ph0, ph1);
             }
+        }
         }
     }
 #pragma unroll
@@ -507,7 +520,7 @@ struct sd_batch {
     int dev = 0, sms = 0, max_smem = 0;
     cudaStream_t st = nullptr;
     int B = 0, W = 0, max_seq = 0, M_max = 0;
-    int chunk = 256, max_chunks = 0, kp_max = 8;
+    int chunk = 512, max_chunks = 0, kp_max = 8;  // attention: positions per item (partials per 512 positions)
     __half *kc = nullptr, *vc = nullptr;  // [n_layers][B][max_seq][kv_rows]
     size_t kv_stream = 0, kv_layer = 0;
     float *x = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr;
@@ -949,6 +962,9 @@ int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_b
     cudaMemsetAsync(b->img_h, 0, wimg_bytes((int)M, m.hidden), b->st);
     cudaMemsetAsync(b->x, 0, M * m.dim * sizeof(float), b->st);
     cudaMemsetAsync(b->ctrl, 0, sizeof(DevCtrl) * n_streams, b->st);
+    // rings start as fp16 zeros (positions never written read as zeros, never as stale bytes)
+    cudaMemsetAsync(b->kc, 0, (size_t)m.n_layers * b->kv_layer * sizeof(__half), b->st);
+    cudaMemsetAsync(b->vc, 0, (size_t)m.n_layers * b->kv_layer * sizeof(__half), b->st);
     cudaMemsetAsync(b->gs, 0, sizeof(GenState) * n_streams, b->st);
     if ((rc = finish(b))) return bail(rc);
     *out = b;

@@ -14,6 +14,10 @@ value = all ranks' tokens / max-over-ranks time (weak scaling).
 
 --impl reference: the reference's CPU decode path, restated in C (oracle/, the reference itself needs
 arm_neon.h / GCD / Accelerate and does not compile on x86), timed on the host cores on a bounded sample.
+
+Other workloads (--workload): selfspec = config 4 (self-speculation, 32K context), gemv = config 1 (single
+W4A8 matvec), serving = config 5 (64 streams per GPU through the batched path, 4096-token contexts, K=4 n-gram,
+one batch per rank under torchrun), forward / serving-forward = single forwards for profiling.
 """
 from __future__ import annotations
 
@@ -444,6 +448,47 @@ def run_serving(args, ctx_path, rank, world, local, dist, peaks):
     ctx.close()
 
 
+def run_serving_forward(args):
+    """One batched verify forward (T = K+1 tokens of each of --streams streams at position --ctx-serve) on a
+    Mistral-7B-shaped model with --layers layers; the rings hold zeros (attention reads every position of
+    the window all the same).  For per-kernel timing and ncu captures of the batched path; CUDA events around
+    --steps forwards."""
+    import dataclasses
+    import torch
+    from anetransformers_b200 import gguf as G
+    from anetransformers_b200.engine import BatchContext, Context
+    cfg = dataclasses.replace(G.MISTRAL_7B, n_layers=args.layers)
+    path = os.path.join(tempfile.gettempdir(), f"specdec_mistral7b_{args.layers}l_q4_0_seed0.gguf")
+    if args.layers == 32:
+        path = os.path.join(tempfile.gettempdir(), "specdec_mistral7b_q4_0_seed0.gguf")
+    if not os.path.exists(path):
+        G.write_synthetic_gguf_parallel(path, cfg, seed=0)
+    T = args.S or SPEC_K + 1
+    ctx = Context(path, max_seq=64)
+    bc = BatchContext(ctx, args.streams, max_seq=args.ctx_serve + T + 64, width=8)
+    rng = np.random.default_rng(5)
+    toks = rng.integers(3, 32000, (args.streams, T)).astype(np.int32)
+    pos = np.full(args.streams, args.ctx_serve, np.int32)
+    for _ in range(args.warmup):
+        bc.forward(toks, pos, want_logits=False)
+    stream = torch.cuda.ExternalStream(bc.stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        bc.forward(toks, pos, want_logits=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    wbytes = args.layers * 122_683_392
+    kv = args.layers * 2 * 1024 * 2 * (args.ctx_serve + T) * args.streams
+    print(json.dumps({"workload": "serving-forward", "layers": args.layers, "streams": args.streams, "T": T,
+                      "ctx": args.ctx_serve, "ms_per_forward": round(ms, 3),
+                      "weight_plus_kv_gbs": round((wbytes + kv) / (ms * 1e-3) / 1e9, 1)}), flush=True)
+    bc.close()
+    ctx.close()
+
+
 def run_forward(args):
     """Single verify forwards of S tokens (default K+1 = 5) after a ctx-token prefill, on a Mistral-7B-shaped
     synthetic model with --layers layers (a few layers keep ncu captures small while every matrix keeps its
@@ -491,7 +536,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=None, help="generated tokens per step (default: the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="specdec", choices=["specdec", "selfspec", "gemv", "forward", "serving"],
+    ap.add_argument("--workload", default="specdec",
+                    choices=["specdec", "selfspec", "gemv", "forward", "serving", "serving-forward"],
                     help="specdec = BASELINE config 3 (the default line), selfspec = config 4, gemv = config 1, "
                          "serving = config 5 (batched streams), forward = single verify forwards (profiling: "
                          "--layers, --S, --ctx)")
@@ -516,6 +562,9 @@ def main():
         return
     if args.workload == "forward":
         run_forward(args)
+        return
+    if args.workload == "serving-forward":
+        run_serving_forward(args)
         return
     args.warmup = max(args.warmup, 3)
 
