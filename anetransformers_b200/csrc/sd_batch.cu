@@ -243,10 +243,10 @@ __device__ __forceinline__ void battn_issue(const AttnArgs& a, __half* ring, int
 }
 
 __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi_max, int kvh, int c, __half* qh,
-                           __half* ring, int tid) {
+                           __half* ring, float* xch, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int nt = warp & 3, dh = warp >> 2;
+    const int nt = warp & 3, ph = warp >> 2;  // n-tile; which 16 positions of each sub-block (m-tile ph)
     const bool active = 2 * nt < nv;
     const int p0 = max(c * a.chunk, lo_min);
     const int p1 = min((c + 1) * a.chunk, hi_max + 1);
@@ -254,8 +254,7 @@ __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int h
     const int col0 = kvh * kHD;
     const int nsb = (p1 - p0 + kSub - 1) / kSub;
     const int npair = (nsb + kBPair - 1) / kBPair;
-    __syncthreads();  // the previous item is done with Q and the ring
-    // pairs 0 and 1 in flight (one commit group per pair); sub-block ib lives in slot ib % kBStages
+    __syncthreads();  // the previous item is done with Q, the ring and the exchange buffer
 #pragma unroll
     for (int jp = 0; jp < 2; ++jp) {
 #pragma unroll
@@ -277,12 +276,13 @@ __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int h
     }
     const int lr = lane & 7, lq = lane >> 3;
     const uint32_t q_a = smem_u32(qh + (nt * 8 + lr) * kQStride + (lq & 1) * 8);
-    const uint32_t k_off = (uint32_t)(((lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8) * 2);
-    const uint32_t v_off = (uint32_t)(((kSub + lr + (lq >> 1) * 8) * kQStride + dh * 64 + (lq & 1) * 8) * 2);
+    // K (A of S^T) for m-tile ph; V (A of O^T via .trans) for the same 16 positions, all 128 dims
+    const uint32_t k_off = (uint32_t)(((ph * 16 + lr + (lq & 1) * 8) * kQStride + (lq >> 1) * 8) * 2);
+    const uint32_t v_off = (uint32_t)(((kSub + ph * 16 + lr + (lq >> 1) * 8) * kQStride + (lq & 1) * 8) * 2);
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float o[4][4];
+    float o[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     for (int jp = 0; jp < npair; ++jp) {
         cp_async_wait_pair();
         __syncthreads();  // pair jp landed for every thread; the slots of pair jp - 1 are free
@@ -295,97 +295,120 @@ __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int h
         if (!active) continue;
 #pragma unroll 1
         for (int h = 0; h < kBPair; ++h) {
-        const int ib = jp * kBPair + h;
-        if (ib >= nsb) break;
-        const int sb = p0 + ib * kSub;
-        const uint32_t slot = smem_u32(ring + (size_t)(ib % kBStages) * kBStageHalves);
-        const uint32_t k_a = slot + k_off, v_a = slot + v_off;
-        // ---- S^T: positions sb + 16 mt + (g, g+8) x rows 8 nt + (2t, 2t+1) ----
-        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            const int ib = jp * kBPair + h;
+            if (ib >= nsb) break;
+            const int sb = p0 + ib * kSub;
+            const uint32_t slot = smem_u32(ring + (size_t)(ib % kBStages) * kBStageHalves);
+            const uint32_t k_a = slot + k_off, v_a = slot + v_off;
+            // ---- S^T: positions sb + 16 ph + (g, g+8) x rows 8 nt + (2t, 2t+1) ----
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < kHD / 16; ++ks) {
-            uint32_t b0, b1;
-            ldsm_x2(q_a + ks * 32, b0, b1);
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                uint32_t k0, k1, k2, k3;
-                ldsm_x4(k_a + (uint32_t)(mt * 16 * kQStride * 2) + ks * 32, k0, k1, k2, k3);
-                mma_f16(sc[mt], k0, k1, k2, k3, b0, b1);
+            for (int ks = 0; ks < kHD / 16; ++ks) {
+                uint32_t b0, b1, k0, k1, k2, k3;
+                ldsm_x2(q_a + ks * 32, b0, b1);
+                ldsm_x4(k_a + ks * 32, k0, k1, k2, k3);
+                mma_f16(sc, k0, k1, k2, k3, b0, b1);
             }
-        }
-        if (sb + kSub > p1 || sb + kSub - 1 > pos || sb < lo_max) {
-            const int s = 2 * nt + (t >> 1);
-            const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+            const int pb = sb + ph * 16;
+            if (pb + 16 > p1 || pb + 15 > pos || pb < lo_max) {
+                const int s = 2 * nt + (t >> 1);
+                const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int p = sb + mt * 16 + g + (e >> 1) * 8;
-                    if (!(s < nv && p < p1 && p >= lo && p <= hi)) sc[mt][e] = -INFINITY;
+                    const int p = pb + g + (e >> 1) * 8;
+                    if (!(s < nv && p < p1 && p >= lo && p <= hi)) sc[e] = -INFINITY;
                 }
-        }
-        float x0 = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
-        float x1 = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+            }
+            float x0 = fmaxf(sc[0], sc[2]), x1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
-        for (int o2 = 4; o2 < 32; o2 <<= 1) {
-            x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
-            x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
-        }
-        const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
-        const float c0 = (m0 == -INFINITY) ? 0.f : exp_fast(m0 - n0);
-        const float c1 = (m1 == -INFINITY) ? 0.f : exp_fast(m1 - n1);
+            for (int o2 = 4; o2 < 32; o2 <<= 1) {
+                x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o2));
+                x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o2));
+            }
+            const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+            const float c0 = (m0 == -INFINITY) ? 0.f : exp_fast(m0 - n0);
+            const float c1 = (m1 == -INFINITY) ? 0.f : exp_fast(m1 - n1);
+            sc[0] = sc[0] == -INFINITY ? 0.f : exp_fast(sc[0] - n0);
+            sc[1] = sc[1] == -INFINITY ? 0.f : exp_fast(sc[1] - n1);
+            sc[2] = sc[2] == -INFINITY ? 0.f : exp_fast(sc[2] - n0);
+            sc[3] = sc[3] == -INFINITY ? 0.f : exp_fast(sc[3] - n1);
+            m0 = n0;
+            m1 = n1;
+            l0 = l0 * c0 + (sc[0] + sc[2]);
+            l1 = l1 * c1 + (sc[1] + sc[3]);
+            if (c0 != 1.0f || c1 != 1.0f) {
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            sc[mt][0] = sc[mt][0] == -INFINITY ? 0.f : exp_fast(sc[mt][0] - n0);
-            sc[mt][1] = sc[mt][1] == -INFINITY ? 0.f : exp_fast(sc[mt][1] - n1);
-            sc[mt][2] = sc[mt][2] == -INFINITY ? 0.f : exp_fast(sc[mt][2] - n0);
-            sc[mt][3] = sc[mt][3] == -INFINITY ? 0.f : exp_fast(sc[mt][3] - n1);
-        }
-        m0 = n0;
-        m1 = n1;
-        l0 = l0 * c0 + ((sc[0][0] + sc[0][2]) + (sc[1][0] + sc[1][2]));
-        l1 = l1 * c1 + ((sc[0][1] + sc[0][3]) + (sc[1][1] + sc[1][3]));
+                for (int i = 0; i < 8; ++i) {
+                    o[i][0] *= c0;
+                    o[i][1] *= c1;
+                    o[i][2] *= c0;
+                    o[i][3] *= c1;
+                }
+            }
+            // ---- O^T (dims 16 i + (g, g+8) x rows 2t, 2t+1) += V^T P^T over the 16 positions ----
+            const uint32_t ph0 = movm_t(h2u(__floats2half2_rn(sc[0], sc[1])));
+            const uint32_t ph1 = movm_t(h2u(__floats2half2_rn(sc[2], sc[3])));
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            o[i][0] *= c0;
-            o[i][1] *= c1;
-            o[i][2] *= c0;
-            o[i][3] *= c1;
-        }
-        // ---- O^T (dims 64 dh + 16 i + (g, g+8) x rows 2t, 2t+1) += V^T P^T ----
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            const uint32_t ph0 = movm_t(h2u(__floats2half2_rn(sc[mt][0], sc[mt][1])));
-            const uint32_t ph1 = movm_t(h2u(__floats2half2_rn(sc[mt][2], sc[mt][3])));
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < 8; ++i) {
                 uint32_t v0, v1, v2, v3;
-                ldsm_x4_t(v_a + (uint32_t)(mt * 16 * kQStride * 2) + i * 32, v0, v1, v2, v3);
+                ldsm_x4_t(v_a + i * 32, v0, v1, v2, v3);
                 mma_f16(o[i], v0, v1, v2, v3, ph0, ph1);
             }
         }
-        }
     }
+    // ---- merge the two position halves of each n-tile (warp nt + 4 hands its state to warp nt) ----
 #pragma unroll
     for (int o2 = 4; o2 < 32; o2 <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, o2);
         l1 += __shfl_xor_sync(0xffffffffu, l1, o2);
     }
+    float* xw = xch + (size_t)nt * (36 * 32);  // [36][32]: o[8][4], m0, m1, l0, l1 per lane
+    __syncthreads();  // the exchange buffer overlays the ring: every warp is done with the last sub-blocks
+    if (ph == 1 && active) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) xw[(i * 4 + e) * 32 + lane] = o[i][e];
+        xw[32 * 32 + lane] = m0;
+        xw[33 * 32 + lane] = m1;
+        xw[34 * 32 + lane] = l0;
+        xw[35 * 32 + lane] = l1;
+    }
+    __syncthreads();
+    if (ph != 0 || !active) return;
+    {
+        const float bm0 = xw[32 * 32 + lane], bm1 = xw[33 * 32 + lane];
+        const float bl0 = xw[34 * 32 + lane], bl1 = xw[35 * 32 + lane];
+        const float M0 = fmaxf(m0, bm0), M1 = fmaxf(m1, bm1);
+        const float fa0 = (m0 == -INFINITY) ? 0.f : exp_fast(m0 - M0), fb0 = (bm0 == -INFINITY) ? 0.f : exp_fast(bm0 - M0);
+        const float fa1 = (m1 == -INFINITY) ? 0.f : exp_fast(m1 - M1), fb1 = (bm1 == -INFINITY) ? 0.f : exp_fast(bm1 - M1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            o[i][0] = o[i][0] * fa0 + xw[(i * 4 + 0) * 32 + lane] * fb0;
+            o[i][1] = o[i][1] * fa1 + xw[(i * 4 + 1) * 32 + lane] * fb1;
+            o[i][2] = o[i][2] * fa0 + xw[(i * 4 + 2) * 32 + lane] * fb0;
+            o[i][3] = o[i][3] * fa1 + xw[(i * 4 + 3) * 32 + lane] * fb1;
+        }
+        l0 = l0 * fa0 + bl0 * fb0;
+        l1 = l1 * fa1 + bl1 * fb1;
+        m0 = M0;
+        m1 = M1;
+    }
     const int r0 = nt * 8 + 2 * t;
     const int s = 2 * nt + (t >> 1);
-    if (active && s < nv) {
+    if (s < nv) {
         const size_t pi = ((size_t)s * a.n_heads + kvh * kGQA + (r0 & 3)) * a.max_chunks + c;
-        float* acc0 = a.part_acc + pi * kHD + dh * 64;
+        float* acc0 = a.part_acc + pi * kHD;
         float* acc1 = acc0 + (size_t)a.max_chunks * kHD;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 8; ++i) {
             const int d = 16 * i + g;
             acc0[d] = o[i][0];
             acc1[d] = o[i][1];
             acc0[d + 8] = o[i][2];
             acc1[d + 8] = o[i][3];
         }
-        if (dh == 0 && g == 0) {
+        if (g == 0) {
             a.part_ml[pi] = make_float2(m0, l0);
             a.part_ml[pi + a.max_chunks] = make_float2(m1, l1);
         }
@@ -407,8 +430,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_battn_partial(const BAttnAr
     const int n_items = (c_last - c_first + 1) * a.n_kvh;
     __half* qh = reinterpret_cast<__half*>(dsm);
     __half* ring = qh + kQRows * kQStride;
+    float* xch = reinterpret_cast<float*>(ring);  // merge buffer of the two position halves, after the ring is drained
     for (int item = blockIdx.x; item < n_items; item += gridDim.x)
-        battn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, qh, ring, threadIdx.x);
+        battn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, qh, ring, xch, threadIdx.x);
     cp_async_wait_all();
 }
 

@@ -77,13 +77,18 @@ struct WgProducer {
         asrc = a.act + (size_t)n0 * kWSeg;
     }
 
-    // Issue stages while fewer than `limit` have been issued; false if a wait for a free slot ran out.
+    // Issue stages while fewer than `limit` have been issued.  block: wait (bounded) for a free slot, false if
+    // the wait ran out; otherwise stop at the first slot still in use.
     __device__ __forceinline__ bool fill(const WGemmArgs& a, int n_units, int limit, uint8_t* smem, uint32_t SB,
-                                         uint64_t* full, uint64_t* empty, int nstage) {
+                                         uint64_t* full, uint64_t* empty, int nstage, bool block = true) {
         while (live && s < limit) {
-            if (s >= nstage && !mbar_wait(&empty[rp.slot], rp.phase ^ 1)) {
-                live = false;
-                return false;
+            if (s >= nstage) {
+                if (!block) {
+                    if (!mbar_try_wait(&empty[rp.slot], rp.phase ^ 1)) return true;
+                } else if (!mbar_wait(&empty[rp.slot], rp.phase ^ 1)) {
+                    live = false;
+                    return false;
+                }
             }
             uint8_t* dst = smem + (size_t)rp.slot * SB;
             mbar_arrive_expect_tx(&full[rp.slot], bytes);
@@ -148,9 +153,14 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgemm(const WGemmArgs a) {
 #pragma unroll
             for (int n = 0; n < kWgMaxN8; ++n) accL[r][n] = accH[r][n] = make_float2(0.f, 0.f);
         for (int q = w.q0; q < w.q1; ++q, ++s, rp.advance(nstage)) {
-            // keep nstage - 1 stages in flight beyond this one (waits for the slot of stage s - 1 to drain)
-            if (producer && !P.fill(a, n_units, s + nstage, smem, SB, full, empty, nstage))
-                set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
+            // the stage this warp consumes next must be issued (a bounded wait only if the ring fell behind);
+            // beyond it, issue into whatever slots the slowest warp has already released
+            if (producer) {
+                if (!P.fill(a, n_units, s + 1, smem, SB, full, empty, nstage))
+                    set_dev_error(a.err, DEV_ERR_EMPTY_WAIT);
+                else
+                    P.fill(a, n_units, s + nstage, smem, SB, full, empty, nstage, false);
+            }
             __syncwarp();
             if (!mbar_wait(&full[rp.slot], rp.phase)) {
                 set_dev_error(a.err, DEV_ERR_FULL_WAIT);
