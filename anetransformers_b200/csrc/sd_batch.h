@@ -19,7 +19,7 @@ namespace sd {
 constexpr int kWgWarps = 16;                      // 2 row halves x 8 token groups; warp 0 lane 0 also produces
 constexpr int kWgThreads = kWgWarps * 32;
 constexpr int kWgRG = 8;                          // row-groups per row tile (128 rows)
-constexpr int kWgMaxN8 = 3;                       // n8 tiles per warp at most
+constexpr int kWgMaxN8 = 2;                       // n8 tiles per warp at most
 constexpr int kWgTokGroups = 8;
 constexpr int kWgMaxTT = kWgTokGroups * kWgMaxN8; // n8 tiles per token tile at most (192 tokens)
 constexpr int kWgWStage = kWgRG * kTileBytes;     // 9216

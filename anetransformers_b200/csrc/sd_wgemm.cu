@@ -188,22 +188,31 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgemm(const WGemmArgs a) {
                         A[r][3] = (whi >> 4) & 0x0F0F0F0Fu;
                         wd[r] = h2x2f(pick4(sc, r));
                     }
+                    uint2 bf[kWgMaxN8];
+                    float2 xd[kWgMaxN8], off[kWgMaxN8];
+                    int d[kWgMaxN8][4][4];
 #pragma unroll
                     for (int n = 0; n < kWgMaxN8; ++n) {
                         if (n < nw) {
-                            const uint2 bf = lds64(ab + n * kWSeg + blk * 256);
+                            bf[n] = lds64(ab + n * kWSeg + blk * 256);
                             const uint4 mu = lds128(mb + n * kWSeg + blk * 64);
-                            const float2 xd = make_float2(__uint_as_float(mu.x), __uint_as_float(mu.y));
-                            const float2 off = make_float2(__uint_as_float(mu.z), __uint_as_float(mu.w));
+                            xd[n] = make_float2(__uint_as_float(mu.x), __uint_as_float(mu.y));
+                            off[n] = make_float2(__uint_as_float(mu.z), __uint_as_float(mu.w));
+#pragma unroll
+                            for (int r = 0; r < 4; ++r)
+                                mma_u8s8_pure(d[n][r], A[r][0], A[r][1], A[r][2], A[r][3], bf[n].x, bf[n].y);
+                        }
+                    }
+#pragma unroll
+                    for (int n = 0; n < kWgMaxN8; ++n) {
+                        if (n < nw) {
 #pragma unroll
                             for (int r = 0; r < 4; ++r) {
-                                int d[4];
-                                mma_u8s8_pure(d, A[r][0], A[r][1], A[r][2], A[r][3], bf.x, bf.y);
-                                const float2 fL = __fadd2_rn(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), off);
-                                const float2 fH = __fadd2_rn(make_float2(__int_as_float(d[2]), __int_as_float(d[3])), off);
+                                const float2 fL = __fadd2_rn(make_float2(__int_as_float(d[n][r][0]), __int_as_float(d[n][r][1])), off[n]);
+                                const float2 fH = __fadd2_rn(make_float2(__int_as_float(d[n][r][2]), __int_as_float(d[n][r][3])), off[n]);
                                 // (wd*xd) * (float)isum accumulated per block, as mistral/dequant.h:1085
-                                const float2 sL = __fmul2_rn(make_float2(wd[r].x, wd[r].x), xd);
-                                const float2 sH = __fmul2_rn(make_float2(wd[r].y, wd[r].y), xd);
+                                const float2 sL = __fmul2_rn(make_float2(wd[r].x, wd[r].x), xd[n]);
+                                const float2 sH = __fmul2_rn(make_float2(wd[r].y, wd[r].y), xd[n]);
                                 accL[r][n] = __ffma2_rn(sL, fL, accL[r][n]);
                                 accH[r][n] = __ffma2_rn(sH, fH, accH[r][n]);
                             }
