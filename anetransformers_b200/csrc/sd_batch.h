@@ -21,7 +21,7 @@ constexpr int kWgThreads = kWgWarps * 32;
 constexpr int kWgRG = 8;                          // row-groups per row tile (128 rows)
 constexpr int kWgMaxN8 = 2;                       // n8 tiles per warp at most
 constexpr int kWgTokGroups = 8;
-constexpr int kWgMaxTT = kWgTokGroups * kWgMaxN8; // n8 tiles per token tile at most (192 tokens)
+constexpr int kWgMaxTT = kWgTokGroups * kWgMaxN8; // n8 tiles per token tile at most (128 tokens)
 constexpr int kWgWStage = kWgRG * kTileBytes;     // 9216
 constexpr int kWgMaxStages = 8;
 

@@ -5,7 +5,7 @@
 //   isum = sum_j (q_j - 8) * x8_j (exact int32, the reference's SDOT block sum, mistral/dequant.h:1068-1087)
 // with the same per-block fp32 arithmetic as the matvec (sd_gemv.cu), so a token's value over a K slice does
 // not depend on the batch.  The matvec reads every weight once per 8 tokens; here a weight tile is read once
-// per token tile of up to 160 tokens, which turns the M = (streams x verify width) contraction of batched
+// per token tile of up to 128 tokens, which turns the M = (streams x verify width) contraction of batched
 // serving from weight-bandwidth bound into a dense int8 contraction.
 //
 // CTA = 16 warps, one CTA per SM, persistent over units.  Unit = (row tile of 128 rows, K slice, token tile
