@@ -485,9 +485,9 @@ struct WgPlan {
     size_t smem = 0;
 };
 
-// Cost model in ns: a quad (128 columns) of a unit costs (0.8 + n8 tiles per warp) x 126 ns (the A-fragment
-// work of a quad is worth most of one n8 tile); a unit adds about one quad of fill / epilogue; K-split partial
-// slices are written and read back at ~6.5 TB/s.
+// Cost model in ns: a quad (128 columns) of a unit costs (0.8 + n8 tiles per warp) x 800 ns (the A-fragment
+// work of a quad is worth most of one n8 tile; 800 ns is the measured QKV unit time at M = 320 over its quads);
+// a unit adds about one quad of fill / epilogue; K-split partial slices are written and read back at ~6.5 TB/s.
 void wg_plan(WgPlan& p, int epi, int rows, int K, int M, int kp_lo, int kp_max, int sms, int max_smem) {
     const int n_rt = wide_row_tiles(rows);
     const int nq = K / 128;
@@ -502,7 +502,7 @@ void wg_plan(WgPlan& p, int epi, int rows, int K, int M, int kp_lo, int kp_max, 
             if (kp > kp_lo && nq / kp < 2) break;
             const long long units = (long long)n_rt * kp * n_tt;
             const long long waves = (units + sms - 1) / sms;
-            double t = (double)waves * ((double)nq / kp + 1.0) * (0.8 + per) * 126.0;
+            double t = (double)waves * ((double)nq / kp + 1.0) * (0.8 + per) * 800.0;
             if (kp > 1) t += (double)kp * M * rows * 8.0 / 6500.0;
             if (t < best * 0.999) {
                 best = t;
@@ -592,9 +592,10 @@ double now_ms() {
     return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
 
-// Plans for T tokens per stream.  The K split of each matrix is the one chosen for the widest forward and is
-// kept for every T, so a token's sums (slice partials added in slice order) do not depend on T: a verify of
-// T = K+1 and a one-token decode give a stream bit-identical logits.  Only the token tiling follows T.
+// Plans for T tokens per stream.  The K split of each matrix is the one chosen for the batch width (the widest
+// forward, normally the verify width K+1) and is kept for every T, so a token's sums (slice partials added in
+// slice order) do not depend on T: a verify of T = K+1 and a one-token decode give a stream bit-identical
+// logits.  Only the token tiling follows T.
 BPlans& plans_for(sd_batch* b, int T) {
     BPlans& P = b->plans[T];
     if (P.ready) return P;

@@ -353,7 +353,8 @@ def run_serving(args, ctx_path, rank, world, local, dist, peaks):
     from anetransformers_b200.engine import BatchContext, Context
     B, n_ctx = args.streams, args.ctx_serve
     ctx = Context(ctx_path, device=local, max_seq=64)
-    bc = BatchContext(ctx, B, max_seq=n_ctx + args.tokens + 64, width=8)
+    # batch width = the verify width: the GEMMs' K splits are planned for it (prefill runs in chunks of it)
+    bc = BatchContext(ctx, B, max_seq=n_ctx + args.tokens + 64, width=SPEC_K + 1)
     rng = np.random.default_rng(2024 + rank)
     prompts = rng.integers(3, 32000, (B, n_ctx)).astype(np.int32)
     t = time.perf_counter()
@@ -465,7 +466,7 @@ def run_serving_forward(args):
         G.write_synthetic_gguf_parallel(path, cfg, seed=0)
     T = args.S or SPEC_K + 1
     ctx = Context(path, max_seq=64)
-    bc = BatchContext(ctx, args.streams, max_seq=args.ctx_serve + T + 64, width=8)
+    bc = BatchContext(ctx, args.streams, max_seq=args.ctx_serve + T + 64, width=T)
     rng = np.random.default_rng(5)
     toks = rng.integers(3, 32000, (args.streams, T)).astype(np.int32)
     pos = np.full(args.streams, args.ctx_serve, np.int32)
