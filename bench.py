@@ -443,7 +443,8 @@ def run_serving(args, ctx_path, rank, world, local, dist, peaks):
                 "tokens_per_stream_iteration": round(tokens / max(iters, 1), 3),
                 "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "setup_s": {"prefill": round(t_prefill, 2)},
-                "gpu_launches": int(fwds * (4 + 32 * 10 + 2))}
+                # per verify iteration: prepare, embed-norm, 9 per layer, LM GEMM, argmax, commit, done count
+                "gpu_launches": int(fwds * (32 * 9 + 6))}
         print(json.dumps(line), flush=True)
     bc.close()
     ctx.close()
