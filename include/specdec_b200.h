@@ -279,7 +279,9 @@ typedef struct {
 } sd_batch_stats;
 
 /* n_streams >= 1; max_seq ring positions per stream; max_width tokens per stream per forward
- * (1..SD_BATCH_MAX_WIDTH; the verify width spec_k + 1 and the prefill chunk). */
+ * (1..SD_BATCH_MAX_WIDTH; the verify width spec_k + 1 and the prefill chunk; the GEMMs' K splits are planned
+ * for it).  The batch reads the context's weights: free every batch before its context.  A batch, like a
+ * context, is used by one host thread at a time. */
 SD_API int sd_batch_create(sd_ctx *ctx, int n_streams, int max_seq, int max_width, sd_batch **out);
 SD_API void sd_batch_free(sd_batch *b);
 /* The CUDA stream (cudaStream_t) every sd_batch_* call of this batch is ordered on. */
