@@ -208,11 +208,14 @@ __device__ __forceinline__ AttnArgs stream_view(const BAttnArgs& ba, int b) {
 
 // ---------------------------------------------------------------------------------------------
 // Batched attention item: every query row (4 heads x nv tokens) of one stream's kv head kvh over chunk c.
-// The layout and online softmax are those of attn_item (sd_dev.cuh), with two changes for throughput over
-// the many streams' rings (together ~1 GB of K/V per layer at 64 x 4096 positions): K/V sub-blocks stream
-// into a kBStages-deep shared-memory ring by cp.async (no register round trip, three sub-blocks in flight,
-// one barrier per sub-block), and Q and the probabilities P enter the fp16 MMAs as single fp16 values
-// (relative error ~5e-4 on the head outputs, which are then quantised to Q8_0 with steps of 1/254).
+// The online softmax is that of attn_item (sd_dev.cuh), with three changes for throughput over the many
+// streams' rings (together ~1 GB of K/V per layer at 64 x 4096 positions):
+//  - K/V sub-blocks of 32 positions stream into a kBStages-slot shared-memory ring by cp.async (no register
+//    round trip; two pairs of sub-blocks in flight while one pair is computed, one barrier per pair);
+//  - Q and the probabilities P enter the fp16 MMAs as single fp16 values (relative error ~5e-4 on the head
+//    outputs, which are then quantised to Q8_0 with steps of 1/254);
+//  - the two warps of an n-tile split each sub-block's positions (16 each) and keep separate running states
+//    over all 128 output dims, merged at the end of the item, so no score tile is computed twice.
 // ---------------------------------------------------------------------------------------------
 constexpr int kBPair = 2;    // sub-blocks per barrier
 constexpr int kBStages = 6;  // ring slots: three pairs (one computed, two in flight)
