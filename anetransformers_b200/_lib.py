@@ -76,6 +76,7 @@ _SIGS = {
     "sd_matvec_q4_0_q8_0_dev": (i32, [vp, Q8Dev, vp, i32, vp]),
     "sd_block_sums_dev": (i32, [vp, Q8Dev, vp, vp]),
     "sd_matvec_q4_0_q8_0_noalloc_dev": (i32, [vp, Q8Dev, vp, i32, vp]),
+    "sd_device_error": (i32, [i32]),
     "sd_host_quantize_f32_to_q8_0": (None, [vp, vp, i32]),
     "sd_host_q4_0_q8_0_matvec": (None, [vp, vp, vp, i32, i32]),
     "sd_host_cache_clear": (None, []),
@@ -98,6 +99,12 @@ _SIGS = {
     "sd_kv_read": (i32, [vp, i32, i32, i32, vp, vp]),
     "sd_ngram_draft": (i32, [vp, i32, i32, i32, i32, vp, vp]),
     "sd_spec_accept": (i32, [vp, vp, vp, vp, i32, f32, i32, u64, vp, vp]),
+    "sd_sample_token": (i32, [vp, vp, i32, f32, i32, f32, f32, vp, i32, u64, vp]),
+    "sd_spec_softmax": (i32, [vp, vp, vp, i32, f32]),
+    "sd_spec_sample_probs": (i32, [vp, vp, i32, u64, vp]),
+    "sd_embed_token": (i32, [vp, i32, vp]),
+    "sd_layer_decode": (i32, [vp, vp, i32, i32]),
+    "sd_logits": (i32, [vp, vp, i32, vp]),
     "sd_gen_params_default": (None, [vp]),
     "sd_generate": (i32, [vp, vp, vp, i32, vp, i32, vp]),
     "sd_decode": (i32, [vp, vp, vp, i32, i32, vp, i32, vp]),

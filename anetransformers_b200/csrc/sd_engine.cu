@@ -516,14 +516,106 @@ int tp_reduce(sd_ctx* c, int S, int* yparts) {
     return nccl_allreduce_sum(c->nccl, c->y, n, c->st);
 }
 
-// One forward of S <= MB (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the position,
-// the tokens and how many of the S are valid.  Logits / argmax go to rows row0.. of c->logits / c->argmax.
-int enqueue_forward_one(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax,
-                        int row0) {
-    // tensor parallel contexts use the persistent kernel once their peers are connected
-    if (c->fused && (c->tp_size == 1 || c->tpx.n > 1))
-        return enqueue_forward_fused(c, S, n_layers, k, v, ctrl, logits_and_argmax, row0);
+// One decode layer l of S tokens in the kernel-per-op path (mistral/mistral_model.h:818-899): the Q8_0 input of
+// the attention norm is in c->act; ends with x updated and the Q8_0 of the next norm (weight w_next) in c->act.
+int enqueue_layer_perop(sd_ctx* c, int l, int S, __half* k, __half* v, DevCtrl* ctrl, NormArgs& na, const float* w_next) {
     const bool pdl = c->use_pdl;
+    const size_t kv_layer = (size_t)c->max_seq * c->kv_rows;
+    LayerW& W = c->L[l];
+    // QKV + RoPE + KV write
+    Plan pq;
+    int rc = build_plan(c, pq, EPI_QKV, W.qkv, c->qkv_rows, c->dim, kRPW, S, 1);
+    if (rc) return rc;
+    pq.a.act = c->act;
+    pq.a.ctrl = ctrl;
+    pq.a.q_out = c->q;
+    pq.a.k_cache = k + l * kv_layer;
+    pq.a.v_cache = v + l * kv_layer;
+    pq.a.q_rows = c->q_rows;
+    pq.a.kv_rows = c->kv_rows;
+    pq.a.max_seq = c->max_seq;
+    pq.a.head_dim = c->hd;
+    pq.a.theta_inv = c->theta_inv;
+    pq.a.q_scale = 1.0f / sqrtf((float)c->hd);
+    if ((rc = launch_plan(c, EPI_QKV, pq))) return rc;
+    // attention
+    AttnArgs aa{};
+    aa.q = c->q;
+    aa.q_ld = c->q_rows;
+    aa.k = k + l * kv_layer;
+    aa.v = v + l * kv_layer;
+    aa.kv_ld = c->kv_rows;
+    aa.n_heads = c->nh_l;
+    aa.n_kvh = c->nkv_l;
+    aa.S = S;
+    aa.max_seq = c->max_seq;
+    aa.chunk = c->attn_chunk;
+    aa.max_chunks = c->max_chunks;
+    aa.part_ml = c->part_ml;
+    aa.part_acc = c->part_acc;
+    aa.out = c->act;
+    aa.ctrl = ctrl;
+    CK(launch_attention(aa, 4 * device_sm_count(c->dev), c->st, pdl), "attention");
+    // o-proj (K-split partials summed by the next norm)
+    Plan po;
+    int kp_o = 0, kp_d = 0;
+    if ((rc = fixed_kparts(c, c->dim, c->q_rows, &kp_o))) return rc;
+    if ((rc = fixed_kparts(c, c->dim, c->hid_l, &kp_d))) return rc;
+    if ((rc = build_plan(c, po, EPI_STORE, W.wo, c->dim, c->q_rows, kRPW, S, kp_o))) return rc;
+    po.a.act = c->act;
+    po.a.ctrl = ctrl;
+    po.a.out = tp_out(c, 2 * l);
+    po.a.out_ld = c->dim;
+    po.a.part_stride = (size_t)c->MB * c->dim;
+    if (po.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "o-proj K split %d too wide", po.a.kparts);
+    if ((rc = launch_plan(c, EPI_STORE, po))) return rc;
+    na.w = W.rms_ffn;
+    na.yparts = po.a.kparts;
+    if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
+    na.tp = tp_args(c, 2 * l);
+    CK(launch_norm_quant(1, na, c->st, pdl), "norm");
+    // gate/up + SiLU + Q8_0
+    Plan pg;
+    if ((rc = build_plan(c, pg, EPI_SILU_Q8, W.w13, 2 * c->hid_l, c->dim, 4, S, 1))) return rc;
+    pg.a.act = c->act;
+    pg.a.ctrl = ctrl;
+    pg.a.h = c->hact;
+    pg.a.hidden = c->hid_l;
+    if ((rc = launch_plan(c, EPI_SILU_Q8, pg))) return rc;
+    // down
+    Plan pd;
+    if ((rc = build_plan(c, pd, EPI_STORE, W.w2, c->dim, c->hid_l, kRPW, S, kp_d))) return rc;
+    pd.a.act = c->hact;
+    pd.a.ctrl = ctrl;
+    pd.a.out = tp_out(c, 2 * l + 1);
+    pd.a.out_ld = c->dim;
+    pd.a.part_stride = (size_t)c->MB * c->dim;
+    if (pd.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "down K split %d too wide", pd.a.kparts);
+    if ((rc = launch_plan(c, EPI_STORE, pd))) return rc;
+    na.w = w_next;
+    na.yparts = pd.a.kparts;
+    if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
+    na.tp = tp_args(c, 2 * l + 1);
+    CK(launch_norm_quant(1, na, c->st, pdl), "norm");
+    return SD_OK;
+}
+
+// LM head of the Q8_0 final-norm output in c->act -> logits rows row0.. (and their argmax).
+int enqueue_head_perop(sd_ctx* c, int S, DevCtrl* ctrl, int row0) {
+    Plan pl;
+    int rc = build_plan(c, pl, EPI_STORE, c->lm, c->vocab, c->dim, kRPW, S, 1);
+    if (rc) return rc;
+    pl.a.act = c->act;
+    pl.a.ctrl = ctrl;
+    pl.a.out = c->logits + (size_t)row0 * c->vocab;
+    pl.a.out_ld = c->vocab;
+    if ((rc = launch_plan(c, EPI_STORE, pl))) return rc;
+    CK(launch_argmax(c->logits + (size_t)row0 * c->vocab, c->vocab, S, c->argmax + row0, ctrl, c->st, c->use_pdl),
+       "argmax");
+    return SD_OK;
+}
+
+NormArgs norm_args(sd_ctx* c, int S, DevCtrl* ctrl) {
     NormArgs na{};
     na.x = c->x;
     na.y = c->y;
@@ -537,99 +629,27 @@ int enqueue_forward_one(sd_ctx* c, int S, int n_layers, __half* k, __half* v, De
     na.yparts = 1;
     na.ystride = (size_t)c->MB * c->dim;
     na.err = c->err;
+    return na;
+}
+
+// One forward of S <= MB (template) tokens over n_layers layers on kv ring (k, v); ctrl gives the position,
+// the tokens and how many of the S are valid.  Logits / argmax go to rows row0.. of c->logits / c->argmax.
+int enqueue_forward_one(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax,
+                        int row0) {
+    // tensor parallel contexts use the persistent kernel once their peers are connected
+    if (c->fused && (c->tp_size == 1 || c->tpx.n > 1))
+        return enqueue_forward_fused(c, S, n_layers, k, v, ctrl, logits_and_argmax, row0);
+    NormArgs na = norm_args(c, S, ctrl);
     // a slice's control block was just written by the previous kernel: launch after it in full order
-    CK(launch_norm_quant(0, na, c->st, pdl && row0 == 0), "embed");
-    const size_t kv_layer = (size_t)c->max_seq * c->kv_rows;
+    CK(launch_norm_quant(0, na, c->st, c->use_pdl && row0 == 0), "embed");
     for (int l = 0; l < n_layers; ++l) {
-        LayerW& W = c->L[l];
-        // QKV + RoPE + KV write
-        Plan pq;
-        int rc = build_plan(c, pq, EPI_QKV, W.qkv, c->qkv_rows, c->dim, kRPW, S, 1);
+        const float* w_next = (l + 1 < n_layers) ? c->L[l + 1].rms_att : c->rms_final;
+        int rc = enqueue_layer_perop(c, l, S, k, v, ctrl, na, w_next);
         if (rc) return rc;
-        pq.a.act = c->act;
-        pq.a.ctrl = ctrl;
-        pq.a.q_out = c->q;
-        pq.a.k_cache = k + l * kv_layer;
-        pq.a.v_cache = v + l * kv_layer;
-        pq.a.q_rows = c->q_rows;
-        pq.a.kv_rows = c->kv_rows;
-        pq.a.max_seq = c->max_seq;
-        pq.a.head_dim = c->hd;
-        pq.a.theta_inv = c->theta_inv;
-        pq.a.q_scale = 1.0f / sqrtf((float)c->hd);
-        if ((rc = launch_plan(c, EPI_QKV, pq))) return rc;
-        // attention
-        AttnArgs aa{};
-        aa.q = c->q;
-        aa.q_ld = c->q_rows;
-        aa.k = k + l * kv_layer;
-        aa.v = v + l * kv_layer;
-        aa.kv_ld = c->kv_rows;
-        aa.n_heads = c->nh_l;
-        aa.n_kvh = c->nkv_l;
-        aa.S = S;
-        aa.max_seq = c->max_seq;
-        aa.chunk = c->attn_chunk;
-        aa.max_chunks = c->max_chunks;
-        aa.part_ml = c->part_ml;
-        aa.part_acc = c->part_acc;
-        aa.out = c->act;
-        aa.ctrl = ctrl;
-        CK(launch_attention(aa, 4 * device_sm_count(c->dev), c->st, pdl), "attention");
-        // o-proj (K-split partials summed by the next norm)
-        Plan po;
-        int kp_o = 0, kp_d = 0;
-        if ((rc = fixed_kparts(c, c->dim, c->q_rows, &kp_o))) return rc;
-        if ((rc = fixed_kparts(c, c->dim, c->hid_l, &kp_d))) return rc;
-        if ((rc = build_plan(c, po, EPI_STORE, W.wo, c->dim, c->q_rows, kRPW, S, kp_o))) return rc;
-        po.a.act = c->act;
-        po.a.ctrl = ctrl;
-        po.a.out = tp_out(c, 2 * l);
-        po.a.out_ld = c->dim;
-        po.a.part_stride = (size_t)c->MB * c->dim;
-        if (po.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "o-proj K split %d too wide", po.a.kparts);
-        if ((rc = launch_plan(c, EPI_STORE, po))) return rc;
-        na.w = W.rms_ffn;
-        na.yparts = po.a.kparts;
-        if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
-        na.tp = tp_args(c, 2 * l);
-        CK(launch_norm_quant(1, na, c->st, pdl), "norm");
-        // gate/up + SiLU + Q8_0
-        Plan pg;
-        if ((rc = build_plan(c, pg, EPI_SILU_Q8, W.w13, 2 * c->hid_l, c->dim, 4, S, 1))) return rc;
-        pg.a.act = c->act;
-        pg.a.ctrl = ctrl;
-        pg.a.h = c->hact;
-        pg.a.hidden = c->hid_l;
-        if ((rc = launch_plan(c, EPI_SILU_Q8, pg))) return rc;
-        // down
-        Plan pd;
-        if ((rc = build_plan(c, pd, EPI_STORE, W.w2, c->dim, c->hid_l, kRPW, S, kp_d))) return rc;
-        pd.a.act = c->hact;
-        pd.a.ctrl = ctrl;
-        pd.a.out = tp_out(c, 2 * l + 1);
-        pd.a.out_ld = c->dim;
-        pd.a.part_stride = (size_t)c->MB * c->dim;
-        if (pd.a.kparts > c->ypart_max) return fail(SD_ERR_INVALID, "down K split %d too wide", pd.a.kparts);
-        if ((rc = launch_plan(c, EPI_STORE, pd))) return rc;
-        na.w = (l + 1 < n_layers) ? c->L[l + 1].rms_att : c->rms_final;
-        na.yparts = pd.a.kparts;
-        if ((rc = tp_reduce(c, S, &na.yparts))) return rc;
-        na.tp = tp_args(c, 2 * l + 1);
-        CK(launch_norm_quant(1, na, c->st, pdl), "norm");
     }
     if (c->tpx.n > 1) CK(launch_tp_advance(c->tp_base, 2 * n_layers, c->st), "tp advance");
     if (!logits_and_argmax) return SD_OK;
-    Plan pl;
-    int rc = build_plan(c, pl, EPI_STORE, c->lm, c->vocab, c->dim, kRPW, S, 1);
-    if (rc) return rc;
-    pl.a.act = c->act;
-    pl.a.ctrl = ctrl;
-    pl.a.out = c->logits + (size_t)row0 * c->vocab;
-    pl.a.out_ld = c->vocab;
-    if ((rc = launch_plan(c, EPI_STORE, pl))) return rc;
-    CK(launch_argmax(c->logits + (size_t)row0 * c->vocab, c->vocab, S, c->argmax + row0, ctrl, c->st, pdl), "argmax");
-    return SD_OK;
+    return enqueue_head_perop(c, S, ctrl, row0);
 }
 
 // Enqueue the forward of S <= kMaxVerify tokens.  A batch wider than MB runs as consecutive forwards of
@@ -1063,6 +1083,62 @@ int sd_forward_layers(sd_ctx* c, int n_layers, const int32_t* tokens, int S, int
     return finish(c);
 }
 
+// Single-op model layer (kernel-per-op path, single-GPU contexts).  x travels through c->x; ctrl carries the
+// position, the token (embedding) and the valid count.
+static int single_op_ready(sd_ctx* c, const char* what) {
+    if (!c) return fail(SD_ERR_INVALID, "%s: null context", what);
+    if (c->tp_size > 1) return fail(SD_ERR_UNSUPPORTED, "%s: single-GPU contexts only", what);
+    cudaSetDevice(c->dev);
+    return SD_OK;
+}
+
+int sd_embed_token(sd_ctx* c, int token, float* out) {
+    clear_error();
+    int rc = single_op_ready(c, "sd_embed_token");
+    if (rc) return rc;
+    if (!out) return fail(SD_ERR_INVALID, "sd_embed_token: null output");
+    if ((rc = check_tokens(c, &token, 1))) return rc;
+    if ((rc = set_ctrl(c, c->ctrl, &token, 1, 0, true))) return rc;
+    NormArgs na = norm_args(c, 1, c->ctrl);
+    CK(launch_norm_quant(0, na, c->st, false), "embed");
+    CK(cudaMemcpyAsync(out, c->x, (size_t)c->dim * 4, cudaMemcpyDeviceToHost, c->st), "download");
+    return finish(c);
+}
+
+int sd_layer_decode(sd_ctx* c, float* x, int layer, int pos) {
+    clear_error();
+    int rc = single_op_ready(c, "sd_layer_decode");
+    if (rc) return rc;
+    if (!x || layer < 0 || layer >= c->n_layers || pos < 0 || pos >= c->max_seq)
+        return fail(SD_ERR_INVALID, "sd_layer_decode: bad arguments");
+    const int32_t tok = 0;
+    if ((rc = set_ctrl(c, c->ctrl, &tok, 1, pos, true))) return rc;
+    CK(cudaMemcpyAsync(c->x, x, (size_t)c->dim * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    NormArgs na = norm_args(c, 1, c->ctrl);
+    na.w = c->L[layer].rms_att;
+    CK(launch_norm_quant(2, na, c->st, false), "norm");
+    const float* w_next = layer + 1 < c->n_layers ? c->L[layer + 1].rms_att : c->rms_final;
+    if ((rc = enqueue_layer_perop(c, layer, 1, c->kc, c->vc, c->ctrl, na, w_next))) return rc;
+    CK(cudaMemcpyAsync(x, c->x, (size_t)c->dim * 4, cudaMemcpyDeviceToHost, c->st), "download");
+    return finish(c);
+}
+
+int sd_logits(sd_ctx* c, const float* x, int S, float* logits) {
+    clear_error();
+    int rc = single_op_ready(c, "sd_logits");
+    if (rc) return rc;
+    if (!x || !logits || S < 1 || S > c->MB) return fail(SD_ERR_INVALID, "sd_logits: bad arguments (S <= %d)", c->MB);
+    int32_t toks[kMaxS] = {0};
+    if ((rc = set_ctrl(c, c->ctrl, toks, S, 0, true))) return rc;
+    CK(cudaMemcpyAsync(c->x, x, (size_t)S * c->dim * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    NormArgs na = norm_args(c, S, c->ctrl);
+    na.w = c->rms_final;
+    CK(launch_norm_quant(2, na, c->st, false), "final norm");
+    if ((rc = enqueue_head_perop(c, S, c->ctrl, 0))) return rc;
+    CK(cudaMemcpyAsync(logits, c->logits, (size_t)S * c->vocab * 4, cudaMemcpyDeviceToHost, c->st), "download");
+    return finish(c);
+}
+
 int sd_prefill(sd_ctx* c, const int32_t* tokens, int n, int start_pos) {
     clear_error();
     if (!c || !tokens || n < 0 || start_pos < 0) return fail(SD_ERR_INVALID, "sd_prefill: bad arguments");
@@ -1147,6 +1223,69 @@ int sd_spec_accept(sd_ctx* c, const float* draft_probs, const float* logits, con
     CK(cudaMemcpy(accepted, d_acc, na * 4, cudaMemcpyDeviceToHost), "download");
     if (counter) *counter = ctr;
     return na;
+}
+
+int sd_sample_token(sd_ctx* c, float* logits, int n, float temp, int top_k, float top_p, float rep_penalty,
+                    const int32_t* prev_tokens, int n_prev, uint64_t seed, uint64_t* counter) {
+    clear_error();
+    constexpr int kMaxPrev = 4096;
+    if (!c || !logits || n < 1 || n > c->vocab || n_prev < 0 || n_prev > kMaxPrev || (n_prev > 0 && !prev_tokens))
+        return fail(SD_ERR_INVALID, "sd_sample_token: bad arguments (n <= vocab, n_prev <= %d)", kMaxPrev);
+    if (temp > 0 && top_k > kMaxTopK)
+        return fail(SD_ERR_INVALID, "sd_sample_token: top_k %d above the device limit %d", top_k, kMaxTopK);
+    cudaSetDevice(c->dev);
+    // scratch: the row in c->logits, its copy in c->probs, prev tokens / result / counter in c->y
+    int* d_prev = reinterpret_cast<int*>(c->y);
+    int* d_out = reinterpret_cast<int*>(c->y) + kMaxPrev;
+    unsigned long long* d_ctr = reinterpret_cast<unsigned long long*>(c->y + kMaxPrev + 4);
+    unsigned long long ctr = counter ? *counter : 0;
+    GenParamsDev p{};
+    p.temp = temp;
+    p.top_k = top_k;
+    p.top_p = top_p;
+    p.rep_penalty = rep_penalty;
+    CK(cudaMemcpyAsync(c->logits, logits, (size_t)n * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    if (n_prev > 0) CK(cudaMemcpyAsync(d_prev, prev_tokens, (size_t)n_prev * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    CK(cudaMemcpyAsync(d_ctr, &ctr, 8, cudaMemcpyHostToDevice, c->st), "upload");
+    CK(launch_sample_token(c->logits, c->probs, n, p, d_prev, n_prev, seed, d_ctr, d_out, c->st), "sample_token");
+    int tok = -1;
+    CK(cudaMemcpyAsync(&tok, d_out, 4, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaMemcpyAsync(&ctr, d_ctr, 8, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaMemcpyAsync(logits, c->logits, (size_t)n * 4, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaStreamSynchronize(c->st), "sample_token");
+    if (tok < 0 || tok >= n) return fail(SD_ERR_CUDA, "sample_token returned %d", tok);
+    if (counter) *counter = ctr;
+    return tok;
+}
+
+int sd_spec_softmax(sd_ctx* c, const float* logits, float* probs, int n, float temp) {
+    clear_error();
+    if (!c || !logits || !probs || n < 1 || n > c->vocab) return fail(SD_ERR_INVALID, "sd_spec_softmax: bad arguments");
+    cudaSetDevice(c->dev);
+    CK(cudaMemcpyAsync(c->logits, logits, (size_t)n * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    CK(launch_spec_softmax(c->logits, c->probs, n, temp, c->st), "spec_softmax");
+    CK(cudaMemcpyAsync(probs, c->probs, (size_t)n * 4, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaStreamSynchronize(c->st), "spec_softmax");
+    return SD_OK;
+}
+
+int sd_spec_sample_probs(sd_ctx* c, const float* probs, int n, uint64_t seed, uint64_t* counter) {
+    clear_error();
+    if (!c || !probs || n < 1 || n > c->vocab) return fail(SD_ERR_INVALID, "sd_spec_sample_probs: bad arguments");
+    cudaSetDevice(c->dev);
+    int* d_out = reinterpret_cast<int*>(c->y);
+    unsigned long long* d_ctr = reinterpret_cast<unsigned long long*>(c->y + 4);
+    unsigned long long ctr = counter ? *counter : 0;
+    CK(cudaMemcpyAsync(c->probs, probs, (size_t)n * 4, cudaMemcpyHostToDevice, c->st), "upload");
+    CK(cudaMemcpyAsync(d_ctr, &ctr, 8, cudaMemcpyHostToDevice, c->st), "upload");
+    CK(launch_spec_sample_probs(c->probs, n, seed, d_ctr, d_out, c->st), "spec_sample_probs");
+    int tok = -1;
+    CK(cudaMemcpyAsync(&tok, d_out, 4, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaMemcpyAsync(&ctr, d_ctr, 8, cudaMemcpyDeviceToHost, c->st), "download");
+    CK(cudaStreamSynchronize(c->st), "spec_sample_probs");
+    if (tok < 0 || tok >= n) return fail(SD_ERR_CUDA, "spec_sample_probs returned %d", tok);
+    if (counter) *counter = ctr;
+    return tok;
 }
 
 void sd_gen_params_default(sd_gen_params* p) {

@@ -11,6 +11,7 @@ int device_sm_count(int dev);
 int device_max_smem(int dev);
 int* device_error_word(int dev);
 int check_device_error(int* word, cudaStream_t st);
+int check_current_device(int dev, const char* what);
 int repack_matrix(const uint8_t* aos_dev, int rows, int cols, RowMap map, uint8_t* dst, cudaStream_t st);
 // Plan + launch a matvec.  a.kparts <= 0 lets the planner choose; a.kparts == 1 forces one slice.
 // For EPI_STORE with a K split the partial outputs go to a.out + p*a.part_stride (the caller sums).

@@ -63,19 +63,38 @@ int device_max_smem(int dev) {
     return cache[dev];
 }
 
-// Per-device error word for calls that do not belong to a context.
+// Per-device error word for calls that do not belong to a context: a file-scope device variable (zero at
+// module load), so neither the word nor reading it allocates.  Its address is looked up once per device with
+// that device current; the name itself is only a host-side stand-in in host code.
+static __device__ int g_device_err;
+
 int* device_error_word(int dev) {
     static int* words[64] = {nullptr};
     static std::mutex mu;
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64) return nullptr;
     if (!words[dev]) {
+        int prev = -1;
+        if (cudaGetDevice(&prev) != cudaSuccess) return nullptr;
+        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return nullptr;
         int* p = nullptr;
-        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
-        cudaMemset(p, 0, sizeof(int));
+        const cudaError_t e = cudaGetSymbolAddress((void**)&p, g_device_err);
+        if (prev != dev) cudaSetDevice(prev);
+        if (e != cudaSuccess) return nullptr;
         words[dev] = p;
     }
     return words[dev];
+}
+
+// The single-op device entry points run on the matrix's device; a caller whose current device differs
+// would launch on one GPU with another GPU's pointers.
+int check_current_device(int dev, const char* what) {
+    int cur = -1;
+    const cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != dev)
+        return fail(SD_ERR_INVALID, "%s: the current device is %d but the matrix lives on device %d", what, cur, dev);
+    return SD_OK;
 }
 
 int check_device_error(int* word, cudaStream_t st) {
@@ -271,8 +290,9 @@ int sd_blocks_to_q8_dev(const sd_block_q8_0* in, sd_q8_dev out, int S, int n, vo
 static int matvec_common(int epi, const sd_qmat* W, sd_q8_dev x, float* y, int32_t* isum, int S, void* stream) {
     if (!W || !x.qs || !x.d || !x.sum) return fail(SD_ERR_INVALID, "matvec: null argument");
     int dev = W->device;
-    int prc = gemv_prepare_device(dev);
+    int prc = check_current_device(dev, "matvec");
     if (prc) return prc;
+    if ((prc = gemv_prepare_device(dev))) return prc;
     cudaStream_t st = (cudaStream_t)stream;
     GemvArgs a = {};
     a.w = W->w;
@@ -427,6 +447,17 @@ void sd_host_q4_0_q8_0_matvec(const void* W, const sd_block_q8_0* x, float* y, i
     if (rc != SD_OK) fprintf(stderr, "specdec_b200: %s\n", sd_last_error());
 }
 
+int sd_device_error(int device) {
+    clear_error();
+    int* w = device_error_word(device);
+    if (!w) return fail(SD_ERR_INVALID, "sd_device_error: no error word on device %d", device);
+    int h = 0;
+    cudaError_t e = cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+    if (h != 0 && (e = cudaMemset(w, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+    return h;
+}
+
 void sd_host_cache_clear(void) {
     std::lock_guard<std::mutex> lk(g_host_mu);
     for (auto& kv : g_wcache) sd_qmat_free(kv.second);
@@ -473,8 +504,9 @@ extern "C" int sd_matvec_q4_0_q8_0_noalloc_dev(const sd_qmat* W, sd_q8_dev x, fl
     clear_error();
     if (!W || !x.qs || !x.d || !x.sum || !y) return fail(SD_ERR_INVALID, "no-alloc matvec: null argument");
     const int dev = W->device;
-    int rc = gemv_prepare_device(dev);
+    int rc = check_current_device(dev, "no-alloc matvec");
     if (rc) return rc;
+    if ((rc = gemv_prepare_device(dev))) return rc;
     float* scratch = nullptr;
     if ((rc = noalloc_scratch(dev, &scratch))) return rc;
     GemvArgs a = {};
@@ -487,7 +519,7 @@ extern "C" int sd_matvec_q4_0_q8_0_noalloc_dev(const sd_qmat* W, sd_q8_dev x, fl
     a.act = Q8Planes{x.qs, x.d, x.sum};
     a.S = S;
     a.ctrl = nullptr;
-    a.err = nullptr;  // no error word: it would need an allocation; the device waits stay bounded
+    a.err = device_error_word(dev);  // a file-scope device variable: no allocation (sd_device_error reads it)
     a.out_ld = W->rows;
     a.out_rows = W->rows;
     a.kparts = 0;

@@ -727,6 +727,71 @@ cudaError_t launch_spec_accept(const float* logits, float* probs, const int* dra
     return cudaGetLastError();
 }
 
+// Stand-alone sample_token (mistral/mistral_model.h:1145-1240) for the C ABI.  logits [n] receives the
+// repetition penalty in place, as the reference's call does (its later steps leave the array as penalised);
+// the top-k selection then runs on the scratch copy.  out[0] = the token; *counter advances by the draws.
+__global__ void __launch_bounds__(kSampleThreads) k_sample_token(float* logits, float* scratch, int n, GenParamsDev p,
+                                                                 const int* prev, int n_prev, unsigned long long seed,
+                                                                 unsigned long long* counter, int* out) {
+    __shared__ GenState g;
+    if (threadIdx.x == 0) {
+        g.seed = seed;
+        g.rng_counter = *counter;
+        if (p.rep_penalty != 1.0f)
+            for (int i = 0; i < n_prev; ++i) {
+                const int t = prev[i];
+                if (t < 0 || t >= n) continue;
+                if (logits[t] > 0) logits[t] /= p.rep_penalty;
+                else logits[t] *= p.rep_penalty;
+            }
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < n; j += blockDim.x) scratch[j] = logits[j];
+    __syncthreads();
+    GenParamsDev q = p;
+    q.rep_penalty = 1.0f;  // applied above
+    const int tok = sample_token_dev(scratch, n, q, nullptr, 0, &g);
+    if (threadIdx.x == 0) {
+        out[0] = tok;
+        *counter = g.rng_counter;
+    }
+}
+
+// spec_softmax (speculative.h:37-57) of one row, and spec_sample_probs (speculative.h:60-68): the linear CDF
+// draw of one uniform from (seed, *counter) over probs [n].  out[0] = the drawn index.
+__global__ void __launch_bounds__(kSampleThreads) k_spec_softmax(const float* logits, float* probs, int n, float temp) {
+    spec_softmax_dev(logits, probs, n, temp);
+}
+
+__global__ void __launch_bounds__(kSampleThreads) k_spec_sample_probs(const float* probs, int n, unsigned long long seed,
+                                                                      unsigned long long* counter, int* out) {
+    __shared__ float r_s;
+    if (threadIdx.x == 0) r_s = (float)philox_u32(seed, *counter) / (float)0xFFFFFFFFu;
+    __syncthreads();
+    const int t = block_cdf_draw(probs, n, r_s, 1.0f);
+    if (threadIdx.x == 0) {
+        out[0] = t;
+        *counter = *counter + 1;
+    }
+}
+
+cudaError_t launch_sample_token(float* logits, float* scratch, int n, const GenParamsDev& p, const int* prev, int n_prev,
+                                unsigned long long seed, unsigned long long* counter, int* out, cudaStream_t st) {
+    k_sample_token<<<1, kSampleThreads, 0, st>>>(logits, scratch, n, p, prev, n_prev, seed, counter, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_spec_softmax(const float* logits, float* probs, int n, float temp, cudaStream_t st) {
+    k_spec_softmax<<<1, kSampleThreads, 0, st>>>(logits, probs, n, temp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_spec_sample_probs(const float* probs, int n, unsigned long long seed, unsigned long long* counter,
+                                     int* out, cudaStream_t st) {
+    k_spec_sample_probs<<<1, kSampleThreads, 0, st>>>(probs, n, seed, counter, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_ngram_scan(const int* h, int hlen, int n, int max_draft, int cur, int* out, cudaStream_t st) {
     k_ngram_scan<<<1, kSampleThreads, 0, st>>>(h, hlen, n, max_draft, cur, out);
     return cudaGetLastError();

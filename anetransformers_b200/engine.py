@@ -214,6 +214,52 @@ class Context:
             _lib.check(n, "sd_spec_accept")
         return acc[:n].tolist(), ctr.value
 
+    # -- single-op model layer (mistral_model.h / speculative.h helpers) ---------------------------------
+    def sample_token(self, logits, temp: float, top_k: int = 40, top_p: float = 0.9, rep_penalty: float = 1.0,
+                     prev_tokens=(), seed: int = 0, counter: int = 0):
+        """mistral_model.h sample_token on the device.  Returns (token, counter, logits after the in-place
+        repetition penalty)."""
+        lg = np.array(logits, dtype=np.float32, copy=True)
+        prev = _i32(prev_tokens)
+        ctr = C.c_uint64(counter)
+        n = _lib.lib().sd_sample_token(self.h, lg.ctypes.data, lg.size, temp, top_k, top_p, rep_penalty,
+                                       prev.ctypes.data if prev.size else None, prev.size, seed, C.byref(ctr))
+        if n < 0:
+            _lib.check(n, "sd_sample_token")
+        return n, ctr.value, lg
+
+    def spec_softmax(self, logits, temp: float) -> np.ndarray:
+        lg = np.ascontiguousarray(logits, np.float32)
+        out = np.empty_like(lg)
+        _lib.check(_lib.lib().sd_spec_softmax(self.h, lg.ctypes.data, out.ctypes.data, lg.size, temp), "sd_spec_softmax")
+        return out
+
+    def spec_sample_probs(self, probs, seed: int = 0, counter: int = 0):
+        p = np.ascontiguousarray(probs, np.float32)
+        ctr = C.c_uint64(counter)
+        n = _lib.lib().sd_spec_sample_probs(self.h, p.ctypes.data, p.size, seed, C.byref(ctr))
+        if n < 0:
+            _lib.check(n, "sd_spec_sample_probs")
+        return n, ctr.value
+
+    def embed_token(self, token: int) -> np.ndarray:
+        out = np.empty(self.info.dim, np.float32)
+        _lib.check(_lib.lib().sd_embed_token(self.h, token, out.ctypes.data), "sd_embed_token")
+        return out
+
+    def layer_decode(self, x, layer: int, pos: int) -> np.ndarray:
+        """mistral_layer_decode_parallel: x [dim] through one layer at pos (writes that layer's K/V)."""
+        xv = np.array(x, dtype=np.float32, copy=True)
+        _lib.check(_lib.lib().sd_layer_decode(self.h, xv.ctypes.data, layer, pos), "sd_layer_decode")
+        return xv
+
+    def logits_of(self, x) -> np.ndarray:
+        """mistral_logits: final RMSNorm + Q8_0 + LM head of hidden states x [S, dim] (or [dim])."""
+        xv = np.ascontiguousarray(np.atleast_2d(np.asarray(x, np.float32)))
+        out = np.empty((xv.shape[0], self.vocab), np.float32)
+        _lib.check(_lib.lib().sd_logits(self.h, xv.ctypes.data, xv.shape[0], out.ctypes.data), "sd_logits")
+        return out
+
 
 class BatchContext:
     """Many independent streams on one GPU sharing a Context's weights (sd_batch_* of the C ABI).  Every

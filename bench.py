@@ -9,8 +9,11 @@ HBM; every step re-decodes the same 512 positions).  value = generated tokens / 
 
 Every forward streams the 4.0 GB of Q4_0 weights (> 126 MB L2), so no L2 flush is needed between steps.
 
-N > 1 (torchrun): data-parallel replicas, one full model per GPU, no collective on the data path;
-value = all ranks' tokens / max-over-ranks time (weak scaling).
+N > 1 (torchrun): configs 3 and 4 run tensor-parallel (BASELINE's layout): Wq/Wk/Wv/W1/W3 split by rows,
+Wo/W2 by columns, the sum all-reduce after o-proj and down-proj over NVLink peer memory (or NCCL with
+--tp-allreduce nccl); value = the one stream's tokens / max-over-ranks time (strong scaling).  --parallel dp
+runs one independent stream per GPU instead; config 5 (serving) is always data-parallel replicas (weak
+scaling, value = all ranks' tokens / max-over-ranks time).
 
 --impl reference: the reference's CPU decode path, restated in C (oracle/, the reference itself needs
 arm_neon.h / GCD / Accelerate and does not compile on x86), timed on the host cores on a bounded sample.
@@ -178,24 +181,78 @@ def matvec_timing(rows, cols, S, n=64, copies=None, seed=7):
     return us, alg
 
 
-def dominant_kernel_roofline(peaks):
-    """The dominant kernel -- the fused gate|up matvec (28672 x 4096 Q4_0, 66 MB) at the verify shape
-    S = K+1 = 5 -- timed live with CUDA events (matvec_timing)."""
-    rows, cols, S = 28672, 4096, SPEC_K + 1
+def gemv_roofline(peaks, rows=28672, cols=4096, S=SPEC_K + 1):
+    """The stand-alone W4A8 matvec k_gemv (default: the fused gate|up shape, 28672 x 4096 Q4_0, 66 MB, at the
+    verify width S = K+1 = 5), timed live with CUDA events (matvec_timing).  The default decode path runs the
+    same tile math inside k_forward and never launches k_gemv; this entry is config 1's kernel."""
     us, alg = matvec_timing(rows, cols, S)
     achieved = alg / (us * 1e-6) / 1e9
     peak = peaks.get("hbm_gbs", 6650.0)
-    traffic = None
+    return {"bound": "hbm", "kernel": f"k_gemv<EPI_STORE> {rows}x{cols} Q4_0, S={S}", "achieved": round(achieved, 1),
+            "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "us_per_launch": round(us, 2), "algorithmic_bytes": alg}
+
+
+def config1_numbers(peaks):
+    """the 4096 x 4096 W4A8 matvec at S = 1 and S = 5 (GB/s of algorithmic bytes and the
+    fraction of the measured HBM copy peak), on rotating weight copies (> L2)."""
+    peak = peaks.get("hbm_gbs", 6650.0)
+    out = {}
+    for S in (1, 5):
+        us, alg = matvec_timing(4096, 4096, S)
+        gbs = alg / (us * 1e-6) / 1e9
+        out[f"S{S}"] = {"us_per_launch": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                        "algorithmic_bytes": alg}
+    return out
+
+
+def profile_traffic(name: str):
+    """traffic_bytes_per_full_forward from a committed ncu summary (the capture itself is too large to take
+    on the full workload; the summary states how its figure was scaled)."""
     try:
-        for line in open(os.path.join(ROOT, "profiles", "gemv_w13_s5.md")):
-            if line.startswith("traffic_bytes_per_launch:"):
-                traffic = int(line.split(":")[1])
+        for line in open(os.path.join(ROOT, "profiles", name)):
+            if line.startswith("traffic_bytes_per_full_forward:"):
+                return int(line.split(":")[1])
     except Exception:
         pass
-    return {"bound": "hbm", "kernel": "k_gemv<EPI_STORE> 28672x4096 Q4_0, S=5", "achieved": round(achieved, 1),
-            "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": traffic, "us_per_launch": round(us, 2),
-            "algorithmic_bytes": alg}
+    return None
+
+
+def forward_roofline(ctx, peaks, world: int, tp: bool, S: int = SPEC_K + 1, pos: int = PROMPT_LEN + GEN_TOKENS // 2,
+                     n: int = 20):
+    """The dominant kernel of the timed path, k_forward (one persistent kernel per verify forward; 99.5 % of the
+    decode step's launch time): n stream-ordered verify forwards of S tokens at the decode step's middle context,
+    timed with CUDA events on the context's stream.  Each forward also runs the control-block upload, the
+    sync-word memset and the 32-thread argmax-key decode (< 1 % of its time).  Algorithmic bytes per forward:
+    this rank's Q4_0 weights (32 layers / tp ranks + the replicated LM head) + the fp16 K/V it attends."""
+    import torch
+    toks = torch.tensor(np.random.default_rng(9).integers(3, 32000, S), dtype=torch.int32, device="cuda")
+    am = torch.empty(S, dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        ctx.forward_dev(toks, pos, argmax_dev=am)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        ctx.forward_dev(toks, pos, argmax_dev=am)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n
+    ranks = world if tp else 1
+    wbytes = (BYTES_PER_FORWARD - 73_728_000) // ranks + 73_728_000
+    kvbytes = KV_BYTES_PER_POS * (pos + S) // ranks
+    alg = wbytes + kvbytes
+    achieved = alg / (us * 1e-6) / 1e9
+    peak = peaks.get("hbm_gbs", 6650.0)
+    traffic = profile_traffic("forward_4layer_s5.md") if ranks == 1 else None
+    return {"bound": "hbm", "kernel": f"k_forward (persistent verify forward, S={S}, context {pos + S})",
+            "achieved": round(achieved, 1), "peak": peak,
+            "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback",
+            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+            "traffic_source": "profiles/forward_4layer_s5.md: ncu dram bytes of a 4-layer capture, scaled to 32 "
+                              "layers by the layer count" if traffic else None,
+            "us_per_launch": round(us, 2), "algorithmic_bytes": alg}
 
 
 def cpu_decode_sample(path: str, n_tokens: int, threads: int):
@@ -406,8 +463,9 @@ def run_serving(args, ctx_path, rank, world, local, dist, peaks):
     e2e_s, e2e_tok = aggregate_ranks(dist, e2e_s, e2e_tok, False)
     e2e = {"value": round(e2e_tok / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": int(hist.nbytes + first.nbytes),
            "d2h_bytes_per_step": int(4 * tokens / max(args.steps, 1)),
-           "what": "sd_batch_decode per step: 64 histories (4096-token context + first token) from pinned host "
-                   "memory, 256-token n-gram spec decode of every stream, tokens back to host; wall clock"}
+           "what": f"sd_batch_decode per step: {B} histories ({n_ctx}-token context + first token) from pinned "
+                   f"host memory, {args.tokens}-token n-gram spec decode of every stream, tokens back to host; "
+                   "wall clock"}
     fwd_ms = ms / max(fwds, 1)
     ctx_mid = n_ctx + args.tokens / 2
     wbytes = BYTES_PER_FORWARD
@@ -549,14 +607,17 @@ def main():
     ap.add_argument("--ctx", type=int, default=1024, help="forward workload: context positions before the forward")
     ap.add_argument("--forward-kernel", type=int, default=None, choices=[0, 1],
                     help="1 = one persistent kernel per forward, 0 = one kernel per op (default: library default)")
-    ap.add_argument("--parallel", default="dp", choices=["tp", "dp"],
-                    help="with --gpus > 1: dp = one independent stream per GPU (aggregate tok/s, weak scaling), "
-                         "tp = one stream tensor-parallel over the GPUs (BASELINE config 3's layout, strong scaling)")
+    ap.add_argument("--parallel", default=None, choices=["tp", "dp"],
+                    help="with --gpus > 1: tp = one stream tensor-parallel over the GPUs (BASELINE configs 3 and 4, "
+                         "the default for specdec / selfspec, strong scaling), dp = one independent stream per GPU "
+                         "(aggregate tok/s, weak scaling; serving is always dp: config 5's 8 replicas)")
     ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
                     help="tp: all-reduce inside the norm kernels over peer memory, or by NCCL")
     ap.add_argument("--shape", default="4096x4096")
     ap.add_argument("--S", type=int, default=0)
     args = ap.parse_args()
+    if args.parallel is None:
+        args.parallel = "dp" if args.workload == "serving" else "tp"
     if args.tokens is None:
         args.tokens = {"selfspec": SELF_TOKENS, "serving": SERVE_TOKENS}.get(args.workload, GEN_TOKENS)
     if args.workload == "gemv":
@@ -689,7 +750,9 @@ def main():
     e2e_request = {"value": round(len(out) / req_s, 2), "unit": UNIT, "ms_per_request": round(1e3 * req_s, 2),
                    "what": "sd_generate: 1024-token prompt from host, prefill in 8-token W4A8 forwards, first token, "
                            "512-token decode, tokens to host"}
-    roof = dominant_kernel_roofline(peaks)
+    roof = forward_roofline(ctx, peaks, world, tp)
+    roof_gemv = gemv_roofline(peaks) if rank == 0 else None
+    cfg1 = config1_numbers(peaks) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -716,7 +779,7 @@ def main():
                 "acceptance_rate": round(stats["acceptance_rate"], 4) if stats else None,
                 "tokens_per_iteration": round(tokens / max(iters, 1), 3),
                 "step_roofline": step_roof,
-                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "e2e_request": e2e_request, "clocks": clk,
+                "roofline": roof, "roofline_gemv": roof_gemv, "config1_gemv": cfg1, "cpu_baseline": cpu, "e2e": e2e, "e2e_request": e2e_request, "clocks": clk,
                 "gpu_launches": int(iters * kernels_per_iter(bool(ctx.info.forward_kernel), tp and args.tp_allreduce == "peer",
                                                              tp and args.tp_allreduce == "nccl"))}
         print(json.dumps(line), flush=True)

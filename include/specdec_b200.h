@@ -100,9 +100,17 @@ SD_API int sd_block_sums_dev(const sd_qmat *W, sd_q8_dev x, int32_t *isum, void 
  * that array's address (and may load the library's device code): make it before any stream capture.
  * All calls on one device share the array, so calls that overlap on the GPU (different streams, or
  * different threads) race and give wrong results; serialise them.  Results equal those of
- * sd_matvec_q4_0_q8_0_dev bit for bit.  Device waits that run out are not reported. */
+ * sd_matvec_q4_0_q8_0_dev bit for bit.  Both entry points must be called with W's device current
+ * (SD_ERR_INVALID otherwise).  A bounded device wait that runs out records its code in the device's error
+ * word (a file-scope device variable, no allocation), which sd_device_error reads. */
 #define SD_NOALLOC_SCRATCH_BYTES (1u << 20)
 SD_API int sd_matvec_q4_0_q8_0_noalloc_dev(const sd_qmat *W, sd_q8_dev x, float *y, int S, void *stream);
+
+/* Read and clear the error word of `device` that the single-op device entry points above (matvec, block
+ * sums, no-alloc matvec) share: 0 if no bounded device wait ran out since the last read, else the positive
+ * device error code; negative on a CUDA failure.  Synchronises the device.  No reference counterpart (the
+ * reference's CPU calls cannot time out). */
+SD_API int sd_device_error(int device);
 
 /* Host-pointer drop-ins with the reference signatures (mistral/dequant.h:545 and :1022).  They run
  * on the current device; the matvec uploads and repacks W on first use and caches it keyed by the
@@ -195,6 +203,19 @@ SD_API int sd_prefill(sd_ctx *ctx, const int32_t *tokens, int n, int start_pos);
 /* First n_layers layers only (self-speculative drafter depth); same contract as sd_forward. */
 SD_API int sd_forward_layers(sd_ctx *ctx, int n_layers, const int32_t *tokens, int S, int pos, float *logits,
                       int32_t *argmax);
+/* Single-op model layer for whole-model parity and host-driven loops (single-GPU contexts; the kernel-per-op
+ * path, not graph-captured).  Host pointers; each returns when its result is in host memory.
+ *   sd_embed_token   replaces embed_token (mistral/mistral_model.h:125-157): out [dim] = row `token` of the
+ *                    Q4_0 embedding, dequantised.
+ *   sd_layer_decode  replaces mistral_layer_decode_parallel (mistral/mistral_model.h:818-899): x [dim] in/out
+ *                    through layer `layer` at position pos, writing that layer's K/V into the ring slot
+ *                    pos % max_seq (attention covers positions max(0, pos+1-max_seq) .. pos).
+ *   sd_logits        replaces mistral_logits (mistral/mistral_model.h:1110-1122): final RMSNorm, Q8_0 and the
+ *                    Q4_0 LM head of S <= max_batch hidden states x [S][dim] -> logits [S][vocab]. */
+SD_API int sd_embed_token(sd_ctx *ctx, int token, float *out);
+SD_API int sd_layer_decode(sd_ctx *ctx, float *x, int layer, int pos);
+SD_API int sd_logits(sd_ctx *ctx, const float *x, int S, float *logits);
+
 /* Copy n ring slots [pos0, pos0+n) of one layer's K and V (fp16 bits) to host buffers
  * [n][kv_dim_local].  The ring itself lives in HBM (mistral/kv_cache.h layout). */
 SD_API int sd_kv_read(sd_ctx *ctx, int layer, int pos0, int n, uint16_t *k, uint16_t *v);
@@ -218,6 +239,20 @@ SD_API int sd_ngram_draft(const int32_t *history, int hlen, int ngram_n, int max
 SD_API int sd_spec_accept(sd_ctx *ctx, const float *draft_probs, const float *logits, const int32_t *draft,
                    int n_draft, float temp, int bonus_mode, uint64_t seed, uint64_t *counter,
                    int32_t *accepted);
+
+/* Replaces sample_token (mistral/mistral_model.h:1145-1240) on the device of ctx: repetition penalty over
+ * prev_tokens[0..n_prev) (applied to logits in place, as the reference does), then at temp <= 0 the argmax
+ * (first index on ties), else top-k (top_k <= 64; 0 = 40), tempered softmax, top-p cut and renormalisation,
+ * and a linear-CDF draw of one uniform from the Philox stream (seed, *counter) (arc4random in the reference),
+ * advancing *counter.  logits: host [n], n <= vocab; n_prev <= 4096.  Returns the token or < 0. */
+SD_API int sd_sample_token(sd_ctx *ctx, float *logits, int n, float temp, int top_k, float top_p, float rep_penalty,
+                           const int32_t *prev_tokens, int n_prev, uint64_t seed, uint64_t *counter);
+/* Replace spec_softmax (mistral/speculative.h:37-57: probs = softmax((logits - max) / temp), host arrays [n])
+ * and spec_sample_probs (mistral/speculative.h:60-68: first i with r < cumsum(probs[0..i]), n-1 if none, r one
+ * uniform of the Philox stream (seed, *counter), advanced by one).  n <= vocab.  sd_spec_sample_probs returns the
+ * index or < 0. */
+SD_API int sd_spec_softmax(sd_ctx *ctx, const float *logits, float *probs, int n, float temp);
+SD_API int sd_spec_sample_probs(sd_ctx *ctx, const float *probs, int n, uint64_t seed, uint64_t *counter);
 
 /* ======================================================================================
  * Generation loops (mistral/mistral_infer.m:579-716, speculative.h:217-379)
@@ -265,7 +300,9 @@ SD_API int sd_decode(sd_ctx *ctx, const sd_gen_params *p, const int32_t *history
  * Batched serving: many independent streams on one GPU sharing a context's weights.  Every stream
  * has its own KV ring and generation state; one forward processes T tokens of every stream with the
  * wide-token W4A8 GEMM (M = n_streams * T rows of int8 MMA work per weight tile read).  Per stream
- * the semantics are those of sd_generate / sd_decode (the reference runs one stream per process).
+ * the semantics are those of sd_generate / sd_decode (the reference runs one stream per process), with
+ * one difference at temp > 0: stream s draws its uniforms from the Philox stream of seed p->seed + s
+ * (the stream sd_generate / sd_decode would use with seed + s), so streams of one batch never share draws.
  * Single-GPU contexts only (tp_size 1).
  * ====================================================================================== */
 #define SD_BATCH_MAX_WIDTH 8

@@ -223,6 +223,38 @@ def sample_argmax(logits: np.ndarray) -> int:
     return lib().or_sample_argmax(_p(lc), logits.size)
 
 
+def sample_token(logits, temp: float, top_k: int = 40, top_p: float = 0.9, rep_penalty: float = 1.0, prev_tokens=(),
+                 seed: int = 0, counter: int = 0):
+    """mistral_model.h:1145-1240 on a copy of logits; returns (token, counter, logits after the penalty)."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    prev = np.ascontiguousarray(prev_tokens, np.int32)
+    sp = SampleParams(temp, top_k, top_p, rep_penalty, _p(prev) if prev.size else None, prev.size)
+    rng = Rng(seed, counter)
+    t = lib().or_sample_token(_p(lg), lg.size, C.addressof(sp), C.addressof(rng))
+    return t, rng.counter, lg
+
+
+def spec_softmax(logits, temp: float) -> np.ndarray:
+    """speculative.h:37-57."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    out = np.empty_like(lg)
+    lib().or_spec_softmax(_p(lg), _p(out), lg.size, temp)
+    return out
+
+
+def spec_sample_probs(probs, seed: int = 0, counter: int = 0):
+    """speculative.h:60-68 with the Philox draw; returns (index, counter)."""
+    p = np.ascontiguousarray(probs, np.float32)
+    rng = Rng(seed, counter)
+    t = lib().or_spec_sample_probs(_p(p), p.size, C.addressof(rng))
+    return t, rng.counter
+
+
+def uniform(seed: int, counter: int) -> float:
+    """The draw the oracle and the device use in place of (float)arc4random() / (float)UINT32_MAX."""
+    return float(np.float32(philox(seed, counter)) / np.float32(4294967295.0))
+
+
 def spec_accept(draft_probs, logits, draft_tokens, temp: float, seed: int = 0, counter: int = 0):
     logits = np.ascontiguousarray(logits, np.float32)
     n_draft = len(draft_tokens)

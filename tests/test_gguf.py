@@ -12,7 +12,7 @@ from anetransformers_b200 import gguf as G
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_DUMP = os.path.join(ROOT, "oracle", "_ref", "gguf_dump")
-REF_SRC = "/root/reference/mistral/gguf_loader.h"
+REF_SRC = os.path.join(os.environ.get("ANETRANSFORMERS_REFERENCE", "/root/reference"), "mistral", "gguf_loader.h")
 
 
 @pytest.fixture(scope="module")

@@ -57,3 +57,47 @@ def test_cli_ngram_decode(mini_path):
     assert out2.returncode == 0, out2.stderr
     a, b = out.stdout.strip(), out2.stdout.strip()
     assert a[:min(len(a), len(b))] == b[:min(len(a), len(b))]
+
+
+def test_single_op_model_layer_matches_oracle(mini_path, oracle):
+    """embed_token / mistral_layer_decode_parallel / mistral_logits as single-op entry points
+    (sd_embed_token, sd_layer_decode, sd_logits), token by token with the hidden state carried through the
+    layers on the host, as the reference's spec_verify does (speculative.h:92-101).
+
+    The chain runs the same kernels in the same order as the engine's forward, so its logits equal the
+    forward's (bar 1e-5 of the logit scale); against the oracle the bar is the logits' 1e-2.  Hidden states
+    are not compared layer by layer with the oracle: a last-bit difference in an RMSNorm scale can move one
+    Q8_0 code, and this small random model's sharply peaked attention amplifies that inside a layer."""
+    from anetransformers_b200 import gguf as G
+    from anetransformers_b200.engine import Context
+    ctx = Context(mini_path, max_seq=64)
+    ref_ctx = Context(mini_path, max_seq=64)
+    om = oracle.OracleModel(G.GGUFFile(mini_path), max_seq=64)
+    kv = om.new_kv()
+    try:
+        toks = np.random.default_rng(71).integers(3, ctx.vocab, 6).tolist()
+        for pos, t in enumerate(toks):
+            x = ctx.embed_token(t)
+            np.testing.assert_array_equal(x, om.embed(t))   # Q4_0 row dequantisation is exact
+            for layer in range(ctx.info.n_layers):
+                x = ctx.layer_decode(x, layer, pos)
+            lg = ctx.logits_of(x)[0]
+            lf, _ = ref_ctx.forward([t], pos)
+            assert np.max(np.abs(lg - lf[0])) <= 1e-5 * np.max(np.abs(lf[0])), pos
+            lr = om.forward(kv, t, pos)
+            assert np.max(np.abs(lg - lr)) <= 1e-2 * np.max(np.abs(lr)), pos
+        # mistral_logits of the oracle's own final hidden state (the LM head alone, S = 2 rows)
+        xr = om.embed(toks[0])
+        kv2 = om.new_kv()
+        for layer in range(om.cfg.n_layers):
+            xr = om.layer(kv2, xr, layer, 0)
+        om.free_kv(kv2)
+        lr = om.logits(xr)
+        lg2 = ctx.logits_of(np.stack([xr, xr]))
+        for r in range(2):
+            assert np.max(np.abs(lg2[r] - lr)) <= 1e-2 * np.max(np.abs(lr))
+    finally:
+        om.free_kv(kv)
+        om.close()
+        ctx.close()
+        ref_ctx.close()
