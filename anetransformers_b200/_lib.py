@@ -108,6 +108,15 @@ _SIGS = {
     "sd_gen_params_default": (None, [vp]),
     "sd_generate": (i32, [vp, vp, vp, i32, vp, i32, vp]),
     "sd_decode": (i32, [vp, vp, vp, i32, i32, vp, i32, vp]),
+    "sd_tokenizer_create": (i32, [vp, sz, vp]),
+    "sd_tokenizer_free": (None, [vp]),
+    "sd_tokenizer_info": (i32, [vp, vp, vp, vp]),
+    "sd_tokenizer_entry": (i32, [vp, i32, vp, vp, vp]),
+    "sd_tokenizer_encode": (i32, [vp, C.c_char_p, vp, i32, i32]),
+    "sd_tokenizer_piece": (C.c_char_p, [vp, i32]),
+    "sd_tokenizer_decode": (vp, [vp, vp, i32]),
+    "sd_tokenizer_apply_chat": (vp, [C.c_char_p]),
+    "sd_free": (None, [vp]),
     "sd_batch_create": (i32, [vp, i32, i32, i32, vp]),
     "sd_batch_free": (None, [vp]),
     "sd_batch_stream": (vp, [vp]),

@@ -5,10 +5,11 @@
  *   --speculative      self-speculative decode          (mistral_infer.m:660-689)
  *   --speculative --metal | --draft ngram
  *                      n-gram (prompt-lookup) speculative decode (mistral_infer.m:638-659)
- * Added flags: --prompt-ids (comma-separated token ids; text prompts need the SentencePiece tokenizer,
- * which this build does not include), --ignore-eos, --draft ngram|self, --ngram-n, --seed, --device.
- * Generated tokens go to stdout (vocabulary pieces when the GGUF has them, else ids); stats to stderr
- * in the reference's layout.
+ * --prompt TEXT is tokenized with the model's vocabulary (sd_tokenizer_*, mistral/tokenizer.h semantics, BOS
+ * first), after the instruct template "[INST] TEXT [/INST]" with --chat (mistral_infer.m:538-550).
+ * Added flags: --prompt-ids (comma-separated token ids instead of text), --ignore-eos, --draft ngram|self,
+ * --ngram-n, --seed, --device.  Generated tokens go to stdout as tokenizer_decode_token pieces
+ * (mistral_infer.m:630, U+2581 shown as a space); stats to stderr in the reference's layout.
  */
 #define _GNU_SOURCE
 #include <getopt.h>
@@ -24,7 +25,8 @@
 #include "specdec_b200.h"
 
 static void usage(const char *argv0) {
-    fprintf(stderr, "Usage: %s --model <gguf> --prompt-ids 1,2,3 [--tokens N] [--temp T]\n", argv0);
+    fprintf(stderr, "Usage: %s --model <gguf> (--prompt TEXT [--chat] | --prompt-ids 1,2,3) [--tokens N] [--temp T]\n",
+            argv0);
     fprintf(stderr, "       [--top-p P] [--top-k K] [--rep-penalty R] [--rep-window W]\n");
     fprintf(stderr, "       [--context N] [--speculative] [--spec-k K] [--spec-layers N] [--metal]\n");
     fprintf(stderr, "       [--draft ngram|self] [--ngram-n N] [--ignore-eos] [--seed S] [--device D]\n");
@@ -33,90 +35,24 @@ static void usage(const char *argv0) {
     fprintf(stderr, "  --spec-layers N  self-speculative draft depth (default 8)\n");
 }
 
-/* Vocabulary pieces from the GGUF (tokenizer.ggml.tokens) for printing. */
-typedef struct {
-    char **piece;
-    int n;
-} Vocab;
-
-static uint64_t rdu(const uint8_t *b, size_t *p, int n) {
-    uint64_t v = 0;
-    memcpy(&v, b + *p, n);
-    *p += n;
-    return v;
-}
-
-static int gv_size(uint32_t t) {
-    static const int sz[] = {1, 1, 2, 2, 4, 4, 4, 1, -1, -1, 8, 8, 8};
-    return t < 13 ? sz[t] : -1;
-}
-
-static void gv_skip(const uint8_t *b, size_t *p, uint32_t t) {
-    if (t == 8) {
-        uint64_t n = rdu(b, p, 8);
-        *p += n;
-    } else if (t == 9) {
-        uint32_t at = (uint32_t)rdu(b, p, 4);
-        uint64_t n = rdu(b, p, 8);
-        for (uint64_t i = 0; i < n; i++) gv_skip(b, p, at);
-    } else {
-        *p += gv_size(t);
-    }
-}
-
-static Vocab load_vocab(const uint8_t *b, size_t len) {
-    Vocab v = {0, 0};
-    size_t p = 8;
-    if (len < 24 || memcmp(b, "GGUF", 4) != 0) return v;
-    rdu(b, &p, 8);
-    uint64_t n_kv = rdu(b, &p, 8);
-    for (uint64_t i = 0; i < n_kv && p < len; i++) {
-        uint64_t kl = rdu(b, &p, 8);
-        const char *k = (const char *)b + p;
-        p += kl;
-        uint32_t t = (uint32_t)rdu(b, &p, 4);
-        if (kl == 21 && memcmp(k, "tokenizer.ggml.tokens", 21) == 0 && t == 9) {
-            rdu(b, &p, 4);
-            uint64_t n = rdu(b, &p, 8);
-            v.piece = (char **)calloc(n, sizeof(char *));
-            v.n = (int)n;
-            for (uint64_t j = 0; j < n; j++) {
-                uint64_t sl = rdu(b, &p, 8);
-                v.piece[j] = strndup((const char *)b + p, sl);
-                p += sl;
-            }
-            return v;
+/* A generated token as the reference prints it: the tokenizer's piece with U+2581 shown as a space. */
+static void print_token(const sd_tokenizer *tok, int id) {
+    const char *s = sd_tokenizer_piece(tok, id);
+    for (const char *c = s; *c; c++) {
+        if ((unsigned char)c[0] == 0xE2 && (unsigned char)c[1] == 0x96 && (unsigned char)c[2] == 0x81) {
+            putchar(' ');
+            c += 2;
+        } else {
+            putchar(*c);
         }
-        gv_skip(b, &p, t);
     }
-    return v;
-}
-
-static void print_token(const Vocab *v, int tok) {
-    if (tok >= 0 && tok < v->n && v->piece[tok]) {
-        const char *s = v->piece[tok];
-        /* SentencePiece word boundary U+2581 -> space; <0xNN> byte tokens -> the byte */
-        if (strncmp(s, "<0x", 3) == 0 && strlen(s) == 6) {
-            putchar((int)strtol(s + 3, NULL, 16));
-            return;
-        }
-        for (const char *c = s; *c; c++) {
-            if ((unsigned char)c[0] == 0xE2 && (unsigned char)c[1] == 0x96 && (unsigned char)c[2] == 0x81) {
-                putchar(' ');
-                c += 2;
-            } else {
-                putchar(*c);
-            }
-        }
-    } else {
-        printf("[%d]", tok);
-    }
+    fflush(stdout);
 }
 
 int main(int argc, char **argv) {
     const char *model_path = NULL, *prompt_ids = NULL, *prompt_text = NULL, *draft = NULL;
     int max_tokens = 128, top_k = 40, rep_window = 64, context_len = 0, use_spec = 0, spec_k = 4, spec_layers = 8;
-    int use_metal = 0, ngram_n = 3, ignore_eos = 0, device = 0;
+    int use_metal = 0, ngram_n = 3, ignore_eos = 0, device = 0, chat_mode = 0;
     float temperature = 0.7f, top_p = 0.9f, rep_penalty = 1.1f;
     unsigned long long seed = 0;
     static struct option opts[] = {
@@ -142,7 +78,7 @@ int main(int argc, char **argv) {
             case 'K': top_k = atoi(optarg); break;
             case 'r': rep_penalty = (float)atof(optarg); break;
             case 'w': rep_window = atoi(optarg); break;
-            case 'c': break;
+            case 'c': chat_mode = 1; break;
             case 'C': context_len = atoi(optarg); break;
             case 'S': use_spec = 1; break;
             case 'k': spec_k = atoi(optarg); break;
@@ -162,23 +98,8 @@ int main(int argc, char **argv) {
         usage(argv[0]);
         return 1;
     }
-    if (!prompt_ids) {
-        fprintf(stderr, "%s: text prompts need the SentencePiece tokenizer, which this build does not include; "
-                        "pass token ids with --prompt-ids%s\n", argv[0], prompt_text ? "" : " (no prompt given)");
-        return 1;
-    }
-    int cap = 16, n_prompt = 0;
-    int32_t *prompt = (int32_t *)malloc(sizeof(int32_t) * cap);
-    for (const char *c = prompt_ids; *c;) {
-        char *end;
-        long v = strtol(c, &end, 10);
-        if (end == c) break;
-        if (n_prompt == cap) prompt = (int32_t *)realloc(prompt, sizeof(int32_t) * (cap *= 2));
-        prompt[n_prompt++] = (int32_t)v;
-        c = *end == ',' ? end + 1 : end;
-    }
-    if (n_prompt == 0) {
-        fprintf(stderr, "Empty prompt\n");
+    if (!prompt_ids && !prompt_text) {
+        usage(argv[0]);
         return 1;
     }
     int fd = open(model_path, O_RDONLY);
@@ -194,7 +115,39 @@ int main(int argc, char **argv) {
         perror("mmap");
         return 1;
     }
-    Vocab vocab = load_vocab((const uint8_t *)base, st.st_size);
+    sd_tokenizer *tok = NULL;
+    if (sd_tokenizer_create(base, st.st_size, &tok) != SD_OK) {
+        fprintf(stderr, "Failed to init tokenizer: %s\n", sd_last_error());
+        return 1;
+    }
+    int vocab_n = 0;
+    sd_tokenizer_info(tok, &vocab_n, NULL, NULL);
+    fprintf(stderr, "Tokenizer: %d tokens\n", vocab_n);
+    int cap = 16, n_prompt = 0;
+    int32_t *prompt = NULL;
+    if (prompt_ids) {
+        prompt = (int32_t *)malloc(sizeof(int32_t) * cap);
+        for (const char *c = prompt_ids; *c;) {
+            char *end;
+            long v = strtol(c, &end, 10);
+            if (end == c) break;
+            if (n_prompt == cap) prompt = (int32_t *)realloc(prompt, sizeof(int32_t) * (cap *= 2));
+            prompt[n_prompt++] = (int32_t)v;
+            c = *end == ',' ? end + 1 : end;
+        }
+    } else {
+        char *chat = chat_mode ? sd_tokenizer_apply_chat(prompt_text) : NULL;
+        const char *text = chat ? chat : prompt_text;
+        cap = 3 * (int)strlen(text) + 8;  /* a character can fall back to 3 byte tokens */
+        prompt = (int32_t *)malloc(sizeof(int32_t) * cap);
+        n_prompt = sd_tokenizer_encode(tok, text, prompt, cap, 1);
+        sd_free(chat);
+    }
+    fprintf(stderr, "Prompt: %d tokens\n", n_prompt);
+    if (n_prompt <= 0) {
+        fprintf(stderr, "Empty prompt after tokenization\n");
+        return 1;
+    }
     sd_ctx_opts co;
     sd_ctx_opts_default(&co);
     co.device = device;
@@ -235,7 +188,7 @@ int main(int argc, char **argv) {
         sd_ctx_free(ctx);
         return 1;
     }
-    for (int i = 0; i < n; i++) print_token(&vocab, out[i]);
+    for (int i = 0; i < n; i++) print_token(tok, out[i]);
     printf("\n");
     fprintf(stderr, "\n--- Stats ---\n");
     fprintf(stderr, "Prompt tokens:    %d\n", n_prompt);
@@ -249,6 +202,7 @@ int main(int argc, char **argv) {
                 gs.total_draft > 0 ? 100.0 * (gs.total_accepted - gs.total_iterations) / gs.total_draft : 0.0);
     }
     sd_ctx_free(ctx);
+    sd_tokenizer_free(tok);
     free(out);
     free(prompt);
     return 0;

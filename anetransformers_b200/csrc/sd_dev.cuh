@@ -703,8 +703,8 @@ __device__ void attn_item(const AttnArgs& a, int nv, int pos, int lo_min, int hi
 
 // Merge the chunk partials of (token s, head h) and quantise the 128 outputs to 4 Q8_0 blocks.
 // nwc warps share the row (wi = this warp's index among them, lane owns dims 4*lane..4*lane+3):
-//   1. every warp reads all (max, sum) pairs lane-parallel (up to 512 chunks in one round trip) -> M;
-//      warp 0: L (lane sums in chunk order, then the butterfly);
+//   1. every warp reads all (max, sum) pairs lane-parallel (128 chunks per round trip) -> M, in the same
+//      round trip as its first eight chunk partials; warp 0: L (lane sums in chunk order, then the butterfly);
 //   2. warp wi adds acc_c * exp(m_c - M) over its contiguous share of the chunks, in chunk order, eight
 //      chunks' loads in flight at a time;
 //   3. the partial vectors meet in obuf ([nwc][128], shared) behind rsync(); warp 0 adds them in warp
@@ -721,22 +721,44 @@ __device__ void attn_combine_row(const AttnArgs& a, int nwc, int pos, int s, int
     const int hi = pos + s, lo = max(0, hi + 1 - a.max_seq);
     const int c0 = lo / a.chunk, c1 = hi / a.chunk;
     const size_t base = ((size_t)s * a.n_heads + h) * a.max_chunks;
-    constexpr int kMl = 16;  // (max, sum) pairs per lane per round trip
-    float M = -INFINITY;
-    for (int g0 = c0; g0 <= c1; g0 += 32 * kMl) {
-        float mx[kMl];
+    constexpr int kMl = 4;  // (max, sum) pairs per lane per round trip
+    constexpr int U = 8;    // this warp's chunk partials per round trip
+    // this warp's chunk range
+    const int nc = c1 - c0 + 1, per = (nc + nwc - 1) / nwc;
+    const int ca = c0 + wi * per, cb = min(c1, ca + per - 1);
+    // One round trip for the common case: this warp's first U chunk partials (they do not depend on M) and
+    // every chunk's (max, sum) pair are loaded together.
+    float4 ac[U];
+    float mx[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int c = ca + u;
+        ac[u] = c <= cb ? *reinterpret_cast<const float4*>(a.part_acc + (base + c) * kHD + lane * 4)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        mx[u] = c <= cb ? a.part_ml[base + c].x : -INFINITY;
+    }
+    float M = -INFINITY, L = 0.f;
+    float2 ml0[kMl];  // the first round's pairs, kept for L
+#pragma unroll
+    for (int u = 0; u < kMl; ++u) {
+        const int c = c0 + lane + 32 * u;
+        ml0[u] = c <= c1 ? a.part_ml[base + c] : make_float2(-INFINITY, 0.f);
+        M = fmaxf(M, ml0[u].x);
+    }
+    for (int g0 = c0 + 32 * kMl; g0 <= c1; g0 += 32 * kMl) {
 #pragma unroll
         for (int u = 0; u < kMl; ++u) {
             const int c = g0 + lane + 32 * u;
-            mx[u] = c <= c1 ? a.part_ml[base + c].x : -INFINITY;
+            M = fmaxf(M, c <= c1 ? a.part_ml[base + c].x : -INFINITY);
         }
-#pragma unroll
-        for (int u = 0; u < kMl; ++u) M = fmaxf(M, mx[u]);
     }
     M = warp_max(M);
-    float L = 0.f;
     if (wi == 0) {
-        for (int g0 = c0; g0 <= c1; g0 += 32 * kMl) {
+        // lane l adds chunks c0 + l + 32k in k order, then the butterfly
+#pragma unroll
+        for (int u = 0; u < kMl; ++u)
+            if (c0 + lane + 32 * u <= c1) L += (ml0[u].x == -INFINITY) ? 0.f : ml0[u].y * expf(ml0[u].x - M);
+        for (int g0 = c0 + 32 * kMl; g0 <= c1; g0 += 32 * kMl) {
             float2 ml[kMl];
 #pragma unroll
             for (int u = 0; u < kMl; ++u) {
@@ -749,20 +771,16 @@ __device__ void attn_combine_row(const AttnArgs& a, int nwc, int pos, int s, int
         }
         L = warp_sum(L);
     }
-    // this warp's chunk range
-    const int nc = c1 - c0 + 1, per = (nc + nwc - 1) / nwc;
-    const int ca = c0 + wi * per, cb = min(c1, ca + per - 1);
     float o[4] = {0.f, 0.f, 0.f, 0.f};
-    constexpr int U = 8;
     for (int cc = ca; cc <= cb; cc += U) {
-        float4 ac[U];
-        float mx[U];
+        if (cc > ca) {
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = cc + u;
-            ac[u] = c <= cb ? *reinterpret_cast<const float4*>(a.part_acc + (base + c) * kHD + lane * 4)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            mx[u] = c <= cb ? a.part_ml[base + c].x : -INFINITY;
+            for (int u = 0; u < U; ++u) {
+                const int c = cc + u;
+                ac[u] = c <= cb ? *reinterpret_cast<const float4*>(a.part_acc + (base + c) * kHD + lane * 4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                mx[u] = c <= cb ? a.part_ml[base + c].x : -INFINITY;
+            }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {

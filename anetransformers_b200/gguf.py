@@ -50,6 +50,10 @@ class ModelConfig:
     context_length: int = 32768
     bos_id: int = 1
     eos_id: int = 2
+    # vocabulary written to tokenizer.ggml.*: "plain" (specials, byte tokens, distinct filler pieces, all scores
+    # 0) or "bpe" (a SentencePiece-style vocabulary with learned merges, for tokenizer tests; bpe_vocab)
+    tokenizer: str = "plain"
+    tokenizer_seed: int = 0
 
     @property
     def head_dim(self) -> int:
@@ -127,6 +131,89 @@ def _vocab(cfg: ModelConfig) -> List[bytes]:
     return toks[: cfg.vocab_size]
 
 
+# Characters of the bpe test vocabulary's corpus; those in BPE_OUTSIDE are left out of the vocabulary so
+# that encoding them takes the byte fallback.
+BPE_CHARS = list("abcdefghijklmnoprstuvwyABCDEFGHIJKLMNOPRSTUVWY0123456789.,;:!?'-()") + ["é", "ü", "ß", "ñ", "中", "文", "😀"]
+BPE_OUTSIDE = ["q", "x", "z", "Q", "X", "€", "λ"]
+
+
+def bpe_corpus_words(seed: int, n_words: int = 2000) -> List[str]:
+    """Seeded pseudo-words (consonant-vowel syllables, some capitalised, some with digits, punctuation or
+    multi-byte characters) for the bpe test vocabulary and the tokenizer tests."""
+    rng = np.random.default_rng(seed)
+    cons = list("bcdfghklmnprstvw")
+    vows = list("aeiouy") + ["é", "ü"]
+    syll = [c + v for c in cons for v in vows] + ["ß", "ñ", "中文", "😀"]
+    words = []
+    for _ in range(n_words):
+        w = "".join(rng.choice(syll, int(rng.integers(1, 5))))
+        r = rng.random()
+        if r < 0.15:
+            w = w[0].upper() + w[1:]
+        elif r < 0.2:
+            w += str(int(rng.integers(0, 100)))
+        elif r < 0.3:
+            w += str(rng.choice(list(".,;:!?")))
+        words.append(w)
+    return words
+
+
+def bpe_vocab(size: int, seed: int = 0, max_merges: int = 900) -> Tuple[List[bytes], np.ndarray, np.ndarray]:
+    """A SentencePiece-style vocabulary of `size` pieces for tokenizer tests: <unk> (UNKNOWN), <s> and </s>
+    (CONTROL), the 256 byte tokens <0xNN> (BYTE), U+2581 and the single characters of BPE_CHARS, then merges
+    learned by pair counting on the words of bpe_corpus_words (each word prefixed by U+2581), in merge order
+    (at most max_merges).
+    A merged piece's score is -(rank // 3), so runs of three merges share a score (equal-score merges must
+    resolve in the reference's order).  Pieces are unique; the rest is filled with unmergeable <fN> pieces."""
+    pieces: List[str] = ["<unk>", "<s>", "</s>"] + ["<0x%02X>" % i for i in range(256)]
+    types = [2, 3, 3] + [6] * 256
+    scores = [0.0] * len(pieces)
+    singles = ["\u2581"] + BPE_CHARS
+    for ch in singles:
+        pieces.append(ch)
+        types.append(1)
+        scores.append(-1e6)
+    have = set(pieces)
+    counts: dict = {}
+    for w in bpe_corpus_words(seed):
+        key = tuple(["\u2581"] + [c for c in w])
+        counts[key] = counts.get(key, 0) + 1
+    words = [(list(k), n) for k, n in counts.items()]
+    rank = 0
+    while len(pieces) < size and rank < max_merges:
+        pc: dict = {}
+        for syms, n in words:
+            for a, b in zip(syms, syms[1:]):
+                pc[(a, b)] = pc.get((a, b), 0) + n
+        if not pc:
+            break
+        (a, b), _ = max(pc.items(), key=lambda kv: (kv[1], kv[0]))
+        m = a + b
+        for i, (syms, n) in enumerate(words):
+            j, out = 0, []
+            while j < len(syms):
+                if j + 1 < len(syms) and syms[j] == a and syms[j + 1] == b:
+                    out.append(m)
+                    j += 2
+                else:
+                    out.append(syms[j])
+                    j += 1
+            words[i] = (out, n)
+        if m not in have:
+            have.add(m)
+            pieces.append(m)
+            types.append(1)
+            scores.append(-float(rank // 3))
+            rank += 1
+    k = 0
+    while len(pieces) < size:
+        pieces.append("<f%d>" % k)
+        types.append(1)
+        scores.append(-1e9)
+        k += 1
+    return [p.encode() for p in pieces[:size]], np.array(scores[:size], "<f4"), np.array(types[:size], "<i4")
+
+
 def _kv_str(key: str, val: str) -> bytes:
     k = key.encode()
     v = val.encode()
@@ -158,18 +245,21 @@ def _header(cfg: ModelConfig) -> Tuple[bytes, List[Tuple[str, int, Tuple[int, ..
         _kv_u32("tokenizer.ggml.eos_token_id", cfg.eos_id),
         _kv_u32("tokenizer.ggml.unknown_token_id", 0),
     ]
-    vocab = _vocab(cfg)
+    if cfg.tokenizer == "bpe":
+        vocab, scores, types = bpe_vocab(cfg.vocab_size, cfg.tokenizer_seed)
+    else:
+        vocab = _vocab(cfg)
+        scores = np.zeros(len(vocab), "<f4")
+        types = np.ones(len(vocab), "<i4")
+        types[:3] = 3
+        types[3:259] = 6
     k = b"tokenizer.ggml.tokens"
     arr = struct.pack("<Q", len(k)) + k + struct.pack("<IIQ", _ARR, _STR, len(vocab))
     arr += b"".join(struct.pack("<Q", len(t)) + t for t in vocab)
     kvs.append(arr)
     k = b"tokenizer.ggml.scores"
-    kvs.append(struct.pack("<Q", len(k)) + k + struct.pack("<IIQ", _ARR, _F32, len(vocab))
-               + np.zeros(len(vocab), "<f4").tobytes())
+    kvs.append(struct.pack("<Q", len(k)) + k + struct.pack("<IIQ", _ARR, _F32, len(vocab)) + scores.tobytes())
     k = b"tokenizer.ggml.token_type"
-    types = np.ones(len(vocab), "<i4")
-    types[:3] = 3
-    types[3:259] = 6
     kvs.append(struct.pack("<Q", len(k)) + k + struct.pack("<IIQ", _ARR, _I32, len(vocab)) + types.tobytes())
 
     table = []

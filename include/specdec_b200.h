@@ -297,6 +297,35 @@ SD_API int sd_decode(sd_ctx *ctx, const sd_gen_params *p, const int32_t *history
               int32_t *out_tokens, int out_cap, sd_gen_stats *stats);
 
 /* ======================================================================================
+ * Tokenizer (host code): the SentencePiece-style BPE of the GGUF vocabulary, token for token the reference's
+ * (mistral/tokenizer.h), including its merge order among equal scores.
+ * ====================================================================================== */
+typedef struct sd_tokenizer sd_tokenizer;
+
+/* Replaces tokenizer_init (mistral/tokenizer.h:121-153): tokenizer.ggml.tokens / scores / token_type and the
+ * BOS / EOS ids of the GGUF image (absent scores read as 0, absent types as NORMAL). */
+SD_API int sd_tokenizer_create(const void *gguf_base, size_t gguf_len, sd_tokenizer **out);
+/* Replaces tokenizer_free (mistral/tokenizer.h:431-442). */
+SD_API void sd_tokenizer_free(sd_tokenizer *t);
+SD_API int sd_tokenizer_info(const sd_tokenizer *t, int *vocab_size, int *bos_id, int *eos_id);
+/* Raw vocabulary entry `id`: its piece (valid while t lives), score and SentencePiece type (1 normal,
+ * 2 unknown, 3 control, 4 unused, 6 byte). */
+SD_API int sd_tokenizer_entry(const sd_tokenizer *t, int id, const char **piece, float *score, int *type);
+/* Replaces tokenizer_encode (mistral/tokenizer.h:200-346): ids of text into out (at most max_tokens, BOS first
+ * when add_bos); returns the count or < 0. */
+SD_API int sd_tokenizer_encode(const sd_tokenizer *t, const char *text, int32_t *out, int max_tokens, int add_bos);
+/* Replaces tokenizer_decode_token (mistral/tokenizer.h:348-373): the text of one token ("" for BOS, EOS and ids
+ * out of range; a byte token <0xNN> gives that byte, in a per-thread buffer overwritten by the next call). */
+SD_API const char *sd_tokenizer_piece(const sd_tokenizer *t, int token);
+/* Replaces tokenizer_decode (mistral/tokenizer.h:375-412): U+2581 becomes a space and one leading space is
+ * dropped.  Returns a malloc'd string (release with sd_free) or NULL. */
+SD_API char *sd_tokenizer_decode(const sd_tokenizer *t, const int32_t *tokens, int n);
+/* Replaces tokenizer_apply_chat (mistral/tokenizer.h:416-429): "[INST] " + msg + " [/INST]", malloc'd. */
+SD_API char *sd_tokenizer_apply_chat(const char *user_msg);
+/* Release a string returned by this library. */
+SD_API void sd_free(void *p);
+
+/* ======================================================================================
  * Batched serving: many independent streams on one GPU sharing a context's weights.  Every stream
  * has its own KV ring and generation state; one forward processes T tokens of every stream with the
  * wide-token W4A8 GEMM (M = n_streams * T rows of int8 MMA work per weight tile read).  Per stream

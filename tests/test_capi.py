@@ -70,4 +70,6 @@ def test_cli_usage_and_errors():
     out = subprocess.run([cli], capture_output=True, text=True)
     assert out.returncode == 1 and "--prompt-ids" in out.stderr
     out = subprocess.run([cli, "--model", "/nonexistent", "--prompt", "hi"], capture_output=True, text=True)
-    assert out.returncode == 1 and "tokenizer" in out.stderr
+    assert out.returncode == 1 and "No such file" in out.stderr
+    out = subprocess.run([cli, "--model", "/nonexistent"], capture_output=True, text=True)
+    assert out.returncode == 1 and "--prompt" in out.stderr   # no prompt: usage

@@ -101,3 +101,16 @@ def test_single_op_model_layer_matches_oracle(mini_path, oracle):
         om.close()
         ctx.close()
         ref_ctx.close()
+
+
+def test_cli_text_prompt_with_chat_template(mini_path):
+    """--prompt TEXT --chat: the prompt is "[INST] TEXT [/INST]" tokenized with the model's vocabulary, BOS first
+    (mistral_infer.m:538-550); generation runs and prints decoded pieces."""
+    from anetransformers_b200.tokenizer import Tokenizer, apply_chat
+    cli = os.path.join(ROOT_LIB, "mistral")
+    n_expect = len(Tokenizer(mini_path).encode(apply_chat("hello world")))
+    out = subprocess.run([cli, "--model", mini_path, "--prompt", "hello world", "--chat", "--tokens", "6", "--temp", "0",
+                          "--ignore-eos", "--context", "512"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert f"Prompt: {n_expect} tokens" in out.stderr
+    assert "Generated tokens: 6" in out.stderr
