@@ -86,6 +86,7 @@ _SIGS = {
     "sd_nccl_comm_destroy": (None, [vp]),
     "sd_ctx_tp_handle": (i32, [vp, vp]),
     "sd_ctx_tp_connect": (i32, [vp, vp, i32]),
+    "sd_gguf_describe": (i32, [vp, sz, vp]),
     "sd_ctx_create": (i32, [vp, sz, vp, vp]),
     "sd_ctx_create_file": (i32, [C.c_char_p, vp, vp]),
     "sd_ctx_free": (None, [vp]),

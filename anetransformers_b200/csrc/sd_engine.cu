@@ -61,6 +61,8 @@ struct GGUF {
     int dim = 0, hidden = 0, n_layers = 0, n_heads = 0, n_kv = 0, vocab = 0, ctx_len = 0;
     float theta = 10000.f, eps = 1e-5f;
     int bos = 1, eos = 2;
+    uint32_t version = 0;
+    size_t data_start = 0;
     std::vector<GTensor> t;
     const GTensor* find(const std::string& n) const {
         for (auto& x : t)
@@ -164,6 +166,7 @@ int gguf_parse(const void* base, size_t len, GGUF& g) {
     if (r.u(4) != 0x46554747u) return fail(SD_ERR_FORMAT, "not a GGUF file");
     uint32_t ver = (uint32_t)r.u(4);
     if (ver < 2) return fail(SD_ERR_FORMAT, "GGUF version %u unsupported", ver);
+    g.version = ver;
     uint64_t n_t = r.u(8), n_kv = r.u(8);
     if (!r.ok || n_t > 100000 || n_kv > 100000) return fail(SD_ERR_FORMAT, "GGUF header truncated");
     for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
@@ -202,6 +205,7 @@ int gguf_parse(const void* base, size_t len, GGUF& g) {
     }
     if (!r.ok) return fail(SD_ERR_FORMAT, "GGUF metadata truncated");
     const size_t data_start = (r.pos + 31) / 32 * 32;   // gguf_loader.h:280-281
+    g.data_start = data_start;
     for (auto& t : g.t) {
         t.off += data_start;
         uint64_t nel = t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3];
@@ -923,6 +927,31 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
     if (o.forward_kernel && (rc = setup_fused(c))) return bail(rc);
     if ((rc = ck(cudaDeviceSynchronize(), "context build"))) return bail(rc);
     *out = c;
+    return SD_OK;
+}
+
+int sd_gguf_describe(const void* gguf_base, size_t gguf_len, sd_gguf_desc* out) {
+    clear_error();
+    if (!gguf_base || !out) return fail(SD_ERR_INVALID, "sd_gguf_describe: null argument");
+    GGUF g;
+    int rc = gguf_parse(gguf_base, gguf_len, g);
+    if (rc) return rc;
+    memset(out, 0, sizeof(*out));
+    out->version = g.version;
+    out->n_tensors = (uint32_t)g.t.size();
+    out->dim = g.dim;
+    out->hidden_dim = g.hidden;
+    out->n_layers = g.n_layers;
+    out->n_heads = g.n_heads;
+    out->n_kv_heads = g.n_kv;
+    out->head_dim = g.dim / g.n_heads;
+    out->vocab_size = g.vocab;
+    out->context_length = g.ctx_len;
+    out->rope_theta = g.theta;
+    out->rms_eps = g.eps;
+    out->bos_id = g.bos;
+    out->eos_id = g.eos;
+    out->data_offset = g.data_start;
     return SD_OK;
 }
 

@@ -20,22 +20,36 @@
 
 typedef sd_ctx MetalContext;
 
+/* A model loaded through compat/mistral_model.h from the same mmap'd image already holds the weights and the
+ * KV ring in HBM: metal_context_init then returns that context (shared, not freed by metal_context_free). */
+#ifdef SPECDEC_COMPAT_MISTRAL_MODEL_H
+#define SPECDEC_COMPAT_SHARED_CTX_ (spec_bound_model_ ? spec_bound_model_->ctx : NULL)
+#define SPECDEC_COMPAT_SHARED_BASE_ (spec_bound_model_ ? spec_bound_model_->gguf->mmap_base : NULL)
+#else
+#define SPECDEC_COMPAT_SHARED_CTX_ NULL
+#define SPECDEC_COMPAT_SHARED_BASE_ NULL
+#endif
+
 static inline MetalContext *metal_context_init(void *mmap_base, size_t mmap_len, int dim, int kv_dim, int hidden,
                                                int vocab, int n_heads, int n_layers, int max_seq) {
-    sd_ctx_opts o;
-    sd_ctx_opts_default(&o);
-    o.max_seq = max_seq;
     sd_ctx *c = NULL;
-    if (sd_ctx_create(mmap_base, mmap_len, &o, &c) != SD_OK) {
-        fprintf(stderr, "specdec_b200: context init failed: %s\n", sd_last_error());
-        return NULL;
+    if (SPECDEC_COMPAT_SHARED_CTX_ && SPECDEC_COMPAT_SHARED_BASE_ == mmap_base) {
+        c = SPECDEC_COMPAT_SHARED_CTX_;
+    } else {
+        sd_ctx_opts o;
+        sd_ctx_opts_default(&o);
+        o.max_seq = max_seq;
+        if (sd_ctx_create(mmap_base, mmap_len, &o, &c) != SD_OK) {
+            fprintf(stderr, "specdec_b200: context init failed: %s\n", sd_last_error());
+            return NULL;
+        }
     }
     sd_model_info in;
     sd_ctx_info(c, &in);
     if (in.dim != dim || in.n_kv_heads * in.head_dim != kv_dim || in.hidden_dim != hidden || in.vocab_size != vocab ||
         in.n_heads != n_heads || in.n_layers != n_layers) {
         fprintf(stderr, "specdec_b200: GGUF shape differs from the caller's arguments\n");
-        sd_ctx_free(c);
+        if (c != SPECDEC_COMPAT_SHARED_CTX_) sd_ctx_free(c);
         return NULL;
     }
     return c;
@@ -72,6 +86,8 @@ static inline void metal_wire_kv_cache(MetalContext *ctx, void *kv_ptr) {
     kv->v = NULL;
 }
 
-static inline void metal_context_free(MetalContext *ctx) { sd_ctx_free(ctx); }
+static inline void metal_context_free(MetalContext *ctx) {
+    if (ctx != SPECDEC_COMPAT_SHARED_CTX_) sd_ctx_free(ctx);
+}
 
 #endif

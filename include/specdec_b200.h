@@ -172,6 +172,18 @@ SD_API void sd_nccl_comm_destroy(void *comm);
 SD_API int sd_ctx_tp_handle(sd_ctx *ctx, void *handle_out);
 SD_API int sd_ctx_tp_connect(sd_ctx *ctx, const void *handles, int n_ranks);
 
+/* What mistral/gguf_loader.h's gguf_open (:151-313) extracts from a GGUF v3 image: version, tensor count, the
+ * model configuration (MistralConfig, :51-63, read at :195-259), BOS / EOS ids and the offset of the 32-byte
+ * aligned tensor data section (:280-281). */
+typedef struct {
+    uint32_t version, n_tensors;
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, head_dim, vocab_size, context_length;
+    float rope_theta, rms_eps;
+    int bos_id, eos_id;
+    size_t data_offset;
+} sd_gguf_desc;
+SD_API int sd_gguf_describe(const void *gguf_base, size_t gguf_len, sd_gguf_desc *out);
+
 /* Replaces metal_context_init (mistral/metal_matvec.h:134-225) + mistral_load
  * (mistral/mistral_model.h:262-357): parses the GGUF v3 image at gguf_base (the mmap'd file, as
  * metal_context_init receives it), uploads every tensor and repacks the Q4_0 matrices in HBM,

@@ -19,14 +19,44 @@ def mini_path(tmp_path_factory):
     return p
 
 
+def _between(text, a, b):
+    i = text.index(a) + len(a)
+    return text[i:text.index(b, i)]
+
+
 def test_compat_headers_run(tmp_path, mini_path):
+    """The reference-signature headers (gguf_loader.h, tokenizer.h, mistral_model.h, kv_cache.h, metal_matvec.h,
+    speculative.h, dequant.h) driven by a C program with the reference's argument lists."""
+    from anetransformers_b200.tokenizer import Tokenizer, apply_chat
     exe = build_compat_check(tmp_path)
-    out = subprocess.run([exe, mini_path], capture_output=True, text=True, timeout=300)
-    assert out.returncode == 0, out.stdout + out.stderr
-    lines = out.stdout.splitlines()
-    assert any(l.startswith("ngram n=1 first=4") or l.startswith("ngram n=") for l in lines)
-    assert "batch5=0 batch9=0 batch17=-1" in out.stdout   # verify batches up to SD_MAX_VERIFY = 16
-    assert "verify rc=0 accepted=5" in out.stdout      # drafts = argmax of each row -> all accepted + bonus
+    out = subprocess.run([exe, mini_path], capture_output=True, timeout=600)
+    stdout = out.stdout.decode("utf-8", errors="surrogateescape")
+    assert out.returncode == 0, stdout + out.stderr.decode(errors="replace")
+    lines = stdout.splitlines()
+    assert any(l.startswith("ngram n=") for l in lines)
+    n_tok = len(Tokenizer(mini_path).encode(apply_chat("hello world")))
+    assert f"tokenizer vocab=2048 bos=1 eos=2 n={n_tok} chat=[[INST] hello world [/INST]]" in stdout
+    # metal_context_init shares the loaded model's context; verify batches up to SD_MAX_VERIFY = 16
+    assert "metal shared=1 batch5=0 batch9=0 batch17=-1" in stdout
+    assert "prefill rc=0 kvlen=24" in stdout
+    # embed_token + mistral_layer_decode_parallel + mistral_logits == the batched forward of the same token
+    lp = next(l for l in lines if l.startswith("layer_path"))
+    rel = float(lp.split()[1].split("=")[1])
+    a, b = lp.split("argmax=")[1].split("/")
+    assert rel <= 1e-5 and a == b, lp
+    sl = next(l for l in lines if l.startswith("sample "))
+    assert "in_range=1" in sl and abs(float(sl.split("softmax_sum=")[1].split()[0]) - 1.0) < 1e-4, sl
+    assert "verify rc=0 accepted=5 bonus_ok=1" in stdout
+    # temp-0 speculative output is greedy output, whichever drafter and loop runs it
+    greedy = _between(stdout, "greedy=[", "]\nngram_device=[")
+    dev = _between(stdout, "ngram_device=[", "] iters=")
+    host = _between(stdout, "ngram_host=[", "] iters=")
+    selfs = _between(stdout, "self_host=[", "] iters=")
+    assert len(greedy) > 0
+    for other in (dev, host, selfs):
+        k = min(len(greedy), len(other))
+        assert k > 0 and other[:k] == greedy[:k], (greedy, other)
+    assert "Speculative Decoding Stats" in out.stderr.decode(errors="replace")
 
 
 def test_compat_quantize_matches_oracle(tmp_path, oracle):
