@@ -79,6 +79,7 @@ _SIGS = {
     "sd_device_error": (i32, [i32]),
     "sd_host_quantize_f32_to_q8_0": (None, [vp, vp, i32]),
     "sd_host_q4_0_q8_0_matvec": (None, [vp, vp, vp, i32, i32]),
+    "sd_host_kq_matvec": (None, [i32, vp, vp, vp, i32, i32]),
     "sd_host_cache_clear": (None, []),
     "sd_ctx_opts_default": (None, [vp]),
     "sd_nccl_unique_id": (i32, [vp]),

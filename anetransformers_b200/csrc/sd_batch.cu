@@ -937,6 +937,9 @@ int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_b
     if (rc) return bail(rc);
     const ModelView& m = b->m;
     if (m.tp_size != 1) return bail(fail(SD_ERR_UNSUPPORTED, "batched streams run on single-GPU contexts"));
+    if (m.lm_type != 2 || m.embd_type != 2)
+        return bail(fail(SD_ERR_UNSUPPORTED, "batched streams need a Q4_0 embedding and LM head (this model has "
+                                             "K-quant ones; sd_forward / sd_generate serve it)"));
     if (m.dim > 4096 || m.dim % 1024) return bail(fail(SD_ERR_UNSUPPORTED, "dim %d", m.dim));
     b->ctx = ctx;
     b->dev = m.dev;

@@ -399,6 +399,43 @@ __device__ __forceinline__ float q4_0_value(const uint8_t* blk, int e) {
     return dd * ((float)q - 8.0f);
 }
 
+// Q4_K sub-block scale / min of index j (0..7) from the 12 packed bytes (mistral/dequant.h:47-55).
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* q, int& d, int& m) {
+    if (j < 4) {
+        d = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// Q4_K weight fp16(fp16(q * dsc) - dm) of the reference's fp16 dequant (mistral/dequant.h:63-113): products and
+// differences of fp16 values rounded once to fp16 (evaluated in fp32, which holds the exact product of a 4-bit q
+// and an fp16, and whose rounding before the fp16 one is harmless for a difference of two fp16 values).
+__device__ __forceinline__ float q4k_weight(uint32_t q, float dsc, float dm) {
+    const float p = __half2float(__float2half_rn((float)q * dsc));
+    return __half2float(__float2half_rn(p - dm));
+}
+
+// Value `lane` of 32-value block blk of token `token`'s embedding row: Q4_0 (type 2) or Q4_K (type 12, the
+// reference's fp16 dequant, mistral/mistral_model.h:146-156).
+__device__ __forceinline__ float embed_value(const uint8_t* embd, int type, int token, int dim, int blk, int lane) {
+    if (type == 12) {
+        const uint8_t* b = embd + ((size_t)token * (dim >> 8) + (blk >> 3)) * 144;
+        const int sb = blk & 7;
+        int sc, m;
+        q4k_scale_min(sb, b + 4, sc, m);
+        const float d = __half2float(__ushort_as_half((unsigned short)(b[0] | (b[1] << 8))));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(b[2] | (b[3] << 8))));
+        const float vd = __half2float(__float2half_rn(d * (float)sc));
+        const float vm = __half2float(__float2half_rn(dmin * (float)m));
+        const uint8_t byte = b[16 + 32 * (sb >> 1) + lane];
+        return q4k_weight((sb & 1) ? (byte >> 4) : (byte & 0xF), vd, vm);
+    }
+    return q4_0_value(embd + ((size_t)token * (dim >> 5) + blk) * 18, lane);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Attention work item (kv head, chunk) for a group of 8 warps (256 threads), on the tensor cores.
 //

@@ -32,6 +32,7 @@
 
 #include "sd_attn.h"
 #include "sd_fwd.h"
+#include "sd_kquant.h"
 #include "sd_dev.cuh"
 #include "sd_common.cuh"
 #include "sd_host.h"
@@ -209,7 +210,8 @@ int gguf_parse(const void* base, size_t len, GGUF& g) {
     for (auto& t : g.t) {
         t.off += data_start;
         uint64_t nel = t.ne[0] * t.ne[1] * t.ne[2] * t.ne[3];
-        uint64_t bytes = t.type == 2 ? nel / 32 * 18 : t.type == 0 ? nel * 4 : t.type == 1 ? nel * 2 : 0;
+        uint64_t bytes = t.type == 2 ? nel / 32 * 18 : t.type == 0 ? nel * 4 : t.type == 1 ? nel * 2
+                       : t.type == 12 ? nel / 256 * 144 : t.type == 14 ? nel / 256 * 210 : 0;
         if (bytes == 0 || t.off + bytes > len) return fail(SD_ERR_FORMAT, "tensor %s out of range", t.name.c_str());
     }
     if (g.dim <= 0 || g.n_layers <= 0 || g.n_heads <= 0 || g.n_kv <= 0 || g.hidden <= 0)
@@ -247,6 +249,9 @@ struct sd_ctx {
     std::vector<LayerW> L;
     uint8_t* embd = nullptr;
     uint8_t* lm = nullptr;
+    int embd_type = 2;         // token_embd.weight: Q4_0 (2) or Q4_K (12), rows as in the GGUF
+    int lm_type = 2;           // output.weight: Q4_0 (2, tile layout) or Q6_K (14) / Q4_K (12) (sd_kquant.h layout)
+    float* xn = nullptr;       // [MB][dim] final-norm output for a K-quant LM head
     float *rms_final = nullptr, *theta_inv = nullptr;
     __half *kc = nullptr, *vc = nullptr;      // [n_layers][max_seq][kv_rows]
     __half *dkc = nullptr, *dvc = nullptr;    // self-spec drafter KV [draft_layers][max_seq][kv_rows]
@@ -435,6 +440,17 @@ int setup_fused(sd_ctx* c) {
     return SD_OK;
 }
 
+// A K-quant LM head (Q6_K / Q4_K output.weight) on the final residual c->x: the final RMSNorm in fp32, the
+// fp32-activation K-quant matvec and the argmax (mistral/mistral_model.h:1110-1122 non-Q4_0 branch).  Both forward
+// paths end with the same x, so their logits agree bit for bit.
+int enqueue_kq_head(sd_ctx* c, int S, DevCtrl* ctrl, int row0) {
+    CK(launch_final_norm(c->x, c->rms_final, c->xn, c->dim, c->eps, S, ctrl, c->st), "final norm");
+    CK(launch_kq_matvec(c->lm_type, c->lm, c->vocab, c->dim, c->xn, c->logits + (size_t)row0 * c->vocab, c->vocab, S, ctrl,
+                        c->st), "K-quant LM head");
+    CK(launch_argmax(c->logits + (size_t)row0 * c->vocab, c->vocab, S, c->argmax + row0, ctrl, c->st, false), "argmax");
+    return SD_OK;
+}
+
 // One forward as a single persistent kernel (then the argmax kernel when logits are wanted).
 int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, DevCtrl* ctrl, bool logits_and_argmax,
                           int row0) {
@@ -442,8 +458,9 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     a.layers = c->d_layers;
     a.n_layers = n_layers;
     a.embd = c->embd;
+    a.embd_type = c->embd_type;
     a.rms_out = c->rms_final;
-    a.lm = logits_and_argmax ? c->lm : nullptr;
+    a.lm = logits_and_argmax && c->lm_type == 2 ? c->lm : nullptr;  // a K-quant head runs after the kernel
     a.dim = c->dim;
     a.hidden = c->hid_l;
     a.q_rows = c->q_rows;
@@ -489,10 +506,11 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     CK(cudaMemsetAsync(c->fsync, 0, fwd_sync_words(c->dim) * sizeof(unsigned), c->st), "memset");
     CK(launch_forward(a, c->fwd_grid, c->fwd_smem, c->st), "forward launch");
     if (c->tpx.n > 1) CK(launch_tp_advance(c->tp_base, 2 * n_layers, c->st), "tp advance");
+    if (!logits_and_argmax) return SD_OK;
+    if (c->lm_type != 2) return enqueue_kq_head(c, S, ctrl, row0);
     // the LM head phase reduced the argmax keys (first index on ties) into the sync words
-    if (logits_and_argmax)
-        CK(launch_argmax_keys(reinterpret_cast<const unsigned long long*>(c->fsync + 32), S, c->argmax + row0, ctrl, c->st),
-           "argmax");
+    CK(launch_argmax_keys(reinterpret_cast<const unsigned long long*>(c->fsync + 32), S, c->argmax + row0, ctrl, c->st),
+       "argmax");
     return SD_OK;
 }
 
@@ -606,6 +624,7 @@ int enqueue_layer_perop(sd_ctx* c, int l, int S, __half* k, __half* v, DevCtrl* 
 
 // LM head of the Q8_0 final-norm output in c->act -> logits rows row0.. (and their argmax).
 int enqueue_head_perop(sd_ctx* c, int S, DevCtrl* ctrl, int row0) {
+    if (c->lm_type != 2) return enqueue_kq_head(c, S, ctrl, row0);
     Plan pl;
     int rc = build_plan(c, pl, EPI_STORE, c->lm, c->vocab, c->dim, kRPW, S, 1);
     if (rc) return rc;
@@ -624,6 +643,7 @@ NormArgs norm_args(sd_ctx* c, int S, DevCtrl* ctrl) {
     na.x = c->x;
     na.y = c->y;
     na.embd = c->embd;
+    na.embd_type = c->embd_type;
     na.out = c->act;
     na.dim = c->dim;
     na.S = S;
@@ -762,7 +782,7 @@ void sd_ctx_free(sd_ctx* c) {
     for (auto& W : c->L) {
         cudaFree(W.qkv); cudaFree(W.wo); cudaFree(W.w13); cudaFree(W.w2); cudaFree(W.rms_att); cudaFree(W.rms_ffn);
     }
-    cudaFree(c->embd); cudaFree(c->lm); cudaFree(c->rms_final); cudaFree(c->theta_inv);
+    cudaFree(c->embd); cudaFree(c->lm); cudaFree(c->xn); cudaFree(c->rms_final); cudaFree(c->theta_inv);
     cudaFree(c->kc); cudaFree(c->vc); cudaFree(c->dkc); cudaFree(c->dvc);
     cudaFree(c->x); cudaFree(c->y); cudaFree(c->act.qs); cudaFree(c->act.d); cudaFree(c->act.sum);
     cudaFree(c->hact.qs); cudaFree(c->hact.d); cudaFree(c->hact.sum); cudaFree(c->q);
@@ -867,17 +887,41 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
     if (!rc) {
         const GTensor* te = g.find("token_embd.weight");
         const GTensor* tl = g.find("output.weight");
-        if (!te || te->type != 2 || !tl || tl->type != 2) rc = fail(SD_ERR_FORMAT, "token_embd / output must be Q4_0");
+        // the embedding may be Q4_0 or Q4_K, the LM head Q4_0, Q6_K (the real Mistral Q4_0 files) or Q4_K
+        // (mistral/mistral_model.h:125-157, :1110-1122); every layer matrix is Q4_0
+        if (!te || (te->type != 2 && te->type != 12) || !tl || (tl->type != 2 && tl->type != 12 && tl->type != 14))
+            rc = fail(SD_ERR_FORMAT, "token_embd must be Q4_0 or Q4_K and output Q4_0, Q4_K or Q6_K");
+        else if ((te->type == 12 || tl->type != 2) && c->dim % 256)
+            rc = fail(SD_ERR_FORMAT, "K-quant tensors need dim %% 256 == 0");
         if (!rc) {
-            size_t eb = (size_t)c->vocab * c->dim / 32 * 18;
+            c->embd_type = (int)te->type;
+            size_t eb = te->type == 2 ? (size_t)c->vocab * c->dim / 32 * 18 : (size_t)c->vocab * c->dim / 256 * 144;
             if (!(rc = dalloc(&c->embd, eb, &c->weight_bytes)))
                 rc = ck(cudaMemcpy(c->embd, g.base + te->off, eb, cudaMemcpyHostToDevice), "embedding upload");
         }
-        if (!rc) {
+        if (!rc && tl->type == 2) {
             size_t b = qmat_bytes(c->vocab, c->dim);
             if (!(rc = dalloc(&c->lm, b, &c->weight_bytes))) {
                 cudaMemset(c->lm, 0, b);
                 rc = upload_q4(c, g, tl, 0, c->vocab, 0, c->dim, RowMap{c->vocab, 0, 0}, c->lm, staging, stage_bytes);
+            }
+        } else if (!rc) {
+            c->lm_type = (int)tl->type;
+            const size_t n_blocks = (size_t)c->vocab * (c->dim / 256);
+            const size_t b = (size_t)c->vocab * kq_device_row_bytes(c->lm_type, c->dim);
+            if (!(rc = dalloc(&c->lm, b, &c->weight_bytes)) && !(rc = dalloc(&c->xn, (size_t)c->MB * c->dim))) {
+                if (c->lm_type == 12) {
+                    rc = ck(cudaMemcpy(c->lm, g.base + tl->off, b, cudaMemcpyHostToDevice), "LM head upload");
+                } else {
+                    uint8_t* raw = nullptr;
+                    if (!(rc = dalloc(&raw, n_blocks * kQ6KBytes))) {
+                        rc = ck(cudaMemcpy(raw, g.base + tl->off, n_blocks * kQ6KBytes, cudaMemcpyHostToDevice),
+                                "LM head upload");
+                        if (!rc) rc = ck(launch_repack_q6k(raw, c->lm, n_blocks, c->st), "Q6_K repack");
+                        if (!rc) rc = ck(cudaStreamSynchronize(c->st), "Q6_K repack");
+                        cudaFree(raw);
+                    }
+                }
             }
         }
         if (!rc) rc = upload_f32(c, g, "output_norm.weight", &c->rms_final, c->dim);
@@ -1625,7 +1669,9 @@ int sd_ctx_model_view(sd_ctx* c, ModelView* m) {
         m->rms_ffn[l] = c->L[l].rms_ffn;
     }
     m->embd = c->embd;
+    m->embd_type = c->embd_type;
     m->lm = c->lm;
+    m->lm_type = c->lm_type;
     m->rms_final = c->rms_final;
     m->theta_inv = c->theta_inv;
     m->err = c->err;

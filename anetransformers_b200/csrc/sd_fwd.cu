@@ -520,7 +520,7 @@ __device__ __forceinline__ void embed_phase(const FwdArgs& a, int nv, int tid) {
     for (int wt = blockIdx.x * kComputeWarps + warp; wt < nv * nbd; wt += gridDim.x * kComputeWarps) {
         const int s = wt / nbd, b = wt % nbd;
         const int token = a.tokens ? a.tokens[s] : a.ctrl->tokens[s];
-        const float v = q4_0_value(a.embd + ((size_t)token * nbd + b) * 18, lane);
+        const float v = embed_value(a.embd, a.embd_type, token, a.dim, b, lane);
         finish_block(a, s, b, v, w0[b * 32 + lane], lane);
     }
 }

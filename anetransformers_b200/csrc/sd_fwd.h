@@ -22,7 +22,8 @@ struct FwdLayer {
 struct FwdArgs {
     const FwdLayer* layers;  // device array [n_layers]
     int n_layers;
-    const uint8_t* embd;     // Q4_0 AoS [vocab][dim/32]
+    const uint8_t* embd;     // token embedding rows as in the GGUF: Q4_0 (embd_type 2) or Q4_K (12)
+    int embd_type;
     const float* rms_out;    // final norm weight
     const uint8_t* lm;       // output matrix; null = no LM head
     int dim, hidden, q_rows, kv_rows, vocab, head_dim, n_heads, n_kvh;

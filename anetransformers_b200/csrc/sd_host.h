@@ -31,8 +31,10 @@ struct ModelView {
     int q_rows, kv_rows, qkv_rows;
     const uint8_t *qkv[kMaxLayers], *wo[kMaxLayers], *w13[kMaxLayers], *w2[kMaxLayers];  // tile16x4
     const float *rms_att[kMaxLayers], *rms_ffn[kMaxLayers];
-    const uint8_t* embd;  // Q4_0 AoS [vocab][dim/32]
-    const uint8_t* lm;    // tile16x4 [vocab][dim]
+    const uint8_t* embd;  // Q4_0 AoS [vocab][dim/32] (embd_type 2) or Q4_K rows (12)
+    int embd_type;
+    const uint8_t* lm;    // tile16x4 [vocab][dim] (lm_type 2) or a K-quant layout (sd_kquant.h)
+    int lm_type;
     const float* rms_final;
     const float* theta_inv;
     int* err;             // the context's device error word

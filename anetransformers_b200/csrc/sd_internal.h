@@ -155,7 +155,8 @@ struct TpXchg {
 struct NormArgs {
     float* x;             // [S][dim] residual stream
     const float* y;       // [S][dim] to add (mode 1)
-    const uint8_t* embd;  // Q4_0 AoS [vocab][dim/32] (mode 0)
+    const uint8_t* embd;  // embedding rows as in the GGUF (mode 0): Q4_0 (embd_type 2) or Q4_K (12)
+    int embd_type;
     const float* w;       // [dim] RMSNorm weight
     Q8Planes out;
     int dim, S;

@@ -10,6 +10,7 @@
 
 #include "sd_common.cuh"
 #include "sd_host.h"
+#include "sd_kquant.h"
 #include "specdec_b200.h"
 
 using namespace sd;
@@ -456,6 +457,54 @@ int sd_device_error(int device) {
     if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
     if (h != 0 && (e = cudaMemset(w, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "clearing the device error word");
     return h;
+}
+
+void sd_host_kq_matvec(int type, const void* W, const float* x, float* y, int out_dim, int in_dim) {
+    std::lock_guard<std::mutex> lk(g_host_mu);
+    clear_error();
+    int rc = (W && x && y && out_dim > 0 && in_dim > 0 && in_dim % 256 == 0 && (type == kTypeQ6K || type == kTypeQ4K))
+                 ? host_prepare(in_dim, out_dim)
+                 : fail(SD_ERR_INVALID, "kq matvec: bad arguments (type 12 or 14, in_dim %% 256 == 0)");
+    HostScratch& h = g_hs;
+    uint8_t* wd = nullptr;
+    if (rc == SD_OK) {
+        // the device copy of W (the layout of sd_kquant.h), cached per (address, type, shape, device) like the Q4_0 one
+        static std::map<std::tuple<const void*, int, int, int, int>, uint8_t*> cache;
+        auto key = std::make_tuple(W, type, out_dim, in_dim, h.dev);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            wd = it->second;
+        } else {
+            const size_t n_blocks = (size_t)out_dim * (in_dim / 256);
+            const size_t raw = n_blocks * (type == kTypeQ6K ? kQ6KBytes : kQ4KBytes);
+            cudaError_t e = cudaMalloc(&wd, (size_t)out_dim * kq_device_row_bytes(type, in_dim));
+            if (e == cudaSuccess && type == kTypeQ4K) {
+                e = cudaMemcpy(wd, W, raw, cudaMemcpyHostToDevice);
+            } else if (e == cudaSuccess) {
+                uint8_t* tmp = nullptr;
+                e = cudaMalloc(&tmp, raw);
+                if (e == cudaSuccess) e = cudaMemcpy(tmp, W, raw, cudaMemcpyHostToDevice);
+                if (e == cudaSuccess) e = launch_repack_q6k(tmp, wd, n_blocks, h.st);
+                if (e == cudaSuccess) e = cudaStreamSynchronize(h.st);
+                cudaFree(tmp);
+            }
+            if (e != cudaSuccess) {
+                cudaFree(wd);
+                wd = nullptr;
+                rc = cuda_fail(e, "kq matvec upload");
+            } else {
+                cache[key] = wd;
+            }
+        }
+    }
+    if (rc == SD_OK) {
+        cudaError_t e = cudaMemcpyAsync(h.x, x, (size_t)in_dim * 4, cudaMemcpyHostToDevice, h.st);
+        if (e == cudaSuccess) e = launch_kq_matvec(type, wd, out_dim, in_dim, h.x, h.y, out_dim, 1, nullptr, h.st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(y, h.y, (size_t)out_dim * 4, cudaMemcpyDeviceToHost, h.st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(h.st);
+        if (e != cudaSuccess) rc = cuda_fail(e, "kq matvec");
+    }
+    if (rc != SD_OK) fprintf(stderr, "specdec_b200: %s\n", sd_last_error());
 }
 
 void sd_host_cache_clear(void) {

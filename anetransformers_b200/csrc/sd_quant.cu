@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(const NormArgs a) {
             wv[k] = a.w[e];
             if constexpr (MODE == 0) {
                 const int token = a.tokens ? a.tokens[tok] : a.ctrl->tokens[tok];
-                v[k] = q4_0_value(a.embd + ((size_t)token * nb + (warp + kNormWarps * k)) * 18, lane);
+                v[k] = embed_value(a.embd, a.embd_type, token, a.dim, warp + kNormWarps * k, lane);
             } else {
                 v[k] = x[e];
             }

@@ -125,3 +125,20 @@ def block_sums_dev(W: QMat, act: Q8Act):
     out = torch.zeros(W.rows, W.cols // QK, dtype=torch.int32, device=act.qs.device)
     _lib.check(_lib.lib().sd_block_sums_dev(W.h, act.ptrs(), out.data_ptr(), _stream()), "block_sums")
     return out
+
+
+def kq_matvec(W: np.ndarray, x: np.ndarray, ttype: int) -> np.ndarray:
+    """The reference's fp32 K-quant matvec (q4_matvec for Q6_K = 14 / Q4_K = 12, mistral/mistral_model.h:211-242):
+    y = W x for W [out_dim, in_dim/256] GGUF super-blocks and fp32 x."""
+    W = np.ascontiguousarray(W)
+    x = np.ascontiguousarray(x, np.float32)
+    out_dim, in_dim = W.shape[0], x.size
+    if W.shape[1] * 256 != in_dim:
+        raise ValueError("shape mismatch")
+    y = np.zeros(out_dim, dtype=np.float32)
+    L = _lib.lib()
+    L.sd_host_kq_matvec(ttype, W.ctypes.data, x.ctypes.data, y.ctypes.data, out_dim, in_dim)
+    err = _lib.last_error()
+    if err:
+        raise _lib.SpecDecError(-3, err)
+    return y

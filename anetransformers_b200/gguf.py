@@ -26,6 +26,13 @@ GGUF_MAGIC = 0x46554747
 GGML_TYPE_F32 = 0
 GGML_TYPE_F16 = 1
 GGML_TYPE_Q4_0 = 2
+GGML_TYPE_Q4_K = 12
+GGML_TYPE_Q6_K = 14
+# K-quant super-blocks of 256 values (mistral/dequant.h:23-30, :283-289)
+Q4_K_DTYPE = np.dtype([("d", "<f2"), ("dmin", "<f2"), ("scales", "u1", (12,)), ("qs", "u1", (128,))])
+Q6_K_DTYPE = np.dtype([("ql", "u1", (128,)), ("qh", "u1", (64,)), ("scales", "i1", (16,)), ("d", "<f2")])
+assert Q4_K_DTYPE.itemsize == 144 and Q6_K_DTYPE.itemsize == 210
+_TYPE_NAMES = {"q4_0": 2, "q4_k": 12, "q6_k": 14}
 ALIGN = 32
 
 # GGUF metadata value types (gguf_loader.h:20-28)
@@ -54,6 +61,10 @@ class ModelConfig:
     # 0) or "bpe" (a SentencePiece-style vocabulary with learned merges, for tokenizer tests; bpe_vocab)
     tokenizer: str = "plain"
     tokenizer_seed: int = 0
+    # types of output.weight ("q4_0", "q6_k" as in the real Mistral Q4_0 GGUFs, or "q4_k") and of
+    # token_embd.weight ("q4_0" or "q4_k"); every other 2-D tensor is Q4_0
+    lm_head_type: str = "q4_0"
+    embd_type: str = "q4_0"
 
     @property
     def head_dim(self) -> int:
@@ -76,7 +87,8 @@ SMALL = ModelConfig(dim=2048, hidden_dim=5120, n_layers=4, n_heads=16, n_kv_head
 def tensor_names(cfg: ModelConfig) -> List[Tuple[str, int, Tuple[int, ...]]]:
     """(name, ggml type, shape as (rows, cols) or (n,)) in file order, using the reference's names
     (mistral/mistral_model.h:290-318)."""
-    out: List[Tuple[str, int, Tuple[int, ...]]] = [("token_embd.weight", GGML_TYPE_Q4_0, (cfg.vocab_size, cfg.dim))]
+    out: List[Tuple[str, int, Tuple[int, ...]]] = [("token_embd.weight", _TYPE_NAMES[cfg.embd_type],
+                                                    (cfg.vocab_size, cfg.dim))]
     for l in range(cfg.n_layers):
         out += [
             (f"blk.{l}.attn_q.weight", GGML_TYPE_Q4_0, (cfg.dim, cfg.dim)),
@@ -90,7 +102,7 @@ def tensor_names(cfg: ModelConfig) -> List[Tuple[str, int, Tuple[int, ...]]]:
             (f"blk.{l}.ffn_norm.weight", GGML_TYPE_F32, (cfg.dim,)),
         ]
     out += [("output_norm.weight", GGML_TYPE_F32, (cfg.dim,)),
-            ("output.weight", GGML_TYPE_Q4_0, (cfg.vocab_size, cfg.dim))]
+            ("output.weight", _TYPE_NAMES[cfg.lm_head_type], (cfg.vocab_size, cfg.dim))]
     return out
 
 
@@ -102,6 +114,10 @@ def tensor_nbytes(ttype: int, shape: Tuple[int, ...]) -> int:
         return n * 4
     if ttype == GGML_TYPE_F16:
         return n * 2
+    if ttype == GGML_TYPE_Q4_K:
+        return n // 256 * 144
+    if ttype == GGML_TYPE_Q6_K:
+        return n // 256 * 210
     raise ValueError(f"unsupported ggml type {ttype}")
 
 
@@ -114,10 +130,38 @@ def random_q4_0(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
     return blk.reshape(rows, cols // 32)
 
 
+def random_q6_k(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    """[rows, cols/256] Q6_K super-blocks: ql / qh uniform bytes, sub-block scales int8 uniform on -32..31,
+    d = fp16(|N(0, 0.02)| / 128), so that weights are of the Q4_0 tensors' magnitude."""
+    nb = rows * (cols // 256)
+    blk = np.empty(nb, dtype=Q6_K_DTYPE)
+    blk["ql"] = rng.integers(0, 256, size=(nb, 128), dtype=np.uint8)
+    blk["qh"] = rng.integers(0, 256, size=(nb, 64), dtype=np.uint8)
+    blk["scales"] = rng.integers(-32, 32, size=(nb, 16), dtype=np.int8)
+    blk["d"] = (np.abs(rng.standard_normal(nb, dtype=np.float32) * np.float32(0.02)) / np.float32(128)).astype(np.float16)
+    return blk.reshape(rows, cols // 256)
+
+
+def random_q4_k(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    """[rows, cols/256] Q4_K super-blocks: d = fp16(|N(0, 0.02)| / 256), dmin = fp16(|N(0, 0.02)| / 256), packed
+    6-bit scales / mins and nibbles uniform bytes."""
+    nb = rows * (cols // 256)
+    blk = np.empty(nb, dtype=Q4_K_DTYPE)
+    blk["d"] = (np.abs(rng.standard_normal(nb, dtype=np.float32) * np.float32(0.02)) / np.float32(256)).astype(np.float16)
+    blk["dmin"] = (np.abs(rng.standard_normal(nb, dtype=np.float32) * np.float32(0.02)) / np.float32(256)).astype(np.float16)
+    blk["scales"] = rng.integers(0, 256, size=(nb, 12), dtype=np.uint8)
+    blk["qs"] = rng.integers(0, 256, size=(nb, 128), dtype=np.uint8)
+    return blk.reshape(rows, cols // 256)
+
+
 def _tensor_data(cfg: ModelConfig, seed: int, idx: int, name: str, ttype: int, shape) -> np.ndarray:
     if ttype == GGML_TYPE_F32:
         return np.ones(shape, dtype=np.float32)
     rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, idx])))
+    if ttype == GGML_TYPE_Q6_K:
+        return random_q6_k(rng, shape[0], shape[1])
+    if ttype == GGML_TYPE_Q4_K:
+        return random_q4_k(rng, shape[0], shape[1])
     return random_q4_0(rng, shape[0], shape[1])
 
 
@@ -448,6 +492,10 @@ class GGUFFile:
                                  offset=t.offset).reshape(rows, cols // 32)
         if t.ttype == GGML_TYPE_F32:
             return np.frombuffer(self.buf, dtype="<f4", count=int(np.prod(t.shape)), offset=t.offset)
+        if t.ttype in (GGML_TYPE_Q4_K, GGML_TYPE_Q6_K):
+            rows, cols = t.shape
+            dt = Q4_K_DTYPE if t.ttype == GGML_TYPE_Q4_K else Q6_K_DTYPE
+            return np.frombuffer(self.buf, dtype=dt, count=rows * cols // 256, offset=t.offset).reshape(rows, cols // 256)
         raise ValueError(f"unsupported type {t.ttype}")
 
     def close(self):

@@ -118,6 +118,12 @@ SD_API int sd_device_error(int device);
  * reported on stderr and through sd_last_error(); y is left unchanged on failure. */
 SD_API void sd_host_quantize_f32_to_q8_0(const float *x, sd_block_q8_0 *out, int n);
 SD_API void sd_host_q4_0_q8_0_matvec(const void *W, const sd_block_q8_0 *x, float *y, int out_dim, int in_dim);
+/* Replaces the reference's fp32 matvec of K-quant matrices (q4_matvec for Q6_K / Q4_K,
+ * mistral/mistral_model.h:211-242: q6_K_matvec_f32_neon, mistral/dequant.h:349-520; Q4_K: the fp16 dequant of
+ * dequant_q4_K_block_neon, :63-113, then an fp32 sgemv): y = W x for W [out_dim][in_dim/256] GGUF super-blocks
+ * of `type` (14 = Q6_K, 12 = Q4_K) and fp32 x, in_dim % 256 == 0.  Runs on the current device; W is uploaded
+ * once per (address, type, shape) and cached as above. */
+SD_API void sd_host_kq_matvec(int type, const void *W, const float *x, float *y, int out_dim, int in_dim);
 /* Drop the host-drop-in weight cache (frees its device copies). */
 SD_API void sd_host_cache_clear(void);
 

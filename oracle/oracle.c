@@ -414,9 +414,110 @@ int or_kv_alloc(or_kv *kv, int n_layers, int n_kv_heads, int head_dim, int max_s
 
 void or_kv_free(or_kv *kv) { free(kv->k); free(kv->v); kv->k = kv->v = NULL; }
 
-/* mistral/mistral_model.h:125-157 (Q4_0 branch). */
+/* ------------------------------------------------------------------------- */
+/* K-quants -- mistral/dequant.h                                               */
+/* ------------------------------------------------------------------------- */
+/* dequant.h:292-306: value n of a super-block: low 4 bits from ql[n % 128] (low nibble for n < 128, high
+ * nibble above), high 2 bits from qh[n % 64] at shift 2*(n / 128) + 4*((n % 128) >= 64); q = that - 32;
+ * w = d * sc[n / 16] * q, evaluated left to right in fp32. */
+static inline float q6k_value(const or_block_q6_K *b, int n) {
+    const float d = or_f16_to_f32(b->d);
+    const int il = n % 128, is = n / 16, ih = n / 128;
+    const uint8_t lo = (n < 128) ? (b->ql[il] & 0xF) : (b->ql[il] >> 4);
+    const uint8_t hi = (b->qh[il % 64] >> (2 * ih + (il >= 64 ? 4 : 0))) & 3;
+    const int8_t q = (int8_t)((lo | (hi << 4)) - 32);
+    return d * b->scales[is] * q;
+}
+
+void or_dequant_q6_K(const void *blocks, float *out, int n) {
+    const or_block_q6_K *b = (const or_block_q6_K *)blocks;
+    for (int i = 0; i < n; i++) out[i] = q6k_value(&b[i / 256], i % 256);
+}
+
+/* dequant.h:47-55 */
+static inline void q4k_scale_min(int j, const uint8_t *q, uint8_t *d, uint8_t *m) {
+    if (j < 4) {
+        *d = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+/* dequant.h:63-113: per 64-value group j, scale / min pairs (2j, 2j+1) as fp16 products d*sc and dmin*m
+ * (fp32 products rounded to fp16); value = fp16(fp16(q * dsc) - dm), q the low nibbles of 32 qs bytes for the
+ * first 32 values and their high nibbles for the next 32. */
+void or_dequant_q4_K_f16(const void *blocks, uint16_t *out, int n) {
+    const or_block_q4_K *bk = (const or_block_q4_K *)blocks;
+    for (int blk = 0; blk < n / 256; blk++) {
+        const or_block_q4_K *b = &bk[blk];
+        const float d = or_f16_to_f32(b->d), dmin = or_f16_to_f32(b->dmin);
+        for (int j = 0; j < 4; j++) {
+            uint8_t sc1, m1, sc2, m2;
+            q4k_scale_min(2 * j, b->scales, &sc1, &m1);
+            q4k_scale_min(2 * j + 1, b->scales, &sc2, &m2);
+            const float vd1 = or_f16_to_f32(or_f32_to_f16(d * sc1)), vm1 = or_f16_to_f32(or_f32_to_f16(dmin * m1));
+            const float vd2 = or_f16_to_f32(or_f32_to_f16(d * sc2)), vm2 = or_f16_to_f32(or_f32_to_f16(dmin * m2));
+            for (int i = 0; i < 32; i++) {
+                const uint8_t byte = b->qs[32 * j + i];
+                const float lo = or_f16_to_f32(or_f32_to_f16((float)(byte & 0xF) * vd1));
+                const float hi = or_f16_to_f32(or_f32_to_f16((float)(byte >> 4) * vd2));
+                out[blk * 256 + 64 * j + i] = or_f32_to_f16(lo - vm1);
+                out[blk * 256 + 64 * j + 32 + i] = or_f32_to_f16(hi - vm2);
+            }
+        }
+    }
+}
+
+typedef struct {
+    int type;
+    const uint8_t *W;
+    const float *x;
+    float *y;
+    int in_dim;
+    size_t row_bytes;
+} kq_job;
+
+static void kq_rows(void *ctx, int r) {
+    const kq_job *j = (const kq_job *)ctx;
+    const uint8_t *row = j->W + (size_t)r * j->row_bytes;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = 0; b < j->in_dim / 256; b++) {
+        float w[256];
+        if (j->type == OR_TYPE_Q6_K) {
+            const or_block_q6_K *blk = (const or_block_q6_K *)row + b;
+            /* dequant.h:337-352: w = (float)q * (d * sc), exact in fp32 (q 6 bits, d * sc at most 18) */
+            for (int n = 0; n < 256; n++) w[n] = q6k_value(blk, n);
+        } else {
+            uint16_t h[256];
+            or_dequant_q4_K_f16((const or_block_q4_K *)row + b, h, 256);
+            for (int n = 0; n < 256; n++) w[n] = or_f16_to_f32(h[n]);
+        }
+        const float *xb = j->x + (size_t)b * 256;
+        for (int n = 0; n < 256; n++) acc[n & 3] = fmaf(w[n], xb[n], acc[n & 3]);
+    }
+    j->y[r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+void or_matvec_kq_f32(int type, const void *W, const float *x, float *y, int rows, int in_dim) {
+    kq_job j = {type, (const uint8_t *)W, x, y, in_dim,
+                (size_t)(in_dim / 256) * (type == OR_TYPE_Q6_K ? sizeof(or_block_q6_K) : sizeof(or_block_q4_K))};
+    parallel_chunks(rows, kq_rows, &j);
+}
+
+/* mistral/mistral_model.h:125-157 (Q4_0 and Q4_K branches). */
 void or_embed_token(const or_model *m, int token, float *out) {
     int dim = m->cfg.dim;
+    if (m->tok_embd_type == OR_TYPE_Q4_K) {
+        uint16_t h[256];
+        const or_block_q4_K *row = (const or_block_q4_K *)m->tok_embd + (size_t)token * (dim / 256);
+        for (int b = 0; b < dim / 256; b++) {
+            or_dequant_q4_K_f16(row + b, h, 256);
+            for (int i = 0; i < 256; i++) out[b * 256 + i] = or_f16_to_f32(h[i]);
+        }
+        return;
+    }
     const or_block_q4_0 *row = (const or_block_q4_0 *)m->tok_embd + (size_t)token * (dim / 32);
     or_dequant_q4_0(row, out, dim);
 }
@@ -459,6 +560,11 @@ void or_layer_decode(or_model *m, or_kv *kv, float *x, int layer, int pos) {
 /* mistral/mistral_model.h:1110-1122 */
 void or_logits(or_model *m, const float *x) {
     or_rmsnorm(m->xb, x, m->rms_final, m->cfg.dim, m->cfg.rms_eps);
+    if (m->lm_head_type == OR_TYPE_Q6_K || m->lm_head_type == OR_TYPE_Q4_K) {
+        /* non-Q4_0 LM head: the fp32 path on the normalised state (mistral_model.h:1118-1121) */
+        or_matvec_kq_f32(m->lm_head_type, m->lm_head, m->xb, m->logits, m->cfg.vocab_size, m->cfg.dim);
+        return;
+    }
     or_quantize_q8_0(m->xb, m->xb_q8, m->cfg.dim, OR_QUANT_IEEE);
     or_matvec_q4_0_q8_0(m->lm_head, m->xb_q8, m->logits, m->cfg.vocab_size, m->cfg.dim);
 }

@@ -65,7 +65,9 @@ typedef struct {
     or_layer layers[OR_MAX_LAYERS];
     const void *tok_embd;    /* Q4_0 [vocab][dim] */
     const float *rms_final;  /* [dim] */
-    const void *lm_head;     /* Q4_0 [vocab][dim] */
+    const void *lm_head;     /* [vocab][dim] of type lm_head_type */
+    int tok_embd_type;       /* OR_TYPE_Q4_0 (default 0 is read as Q4_0) or OR_TYPE_Q4_K */
+    int lm_head_type;        /* OR_TYPE_Q4_0 (default), OR_TYPE_Q4_K or OR_TYPE_Q6_K */
     float *theta_inv;        /* [head_dim/2] */
     /* scratch (mistral/mistral_model.h:339-350) */
     float *xb, *xb2, *q, *k, *v, *att, *hb, *hb2, *logits;
@@ -96,6 +98,19 @@ void or_matvec_q4_0_q8_0(const void *W, const or_block_q8_0 *x, float *y,
                          int out_dim, int in_dim);
 void or_set_acc_mode(int mode);
 void or_dequant_q4_0(const void *blocks, float *out, int n);
+
+/* K-quant super-blocks of 256 values (GGML type ids) -- mistral/dequant.h:15-30, :280-290. */
+enum { OR_TYPE_Q4_0 = 2, OR_TYPE_Q4_K = 12, OR_TYPE_Q6_K = 14 };
+typedef struct { uint16_t d, dmin; uint8_t scales[12]; uint8_t qs[128]; } or_block_q4_K;            /* 144 B */
+typedef struct { uint8_t ql[128]; uint8_t qh[64]; int8_t scales[16]; uint16_t d; } or_block_q6_K; /* 210 B */
+/* Q6_K -> fp32 (dequant_q6_K_block, mistral/dequant.h:292-306); n a multiple of 256. */
+void or_dequant_q6_K(const void *blocks, float *out, int n);
+/* Q4_K -> fp16 values (bits) in the reference's fp16 arithmetic (dequant_q4_K_block_neon, :63-113). */
+void or_dequant_q4_K_f16(const void *blocks, uint16_t *out, int n);
+/* y[r] = W[r] . x with fp32 activations, the reference's fp32 path for K-quant matrices (q4_matvec,
+ * mistral/mistral_model.h:211-242 -> q6_K_matvec_f32_neon, dequant.h:349-520; Q4_K: fp16 dequant then sgemv).
+ * Accumulation: value i goes into lane i % 4 by fused multiply-add, the four lanes are added pairwise. */
+void or_matvec_kq_f32(int type, const void *W, const float *x, float *y, int rows, int in_dim);
 void or_rmsnorm(float *out, const float *x, const float *w, int dim, float eps);
 void or_rope_theta(float *theta_inv, int head_dim, float theta);
 void or_apply_rope(float *q, float *k, int pos, const float *theta_inv,

@@ -43,7 +43,8 @@ class Layer(C.Structure):
 
 class Model(C.Structure):
     _fields_ = [("cfg", Config), ("layers", Layer * 64), ("tok_embd", C.c_void_p), ("rms_final", C.c_void_p),
-                ("lm_head", C.c_void_p), ("theta_inv", C.c_void_p)] + \
+                ("lm_head", C.c_void_p), ("tok_embd_type", C.c_int), ("lm_head_type", C.c_int),
+                ("theta_inv", C.c_void_p)] + \
                [(n, C.c_void_p) for n in ("xb", "xb2", "q", "k", "v", "att", "hb", "hb2", "logits",
                                          "xb_q8", "hb_q8")] + [("att_cap", C.c_int)]
 
@@ -115,6 +116,8 @@ def lib() -> C.CDLL:
             "or_generate_ngram": (i32, [vp, vp, i32, vp, vp, vp]),
             "or_generate_self_spec": (i32, [vp, vp, i32, vp, vp, vp]),
             "or_f16_to_f32": (f32, [C.c_uint16]), "or_f32_to_f16": (C.c_uint16, [f32]),
+            "or_dequant_q6_K": (None, [vp, vp, i32]), "or_dequant_q4_K_f16": (None, [vp, vp, i32]),
+            "or_matvec_kq_f32": (None, [i32, vp, vp, vp, i32, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -255,6 +258,34 @@ def uniform(seed: int, counter: int) -> float:
     return float(np.float32(philox(seed, counter)) / np.float32(4294967295.0))
 
 
+TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K = 2, 12, 14
+
+
+def dequant_q6_k(W: np.ndarray) -> np.ndarray:
+    """dequant_q6_K_block (mistral/dequant.h:292-306) of [rows, cols/256] Q6_K blocks -> [rows, cols] fp32."""
+    W = np.ascontiguousarray(W)
+    out = np.empty(W.size * 256, np.float32)
+    lib().or_dequant_q6_K(_p(W), _p(out), out.size)
+    return out.reshape(W.shape[0], -1)
+
+
+def dequant_q4_k(W: np.ndarray) -> np.ndarray:
+    """dequant_q4_K_block_neon (mistral/dequant.h:63-113) -> fp16 values (as float16), [rows, cols]."""
+    W = np.ascontiguousarray(W)
+    out = np.empty(W.size * 256, np.uint16)
+    lib().or_dequant_q4_K_f16(_p(W), _p(out), out.size)
+    return out.view(np.float16).reshape(W.shape[0], -1)
+
+
+def matvec_kq(W: np.ndarray, x: np.ndarray, ttype: int) -> np.ndarray:
+    """The reference's fp32 K-quant matvec (q4_matvec -> q6_K_matvec_f32_neon / Q4_K dequant + sgemv)."""
+    W = np.ascontiguousarray(W)
+    xs = np.ascontiguousarray(x, np.float32)
+    y = np.empty(W.shape[0], np.float32)
+    lib().or_matvec_kq_f32(ttype, _p(W), _p(xs), _p(y), W.shape[0], xs.size)
+    return y
+
+
 def spec_accept(draft_probs, logits, draft_tokens, temp: float, seed: int = 0, counter: int = 0):
     logits = np.ascontiguousarray(logits, np.float32)
     n_draft = len(draft_tokens)
@@ -302,6 +333,8 @@ class OracleModel:
         self.m.tok_embd = ptr("token_embd.weight")
         self.m.rms_final = ptr("output_norm.weight")
         self.m.lm_head = ptr("output.weight")
+        self.m.tok_embd_type = gguf.tensors["token_embd.weight"].ttype
+        self.m.lm_head_type = gguf.tensors["output.weight"].ttype
         self.max_seq = max_seq
         if lib().or_model_init(C.addressof(self.m), max_seq) != 0:
             raise MemoryError("oracle model init failed")

@@ -72,3 +72,47 @@ def test_reference_parser_reads_synthetic_model(mini_path):
         assert t["bytes"] == G.tensor_nbytes(mine.ttype, mine.shape)
     assert out["token0"] == "<unk>"
     g.close()
+
+
+def test_reference_parser_reads_kquant_model(tmp_path):
+    """A model with a Q4_K embedding and a Q6_K LM head (the real Mistral Q4_0 files ship a Q6_K head): the
+    reference's parser finds every tensor at the writer's offsets with the writer's types; its own size table
+    (gguf_loader.h:335-344) knows Q4_K (144 bytes per 256 values) but not Q6_K, whose 210-byte block is
+    block_q6_K of mistral/dequant.h:283-289 (checked here through the offsets of the tensors that follow)."""
+    cfg = dataclasses.replace(G.MINI, lm_head_type="q6_k", embd_type="q4_k")
+    path = str(tmp_path / "kq.gguf")
+    G.write_synthetic_gguf(path, cfg, seed=12)
+    out = json.loads(subprocess.check_output([_ref_dump(), path]))
+    g = G.GGUFFile(path)
+    types = {t["name"]: t["type"] for t in out["tensors"]}
+    assert types["token_embd.weight"] == 12 and types["output.weight"] == 14
+    for t in out["tensors"]:
+        mine = g.tensors[t["name"]]
+        assert t["type"] == mine.ttype and g.data_start + t["offset"] == mine.offset
+        if mine.ttype != 14:
+            assert t["bytes"] == G.tensor_nbytes(mine.ttype, mine.shape)
+    assert G.tensor_nbytes(14, (2048, 1024)) == 2048 * 4 * 210
+    assert g.array("output.weight").dtype.itemsize == 210 and g.array("token_embd.weight").dtype.itemsize == 144
+    g.close()
+
+
+def test_kquant_oracle_dequant_properties():
+    """Q6_K / Q4_K dequant of the oracle (mistral/dequant.h:47-113, :292-306): Q6_K values are (d*sc)*q with q in
+    -32..31; Q4_K values are fp16 and lie within [-dmin*63, d*63*15]; the K-quant matvec equals the float64 dot
+    of the dequantised rows to fp32 accumulation error."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(3)
+    W6 = G.random_q6_k(rng, 16, 512)
+    d6 = O.dequant_q6_k(W6)
+    q = d6 / (W6["d"].astype(np.float32)[..., None].repeat(256, axis=-1).reshape(16, 512) *
+              np.repeat(W6["scales"].astype(np.float32), 16, axis=-1).reshape(16, 512))
+    qi = q[np.isfinite(q)]
+    assert np.allclose(qi, np.round(qi)) and qi.min() >= -32 and qi.max() <= 31
+    W4 = G.random_q4_k(rng, 16, 512)
+    d4 = O.dequant_q4_k(W4).astype(np.float32)
+    assert np.all(np.abs(d4) <= 63 * 15 * W4["d"].astype(np.float32).max() + 63 * W4["dmin"].astype(np.float32).max())
+    x = rng.standard_normal(512).astype(np.float32)
+    for W, d, t in ((W6, d6, O.TYPE_Q6_K), (W4, d4, O.TYPE_Q4_K)):
+        y = O.matvec_kq(W, x, t)
+        ref = d.astype(np.float64) @ x
+        assert np.max(np.abs(y - ref)) <= 1e-5 * np.max(np.abs(d) @ np.abs(x))
