@@ -140,7 +140,8 @@ def test_cli_text_prompt_with_chat_template(mini_path):
     cli = os.path.join(ROOT_LIB, "mistral")
     n_expect = len(Tokenizer(mini_path).encode(apply_chat("hello world")))
     out = subprocess.run([cli, "--model", mini_path, "--prompt", "hello world", "--chat", "--tokens", "6", "--temp", "0",
-                          "--ignore-eos", "--context", "512"], capture_output=True, text=True, timeout=300)
-    assert out.returncode == 0, out.stderr
-    assert f"Prompt: {n_expect} tokens" in out.stderr
-    assert "Generated tokens: 6" in out.stderr
+                          "--ignore-eos", "--context", "512"], capture_output=True, timeout=300)
+    err = out.stderr.decode(errors="replace")   # stdout holds raw pieces (byte tokens need not be UTF-8)
+    assert out.returncode == 0, err
+    assert f"Prompt: {n_expect} tokens" in err
+    assert "Generated tokens: 6" in err
