@@ -294,7 +294,6 @@ struct sd_ctx {
     void* img_mem = nullptr;       // activation images (norm input, head outputs, SiLU output)
     ActImage img_un{}, img_attn{}, img_h{};
     unsigned* fsync = nullptr;     // grid barrier + slice counters
-    float* w13_xchg = nullptr;     // gate|up hand-over rows between neighbouring CTAs
     MvPhase ph_qkv{}, ph_wo{}, ph_w13{}, ph_w2{}, ph_lm{};
     int fwd_stages = 0, fwd_grid = 0;
     size_t fwd_smem = 0;
@@ -406,7 +405,7 @@ int setup_fused(sd_ctx* c) {
     if ((rc = fixed_kparts(c, c->dim, c->q_rows, &kp_o)) || (rc = fixed_kparts(c, c->dim, c->hid_l, &kp_d))) return rc;
     if (kp_o > c->ypart_max || kp_d > c->ypart_max) return SD_OK;
     if (!fwd_phase(c->ph_qkv, c->qkv_rows, c->dim, kRPW, 1) || !fwd_phase(c->ph_wo, c->dim, c->q_rows, kRPW, kp_o) ||
-        !fwd_phase(c->ph_w13, 2 * c->hid_l, c->dim, kRPW, 1) || !fwd_phase(c->ph_w2, c->dim, c->hid_l, kRPW, kp_d) ||
+        !fwd_phase(c->ph_w13, 2 * c->hid_l, c->dim, 2 * kRPW, 1) || !fwd_phase(c->ph_w2, c->dim, c->hid_l, kRPW, kp_d) ||
         !fwd_phase(c->ph_lm, c->vocab, c->dim, kRPW, 1))
         return SD_OK;
     const int max_smem = device_max_smem(c->dev);
@@ -418,12 +417,10 @@ int setup_fused(sd_ctx* c) {
     CK(fwd_blocks_per_sm(c->fwd_smem, &per_sm), "occupancy");
     if (per_sm < 1) return SD_OK;
     c->fwd_grid = device_sm_count(c->dev);
-    if (c->fwd_grid > kMaxFwdGrid) c->fwd_grid = kMaxFwdGrid;
     std::vector<FwdLayer> hl(c->n_layers);
     for (int l = 0; l < c->n_layers; ++l)
         hl[l] = FwdLayer{c->L[l].qkv, c->L[l].wo, c->L[l].w13, c->L[l].w2, c->L[l].rms_att, c->L[l].rms_ffn};
     if ((rc = dalloc(&c->d_layers, hl.size())) || (rc = dalloc(&c->ssq, (size_t)c->MB * (c->dim / 16))) ||
-        (rc = dalloc(&c->w13_xchg, (size_t)kMaxFwdGrid * kEpiWarps * 128)) ||
         (rc = dalloc(&c->fsync, fwd_sync_words(c->dim))))
         return rc;
     {
@@ -497,8 +494,6 @@ int enqueue_forward_fused(sd_ctx* c, int S, int n_layers, __half* k, __half* v, 
     a.yparts = c->y;
     a.ypart_stride = (size_t)c->MB * c->dim;
     a.sync = c->fsync;
-    a.w13_flags = c->fsync + kW13FlagWord;
-    a.w13_xchg = c->w13_xchg;
     a.part_ml = c->part_ml;
     a.part_acc = c->part_acc;
     a.attn_chunk = c->attn_chunk;
@@ -793,7 +788,7 @@ void sd_ctx_free(sd_ctx* c) {
     cudaFree(c->hact.qs); cudaFree(c->hact.d); cudaFree(c->hact.sum); cudaFree(c->q);
     cudaFree(c->part_ml); cudaFree(c->part_acc); cudaFree(c->logits); cudaFree(c->probs); cudaFree(c->argmax);
     cudaFree(c->ctrl); cudaFree(c->dctrl); cudaFree(c->ctrl_sub); cudaFree(c->err); cudaFree(c->gs); cudaFree(c->g_out); cudaFree(c->g_hist);
-    cudaFree(c->d_layers); cudaFree(c->ssq); cudaFree(c->fsync); cudaFree(c->w13_xchg);
+    cudaFree(c->d_layers); cudaFree(c->ssq); cudaFree(c->fsync);
     cudaFree(c->img_mem);
     for (void* p : c->tp_opened) cudaIpcCloseMemHandle(p);
     cudaFree(c->tp_mem);

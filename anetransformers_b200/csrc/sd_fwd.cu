@@ -123,11 +123,6 @@ struct Items {
     int i0, i1;
 };
 
-// The CTA whose my_items range holds item j of n (the inverse of the range split below).
-__device__ __forceinline__ int item_owner(int j, int n) {
-    return (int)(((long long)(j + 1) * gridDim.x - 1) / n);
-}
-
 __device__ __forceinline__ Items my_items(const MvPhase& p) {
     const int n = p.n_units * p.kparts, G = gridDim.x, c = blockIdx.x;
     return Items{(int)((long long)c * n / G), (int)((long long)(c + 1) * n / G)};
@@ -374,53 +369,14 @@ __device__ __forceinline__ void mv_phase(const FwdArgs& a, int kind, int layer, 
                 if (lane == 0) mbar_arrive(&R.red_empty[slot]);
             }
             if (kind == PH_W13) {
-                // items are single pairs: item 2u holds the gate rows (lo, hi) of 32-row unit u, item 2u + 1 its up
-                // rows.  A unit cut by the end of this CTA's range is finished here with the up rows the next CTA
-                // published from its first item (ranges are contiguous, so every CTA publishes before it waits).
-                const int hu = i & 1, wunit = i >> 1;
-                if (hu == 1 && i == it.i0) {
-                    float* dst = a.w13_xchg + ((size_t)blockIdx.x * kEpiWarps + r) * 128;
+                // unit of 4 row-groups = 2 pairs: (gate lo, gate hi), (up lo, up hi)
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = v[k];
+                for (int k = 0; k < 4; ++k) R.ubuf[(pr * 2 + r) * 128 + lane + 32 * k] = v[k];
+                if (pr == 1) {
                     named_sync(kBarEpi, kEpiWarps * 32);
-                    if (r == 0 && lane == 0 && !ab) {
-                        __threadfence();
-                        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.w13_flags + blockIdx.x),
-                                     "r"((uint32_t)layer + 1) : "memory");
-                    }
-                    continue;
+                    if (!ab) epi_silu_q8(R.ubuf, r, lane, unit, nv, a.h, a.hidden, &a.h_img);
+                    named_sync(kBarEpi, kEpiWarps * 32);
                 }
-#pragma unroll
-                for (int k = 0; k < 4; ++k) R.ubuf[(hu * 2 + r) * 128 + lane + 32 * k] = v[k];
-                if (hu == 0) {
-                    if (i + 1 < it.i1) continue;  // the up rows are this CTA's next item
-                    // the up rows are the first item of the CTA that owns item i + 1 (the next CTA with items)
-                    const int owner = item_owner(i + 1, p.n_units * p.kparts);
-                    const unsigned* fl = a.w13_flags + owner;
-                    if (!ab) {
-                        uint32_t f = 0;
-                        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(fl) : "memory");
-                        if (f < (uint32_t)layer + 1) {
-                            const uint64_t t0 = global_ns();
-                            for (;;) {
-                                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(fl) : "memory");
-                                if (f >= (uint32_t)layer + 1) break;
-                                if (*abort_flag || global_ns() - t0 > kWaitLimitNs) {
-                                    set_dev_error(a.err, DEV_ERR_PEER_WAIT);
-                                    m->abort = 1;
-                                    break;
-                                }
-                            }
-                        }
-                        ab = ab || !__all_sync(0xffffffffu, f >= (uint32_t)layer + 1);
-                    }
-                    const float* src = a.w13_xchg + ((size_t)owner * kEpiWarps + r) * 128;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) R.ubuf[(2 + r) * 128 + lane + 32 * k] = ab ? 0.f : __ldcg(src + lane + 32 * k);
-                }
-                named_sync(kBarEpi, kEpiWarps * 32);
-                if (!ab) epi_silu_q8(R.ubuf, r, lane, wunit, nv, a.h, a.hidden, &a.h_img);
-                named_sync(kBarEpi, kEpiWarps * 32);
             } else if (kind == PH_WO && p.kparts == 1 && a.tp.n <= 1) {
                 // the pair is one 32-row block (unit): finish it here for every token, warp r taking
                 // tokens r, r + 2, ... (lane = row); x and the norm weight are loaded up front
@@ -723,9 +679,8 @@ int fwd_pick_stages(int max_smem) {
     return 0;
 }
 
-// word 0: the grid barrier counter; words 32..: the argmax keys (u64 per token); words kW13FlagWord..: the gate|up
-// hand-over flags, one per CTA (the layer + 1 whose up rows that CTA published)
-size_t fwd_sync_words(int) { return kW13FlagWord + kMaxFwdGrid; }
+// word 0: the grid barrier counter; words 32..: the argmax keys (u64 per token)
+size_t fwd_sync_words(int) { return 32 + 2 * kMaxS; }
 
 cudaError_t fwd_init_attrs(int max_smem) {
     return cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);

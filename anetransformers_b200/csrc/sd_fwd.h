@@ -45,8 +45,6 @@ struct FwdArgs {
     float* yparts;              // [kparts][S][dim] K-slice partials
     size_t ypart_stride;
     unsigned* sync;             // [0] grid barrier counter; from word 32: argmax keys [kMaxS] u64; zero at launch
-    unsigned* w13_flags;        // sync + kW13FlagWord: per CTA, the layer + 1 whose up rows it published
-    float* w13_xchg;            // [grid][kEpiWarps][128] up rows of a gate|up unit cut by a CTA range
     float2* part_ml;            // attention partials
     float* part_acc;
     int attn_chunk, max_chunks;
@@ -58,8 +56,6 @@ struct FwdArgs {
 };
 
 constexpr int kFwdAttnGroups = 2;  // 128-thread attention groups per CTA
-constexpr int kMaxFwdGrid = 256;    // CTAs of the persistent forward (one per SM)
-constexpr int kW13FlagWord = 64;    // first sync word of the gate|up hand-over flags
 
 size_t fwd_smem_bytes(int nstage);
 int fwd_pick_stages(int max_smem);
