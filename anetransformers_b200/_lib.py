@@ -122,6 +122,7 @@ _SIGS = {
     "sd_batch_create": (i32, [vp, i32, i32, i32, vp]),
     "sd_batch_free": (None, [vp]),
     "sd_batch_stream": (vp, [vp]),
+    "sd_batch_set_gemm": (i32, [vp, i32]),
     "sd_batch_forward": (i32, [vp, vp, i32, vp, vp]),
     "sd_batch_prefill": (i32, [vp, vp, i32]),
     "sd_batch_decode": (i32, [vp, vp, vp, i32, vp, vp, i32, vp, vp]),

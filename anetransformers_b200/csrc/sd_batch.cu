@@ -486,6 +486,7 @@ struct WgPlan {
     WGemmArgs a{};
     int grid = 0;
     size_t smem = 0;
+    bool tc = false;  // tcgen05 GEMM (sd_tcgemm.cu) instead of k_wgemm
 };
 
 // Cost model in ns: a quad (128 columns) of a unit costs (0.8 + n8 tiles per warp) x 800 ns (the A-fragment
@@ -530,8 +531,26 @@ void wg_plan(WgPlan& p, int epi, int rows, int K, int M, int kp_lo, int kp_max, 
     p.smem = wgemm_smem_bytes(bt, a.nstage);
 }
 
+// The tcgen05 form of a k_wgemm plan: the same K split (so both GEMMs give the same bits), token tiles of at
+// most 128 tokens in an even number of n8 tiles (the MMA's N is a multiple of 16), as many ring stages as fit.
+void tc_plan(WgPlan& p, int epi, int sms, int max_smem) {
+    WGemmArgs& a = p.a;
+    const int n_tt = (a.NT + kTcMaxTT - 1) / kTcMaxTT;
+    int tt = (a.NT + n_tt - 1) / n_tt;
+    tt += tt & 1;
+    a.tt_n8 = tt;
+    a.n_tt = (a.NT + tt - 1) / tt;
+    a.stage_bytes = kWgWStage + tt * kWSeg + kTcAStage;
+    a.nstage = std::min(kTcMaxStages, (int)(((size_t)max_smem - tcgemm_smem_bytes(tt, 0, epi)) / a.stage_bytes));
+    const long long units = (long long)a.n_rt * a.kparts * a.n_tt;
+    p.grid = (int)std::min<long long>(units, sms);
+    p.smem = tcgemm_smem_bytes(tt, a.nstage, epi);
+    p.tc = true;
+}
+
 struct BPlans {
     bool ready = false;
+    bool tc = false;  // this width's forwards use the tcgen05 GEMM and the tensor-core image arrangement
     WgPlan qkv, wo, w13, w2, lm;
 };
 
@@ -567,6 +586,7 @@ struct sd_batch {
     int g_cap = 0;
     int* ndone = nullptr;     // [2]: streams done, most tokens a live stream still has to generate
     int* ndone_h = nullptr;   // pinned copy
+    int gemm_mode = SD_BATCH_GEMM_AUTO;
     BPlans plans[SD_BATCH_MAX_WIDTH + 1];
     cudaGraphExec_t fwd_graph[SD_BATCH_MAX_WIDTH + 1][2] = {};
     cudaGraphExec_t iter_graph = nullptr;
@@ -614,6 +634,14 @@ BPlans& plans_for(sd_batch* b, int T) {
     plan(P.w13, WG_SILU, 2 * m.hidden, m.dim, 1);
     plan(P.w2, WG_STORE, m.dim, m.hidden, b->kp_max);
     plan(P.lm, WG_STORE, m.vocab, m.dim, 1);
+    P.tc = b->gemm_mode == SD_BATCH_GEMM_TC || (b->gemm_mode == SD_BATCH_GEMM_AUTO && M >= kTcMinTokens);
+    if (P.tc) {
+        tc_plan(P.qkv, WG_STORE, b->sms, b->max_smem);
+        tc_plan(P.wo, WG_STORE, b->sms, b->max_smem);
+        tc_plan(P.w13, WG_SILU, b->sms, b->max_smem);
+        tc_plan(P.w2, WG_STORE, b->sms, b->max_smem);
+        tc_plan(P.lm, WG_STORE, b->sms, b->max_smem);
+    }
     P.ready = true;
     return P;
 }
@@ -622,7 +650,10 @@ int run_wgemm(sd_batch* b, int epi, WgPlan p, const uint8_t* w, const uint8_t* a
     p.a.w = w;
     p.a.act = act;
     p.a.err = b->m.err;
-    CK(launch_wgemm(epi, p.a, p.grid, p.smem, b->st), "wide gemm");
+    if (p.tc)
+        CK(launch_tcgemm(epi, p.a, p.grid, p.smem, b->st), "tcgen05 gemm");
+    else
+        CK(launch_wgemm(epi, p.a, p.grid, p.smem, b->st), "wide gemm");
     return SD_OK;
 }
 
@@ -636,7 +667,8 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
     na.y = b->y;
     na.ystride = (size_t)b->M_max * m.dim;
     na.embd = m.embd;
-    na.out = WImg{b->img_x, NT};
+    const int tcimg = P.tc ? 1 : 0;
+    na.out = WImg{b->img_x, NT, tcimg};
     na.dim = m.dim;
     na.T = T;
     na.eps = m.eps;
@@ -686,7 +718,7 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         ba.a.max_chunks = b->max_chunks;
         ba.a.part_ml = b->part_ml;
         ba.a.part_acc = b->part_acc;
-        ba.a.wimg = WImg{b->img_attn, NT};
+        ba.a.wimg = WImg{b->img_attn, NT, tcimg};
         ba.kv_stream = b->kv_stream;
         ba.T = T;
         ba.ctrl = b->ctrl;
@@ -708,7 +740,7 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         CK(cudaGetLastError(), "norm");
         // gate|up + SiLU + Q8_0
         WgPlan pg = P.w13;
-        pg.a.h = WImg{b->img_h, NT};
+        pg.a.h = WImg{b->img_h, NT, tcimg};
         pg.a.hidden = m.hidden;
         if ((rc = run_wgemm(b, WG_SILU, pg, b->ww13[l], b->img_x))) return rc;
         // down, residual + next norm
@@ -926,6 +958,25 @@ void sd_batch_free(sd_batch* b) {
 
 void* sd_batch_stream(sd_batch* b) { return b ? (void*)b->st : nullptr; }
 
+int sd_batch_set_gemm(sd_batch* b, int mode) {
+    if (!b || mode < SD_BATCH_GEMM_AUTO || mode > SD_BATCH_GEMM_TC) return fail(SD_ERR_INVALID, "bad batch or gemm mode");
+    clear_error();
+    if (mode == b->gemm_mode) return SD_OK;
+    cudaSetDevice(b->dev);
+    CK(cudaStreamSynchronize(b->st), "sync");
+    b->gemm_mode = mode;
+    for (auto& P : b->plans) P.ready = false;
+    for (auto& row : b->fwd_graph)
+        for (auto& gr : row)
+            if (gr) {
+                cudaGraphExecDestroy(gr);
+                gr = nullptr;
+            }
+    if (b->iter_graph) cudaGraphExecDestroy(b->iter_graph);
+    b->iter_graph = nullptr;
+    return SD_OK;
+}
+
 int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_batch** out) {
     clear_error();
     if (!ctx || !out || n_streams < 1 || max_seq < 16 || max_width < 1 || max_width > SD_BATCH_MAX_WIDTH)
@@ -953,6 +1004,7 @@ int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_b
     if (cudaSetDevice(b->dev) != cudaSuccess) return bail(fail(SD_ERR_INVALID, "bad device %d", b->dev));
     if ((rc = ck(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking), "stream"))) return bail(rc);
     if ((rc = ck(wgemm_init_attrs(b->max_smem), "gemm attributes"))) return bail(rc);
+    if ((rc = ck(tcgemm_init_attrs(b->max_smem), "tcgen05 gemm attributes"))) return bail(rc);
     if ((rc = ck(cudaFuncSetAttribute(k_battn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)battn_smem_bytes()),
                  "attention attributes")))
         return bail(rc);

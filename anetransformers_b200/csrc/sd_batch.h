@@ -54,6 +54,15 @@ struct WGemmArgs {
 };
 
 size_t wgemm_smem_bytes(int tt_n8, int nstage);
+// The same GEMM on tcgen05 (sd_tcgemm.cu): WGemmArgs with tt_n8 even and <= kTcMaxTT, stage_bytes =
+// kWgWStage + tt_n8 * kWSeg + 16384, the activation image in the tensor-core arrangement (WImg::tc).
+constexpr int kTcMaxTT = 16;      // n8 tiles per token tile (128 tokens)
+constexpr int kTcMinTokens = 64;  // forwards of at least this many tokens take the tcgen05 GEMM by default
+constexpr int kTcMaxStages = 4;
+constexpr int kTcAStage = 4 * 4096;
+size_t tcgemm_smem_bytes(int tt_n8, int nstage, int epi);
+cudaError_t tcgemm_init_attrs(int max_smem);
+cudaError_t launch_tcgemm(int epi, const WGemmArgs& a, int grid, size_t smem, cudaStream_t st);
 cudaError_t wgemm_init_attrs(int max_smem);
 cudaError_t launch_wgemm(int epi, const WGemmArgs& a, int grid, size_t smem, cudaStream_t st);
 // tile16x4 matrix (n_rg row-groups, nq quads) -> wide layout (zero-padded row tiles)

@@ -84,7 +84,10 @@ __device__ __forceinline__ uint8_t* wimg_seg(const WImg& im, int m, int blk) {
     return im.p + ((size_t)(blk >> 2) * im.NT + (m >> 3)) * kWSeg;
 }
 __device__ __forceinline__ void wimg_put_word(const WImg& im, int m, int blk, int w, uint32_t word) {
-    reinterpret_cast<uint32_t*>(wimg_seg(im, m, blk) + (blk & 3) * 256 + (4 * (m & 7) + (w & 3)) * 8)[w >> 2] = word;
+    if (im.tc)
+        reinterpret_cast<uint32_t*>(wimg_seg(im, m, blk) + (blk & 3) * 256 + (w >> 2) * 128 + (m & 7) * 16)[w & 3] = word;
+    else
+        reinterpret_cast<uint32_t*>(wimg_seg(im, m, blk) + (blk & 3) * 256 + (4 * (m & 7) + (w & 3)) * 8)[w >> 2] = word;
 }
 __device__ __forceinline__ void wimg_put_meta(const WImg& im, int m, int blk, float d, int sum) {
     float* mp = reinterpret_cast<float*>(wimg_seg(im, m, blk) + 1024 + (blk & 3) * 64 + ((m & 7) >> 1) * 16);

@@ -64,9 +64,14 @@ struct ActImage {
 // ---------------------------------------------------------------------------------------------
 constexpr int kWSeg = 1280;
 
+//
+// Tensor-core arrangement (tc = 1; read by the tcgen05 GEMM): the same segments and meta, but the codes of
+// block bq are [kc][8 tokens][16 bytes] at bq * 256 (kc = 0: elements 0..15, kc = 1: elements 16..31), the
+// canonical K-major operand layout of tcgen05.mma (8-row x 16-byte core matrices).
 struct WImg {
     uint8_t* p;
     int NT;
+    int tc = 0;
 };
 
 inline size_t wimg_bytes(int M, int K) { return (size_t)(K / 128) * ((M + 7) / 8) * kWSeg; }

@@ -287,6 +287,13 @@ class BatchContext:
     def stream(self) -> int:
         return _lib.lib().sd_batch_stream(self.h) or 0
 
+    GEMM_AUTO, GEMM_MMA, GEMM_TC = 0, 1, 2
+
+    def set_gemm(self, mode: int):
+        """Tensor-core GEMM of the forwards: GEMM_AUTO (tcgen05 from 64 tokens per forward), GEMM_MMA
+        (mma.sync always) or GEMM_TC (tcgen05 always); the results are bit-identical."""
+        _lib.check(_lib.lib().sd_batch_set_gemm(self.h, int(mode)), "sd_batch_set_gemm")
+
     def forward(self, tokens, pos, want_logits: bool = True) -> np.ndarray:
         """tokens [n_streams, T] at positions pos[s] ..; returns logits [n_streams, T, vocab] (or None)."""
         t = np.ascontiguousarray(tokens, np.int32)

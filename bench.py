@@ -399,6 +399,7 @@ def run_selfspec(args, ctx, rank, world, local, dist, tp, peaks):
 
 # batched speculative serving, 64 streams per GPU, 4096-token random contexts, K = 4 n-gram drafts
 SERVE_STREAMS, SERVE_CTX, SERVE_TOKENS = 64, 4096, 256
+GEMM_MODES = {"auto": 0, "mma": 1, "tc": 2}  # sd_batch_set_gemm modes
 
 
 def run_serving(args, ctx_path, rank, world, local, dist, peaks):
@@ -412,6 +413,7 @@ def run_serving(args, ctx_path, rank, world, local, dist, peaks):
     ctx = Context(ctx_path, device=local, max_seq=64)
     # batch width = the verify width: the GEMMs' K splits are planned for it (prefill runs in chunks of it)
     bc = BatchContext(ctx, B, max_seq=n_ctx + args.tokens + 64, width=SPEC_K + 1)
+    bc.set_gemm(GEMM_MODES[args.gemm])
     rng = np.random.default_rng(2024 + rank)
     prompts = rng.integers(3, 32000, (B, n_ctx)).astype(np.int32)
     t = time.perf_counter()
@@ -526,6 +528,7 @@ def run_serving_forward(args):
     T = args.S or SPEC_K + 1
     ctx = Context(path, max_seq=64)
     bc = BatchContext(ctx, args.streams, max_seq=args.ctx_serve + T + 64, width=T)
+    bc.set_gemm(GEMM_MODES[args.gemm])
     rng = np.random.default_rng(5)
     toks = rng.integers(3, 32000, (args.streams, T)).astype(np.int32)
     pos = np.full(args.streams, args.ctx_serve, np.int32)
@@ -602,6 +605,8 @@ def main():
                          "serving = config 5 (batched streams), forward = single verify forwards (profiling: "
                          "--layers, --S, --ctx)")
     ap.add_argument("--streams", type=int, default=SERVE_STREAMS, help="serving: streams per GPU")
+    ap.add_argument("--gemm", default="auto", choices=sorted(GEMM_MODES),
+                    help="serving: batched GEMM (auto = tcgen05 from 64 tokens per forward, mma = mma.sync, tc = tcgen05)")
     ap.add_argument("--ctx-serve", type=int, default=SERVE_CTX, help="serving: context tokens per stream")
     ap.add_argument("--layers", type=int, default=32, help="forward workload: layers of the 7B-shaped model")
     ap.add_argument("--ctx", type=int, default=1024, help="forward workload: context positions before the forward")

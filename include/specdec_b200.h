@@ -370,6 +370,14 @@ SD_API int sd_batch_create(sd_ctx *ctx, int n_streams, int max_seq, int max_widt
 SD_API void sd_batch_free(sd_batch *b);
 /* The CUDA stream (cudaStream_t) every sd_batch_* call of this batch is ordered on. */
 SD_API void *sd_batch_stream(sd_batch *b);
+/* Which tensor-core GEMM the batch's forwards use (no reference counterpart: the reference has one
+ * Metal GEMM, q4_0_gemm at mistral/q4_0_metal.metal:264-383).  AUTO (the default): tcgen05 MMA with TMEM
+ * accumulators for forwards of at least 64 tokens (n_streams * T), the mma.sync GEMM below that; MMA: always
+ * mma.sync; TC: always tcgen05.  Both give bit-identical results.  Drops the batch's captured graphs. */
+#define SD_BATCH_GEMM_AUTO 0
+#define SD_BATCH_GEMM_MMA 1
+#define SD_BATCH_GEMM_TC 2
+SD_API int sd_batch_set_gemm(sd_batch *b, int mode);
 /* One forward of T <= max_width tokens per stream: tokens [n_streams][T] at positions pos[s] .. pos[s]+T-1
  * (K/V written to each stream's ring); logits: host [n_streams][T][vocab] or NULL. */
 SD_API int sd_batch_forward(sd_batch *b, const int32_t *tokens, int T, const int32_t *pos, float *logits);
