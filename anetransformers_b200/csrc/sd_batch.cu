@@ -190,6 +190,7 @@ struct BAttnArgs {
     AttnArgs a;        // stream 0's view (q, ring, partial buffers); a.S = T, a.wimg = o-proj input image
     size_t kv_stream;  // halves between consecutive streams' rings
     int T;
+    int n_streams;
     const DevCtrl* ctrl;
 };
 
@@ -418,24 +419,29 @@ __device__ void battn_item(const AttnArgs& a, int nv, int pos, int lo_min, int h
     }
 }
 
-// Work items (kv head, chunk) of stream blockIdx.y, grid-strided over blockIdx.x.
+// Work items (stream, kv head, chunk): every stream owns max_chunks * n_kvh item slots (the slots past its
+// ring's chunks, and those of finished streams, are skipped), and one resident wave of CTAs (two per SM)
+// walks the whole list with a grid stride, so no CTA runs in a second, nearly empty wave.
 __global__ void __launch_bounds__(kAttnThreads, 2) k_battn_partial(const BAttnArgs ba) {
     extern __shared__ __align__(16) uint8_t dsm[];
-    const int b = blockIdx.y;
-    const DevCtrl& c = ba.ctrl[b];
-    const int nv = c.done ? 0 : min(c.n_valid, ba.T);
-    if (nv <= 0) return;
-    const AttnArgs a = stream_view(ba, b);
-    const int pos = c.pos;
-    const int hi_max = pos + nv - 1;
-    const int lo_min = max(0, pos + 1 - a.max_seq);
-    const int c_first = lo_min / a.chunk, c_last = hi_max / a.chunk;
-    const int n_items = (c_last - c_first + 1) * a.n_kvh;
     __half* qh = reinterpret_cast<__half*>(dsm);
     __half* ring = qh + kQRows * kQStride;
     float* xch = reinterpret_cast<float*>(ring);  // merge buffer of the two position halves, after the ring is drained
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x)
-        battn_item(a, nv, pos, lo_min, hi_max, item % a.n_kvh, c_first + item / a.n_kvh, qh, ring, xch, threadIdx.x);
+    const int per_stream = ba.a.max_chunks * ba.a.n_kvh;
+    const int n_slots = ba.n_streams * per_stream;
+    for (int item = blockIdx.x; item < n_slots; item += gridDim.x) {
+        const int b = item / per_stream, local = item - b * per_stream;
+        const DevCtrl& c = ba.ctrl[b];
+        const int nv = c.done ? 0 : min(c.n_valid, ba.T);
+        if (nv <= 0) continue;
+        const AttnArgs a = stream_view(ba, b);
+        const int pos = c.pos;
+        const int hi_max = pos + nv - 1;
+        const int lo_min = max(0, pos + 1 - a.max_seq);
+        const int c_first = lo_min / a.chunk, c_last = hi_max / a.chunk;
+        if (local >= (c_last - c_first + 1) * a.n_kvh) continue;
+        battn_item(a, nv, pos, lo_min, hi_max, local % a.n_kvh, c_first + local / a.n_kvh, qh, ring, xch, threadIdx.x);
+    }
     cp_async_wait_all();
 }
 
@@ -722,8 +728,8 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         ba.kv_stream = b->kv_stream;
         ba.T = T;
         ba.ctrl = b->ctrl;
-        const int per_stream = std::max(1, (2 * b->sms + b->B - 1) / b->B);
-        k_battn_partial<<<dim3(per_stream, b->B), kAttnThreads, battn_smem_bytes(), b->st>>>(ba);
+        ba.n_streams = b->B;
+        k_battn_partial<<<std::min(2 * b->sms, b->B * b->max_chunks * m.n_kv), kAttnThreads, battn_smem_bytes(), b->st>>>(ba);
         CK(cudaGetLastError(), "attention");
         k_battn_combine<<<M * m.n_heads, combine_warps(b->max_seq) * 32, 0, b->st>>>(ba);
         CK(cudaGetLastError(), "combine");

@@ -5,10 +5,13 @@
 //   Y[m][r] = sum_b (wd[r,b] * xd[m,b]) * isum[r,m,b],  isum = sum_j (q_j - 8) * x8_j
 // (the reference's per-block SDOT sum and fp32 scale, mistral/dequant.h:1068-1087).  One MMA of M = 128
 // weight rows x N tokens x K = 32 is exactly one Q4_0 block, so the int32 block sums come out of the tensor
-// core exact and separate.  Each TMEM accumulator slot is preset to the bits of kMagic, so after the MMA its
-// bits read as the fp32 value kMagic + sum(q * x); the epilogue then runs k_wgemm's three fp32 operations per
-// element (one exact FADD of the image's offset, the scale product, the FMA into the running sum), block by
-// block in K order.  Both GEMMs therefore give bit-identical outputs for the same K split.
+// core exact and separate: each MMA overwrites its TMEM accumulator slot with sum(q * x) (q the 0..15 nibbles).
+// The epilogue adds the bits of kMagic with one integer add, so the word reads as the fp32 value
+// kMagic + sum(q * x), and then runs k_wgemm's three fp32 operations per element (one exact FADD of the
+// image's offset, the scale product, the FMA into the running sum), block by block in K order.  Both GEMMs
+// therefore give bit-identical outputs for the same K split.  (Presetting the slots to kMagic instead, by
+// tcgen05.cp from shared memory, cost the MMA thread ~900 cycles per block and measured 16 % slower; 16
+// epilogue warps of at most 32 columns instead of 8 of at most 64 measured 12 % slower.)
 //
 // Shapes.  A unit is (row tile of 128 rows, K slice, token tile of N <= 128 tokens); CTAs are persistent
 // (one per SM) and walk units u = blockIdx.x, += gridDim.x, with the token tiles of a row tile adjacent so
@@ -26,7 +29,7 @@
 //   warps 2-3   unpack each stage's nibbles into A (a generic-proxy write, fenced for the async proxy)
 //   warps 4-11  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (the tile's rows) and token columns
 //               [c * N/2, (c + 1) * N/2), c = (w - 4) / 4; it keeps that row x column block's fp32 sums
-//               in registers over the unit's blocks, presets each slot again after reading it, and at the
+//               in registers over the unit's blocks, releases each slot once it is read, and at the
 //               end of the unit stores the K-slice partial (WG_STORE) or, for gate|up units, hands the gate
 //               sums to the warp holding the matching up rows, which forms SiLU(g) * u and writes its Q8_0
 //               block into the next image (WG_SILU).
@@ -48,7 +51,6 @@ constexpr uint32_t kTcCols = kTcSlots * kTcSlotCols;  // 512: the whole TMEM of 
 constexpr int kTcABytes = kTcAStage;             // unpacked A tiles of a stage
 constexpr int kTcPairs = 4;                      // (gate warp, up warp) pairs of a gate|up unit
 constexpr int kTcXchgBytes = kTcPairs * 2 * 32 * 33 * 4;  // per pair: two halves of <= 32 token rows of 33 floats
-constexpr int kTcMagicBytes = 4096;             // preset tile of kMagic words (tcgen05.cp source)
 
 // Shared-memory matrix descriptor of a K-major operand without swizzle: start address, leading byte offset
 // (distance between the two 16-byte K chunks of a 32-byte K step) and stride byte offset (distance between
@@ -78,10 +80,10 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// D[tmem] += A[smem] x B[smem] (u8 x s8 -> s32), issued by one thread.
+// D[tmem] = A[smem] x B[smem] (u8 x s8 -> s32, the accumulator overwritten), issued by one thread.
 __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, 1, 0;\n"
+        "{\n .reg .pred p;\n setp.ne.b32 p, 0, 0;\n"
         " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
         "l"(a), "l"(b), "r"(idesc)
         : "memory");
@@ -115,12 +117,6 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[32]) {
                  :
                  : "memory");
 }
-// Copy 128 lanes x 8 columns from shared memory into TMEM (issued by one thread; ordered before the
-// thread's next tcgen05.mma).
-__device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
-    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
 __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
     asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
@@ -156,7 +152,7 @@ struct TcCtl {
     uint64_t aready[kTcMaxStages];  // stage's A unpacked (64 unpack threads)
     uint64_t sempty[kTcMaxStages];  // stage free again (MMA commit + 8 epilogue warps)
     uint64_t tfull[kTcSlots];       // accumulator slot holds a finished block (MMA commit)
-    uint64_t tempty[kTcSlots];      // accumulator slot read and preset (8 epilogue warps)
+    uint64_t tempty[kTcSlots];      // accumulator slot read (8 epilogue warps)
     uint64_t xg[kTcPairs];          // gate warp's hand-over written (32 lanes)
     uint64_t xu[kTcPairs];          // up warp's hand-over written (32 lanes)
     uint64_t xempty[kTcPairs];      // both warps of the pair done with the exchange rows (64 lanes)
@@ -176,7 +172,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcCtl* c
 }  // namespace
 
 size_t tcgemm_smem_bytes(int tt_n8, int nstage, int epi) {
-    return (size_t)nstage * ((size_t)kWgWStage + (size_t)tt_n8 * kWSeg + kTcABytes) + kTcMagicBytes +
+    return (size_t)nstage * ((size_t)kWgWStage + (size_t)tt_n8 * kWSeg + kTcABytes) +
            (epi == WG_SILU ? (size_t)kTcXchgBytes : 0) + sizeof(TcCtl) + 128;
 }
 
@@ -191,9 +187,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tcgemm(const WGemmArgs a) {
     const int nstage = a.nstage;
     const uint32_t SB = (uint32_t)a.stage_bytes;  // kWgWStage + tt_n8 * kWSeg + kTcABytes
     const uint32_t xoff = kWgWStage, aoff = kWgWStage + (uint32_t)a.tt_n8 * kWSeg;
-    uint32_t* magic = reinterpret_cast<uint32_t*>(smem + (size_t)nstage * SB);
-    float* xchg = reinterpret_cast<float*>(smem + (size_t)nstage * SB + kTcMagicBytes);
-    TcCtl* ctl = reinterpret_cast<TcCtl*>(smem + (size_t)nstage * SB + kTcMagicBytes + (EPI == WG_SILU ? kTcXchgBytes : 0));
+    float* xchg = reinterpret_cast<float*>(smem + (size_t)nstage * SB);
+    TcCtl* ctl = reinterpret_cast<TcCtl*>(smem + (size_t)nstage * SB + (EPI == WG_SILU ? kTcXchgBytes : 0));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_units = a.n_rt * a.kparts * a.n_tt;
     const uint32_t sbase = smem_u32(smem);
@@ -217,9 +212,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tcgemm(const WGemmArgs a) {
         ctl->abort = 0;
         fence_mbar_init();
     }
-    // the accumulator preset: every word the bits of kMagic (read by tcgen05.cp, an async-proxy read)
-    for (int i = tid; i < kTcMagicBytes / 4; i += kTcThreads) magic[i] = (uint32_t)kMagicI;
-    fence_async_smem();
     if (warp == 1) {
         tmem_alloc(&ctl->tmem, kTcCols);
         tmem_relinquish();
@@ -263,8 +255,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tcgemm(const WGemmArgs a) {
         if (lane == 0) {
             RingPos rp, ts;
             constexpr uint32_t idesc = idesc_u8s8(N);
-            // any reading of the preset descriptor stays inside the 4 KB magic tile (strides of 128 bytes)
-            const uint64_t md = kmajor_desc(smem_u32(magic), 128, 128);
             bool ok = true;
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const TcUnit w = tc_unit(a, u);
@@ -281,8 +271,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tcgemm(const WGemmArgs a) {
                         }
                         tc_fence_after();
                         const uint32_t d = tmem + ts.slot * kTcSlotCols;
-#pragma unroll
-                        for (int c = 0; c < N / 8; ++c) tc_cp_128x256b(d + c * 8, md);
                         const uint64_t ad = kmajor_desc(st + aoff + bq * 4096, 2048, 128);
                         const uint64_t bd = kmajor_desc(st + xoff + bq * 256, 128, kWSeg);
                         tc_mma(d, ad, bd, idesc);
@@ -382,7 +370,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tcgemm(const WGemmArgs a) {
                             const float2 xd = make_float2(__uint_as_float(mu.x), __uint_as_float(mu.y));
                             const float2 off = make_float2(__uint_as_float(mu.z), __uint_as_float(mu.w));
                             const int j = (gi & 3) * 8 + 2 * t;
-                            const float2 f = __fadd2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), off);
+                            // the bits of kMagic + sum(q * x): exact while |sum| < 2^22 (|sum| <= 32 * 15 * 128)
+                            const float2 f = __fadd2_rn(make_float2(__uint_as_float(v[j] + (uint32_t)kMagicI),
+                                                                    __uint_as_float(v[j + 1] + (uint32_t)kMagicI)), off);
                             const float2 sc = __fmul2_rn(wd2, xd);
                             acc[gi * 4 + t] = __ffma2_rn(sc, f, acc[gi * 4 + t]);
                         }
