@@ -226,6 +226,7 @@ def forward_roofline(ctx, peaks, world: int, tp: bool, S: int = SPEC_K + 1, pos:
     sync-word memset and the 32-thread argmax-key decode (< 1 % of its time).  Algorithmic bytes per forward:
     this rank's Q4_0 weights (32 layers / tp ranks + the replicated LM head) + the fp16 K/V it attends."""
     import torch
+    pos = min(pos, ctx.info.max_seq - S - 1)  # a shorter run (--tokens) has a shorter ring
     toks = torch.tensor(np.random.default_rng(9).integers(3, 32000, S), dtype=torch.int32, device="cuda")
     am = torch.empty(S, dtype=torch.int32, device="cuda")
     for _ in range(3):
