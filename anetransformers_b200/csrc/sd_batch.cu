@@ -445,16 +445,86 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_battn_partial(const BAttnAr
     cp_async_wait_all();
 }
 
-// Merge of one (token, head) row and its Q8_0 quantisation into the o-proj image.
-__global__ void __launch_bounds__(kCombineWarpsMax * 32) k_battn_combine(const BAttnArgs ba) {
-    __shared__ __align__(16) float obuf[kCombineWarpsMax * kHD];
-    const int row = blockIdx.x;
+// Merge of the chunk partials of one (token, head) row and its Q8_0 quantisation into the o-proj image: one
+// warp per row, eight rows per CTA.  Lane l holds the (max, sum) pair of chunk c0 + l; every chunk's max and sum
+// and the first eight chunks' 128-dim partials (lane = 4 dims) are loaded in one round trip.  The chunks are
+// merged in chunk order (M = max of the maxima, L = sum of sum * exp(max - M) in lane order then butterfly,
+// o = sum of partial * exp(max - M) in chunk order, o / L), the arithmetic of the single-stream combine with all
+// chunks in one warp, so a row's result depends only on its own partials.
+constexpr int kBCombWarps = 8;
+
+__global__ void __launch_bounds__(kBCombWarps * 32) k_battn_combine(const BAttnArgs ba) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kBCombWarps + warp;
+    if (row >= ba.n_streams * ba.T * ba.a.n_heads) return;
     const int m = row / ba.a.n_heads, h = row - m * ba.a.n_heads;
     int b, s;
     if (!token_valid(ba.ctrl, m, ba.T, &b, &s)) return;
     const AttnArgs a = stream_view(ba, b);
-    attn_combine_row(a, blockDim.x >> 5, ba.ctrl[b].pos, s, h, threadIdx.x >> 5, threadIdx.x & 31, obuf,
-                     [] { __syncthreads(); });
+    const int hi = ba.ctrl[b].pos + s, lo = max(0, hi + 1 - a.max_seq);
+    const int c0 = lo / a.chunk, c1 = hi / a.chunk;
+    const size_t base = ((size_t)s * a.n_heads + h) * a.max_chunks;
+    constexpr int U = 8;
+    float4 ac[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+        ac[u] = c0 + u <= c1 ? *reinterpret_cast<const float4*>(a.part_acc + (base + c0 + u) * kHD + lane * 4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float2 ml0 = c0 + lane <= c1 ? a.part_ml[base + c0 + lane] : make_float2(-INFINITY, 0.f);
+    float M = ml0.x;
+    for (int c = c0 + 32 + lane; c <= c1; c += 32) M = fmaxf(M, a.part_ml[base + c].x);
+    M = warp_max(M);
+    float L = (ml0.x == -INFINITY) ? 0.f : ml0.y * expf(ml0.x - M);
+    for (int c = c0 + 32 + lane; c <= c1; c += 32) {
+        const float2 ml = a.part_ml[base + c];
+        L += (ml.x == -INFINITY) ? 0.f : ml.y * expf(ml.x - M);
+    }
+    L = warp_sum(L);
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int cc = c0; cc <= c1; cc += U) {
+        if (cc > c0) {
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                ac[u] = cc + u <= c1 ? *reinterpret_cast<const float4*>(a.part_acc + (base + cc + u) * kHD + lane * 4)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = cc + u;
+            if (c > c1) break;
+            const float mx = c - c0 < 32 ? __shfl_sync(0xffffffffu, ml0.x, c - c0) : a.part_ml[base + c].x;
+            const float f = (mx == -INFINITY) ? 0.f : expf(mx - M);
+            o[0] = fmaf(ac[u].x, f, o[0]);
+            o[1] = fmaf(ac[u].y, f, o[1]);
+            o[2] = fmaf(ac[u].z, f, o[2]);
+            o[3] = fmaf(ac[u].w, f, o[3]);
+        }
+    }
+    const float inv = 1.0f / L;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] *= inv;
+    // Q8_0 blocks: dims [32*bk, 32*bk+32) are lanes 8*bk..8*bk+7 (4 values each), as attn_combine_row
+    float am = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    const float d = __fdiv_rn(am, 127.0f);
+    int q[4] = {0, 0, 0, 0};
+    if (am != 0.0f) {
+        const float id = __fdiv_rn(1.0f, d);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int r = __float2int_rn(__fmul_rn(o[e], id));
+            q[e] = r > 127 ? 127 : (r < -128 ? -128 : r);
+        }
+    }
+    int qsum = q[0] + q[1] + q[2] + q[3];
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, off);
+    const uint32_t packed = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
+                            ((uint32_t)(q[3] & 0xFF) << 24);
+    const int blk = h * (kHD / 32) + (lane >> 3);
+    wimg_put_word(a.wimg, a.tok0 + s, blk, lane & 7, packed);
+    if ((lane & 7) == 0) wimg_put_meta(a.wimg, a.tok0 + s, blk, d, qsum);
 }
 
 // Control blocks of a forward of T tokens per stream: tokens[b * stride + col0 + j], position pos[b] (or col0).
@@ -731,7 +801,7 @@ int enqueue_bforward(sd_batch* b, int T, bool logits) {
         ba.n_streams = b->B;
         k_battn_partial<<<std::min(2 * b->sms, b->B * b->max_chunks * m.n_kv), kAttnThreads, battn_smem_bytes(), b->st>>>(ba);
         CK(cudaGetLastError(), "attention");
-        k_battn_combine<<<M * m.n_heads, combine_warps(b->max_seq) * 32, 0, b->st>>>(ba);
+        k_battn_combine<<<(M * m.n_heads + kBCombWarps - 1) / kBCombWarps, kBCombWarps * 32, 0, b->st>>>(ba);
         CK(cudaGetLastError(), "combine");
         // o-proj, residual + norm
         WgPlan po = P.wo;
