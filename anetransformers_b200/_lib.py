@@ -38,7 +38,7 @@ class ModelInfo(C.Structure):
 class CtxOpts(C.Structure):
     _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("max_batch", C.c_int), ("tp_rank", C.c_int),
                 ("tp_size", C.c_int), ("nccl_comm", C.c_void_p), ("use_graphs", C.c_int), ("use_pdl", C.c_int),
-                ("forward_kernel", C.c_int)]
+                ("forward_kernel", C.c_int), ("prefill_gemm", C.c_int)]
 
 
 class GenParams(C.Structure):

@@ -663,6 +663,7 @@ struct sd_batch {
     int* ndone = nullptr;     // [2]: streams done, most tokens a live stream still has to generate
     int* ndone_h = nullptr;   // pinned copy
     int gemm_mode = SD_BATCH_GEMM_AUTO;
+    bool shared_ring = false;  // kc / vc and st belong to the context (GEMM prefill of a single stream)
     BPlans plans[SD_BATCH_MAX_WIDTH + 1];
     cudaGraphExec_t fwd_graph[SD_BATCH_MAX_WIDTH + 1][2] = {};
     cudaGraphExec_t iter_graph = nullptr;
@@ -1022,13 +1023,17 @@ void sd_batch_free(sd_batch* b) {
     for (auto* v : {&b->wqkv, &b->wwo, &b->ww13, &b->ww2})
         for (uint8_t* p : *v) cudaFree(p);
     cudaFree(b->wlm);
-    cudaFree(b->kc); cudaFree(b->vc); cudaFree(b->x); cudaFree(b->y); cudaFree(b->qkv); cudaFree(b->q);
+    if (!b->shared_ring) {
+        cudaFree(b->kc);
+        cudaFree(b->vc);
+    }
+    cudaFree(b->x); cudaFree(b->y); cudaFree(b->qkv); cudaFree(b->q);
     cudaFree(b->img_x); cudaFree(b->img_attn); cudaFree(b->img_h); cudaFree(b->part_ml); cudaFree(b->part_acc);
     cudaFree(b->logits); cudaFree(b->argmax); cudaFree(b->probs); cudaFree(b->ctrl); cudaFree(b->tok);
     cudaFree(b->pos_dev); cudaFree(b->gs); cudaFree(b->g_out); cudaFree(b->g_hist); cudaFree(b->ndone);
     if (b->gs_h) cudaFreeHost(b->gs_h);
     if (b->ndone_h) cudaFreeHost(b->ndone_h);
-    if (b->st) cudaStreamDestroy(b->st);
+    if (b->st && !b->shared_ring) cudaStreamDestroy(b->st);
     delete b;
 }
 
@@ -1053,10 +1058,17 @@ int sd_batch_set_gemm(sd_batch* b, int mode) {
     return SD_OK;
 }
 
-int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_batch** out) {
-    clear_error();
-    if (!ctx || !out || n_streams < 1 || max_seq < 16 || max_width < 1 || max_width > SD_BATCH_MAX_WIDTH)
-        return fail(SD_ERR_INVALID, "sd_batch_create: bad arguments");
+}  // extern "C"
+
+namespace {
+
+// The context's K/V ring and stream, for a batch whose streams are slices of one prompt.
+struct SharedRing {
+    __half *kc, *vc;
+    cudaStream_t st;
+};
+
+int batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, const SharedRing* shared, sd_batch** out) {
     *out = nullptr;
     sd_batch* b = new sd_batch();
     int rc = sd_ctx_model_view(ctx, &b->m);
@@ -1078,17 +1090,26 @@ int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_b
     b->max_smem = device_max_smem(b->dev) - 1024;  // room for the GEMM's static shared memory
     b->max_chunks = (max_seq + b->chunk - 1) / b->chunk;
     if (cudaSetDevice(b->dev) != cudaSuccess) return bail(fail(SD_ERR_INVALID, "bad device %d", b->dev));
-    if ((rc = ck(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking), "stream"))) return bail(rc);
+    if (shared) {
+        b->shared_ring = true;
+        b->st = shared->st;
+        b->kc = shared->kc;
+        b->vc = shared->vc;
+    } else if ((rc = ck(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking), "stream"))) {
+        return bail(rc);
+    }
     if ((rc = ck(wgemm_init_attrs(b->max_smem), "gemm attributes"))) return bail(rc);
     if ((rc = ck(tcgemm_init_attrs(b->max_smem), "tcgen05 gemm attributes"))) return bail(rc);
     if ((rc = ck(cudaFuncSetAttribute(k_battn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)battn_smem_bytes()),
                  "attention attributes")))
         return bail(rc);
-    b->kv_stream = (size_t)max_seq * m.kv_rows;
-    b->kv_layer = (size_t)n_streams * b->kv_stream;
+    // a shared ring is the context's [layer][max_seq][kv_rows]: every stream of the batch addresses the same rows
+    b->kv_stream = shared ? 0 : (size_t)max_seq * m.kv_rows;
+    b->kv_layer = shared ? (size_t)max_seq * m.kv_rows : (size_t)n_streams * b->kv_stream;
     const size_t M = b->M_max;
     const size_t parts = (size_t)M * m.n_heads * b->max_chunks;
-    if ((rc = dalloc(&b->kc, (size_t)m.n_layers * b->kv_layer)) || (rc = dalloc(&b->vc, (size_t)m.n_layers * b->kv_layer)) ||
+    if ((!shared && ((rc = dalloc(&b->kc, (size_t)m.n_layers * b->kv_layer)) ||
+                     (rc = dalloc(&b->vc, (size_t)m.n_layers * b->kv_layer)))) ||
         (rc = dalloc(&b->x, M * m.dim)) || (rc = dalloc(&b->y, (size_t)b->kp_max * M * m.dim)) ||
         (rc = dalloc(&b->qkv, (size_t)b->kp_max * M * m.qkv_rows)) || (rc = dalloc(&b->q, M * m.q_rows)) ||
         (rc = dalloc(&b->img_x, wimg_bytes((int)M, m.dim))) || (rc = dalloc(&b->img_attn, wimg_bytes((int)M, m.q_rows))) ||
@@ -1122,13 +1143,65 @@ int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_b
     cudaMemsetAsync(b->x, 0, M * m.dim * sizeof(float), b->st);
     cudaMemsetAsync(b->ctrl, 0, sizeof(DevCtrl) * n_streams, b->st);
     // rings start as fp16 zeros (positions never written read as zeros, never as stale bytes)
-    cudaMemsetAsync(b->kc, 0, (size_t)m.n_layers * b->kv_layer * sizeof(__half), b->st);
-    cudaMemsetAsync(b->vc, 0, (size_t)m.n_layers * b->kv_layer * sizeof(__half), b->st);
+    if (!shared) {
+        cudaMemsetAsync(b->kc, 0, (size_t)m.n_layers * b->kv_layer * sizeof(__half), b->st);
+        cudaMemsetAsync(b->vc, 0, (size_t)m.n_layers * b->kv_layer * sizeof(__half), b->st);
+    }
     cudaMemsetAsync(b->gs, 0, sizeof(GenState) * n_streams, b->st);
     if ((rc = finish(b))) return bail(rc);
     *out = b;
     return SD_OK;
 }
+
+}  // namespace
+
+extern "C" {
+
+int sd_batch_create(sd_ctx* ctx, int n_streams, int max_seq, int max_width, sd_batch** out) {
+    clear_error();
+    if (!ctx || !out || n_streams < 1 || max_seq < 16 || max_width < 1 || max_width > SD_BATCH_MAX_WIDTH)
+        return fail(SD_ERR_INVALID, "sd_batch_create: bad arguments");
+    return batch_create(ctx, n_streams, max_seq, max_width, nullptr, out);
+}
+
+}  // extern "C"
+
+namespace sd {
+
+int batch_create_prefill(sd_ctx* ctx, int n_slices, int width, void* kc, void* vc, int max_seq, cudaStream_t st,
+                         sd_batch** out) {
+    const SharedRing sr{reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), st};
+    return batch_create(ctx, n_slices, max_seq, width, &sr, out);
+}
+
+// Chunks of n_slices x width prompt tokens; slice v of a chunk starting at prompt index i takes tokens
+// [i + width v, i + width v + width) at position start_pos + i + width v (a short last slice has fewer valid
+// tokens, slices past the prompt are marked done).  The RoPE kernel writes every valid token's K/V into the
+// context's ring before the attention kernel reads it, so each slice attends to the whole prefix before it.
+int batch_prefill_ring(sd_batch* b, const int32_t* tokens, int n, int start_pos) {
+    const int W = b->W, chunk = b->B * W;
+    std::vector<DevCtrl> hc(b->B);
+    for (int i = 0; i < n; i += chunk) {
+        for (int v = 0; v < b->B; ++v) {
+            DevCtrl& c = hc[v];
+            memset(&c, 0, sizeof(c));
+            const int first = i + v * W, nv = std::max(0, std::min(W, n - first));
+            c.pos = start_pos + first;
+            c.n_valid = nv;
+            c.done = nv == 0;
+            for (int j = 0; j < nv; ++j) c.tokens[j] = tokens[first + j];
+        }
+        // from pageable memory: the call returns once the host array has been read
+        CK(cudaMemcpyAsync(b->ctrl, hc.data(), sizeof(DevCtrl) * b->B, cudaMemcpyHostToDevice, b->st), "prefill ctrl");
+        int rc = run_bforward(b, W, false);
+        if (rc) return rc;
+    }
+    return SD_OK;
+}
+
+}  // namespace sd
+
+extern "C" {
 
 int sd_batch_forward(sd_batch* b, const int32_t* tokens, int T, const int32_t* pos, float* logits) {
     clear_error();

@@ -240,6 +240,9 @@ struct sd_ctx {
     int dev = 0;
     cudaStream_t st = nullptr;
     bool use_graphs = true, use_pdl = true;
+    bool prefill_gemm = true;       // long prompts through the batched engine's GEMMs (gemm_prefill)
+    bool pf_unsupported = false;    // the batched engine declined this model: matvec prefill only
+    sd_batch* pf = nullptr;         // the prefill batch over this context's ring, made at the first long prompt
     // model
     int dim, hidden, n_layers, n_heads, n_kv, hd, vocab, max_seq, bos, eos;
     float theta, eps;
@@ -768,12 +771,14 @@ void sd_ctx_opts_default(sd_ctx_opts* o) {
     o->use_graphs = 1;
     o->use_pdl = 1;
     o->forward_kernel = 1;
+    o->prefill_gemm = 1;
 }
 
 void sd_ctx_free(sd_ctx* c) {
     if (!c) return;
     cudaSetDevice(c->dev);
     if (c->st) cudaStreamSynchronize(c->st);
+    sd_batch_free(c->pf);  // reads this context's weights and ring
     for (auto& g : c->fwd_graph)
         if (g) cudaGraphExecDestroy(g);
     for (auto& g : c->fwd_graph_kv)
@@ -813,6 +818,7 @@ static int ctx_build(const void* base, size_t len, const sd_ctx_opts* opts, sd_c
     c->dev = o.device;
     c->use_graphs = o.use_graphs != 0;
     c->use_pdl = o.use_pdl != 0;
+    c->prefill_gemm = o.prefill_gemm != 0;
     c->tp_rank = o.tp_rank;
     c->tp_size = o.tp_size < 1 ? 1 : o.tp_size;
     c->nccl = o.nccl_comm;
@@ -1212,6 +1218,36 @@ int sd_logits(sd_ctx* c, const float* x, int S, float* logits) {
     return finish(c);
 }
 
+// Prompt tokens [0, n) at start_pos .. into the ring through the batched engine's GEMMs: 64 slices of 8 tokens per
+// forward (M = 512 on the tcgen05 GEMM), so every weight tile read from HBM serves 512 tokens instead of 8.
+// *used = false (and nothing enqueued) when the prompt is short, the option is off or the batched engine does not
+// serve this model (tensor parallelism, K-quant embedding or LM head).
+namespace {
+
+constexpr int kGemmPrefillMin = 256;
+constexpr int kPrefillSlices = 64;
+
+int gemm_prefill(sd_ctx* c, const int32_t* tokens, int n, int start_pos, bool* used) {
+    *used = false;
+    if (!c->prefill_gemm || c->pf_unsupported || n < kGemmPrefillMin || c->tp_size > 1 || c->lm_type != 2 ||
+        c->embd_type != 2)
+        return SD_OK;
+    if (!c->pf) {
+        const int rc = batch_create_prefill(c, kPrefillSlices, kMaxS, c->kc, c->vc, c->max_seq, c->st, &c->pf);
+        if (rc == SD_ERR_UNSUPPORTED) {
+            c->pf_unsupported = true;
+            clear_error();
+            return SD_OK;
+        }
+        if (rc) return rc;
+    }
+    const int rc = batch_prefill_ring(c->pf, tokens, n, start_pos);
+    if (!rc) *used = true;
+    return rc;
+}
+
+}  // namespace
+
 int sd_prefill(sd_ctx* c, const int32_t* tokens, int n, int start_pos) {
     clear_error();
     if (!c || !tokens || n < 0 || start_pos < 0) return fail(SD_ERR_INVALID, "sd_prefill: bad arguments");
@@ -1219,7 +1255,9 @@ int sd_prefill(sd_ctx* c, const int32_t* tokens, int n, int start_pos) {
     int rc = check_tokens(c, tokens, n);
     if (rc) return rc;
     cudaSetDevice(c->dev);
-    for (int i = 0; i < n; i += c->MB) {
+    bool gemm = false;
+    if ((rc = gemm_prefill(c, tokens, n, start_pos, &gemm))) return rc;
+    for (int i = gemm ? n : 0; i < n; i += c->MB) {
         const int S = std::min(c->MB, n - i);
         if ((rc = set_ctrl(c, c->ctrl, tokens + i, S, start_pos + i, true))) return rc;
         if ((rc = run_forward(c, S, false))) return rc;
@@ -1576,8 +1614,12 @@ int sd_generate(sd_ctx* c, const sd_gen_params* gp, const int32_t* prompt, int n
     if (rc) return rc;
     cudaSetDevice(c->dev);
     const double t0 = now_ms();
-    // prefill (W4A8 chunks of max_batch tokens); logits of the last prompt token
-    for (int i = 0; i < n_prompt; i += c->MB) {
+    // prefill: all but the last chunk through the GEMMs when the prompt is long, the rest in W4A8 chunks of
+    // max_batch tokens; logits of the last prompt token
+    const int tail = (n_prompt - 1) % c->MB + 1;
+    bool gemm = false;
+    if ((rc = gemm_prefill(c, prompt, n_prompt - tail, 0, &gemm))) return rc;
+    for (int i = gemm ? n_prompt - tail : 0; i < n_prompt; i += c->MB) {
         const int S = std::min(c->MB, n_prompt - i);
         if ((rc = set_ctrl(c, c->ctrl, prompt + i, S, i, true))) return rc;
         if ((rc = run_forward(c, S, i + S >= n_prompt))) return rc;  // logits of the last chunk only

@@ -42,4 +42,15 @@ struct ModelView {
 }  // namespace sd
 
 struct sd_ctx;
+struct sd_batch;
 int sd_ctx_model_view(sd_ctx* c, sd::ModelView* out);  // defined in sd_engine.cu
+
+namespace sd {
+// A batch of n_slices x width tokens per forward whose streams all address the context's own K/V ring
+// (kc / vc: [layer][max_seq][kv_rows] fp16) and run on the context's stream: single-stream prompt prefill
+// through the wide GEMMs (sd_batch.cu).  Released with sd_batch_free.
+int batch_create_prefill(sd_ctx* ctx, int n_slices, int width, void* kc, void* vc, int max_seq, cudaStream_t st,
+                         sd_batch** out);
+// Write the K/V of prompt tokens [0, n) at positions start_pos .. into that ring (no logits).
+int batch_prefill_ring(sd_batch* b, const int32_t* tokens, int n, int start_pos);
+}  // namespace sd

@@ -59,7 +59,7 @@ class Context:
 
     def __init__(self, model, device: int = 0, max_seq: int = 0, max_batch: int = 0, use_graphs: bool = True,
                  use_pdl: bool = True, tp_rank: int = 0, tp_size: int = 1, nccl_comm: int = 0,
-                 forward_kernel: Optional[int] = None):
+                 forward_kernel: Optional[int] = None, prefill_gemm: Optional[bool] = None):
         L = _lib.lib()
         o = _lib.CtxOpts()
         L.sd_ctx_opts_default(C.byref(o))
@@ -67,6 +67,8 @@ class Context:
         o.use_graphs, o.use_pdl = int(use_graphs), int(use_pdl)
         if forward_kernel is not None:
             o.forward_kernel = int(forward_kernel)
+        if prefill_gemm is not None:
+            o.prefill_gemm = int(prefill_gemm)
         o.tp_rank, o.tp_size, o.nccl_comm = tp_rank, tp_size, nccl_comm or None
         h = C.c_void_p()
         if isinstance(model, (bytes, bytearray, memoryview)):

@@ -566,7 +566,9 @@ def run_forward(args):
     if not os.path.exists(path):
         G.write_synthetic_gguf_parallel(path, cfg, seed=0)
     S = args.S or SPEC_K + 1
-    ctx = Context(path, max_seq=args.ctx + S * (args.steps + args.warmup) + 64, forward_kernel=args.forward_kernel)
+    # matvec prefill: the workload times verify forwards, and the ncu commands of profiles/ count its launches
+    ctx = Context(path, max_seq=args.ctx + S * (args.steps + args.warmup) + 64, forward_kernel=args.forward_kernel,
+                  prefill_gemm=False)
     rng = np.random.default_rng(5)
     ctx.prefill(rng.integers(3, 32000, args.ctx).tolist(), 0)
     pos = args.ctx
@@ -754,8 +756,11 @@ def main():
     torch.cuda.synchronize()
     req_s = time.perf_counter() - t0
     e2e_request = {"value": round(len(out) / req_s, 2), "unit": UNIT, "ms_per_request": round(1e3 * req_s, 2),
-                   "what": "sd_generate: 1024-token prompt from host, prefill in 8-token W4A8 forwards, first token, "
-                           "512-token decode, tokens to host"}
+                   "what": "sd_generate: 1024-token prompt from host, prefill " +
+                           ("in 8-token W4A8 forwards (tensor parallel)" if tp and world > 1 else
+                            "of the first 1016 tokens through the batched tensor-core GEMMs (64 slices of 8 tokens per "
+                            "forward) and of the last 8 in one W4A8 forward") +
+                           ", first token, 512-token decode, tokens to host"}
     roof = forward_roofline(ctx, peaks, world, tp)
     roof_gemv = gemv_roofline(peaks) if rank == 0 else None
     cfg1 = config1_numbers(peaks) if rank == 0 else None

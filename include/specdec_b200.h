@@ -155,6 +155,11 @@ typedef struct {
     int forward_kernel;   /* 1 = each forward is one persistent kernel (default; tensor-parallel contexts
                              once their peers are connected), 0 = one kernel per op; both give
                              bit-identical logits */
+    int prefill_gemm;     /* 1 (default): sd_prefill / sd_generate run prompts of at least 256 tokens through the
+                             batched engine's tensor-core GEMMs (64 slices of 8 tokens per forward, all writing this
+                             context's K/V ring) instead of 8-token matvec forwards; single-GPU contexts with a
+                             Q4_0 embedding and LM head.  Logits agree with the matvec path within the batched
+                             path's tolerance (its attention uses single fp16 Q and P).  0 = always matvecs. */
 } sd_ctx_opts;
 
 SD_API void sd_ctx_opts_default(sd_ctx_opts *o);
