@@ -326,7 +326,9 @@ static int matvec_common(int epi, const sd_qmat* W, sd_q8_dev x, float* y, int32
             a.out = y;
         }
     }
-    cudaError_t e = launch_gemv(epi, a, grid, smem, st, false);
+    // Programmatic dependent launch: the producer streams the matrix (written once, at sd_qmat_create) while the
+    // stream's previous kernel drains; the kernel waits for that kernel before it reads x or writes y.
+    cudaError_t e = launch_gemv(epi, a, grid, smem, st, true);
     if (e == cudaSuccess && parts) e = launch_sum_parts(parts, y, (int)n_out, a.kparts, n_out, st);
     return e == cudaSuccess ? SD_OK : cuda_fail(e, "matvec launch");
 }
