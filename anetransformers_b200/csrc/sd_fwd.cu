@@ -205,6 +205,7 @@ __device__ void stage_image(const FwdArgs& a, const ActImage& im, const ActSmem&
 // ---------------------------------------------------------------------------------------------
 enum PhaseKind : int { PH_QKV = 0, PH_WO = 1, PH_W13 = 2, PH_W2 = 3, PH_LM = 4 };
 constexpr int kMaxParts = 8;  // K slices of a matvec whose outputs a residual phase adds
+constexpr int kGather = 8;    // (rank, slice) values a reduction lane loads before adding
 
 
 // Argmax key of logit v at row `row`: larger keys for larger logits, and for equal logits for the smaller
@@ -246,15 +247,30 @@ __device__ void red_block(const FwdArgs& a, const float* const* ysrc, int nsrc, 
     const int row = b * 32 + lane;
     const float xv = a.x[(size_t)s * a.dim + row];
     const float w = wn[row];
+    const size_t off = (size_t)s * a.dim + row;
     float t = 0.f;
-    for (int r = 0; r < nsrc; ++r) {
-        float yv[kMaxParts];
+    const int nl = nsrc * kparts;
+    if (nl <= kGather) {
+        // every (rank, slice) value requested before the first add: one NVLink round trip per reduction instead
+        // of one per rank; the adds keep the rank-major, slice-minor order
+        float yv[kGather];
 #pragma unroll
-        for (int p = 0; p < kMaxParts; ++p)
-            yv[p] = p < kparts ? __ldcg(ysrc[r] + (size_t)p * a.ypart_stride + (size_t)s * a.dim + row) : 0.f;
+        for (int i = 0; i < kGather; ++i) {
+            const int r = i / kparts, p = i - r * kparts;
+            yv[i] = i < nl ? __ldcg(ysrc[r] + (size_t)p * a.ypart_stride + off) : 0.f;
+        }
 #pragma unroll
-        for (int p = 0; p < kMaxParts; ++p)
-            if (p < kparts) t += yv[p];
+        for (int i = 0; i < kGather; ++i)
+            if (i < nl) t += yv[i];
+    } else {
+        for (int r = 0; r < nsrc; ++r) {
+            float yv[kMaxParts];
+#pragma unroll
+            for (int p = 0; p < kMaxParts; ++p) yv[p] = p < kparts ? __ldcg(ysrc[r] + (size_t)p * a.ypart_stride + off) : 0.f;
+#pragma unroll
+            for (int p = 0; p < kMaxParts; ++p)
+                if (p < kparts) t += yv[p];
+        }
     }
     finish_block(a, s, b, xv + t, w, lane);
 }
