@@ -112,6 +112,8 @@ def lib() -> C.CDLL:
             "or_spec_sample_probs": (i32, [vp, i32, vp]),
             "or_spec_accept": (i32, [vp, vp, vp, i32, i32, f32, vp, vp]),
             "or_ngram_scan": (i32, [vp, i32, i32, i32, i32, vp, vp]),
+            "or_ngram_init": (i32, [vp, vp, i32, i32, i32]), "or_ngram_push": (None, [vp, i32]),
+            "or_ngram_free": (None, [vp]), "or_ngram_draft": (i32, [vp, i32, vp, vp]),
             "or_generate_greedy": (i32, [vp, vp, i32, vp, vp, vp]),
             "or_generate_ngram": (i32, [vp, vp, i32, vp, vp, vp]),
             "or_generate_self_spec": (i32, [vp, vp, i32, vp, vp, vp]),
@@ -304,6 +306,30 @@ def ngram_scan(history, ngram_n: int, max_draft: int, current: int):
     mp = C.c_int(-1)
     n = lib().or_ngram_scan(_p(h) if h.size else None, h.size, ngram_n, max_draft, current, _p(dt), C.addressof(mp))
     return dt[:n].tolist(), mp.value
+
+
+class NGram(C.Structure):
+    _fields_ = [("history", C.c_void_p), ("history_len", C.c_int), ("history_cap", C.c_int), ("ngram_n", C.c_int),
+                ("max_draft", C.c_int)]
+
+
+def ngram_draft(prompt, pushed, ngram_n: int, max_draft: int, current: int):
+    """speculative.h:395-464 through the oracle's drafter object: init on prompt (ngram_n / max_draft defaults and
+    the SPEC_MAX_DRAFT clip applied there), push each of pushed, draft after current.  Returns (tokens, probs)."""
+    L = lib()
+    pr = np.ascontiguousarray(prompt, np.int32)
+    d = NGram()
+    if L.or_ngram_init(C.addressof(d), _p(pr) if pr.size else None, pr.size, ngram_n, max_draft):
+        raise MemoryError("or_ngram_init")
+    try:
+        for t in pushed:
+            L.or_ngram_push(C.addressof(d), int(t))
+        dt = np.zeros(16, np.int32)
+        dp = np.zeros(16, np.float32)
+        n = L.or_ngram_draft(C.addressof(d), current, _p(dt), _p(dp))
+        return dt[:n].tolist(), dp[:n].tolist()
+    finally:
+        L.or_ngram_free(C.addressof(d))
 
 
 class OracleModel:
