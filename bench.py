@@ -18,7 +18,8 @@ scaling, value = all ranks' tokens / max-over-ranks time).
 --impl reference: the reference's CPU decode path, restated in C (oracle/, the reference itself needs
 arm_neon.h / GCD / Accelerate and does not compile on x86), timed on the host cores on a bounded sample.
 
-Other workloads (--workload): selfspec = config 4 (self-speculation, 32K context), gemv = config 1 (single
+Other workloads (--workload): greedy = config 2 (greedy decode without speculation, 128-token prompt, 256
+tokens), selfspec = config 4 (self-speculation, 32K context), gemv = config 1 (single
 W4A8 matvec), serving = config 5 (64 streams per GPU through the batched path, 4096-token contexts, K=4 n-gram,
 one batch per rank under torchrun), forward / serving-forward = single forwards for profiling.
 """
@@ -42,6 +43,8 @@ UNIT = "tok/s"
 PROMPT_LEN, GEN_TOKENS, NGRAM_N, SPEC_K = 1024, 512, 3, 4
 # self-speculative decode, K = 8 drafts from the first 8 layers, 32768-position KV
 SELF_CTX, SELF_TOKENS, SELF_K, SELF_LAYERS = 32768, 256, 8, 8
+GREEDY_PROMPT, GREEDY_TOKENS = 128, 256
+GREEDY_PUBLISHED = 17.8  # tok/s: the reference's published non-speculative decode of 256 tokens (its README.md:137)
 def kernels_per_iter(persistent: bool, tp_peer: bool = False, tp_nccl: bool = False, layers: int = 32) -> int:
     """Our kernel launches per n-gram decode iteration: prepare + commit around one verify forward, which
     is k_forward + argmax on the persistent path, or embed-norm, 8 per layer, LM head + argmax per op.
@@ -319,6 +322,70 @@ def run_gemv(args):
                       "config": {"workload": f"BASELINE config 1: Q4_0 {rows}x{cols} x Q8_0, rotating weight copies > L2"},
                       "per_S": out, "peak": peaks.get("hbm_gbs"),
                       "frac": round(best / peaks.get("hbm_gbs", 6650.0), 4)}), flush=True)
+
+
+def run_greedy(args, ctx, rank, world, local, dist, tp, peaks):
+    """plain greedy decode, no speculation: a 128-token prompt of uniform-random token ids
+    (prefilled once, outside the timed region), then 256 greedy tokens per step through sd_decode, one S = 1
+    forward per token.  A step = one 256-token decode from the prefilled prompt."""
+    import torch
+    rng = np.random.default_rng(128)
+    prompt = rng.integers(3, 32000, GREEDY_PROMPT).tolist()
+    first, _ = ctx.generate(prompt, mode="greedy", max_tokens=1, temp=0.0, rep_penalty=1.0, ignore_eos=True)
+    hist = prompt + [first[0]]
+    kw = dict(mode="greedy", max_tokens=args.tokens, temp=0.0, rep_penalty=1.0, ignore_eos=True)
+    for _ in range(args.warmup):
+        ctx.decode(hist, first[0], **kw)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    clocks = ClockSampler(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    tokens = 0
+    for _ in range(args.steps):
+        out, _ = ctx.decode(hist, first[0], **kw)
+        tokens += len(out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max, tokens_all = aggregate_ranks(dist, ms, tokens, tp)
+    value = tokens_all / (ms_max * 1e-3)
+    # one S = 1 forward per token: this rank's weights + the K/V it attends (middle of the decode)
+    ranks = world if tp else 1
+    fwd_b = ((BYTES_PER_FORWARD - 73_728_000) // ranks + 73_728_000 +
+             KV_BYTES_PER_POS // ranks * (GREEDY_PROMPT + args.tokens // 2))
+    fwd_per_s = (tokens / args.steps) / (ms / args.steps * 1e-3)
+    step_roof = {"bytes_per_forward": fwd_b, "forwards_per_s": round(fwd_per_s, 2),
+                 "achieved_gbs": round(fwd_b * fwd_per_s / 1e9, 1)}
+    step_roof["frac_of_hbm"] = round(step_roof["achieved_gbs"] / peaks.get("hbm_gbs", 6650.0), 4)
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+                "scaling": "strong" if tp else "weak", "vs_baseline": round(value / GREEDY_PUBLISHED, 2),
+                "vs_baseline_ref": f"{GREEDY_PUBLISHED} tok/s: the reference's published non-speculative decode of 256 "
+                                   "tokens on an M5 (CPU NEON SDOT)",
+                "dtype": "int8 x int4 -> int32 MMA, fp32 accumulate",
+                "data": "synthetic: seeded random-init Q4_0 weights of the Mistral-7B-v0.2 architecture, "
+                        "uniform-random token ids",
+                "config": {"workload": "BASELINE config 2: greedy decode without speculation, 128-token random "
+                                       "prompt, 256 generated tokens per step",
+                           "model": "Mistral-7B-v0.2 (32 x 4096, FFN 14336, 32/8 heads, vocab 32000) Q4_0",
+                           "global_batch": 1 if tp else world, "seq_len": GREEDY_PROMPT + args.tokens,
+                           "parallelism": ((f"tp{world} ({args.tp_allreduce} all-reduce)" if tp else f"dp{world}")
+                                           if world > 1 else "single GPU"),
+                           "l2": "no flush: each forward streams 4.0 GB of weights (> 126 MB L2)"},
+                "step_roofline": step_roof, "clocks": clk,
+                # one iteration per token: prepare + commit around the S = 1 forward
+                "gpu_launches": int(tokens * kernels_per_iter(bool(ctx.info.forward_kernel),
+                                                              tp and args.tp_allreduce == "peer",
+                                                              tp and args.tp_allreduce == "nccl"))}
+        print(json.dumps(line), flush=True)
 
 
 def run_selfspec(args, ctx, rank, world, local, dist, tp, peaks):
@@ -603,8 +670,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=None, help="generated tokens per step (default: the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="specdec",
-                    choices=["specdec", "selfspec", "gemv", "forward", "serving", "serving-forward"],
-                    help="specdec = BASELINE config 3 (the default line), selfspec = config 4, gemv = config 1, "
+                    choices=["specdec", "greedy", "selfspec", "gemv", "forward", "serving", "serving-forward"],
+                    help="specdec = BASELINE config 3 (the default line), greedy = config 2, selfspec = config 4, "
+                         "gemv = config 1, "
                          "serving = config 5 (batched streams), forward = single verify forwards (profiling: "
                          "--layers, --S, --ctx)")
     ap.add_argument("--streams", type=int, default=SERVE_STREAMS, help="serving: streams per GPU")
@@ -627,7 +695,8 @@ def main():
     if args.parallel is None:
         args.parallel = "dp" if args.workload == "serving" else "tp"
     if args.tokens is None:
-        args.tokens = {"selfspec": SELF_TOKENS, "serving": SERVE_TOKENS}.get(args.workload, GEN_TOKENS)
+        args.tokens = {"selfspec": SELF_TOKENS, "serving": SERVE_TOKENS, "greedy": GREEDY_TOKENS}.get(args.workload,
+                                                                                                    GEN_TOKENS)
     if args.workload == "gemv":
         run_gemv(args)
         return
@@ -674,7 +743,7 @@ def main():
             uid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         comm = NcclComm(bytes(uid.cpu().numpy().tobytes()), world, rank, local)
-    n_ctx = SELF_CTX if args.workload == "selfspec" else PROMPT_LEN
+    n_ctx = SELF_CTX if args.workload == "selfspec" else GREEDY_PROMPT if args.workload == "greedy" else PROMPT_LEN
     ctx = Context(path, device=local, max_seq=n_ctx + args.tokens + 64, forward_kernel=args.forward_kernel,
                   tp_rank=rank if tp else 0, tp_size=world if tp else 1, nccl_comm=comm.handle if comm else 0)
     if tp and args.tp_allreduce == "peer":
@@ -682,8 +751,8 @@ def main():
         handles = [None] * world
         dist.all_gather_object(handles, ctx.tp_handle())
         ctx.tp_connect(handles)
-    if args.workload == "selfspec":
-        run_selfspec(args, ctx, rank, world, local, dist, tp, peaks)
+    if args.workload in ("selfspec", "greedy"):
+        (run_selfspec if args.workload == "selfspec" else run_greedy)(args, ctx, rank, world, local, dist, tp, peaks)
         ctx.close()
         if comm:
             comm.close()
