@@ -97,12 +97,14 @@ __device__ __forceinline__ void wimg_put_meta(const WImg& im, int m, int blk, fl
 
 // Stage Q8 planes (global, row stride K) blocks [kb0, kb0 + nb) of tokens < nv into A.  Loads are
 // issued in batches of four per thread before any store, so a staging costs about one memory round trip.
+// The code slots of tokens >= nv are left as they are: each MMA output column depends only on its own
+// token's fragments, and no epilogue reads the columns of tokens >= nv.
 // tok_scale (optional, shared memory): per-token factor applied to the block scales (the RMSNorm
 // scale when the planes hold Q8_0 of x*w).
 __device__ inline void stage_act_from_planes(const ActSmem& A, const Q8Planes& act, int K, int kb0, int nb, int S, int nv,
                                              int tid, int nthr, const float* tok_scale = nullptr) {
     constexpr int U = 4;
-    const int n16 = kMaxS * nb * 2;  // every token slot; tokens >= nv are zero
+    const int n16 = nv * nb * 2;  // 16-byte halves of the valid tokens' blocks
     for (int i0 = tid; i0 < n16; i0 += U * nthr) {
         uint4 v[U];
 #pragma unroll
