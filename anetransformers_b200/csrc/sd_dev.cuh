@@ -96,38 +96,67 @@ __device__ __forceinline__ void wimg_put_meta(const WImg& im, int m, int blk, fl
 }
 
 // Stage Q8 planes (global, row stride K) blocks [kb0, kb0 + nb) of tokens < nv into A.  Loads are
-// issued in batches of four per thread before any store, so a staging costs about one memory round trip.
+// issued in batches before any store, so a staging costs about one memory round trip.
 // The code slots of tokens >= nv are left as they are: each MMA output column depends only on its own
 // token's fragments, and no epilogue reads the columns of tokens >= nv.
 // tok_scale (optional, shared memory): per-token factor applied to the block scales (the RMSNorm
 // scale when the planes hold Q8_0 of x*w).
 __device__ inline void stage_act_from_planes(const ActSmem& A, const Q8Planes& act, int K, int kb0, int nb, int S, int nv,
                                              int tid, int nthr, const float* tok_scale = nullptr) {
-    constexpr int U = 4;
-    const int n16 = nv * nb * 2;  // 16-byte halves of the valid tokens' blocks
-    for (int i0 = tid; i0 < n16; i0 += U * nthr) {
-        uint4 v[U];
+    // Codes, three tokens or more: one warp per block at a time, lane l = 4 s + tt building the B-fragment pair
+    // (word tt, word 4 + tt) of token s -- one 8-byte shared store per lane, the block's 256 bytes contiguous (no bank
+    // conflicts); each warp's loads for up to eight blocks are issued before its stores.  Fewer tokens would leave
+    // most lanes idle: 16-byte pieces per thread then (below).
+    if (nv >= 3) {
+        constexpr int UB = 8;
+        const int lane = tid & 31, w = tid >> 5, nw = nthr >> 5;
+        const int s = lane >> 2, tt = lane & 3;
+        if (s < nv) {
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(act.qs) + (size_t)s * K + (size_t)kb0 * 32 + 4 * tt;
+            for (int b0 = w; b0 < nb; b0 += UB * nw) {
+                uint32_t lo[UB], hi[UB];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = i0 + u * nthr;
-            v[u] = make_uint4(0, 0, 0, 0);
-            if (i < n16) {
-                const int s = i / (nb * 2), rem = i - s * (nb * 2);
-                if (s < nv)
-                    v[u] = *reinterpret_cast<const uint4*>(act.qs + (size_t)s * K + (size_t)(kb0 + (rem >> 1)) * 32 +
-                                                           (rem & 1) * 16);
+                for (int u = 0; u < UB; ++u) {
+                    const int b = b0 + u * nw;
+                    lo[u] = hi[u] = 0;
+                    if (b < nb) {
+                        lo[u] = *reinterpret_cast<const uint32_t*>(src + (size_t)b * 32);
+                        hi[u] = *reinterpret_cast<const uint32_t*>(src + (size_t)b * 32 + 16);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < UB; ++u) {
+                    const int b = b0 + u * nw;
+                    if (b < nb) A.b[(size_t)b * kActStride + lane] = make_uint2(lo[u], hi[u]);
+                }
             }
         }
+    } else {
+        constexpr int U = 4;
+        const int n16 = nv * nb * 2;  // 16-byte halves of the valid tokens' blocks
+        for (int i0 = tid; i0 < n16; i0 += U * nthr) {
+            uint4 v[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = i0 + u * nthr;
-            if (i < n16) {
-                const int s = i / (nb * 2), rem = i - s * (nb * 2);
-                uint32_t* base = reinterpret_cast<uint32_t*>(A.b + (size_t)(rem >> 1) * kActStride + 4 * s) + (rem & 1);
-                base[0] = v[u].x;
-                base[2] = v[u].y;
-                base[4] = v[u].z;
-                base[6] = v[u].w;
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * nthr;
+                v[u] = make_uint4(0, 0, 0, 0);
+                if (i < n16) {
+                    const int s = i / (nb * 2), rem = i - s * (nb * 2);
+                    v[u] = *reinterpret_cast<const uint4*>(act.qs + (size_t)s * K + (size_t)(kb0 + (rem >> 1)) * 32 +
+                                                           (rem & 1) * 16);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * nthr;
+                if (i < n16) {
+                    const int s = i / (nb * 2), rem = i - s * (nb * 2);
+                    uint32_t* base = reinterpret_cast<uint32_t*>(A.b + (size_t)(rem >> 1) * kActStride + 4 * s) + (rem & 1);
+                    base[0] = v[u].x;
+                    base[2] = v[u].y;
+                    base[4] = v[u].z;
+                    base[6] = v[u].w;
+                }
             }
         }
     }
