@@ -108,10 +108,12 @@ def test_matvec_matches_oracle(oracle, dq, rows, cols, S):
         assert np.all(np.abs(ref2 - ref) <= bound)
 
 
-@pytest.mark.parametrize("rows,cols,S", [(4096, 4096, 5), (4096, 14336, 8), (1024, 14336, 5)])
+@pytest.mark.parametrize("rows,cols,S", [(4096, 4096, 5), (4096, 14336, 8), (1024, 14336, 5), (2048, 4096, 2),
+                                         (2048, 4096, 3)])
 def test_matvec_batch_invariant(oracle, dq, rows, cols, S):
     """A token's result does not depend on the other tokens of the batch (S=1 vs S, bitwise), also for
-    long rows whose K range is split across CTAs at the larger S."""
+    long rows whose K range is split across CTAs at the larger S, and on both sides of the staging's switch
+    from per-thread 16-byte pieces (S <= 2) to one warp per block (S >= 3)."""
     import torch
     rng = np.random.default_rng(42 + cols)
     W = rand_q4(rng, rows, cols)
